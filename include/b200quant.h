@@ -1,0 +1,116 @@
+/* b200quant.h -- C ABI of libb200quant.so, the B200 (sm_100a) implementation
+ * of the GGML block-quant matvec/matmul and MoE FFN hot path of the LocalAI
+ * reference engine.
+ *
+ * Part 1 replaces the reference's native library symbol for symbol
+ * (engine/native_quant.cpp:705-768, bound by ctypes in
+ * engine/native_quant.py:76-94).  Pointers are caller-owned HOST memory; the
+ * call copies inputs to the GPU, runs the kernel, copies the result back and
+ * returns when the result is in ``out``.  ``threads`` is accepted for ABI
+ * compatibility and ignored.  The reference functions return nothing; here a
+ * failure is reported through b200q_last_status()/b200q_last_error(), which
+ * the Python wrapper checks after every call.
+ *
+ * Part 2 is the device-pointer API used by the PyTorch host code: all
+ * pointers are device memory, work is enqueued on ``stream`` (a
+ * cudaStream_t, NULL = legacy default stream) and the call returns without
+ * synchronising.  Status: 0 = ok, negative = error (message in
+ * b200q_last_error()).
+ *
+ * Calls are serialised by one library lock, like the reference's pool mutex
+ * (engine/native_quant.cpp:361-363).
+ */
+#ifndef B200QUANT_H
+#define B200QUANT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define B200Q_OK 0
+#define B200Q_EINVAL (-1)      /* bad type, size, pointer or alignment */
+#define B200Q_ECUDA (-2)       /* CUDA runtime error */
+#define B200Q_ETIMEOUT (-3)    /* a device-side wait hit its time limit */
+#define B200Q_ENODEV (-4)      /* no usable CUDA device */
+#define B200Q_EINDEX (-5)      /* a device-side index check failed */
+
+/* ---- Part 1: drop-in for engine/native_quant.cpp ---------------------- */
+/* engine/native_quant.cpp:705-709 */
+void localai_q8_0_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads);
+/* engine/native_quant.cpp:711-717 */
+void localai_q4_0_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads);
+/* engine/native_quant.cpp:719-725 */
+void localai_q4k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads);
+/* engine/native_quant.cpp:726-732 */
+void localai_q5k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads);
+/* engine/native_quant.cpp:733-738 */
+void localai_q6k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads);
+/* engine/native_quant.cpp:744-748; vectors [tokens][cols], out [rows][tokens] */
+void localai_q8_0_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
+                         int threads);
+/* engine/native_quant.cpp:749-753 */
+void localai_q4_0_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
+                         int threads);
+/* engine/native_quant.cpp:754-758 */
+void localai_q4k_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
+                        int threads);
+/* engine/native_quant.cpp:759-763 */
+void localai_q5k_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
+                        int threads);
+/* engine/native_quant.cpp:764-768 */
+void localai_q6k_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
+                        int threads);
+
+/* Status of the last call made by this process (B200Q_* code) and its
+ * message.  Replaces the reference's silent failure / None return
+ * (engine/native_quant.py:66-99). */
+int b200q_last_status(void);
+const char *b200q_last_error(void);
+
+/* Select and initialise the CUDA device used by Part 1 (default 0). */
+int b200q_init(int device);
+
+/* Host weight registry.  Registering an immutable host range (e.g. the
+ * tensor data of an mmap'd GGUF file, engine/gguf_parser.py:153-156) uploads
+ * it once; later Part-1 calls whose ``raw`` lies inside the range use the
+ * device copy instead of copying the weights again.  Unregister before the
+ * host memory is unmapped (GGUFFile.close, engine/gguf_parser.py:83-86). */
+int b200q_register_host(const void *ptr, size_t nbytes);
+int b200q_unregister_host(const void *ptr);
+int b200q_registry_clear(void);
+/* Device address of a registered host byte (NULL if not registered). */
+void *b200q_registered_device_ptr(const void *host_ptr);
+
+/* ---- Part 2: device-pointer API --------------------------------------- */
+/* Exact f32 dequantization of nblocks GGML blocks (engine/dequant.py:27-167). */
+int b200q_dequant_f32_dev(int ggml_type, const void *w, float *out, long long nblocks, void *stream);
+/* bf16 dequantization (rounded from the exact f32 values). */
+int b200q_dequant_bf16_dev(int ggml_type, const void *w, void *out_bf16, long long nblocks, void *stream);
+
+/* y[t*ys_t + r*ys_r] = sum_c W[r][c] * x[t*cols + c], f32 accumulate.
+ * W: raw GGUF bytes of a [rows, cols] matrix (2-byte aligned);
+ * x: f32 [tokens][cols], 16-byte aligned.  Replaces the math of
+ * localai_*_matvec/matmul (engine/native_quant.cpp:126-337, :620-681). */
+int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int rows, int cols, int tokens,
+                   long long ys_t, long long ys_r, void *stream);
+
+/* Device error word: returns and clears the sticky kernel error of the
+ * current device (0 if none).  Synchronises the device. */
+int b200q_check_device_error(void);
+
+/* Tuning knobs of the GEMV (bytes of weights per pipeline stage, stage
+ * count); 0 keeps the current value. */
+void b200q_gemv_tuning(int stage_bytes, int stages);
+
+/* Number of kernel launches made by this library since load. */
+long long b200q_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200QUANT_H */

@@ -1,0 +1,89 @@
+"""ctypes binding of libb200quant.so (C ABI declared in include/b200quant.h).
+
+The library is the only compute path of this package: if it is missing or
+cannot be loaded, every entry point raises -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / 'libb200quant.so'
+HEADER = PKG.parent / 'include' / 'b200quant.h'
+
+B200Q_OK, B200Q_EINVAL, B200Q_ECUDA, B200Q_ETIMEOUT, B200Q_ENODEV, B200Q_EINDEX = 0, -1, -2, -3, -4, -5
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_vp = ctypes.c_void_p
+_i, _ll, _sz = ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t
+
+# name -> (restype, argtypes); every function declared in include/b200quant.h
+SIGNATURES = {
+    'localai_q8_0_matvec': (None, [_u8p, _f32p, _f32p, _i, _i, _i]),
+    'localai_q4_0_matvec': (None, [_u8p, _f32p, _f32p, _i, _i, _i]),
+    'localai_q4k_matvec': (None, [_u8p, _f32p, _f32p, _i, _i, _i]),
+    'localai_q5k_matvec': (None, [_u8p, _f32p, _f32p, _i, _i, _i]),
+    'localai_q6k_matvec': (None, [_u8p, _f32p, _f32p, _i, _i, _i]),
+    'localai_q8_0_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'localai_q4_0_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'localai_q4k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'localai_q5k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'localai_q6k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'b200q_last_status': (_i, []),
+    'b200q_last_error': (ctypes.c_char_p, []),
+    'b200q_init': (_i, [_i]),
+    'b200q_register_host': (_i, [_vp, _sz]),
+    'b200q_unregister_host': (_i, [_vp]),
+    'b200q_registry_clear': (_i, []),
+    'b200q_registered_device_ptr': (_vp, [_vp]),
+    'b200q_dequant_f32_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
+    'b200q_dequant_bf16_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
+    'b200q_gemv_dev': (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _ll, _ll, _vp]),
+    'b200q_check_device_error': (_i, []),
+    'b200q_gemv_tuning': (None, [_i, _i]),
+    'b200q_launch_count': (_ll, []),
+}
+
+_LIB = None
+
+
+class B200QError(RuntimeError):
+    """A libb200quant call failed (message from b200q_last_error)."""
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/b200quant.h."""
+    text = HEADER.read_text()
+    text = re.sub(r'/\*.*?\*/', '', text, flags=re.S)
+    return re.findall(r'\b((?:localai|b200q)_\w+)\s*\(', text)
+
+
+def load() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise B200QError(f'{LIB_PATH.name} is not built; run `python -m localai_b200.build`')
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def check(status: int | None = None) -> None:
+    """Raise B200QError if ``status`` (or the library's last status) is an error."""
+    lib = load()
+    code = lib.b200q_last_status() if status is None else status
+    if code != B200Q_OK:
+        msg = lib.b200q_last_error().decode(errors='replace')
+        raise B200QError(f'libb200quant error {code}: {msg}')
+
+
+def launch_count() -> int:
+    return int(load().b200q_launch_count())

@@ -1,0 +1,365 @@
+// C ABI of libb200quant.so (declared in include/b200quant.h).
+//
+// Part 1 keeps the reference's exported names and signatures
+// (engine/native_quant.cpp:705-768): host pointers in, host result out, with
+// the copies and the kernel launch inside the call.  Part 2 is the
+// device-pointer API used by the PyTorch host code.
+#include "b200quant.h"
+#include "common.cuh"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+namespace b200q {
+cudaError_t launch_dequant_f32(int type, const void *raw, float *out, long long nblocks, int num_sms, cudaStream_t st);
+cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, long long nblocks, int num_sms,
+                                cudaStream_t st);
+cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
+                        int cols, int tokens, int *err, int num_sms, cudaStream_t st);
+void gemv_set_tuning(int stage_target_bytes, int stages);
+
+// Library-wide state shared with the other translation units.
+std::recursive_mutex g_lock;
+long long g_launches = 0;
+
+static int g_status = 0;
+static char g_msg[512] = "ok";
+
+int set_status(int code, const char *fmt, ...)
+{
+    g_status = code;
+    if (fmt) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+        va_end(ap);
+    } else {
+        snprintf(g_msg, sizeof(g_msg), "ok");
+    }
+    return code;
+}
+int cuda_status(cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess) return set_status(B200Q_OK, nullptr);
+    if (e == cudaErrorInvalidValue)
+        return set_status(B200Q_EINVAL, "%s: unsupported shape or argument (%s)", what, cudaGetErrorString(e));
+    return set_status(B200Q_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Per-device resources of the device-pointer API: SM count and the sticky
+// error word that kernels set when a bounded wait or index check fails.
+struct DevInfo {
+    int sms = 0;
+    int *err = nullptr;
+};
+static std::vector<DevInfo> g_devs;
+
+int current_device_info(DevInfo **out)
+{
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_status(B200Q_ENODEV, "no CUDA device: %s", cudaGetErrorString(e));
+    if ((int)g_devs.size() <= dev) g_devs.resize(dev + 1);
+    DevInfo &d = g_devs[dev];
+    if (!d.err) {
+        e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_status(e, "device query");
+        e = cudaMalloc(&d.err, sizeof(int));
+        if (e != cudaSuccess) return cuda_status(e, "error word");
+        e = cudaMemset(d.err, 0, sizeof(int));
+        if (e != cudaSuccess) return cuda_status(e, "error word");
+    }
+    *out = &d;
+    return B200Q_OK;
+}
+
+// ---------------------------------------------------------------- Part 1
+struct HostCtx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    void *w = nullptr;
+    size_t wcap = 0;
+    float *x = nullptr;
+    size_t xcap = 0;
+    float *y = nullptr;
+    size_t ycap = 0;
+    int *herr = nullptr;   // pinned host copy of the error word
+};
+static HostCtx g_host;
+
+struct Registered {
+    const uint8_t *host;
+    size_t n;
+    uint8_t *dev;
+};
+static std::vector<Registered> g_reg;
+
+static int host_init(int device)
+{
+    if (g_host.device == device && g_host.stream) return B200Q_OK;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return set_status(B200Q_ENODEV, "no CUDA device available");
+    if (device < 0 || device >= n) return set_status(B200Q_EINVAL, "device %d out of range [0,%d)", device, n);
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+    if (g_host.stream && g_host.device != device) return set_status(B200Q_EINVAL, "library already bound to device %d", g_host.device);
+    e = cudaStreamCreateWithFlags(&g_host.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_status(e, "stream");
+    e = cudaMallocHost(&g_host.herr, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e, "pinned error word");
+    g_host.device = device;
+    return B200Q_OK;
+}
+
+static int grow(void **p, size_t *cap, size_t need)
+{
+    if (need <= *cap) return B200Q_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    const size_t sz = need + need / 4 + 256;
+    cudaError_t e = cudaMalloc(p, sz);
+    if (e != cudaSuccess) return cuda_status(e, "device buffer");
+    *cap = sz;
+    return B200Q_OK;
+}
+
+static const uint8_t *lookup_registered(const uint8_t *raw, size_t n)
+{
+    for (const Registered &r : g_reg)
+        if (raw >= r.host && raw + n <= r.host + r.n) return r.dev + (raw - r.host);
+    return nullptr;
+}
+
+// One Part-1 call: upload, launch, download, wait, report.
+static void host_call(int type, const uint8_t *raw, const float *x, float *out, int rows, int cols, int tokens,
+                      bool matmul)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    const int vals = type_vals(type), bytes = type_bytes(type);
+    if (!raw || !x || !out) { set_status(B200Q_EINVAL, "null pointer"); return; }
+    if (!bytes || rows < 1 || tokens < 1 || cols < vals || cols % vals) {
+        set_status(B200Q_EINVAL, "invalid shape rows=%d cols=%d tokens=%d for type %d", rows, cols, tokens, type);
+        return;
+    }
+    if (g_host.device < 0 && host_init(0) != B200Q_OK) return;
+    cudaSetDevice(g_host.device);
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return;
+    const size_t wbytes = (size_t)rows * (cols / vals) * bytes;
+    const size_t xbytes = (size_t)tokens * cols * sizeof(float);
+    const size_t ybytes = (size_t)tokens * rows * sizeof(float);
+    cudaStream_t st = g_host.stream;
+    const uint8_t *wdev = lookup_registered(raw, wbytes);
+    if (!wdev) {
+        if (grow(&g_host.w, &g_host.wcap, wbytes) != B200Q_OK) return;
+        cudaError_t e = cudaMemcpyAsync(g_host.w, raw, wbytes, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) { cuda_status(e, "weight upload"); return; }
+        wdev = static_cast<const uint8_t *>(g_host.w);
+    }
+    if (grow((void **)&g_host.x, &g_host.xcap, xbytes) != B200Q_OK) return;
+    if (grow((void **)&g_host.y, &g_host.ycap, ybytes) != B200Q_OK) return;
+    cudaError_t e = cudaMemcpyAsync(g_host.x, x, xbytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) { cuda_status(e, "input upload"); return; }
+    // Reference output layout: matvec [rows]; matmul [rows][tokens]
+    // (engine/native_quant.py:148-156).
+    const long long ys_t = matmul ? 1 : rows, ys_r = matmul ? tokens : 1;
+    e = launch_gemv(type, wdev, g_host.x, g_host.y, ys_t, ys_r, rows, cols, tokens, di->err, di->sms, st);
+    ++g_launches;
+    if (e != cudaSuccess) { cuda_status(e, "gemv launch"); return; }
+    e = cudaMemcpyAsync(out, g_host.y, ybytes, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) { cuda_status(e, "output download"); return; }
+    e = cudaMemcpyAsync(g_host.herr, di->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) { cuda_status(e, "synchronize"); return; }
+    if (*g_host.herr) {
+        const int code = *g_host.herr;
+        cudaMemsetAsync(di->err, 0, sizeof(int), st);
+        cudaStreamSynchronize(st);
+        set_status(code == ERR_WAIT_TIMEOUT ? B200Q_ETIMEOUT : B200Q_EINDEX, "kernel reported error %d", code);
+        return;
+    }
+    set_status(B200Q_OK, nullptr);
+}
+
+} // namespace b200q
+
+using namespace b200q;
+
+#define B200Q_API extern "C" __attribute__((visibility("default")))
+
+B200Q_API void localai_q8_0_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads)
+{
+    (void)threads;
+    host_call(T_Q8_0, raw, x, out, rows, cols, 1, false);
+}
+B200Q_API void localai_q4_0_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads)
+{
+    (void)threads;
+    host_call(T_Q4_0, raw, x, out, rows, cols, 1, false);
+}
+B200Q_API void localai_q4k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads)
+{
+    (void)threads;
+    host_call(T_Q4_K, raw, x, out, rows, cols, 1, false);
+}
+B200Q_API void localai_q5k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads)
+{
+    (void)threads;
+    host_call(T_Q5_K, raw, x, out, rows, cols, 1, false);
+}
+B200Q_API void localai_q6k_matvec(const uint8_t *raw, const float *x, float *out, int rows, int cols, int threads)
+{
+    (void)threads;
+    host_call(T_Q6_K, raw, x, out, rows, cols, 1, false);
+}
+B200Q_API void localai_q8_0_matmul(const uint8_t *raw, const float *v, float *out, int rows, int cols, int tokens,
+                                   int threads)
+{
+    (void)threads;
+    host_call(T_Q8_0, raw, v, out, rows, cols, tokens, true);
+}
+B200Q_API void localai_q4_0_matmul(const uint8_t *raw, const float *v, float *out, int rows, int cols, int tokens,
+                                   int threads)
+{
+    (void)threads;
+    host_call(T_Q4_0, raw, v, out, rows, cols, tokens, true);
+}
+B200Q_API void localai_q4k_matmul(const uint8_t *raw, const float *v, float *out, int rows, int cols, int tokens,
+                                  int threads)
+{
+    (void)threads;
+    host_call(T_Q4_K, raw, v, out, rows, cols, tokens, true);
+}
+B200Q_API void localai_q5k_matmul(const uint8_t *raw, const float *v, float *out, int rows, int cols, int tokens,
+                                  int threads)
+{
+    (void)threads;
+    host_call(T_Q5_K, raw, v, out, rows, cols, tokens, true);
+}
+B200Q_API void localai_q6k_matmul(const uint8_t *raw, const float *v, float *out, int rows, int cols, int tokens,
+                                  int threads)
+{
+    (void)threads;
+    host_call(T_Q6_K, raw, v, out, rows, cols, tokens, true);
+}
+
+B200Q_API int b200q_last_status(void) { return g_status; }
+B200Q_API const char *b200q_last_error(void) { return g_msg; }
+
+B200Q_API int b200q_init(int device)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    return host_init(device) == B200Q_OK ? set_status(B200Q_OK, nullptr) : g_status;
+}
+
+B200Q_API int b200q_register_host(const void *ptr, size_t nbytes)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ptr || !nbytes) return set_status(B200Q_EINVAL, "register: null or empty range");
+    if (g_host.device < 0 && host_init(0) != B200Q_OK) return g_status;
+    cudaSetDevice(g_host.device);
+    const uint8_t *p = static_cast<const uint8_t *>(ptr);
+    for (const Registered &r : g_reg)
+        if (r.host == p && r.n == nbytes) return set_status(B200Q_OK, nullptr);
+    uint8_t *dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, nbytes + 64);
+    if (e != cudaSuccess) return cuda_status(e, "register: cudaMalloc");
+    e = cudaMemcpy(dev, p, nbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return cuda_status(e, "register: upload");
+    }
+    g_reg.push_back({p, nbytes, dev});
+    return set_status(B200Q_OK, nullptr);
+}
+
+B200Q_API int b200q_unregister_host(const void *ptr)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    for (size_t i = 0; i < g_reg.size(); ++i)
+        if (g_reg[i].host == ptr) {
+            cudaFree(g_reg[i].dev);
+            g_reg.erase(g_reg.begin() + i);
+            return set_status(B200Q_OK, nullptr);
+        }
+    return set_status(B200Q_EINVAL, "unregister: pointer not registered");
+}
+
+B200Q_API int b200q_registry_clear(void)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    for (Registered &r : g_reg) cudaFree(r.dev);
+    g_reg.clear();
+    return set_status(B200Q_OK, nullptr);
+}
+
+B200Q_API void *b200q_registered_device_ptr(const void *host_ptr)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    return (void *)lookup_registered(static_cast<const uint8_t *>(host_ptr), 1);
+}
+
+B200Q_API int b200q_dequant_f32_dev(int ggml_type, const void *w, float *out, long long nblocks, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!w || !out || nblocks < 0 || !type_bytes(ggml_type)) return set_status(B200Q_EINVAL, "dequant: bad argument");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_dequant_f32(ggml_type, w, out, nblocks, di->sms, (cudaStream_t)stream), "dequant");
+}
+
+B200Q_API int b200q_dequant_bf16_dev(int ggml_type, const void *w, void *out, long long nblocks, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!w || !out || nblocks < 0 || !type_bytes(ggml_type)) return set_status(B200Q_EINVAL, "dequant: bad argument");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_dequant_bf16(ggml_type, w, static_cast<__nv_bfloat16 *>(out), nblocks, di->sms,
+                                           (cudaStream_t)stream),
+                       "dequant");
+}
+
+B200Q_API int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int rows, int cols, int tokens,
+                             long long ys_t, long long ys_r, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!w || !x || !y) return set_status(B200Q_EINVAL, "gemv: null pointer");
+    if ((reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return set_status(B200Q_EINVAL, "gemv: weights must be 2-byte and x 16-byte aligned");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_gemv(ggml_type, w, x, y, ys_t, ys_r, rows, cols, tokens, di->err, di->sms,
+                                   (cudaStream_t)stream),
+                       "gemv");
+}
+
+B200Q_API int b200q_check_device_error(void)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_status(e, "synchronize");
+    int v = 0;
+    e = cudaMemcpy(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_status(e, "error word read");
+    if (v) cudaMemset(di->err, 0, sizeof(int));
+    set_status(B200Q_OK, nullptr);
+    return v;
+}
+
+B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    gemv_set_tuning(stage_bytes, stages);
+}
+
+B200Q_API long long b200q_launch_count(void) { return g_launches; }

@@ -1,0 +1,86 @@
+"""PyTorch-facing device operations over libb200quant (device-pointer C ABI).
+
+Tensors stay on the GPU; work is enqueued on the current torch stream.  Weight
+tensors are raw GGUF block bytes (``torch.uint8``) of a [rows, cols] matrix.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+BLOCK = {2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def row_bytes(ggml_type: int, cols: int) -> int:
+    vals, nbytes = BLOCK[ggml_type]
+    if cols % vals:
+        raise ValueError(f'cols={cols} not a multiple of block {vals}')
+    return (cols // vals) * nbytes
+
+
+def _check_weights(w: torch.Tensor, ggml_type: int, rows: int, cols: int):
+    if ggml_type not in BLOCK:
+        raise ValueError(f'unsupported GGML type {ggml_type}')
+    if not w.is_cuda or w.dtype != torch.uint8:
+        raise ValueError('weights must be a CUDA uint8 tensor of raw GGUF blocks')
+    if w.numel() < rows * row_bytes(ggml_type, cols):
+        raise ValueError('weight tensor smaller than rows * row_bytes')
+
+
+def dequantize(w: torch.Tensor, ggml_type: int, shape, dtype=torch.float32) -> torch.Tensor:
+    """Exact f32 (or bf16-rounded) dequantization (engine/dequant.py:27-167)."""
+    vals, nbytes = BLOCK[ggml_type]
+    n = 1
+    for s in shape:
+        n *= int(s)
+    if n % vals:
+        raise ValueError(f'{n} elements is not divisible by block size {vals}')
+    nblocks = n // vals
+    if not w.is_cuda or w.dtype != torch.uint8 or w.numel() < nblocks * nbytes:
+        raise ValueError('weights must be a CUDA uint8 tensor holding the blocks')
+    out = torch.empty(tuple(shape), dtype=dtype, device=w.device)
+    lib = _lib.load()
+    if dtype == torch.float32:
+        st = lib.b200q_dequant_f32_dev(ggml_type, w.data_ptr(), out.data_ptr(), nblocks, _stream())
+    elif dtype == torch.bfloat16:
+        st = lib.b200q_dequant_bf16_dev(ggml_type, w.data_ptr(), out.data_ptr(), nblocks, _stream())
+    else:
+        raise ValueError('dtype must be float32 or bfloat16')
+    _lib.check(st)
+    return out
+
+
+def gemv(w: torch.Tensor, x: torch.Tensor, ggml_type: int, rows: int, cols: int,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ W^T with f32 accumulation.
+
+    ``x`` is f32 [cols] or [tokens, cols]; the result is [rows] or
+    [tokens, rows].  Suited to decode (1 token) and small batches.
+    """
+    _check_weights(w, ggml_type, rows, cols)
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.dtype != torch.float32 or x2.shape[-1] != cols or not x2.is_cuda:
+        raise ValueError('x must be a CUDA float32 tensor with cols columns')
+    x2 = x2.contiguous()
+    tokens = x2.shape[0]
+    if out is None:
+        out = torch.empty((tokens, rows), dtype=torch.float32, device=x2.device)
+    elif out.shape != (tokens, rows) or not out.is_contiguous() or out.dtype != torch.float32:
+        raise ValueError('out must be a contiguous f32 [tokens, rows] tensor')
+    st = _lib.load().b200q_gemv_dev(ggml_type, w.data_ptr(), x2.data_ptr(), out.data_ptr(),
+                                    rows, cols, tokens, rows, 1, _stream())
+    _lib.check(st)
+    return out.reshape(rows) if squeeze else out
+
+
+def check_device_error() -> None:
+    """Synchronise and raise if a kernel reported a timed-out wait or bad index."""
+    code = _lib.load().b200q_check_device_error()
+    if code:
+        raise _lib.B200QError(f'kernel error word {code}')

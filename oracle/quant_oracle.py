@@ -1,0 +1,263 @@
+"""CPU oracle for the GGML block-quant matvec/matmul and the MoE FFN.
+
+TEST INFRASTRUCTURE ONLY.  This module restates, in NumPy, the reference
+engine's algorithms for the accelerated path so that the CUDA library can be
+checked against them.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it, and
+only as the checker or the timed CPU baseline -- never as the product path.
+
+What each function restates (paths are relative to the reference project):
+
+* ``LAYOUT`` / ``block_layout``        engine/dequant.py:6-17
+* ``dequantize``                       engine/dequant.py:27-167 (NumPy branch);
+  the numba branch (engine/numba_kernels.py:49-106) gives the same f32 bits.
+* ``matvec_f64`` / ``matmul_f64``      the survey's numeric oracle:
+  ``dequantize(raw) @ x`` evaluated in float64.
+* ``silu``                             engine/zaya.py:305 / engine/model.py:232
+* ``route_topk``                       engine/zaya.py:290-296 generalised to
+  top-k (stable: larger value first, lower index wins ties, as np.argmax).
+* ``moe_forward_f64``                  engine/zaya.py:303-306 per token, summed
+  over the k selected experts with the routing weights.
+
+Rounding contract (bit-exact dequant): every product in the reference
+formulas is exact in f32 (fp16 ``d`` has 11 significant bits; 6-bit scales and
+4/5/6/8-bit quants keep every product within 24 bits), so the only rounding
+is the single f32 subtraction of the Q4_K/Q5_K minimum term.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+# (values per block, bytes per block) -- engine/dequant.py:6-9
+LAYOUT = {
+    0: (1, 4), 1: (1, 2), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24),
+    8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210),
+}
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 8, 12, 13, 14
+MATVEC_TYPES = (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K)   # engine/native_quant.py:104
+
+
+def block_layout(t):
+    """engine/dequant.py:12-17."""
+    if t not in LAYOUT:
+        raise NotImplementedError(f'unsupported tensor type {t}')
+    return LAYOUT[t]
+
+
+def row_bytes(t, cols):
+    block, nbytes = block_layout(t)
+    if cols % block:
+        raise ValueError(f'{cols} columns not divisible by block {block}')
+    return (cols // block) * nbytes
+
+
+def _half(blocks, offset):
+    """fp16 field at byte ``offset`` of every block, widened exactly to f32."""
+    lo = blocks[:, offset].astype(np.uint16)
+    hi = blocks[:, offset + 1].astype(np.uint16)
+    return (lo | (hi << 8)).view(np.float16).astype(np.float32)
+
+
+def k_scales(scales):
+    """Six-bit (scale, min) pairs of a Q4_K/Q5_K super-block.
+
+    engine/dequant.py:108-113: sub-block g<4 reads the low 6 bits of s[g] and
+    s[g+4]; g>=4 combines a nibble of s[g+4] with the top two bits of s[g-4]
+    (scale) or s[g] (min).  Returns two uint8 arrays of shape [blocks, 8].
+    """
+    s = scales.astype(np.uint8)
+    sc = np.empty((s.shape[0], 8), np.uint8)
+    mn = np.empty((s.shape[0], 8), np.uint8)
+    sc[:, :4] = s[:, 0:4] & 63
+    mn[:, :4] = s[:, 4:8] & 63
+    sc[:, 4:] = (s[:, 8:12] & 15) | ((s[:, 0:4] >> 6) << 4)
+    mn[:, 4:] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
+    return sc, mn
+
+
+def _affine_k(q, d, dmin, sc, mn):
+    """fl(q * fl(d*sc)) - fl(dmin*mn) in f32 (engine/dequant.py:117-120)."""
+    step = (d[:, None] * sc.astype(np.float32))            # [blocks, 8], exact
+    low = (dmin[:, None] * mn.astype(np.float32))           # [blocks, 8], exact
+    qf = q.astype(np.float32).reshape(q.shape[0], 8, 32)
+    return (qf * step[:, :, None] - low[:, :, None]).reshape(q.shape[0], 256)
+
+
+def _q4_k(blocks):
+    d, dmin = _half(blocks, 0), _half(blocks, 2)
+    sc, mn = k_scales(blocks[:, 4:16])
+    qs = blocks[:, 16:144].reshape(-1, 4, 32)
+    # 32-byte chunk p: low nibbles -> sub-block 2p, high nibbles -> 2p+1.
+    q = np.stack((qs & 15, qs >> 4), axis=2).reshape(-1, 256)
+    return _affine_k(q, d, dmin, sc, mn)
+
+
+def _q5_k(blocks):
+    d, dmin = _half(blocks, 0), _half(blocks, 2)
+    sc, mn = k_scales(blocks[:, 4:16])
+    qh = blocks[:, 16:48]                                   # [blocks, 32]
+    qs = blocks[:, 48:176].reshape(-1, 4, 32)
+    low = np.stack((qs & 15, qs >> 4), axis=2).reshape(-1, 8, 32)
+    high = (qh[:, None, :] >> np.arange(8, dtype=np.uint8)[None, :, None]) & 1
+    q = (low | (high << 4)).reshape(-1, 256)
+    return _affine_k(q, d, dmin, sc, mn)
+
+
+def _q6_k(blocks):
+    ql = blocks[:, 0:128].reshape(-1, 2, 2, 32)             # [b, half, lo/hi 32, j]
+    qh = blocks[:, 128:192].reshape(-1, 2, 32)              # [b, half, j]
+    sc = blocks[:, 192:208].view(np.int8).reshape(-1, 2, 4, 2)  # [b, half, quad, j//16]
+    d = _half(blocks, 208)
+    out = np.empty((blocks.shape[0], 2, 4, 32), np.float32)
+    for quad in range(4):
+        nib = ql[:, :, quad & 1, :]
+        nib = (nib & 15) if quad < 2 else (nib >> 4)
+        q = nib | (((qh >> (2 * quad)) & 3) << 4)
+        s = np.repeat(sc[:, :, quad, :], 16, axis=2).astype(np.float32)
+        # engine/dequant.py:165 -- ((q-32) * d) * scale, all exact in f32
+        out[:, :, quad, :] = (q.astype(np.int16) - 32).astype(np.float32) * d[:, None, None] * s
+    return out.reshape(-1, 256)
+
+
+def _q8_0(blocks):
+    d = _half(blocks, 0)
+    return blocks[:, 2:34].view(np.int8).astype(np.float32) * d[:, None]
+
+
+def _q4_0(blocks):
+    d = _half(blocks, 0)
+    qs = blocks[:, 2:18]
+    q = np.concatenate((qs & 15, qs >> 4), axis=1).astype(np.float32) - 8.0
+    return q * d[:, None]
+
+
+def _q4_1(blocks):
+    d, m = _half(blocks, 0), _half(blocks, 2)
+    qs = blocks[:, 4:20]
+    q = np.concatenate((qs & 15, qs >> 4), axis=1).astype(np.float32)
+    return q * d[:, None] + m[:, None]
+
+
+def _q5_x(blocks, with_min):
+    d = _half(blocks, 0)
+    m = _half(blocks, 2) if with_min else None
+    off = 4 if with_min else 2
+    qh = blocks[:, off:off + 4]
+    qs = blocks[:, off + 4:off + 20]
+    low = np.concatenate((qs & 15, qs >> 4), axis=1).astype(np.int16)
+    bit = np.arange(32)
+    high = ((qh[:, bit // 8] >> (bit % 8).astype(np.uint8)) & 1).astype(np.int16)
+    q = low | (high << 4)
+    if with_min:
+        return q.astype(np.float32) * d[:, None] + m[:, None]
+    return (q.astype(np.float32) - 16.0) * d[:, None]
+
+
+_DECODERS = {Q4_0: _q4_0, 3: _q4_1, 6: lambda b: _q5_x(b, False),
+             7: lambda b: _q5_x(b, True), Q8_0: _q8_0, Q4_K: _q4_k,
+             Q5_K: _q5_k, Q6_K: _q6_k}
+
+
+def dequantize(raw, t, shape):
+    """Decode packed GGML blocks to f32 -- engine/dequant.py:27-167."""
+    block, nbytes = block_layout(t)
+    n = int(np.prod(shape, dtype=np.int64))
+    if n % block:
+        raise ValueError(f'{n} elements is not divisible by block size {block}')
+    if t == 0:
+        return np.frombuffer(raw, dtype='<f4', count=n).copy().reshape(shape)
+    if t == 1:
+        return np.frombuffer(raw, dtype='<f2', count=n).astype(np.float32).reshape(shape)
+    blocks = np.frombuffer(raw, dtype=np.uint8, count=(n // block) * nbytes)
+    blocks = blocks.reshape(n // block, nbytes)
+    return _DECODERS[t](blocks).reshape(shape)
+
+
+def matvec_f64(raw, t, rows, cols, x):
+    """``dequantize(raw) @ x`` in float64: the GEMV parity oracle."""
+    w = dequantize(raw, t, (rows, cols)).astype(np.float64)
+    return w @ np.asarray(x, np.float64)
+
+
+def matmul_f64(raw, t, rows, cols, vectors):
+    """[tokens, cols] x W[rows, cols]^T in float64 -> [tokens, rows]."""
+    w = dequantize(raw, t, (rows, cols)).astype(np.float64)
+    return np.asarray(vectors, np.float64) @ w.T
+
+
+def normwise_rel_err(got, ref):
+    """max|got-ref| / max|ref| -- the tolerance metric for GEMV/MoE outputs."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    denom = float(np.max(np.abs(ref))) if ref.size else 0.0
+    return float(np.max(np.abs(got - ref))) / max(denom, 1e-300) if ref.size else 0.0
+
+
+def silu(g):
+    """engine/zaya.py:305 -- g / (1 + exp(-clip(g, -80, 80)))."""
+    g = np.asarray(g)
+    return g / (1.0 + np.exp(-np.clip(g, -80, 80)))
+
+
+def softmax_f32(logits):
+    """engine/zaya.py:290 -- max-subtracted softmax, every step in f32, per row."""
+    z = np.asarray(logits, np.float32)
+    z = z - z.max(axis=-1, keepdims=True)
+    p = np.exp(z)
+    return p / p.sum(axis=-1, keepdims=True)
+
+
+def route_topk(logits, k, bias=None, renormalize=True):
+    """Softmax -> optional additive selection bias -> stable top-k -> weights.
+
+    engine/zaya.py:290-296 is the k=1 case (argmax of ``probs + bias``, weight
+    = unbiased ``probs[e]``, not renormalised).  Ties go to the lower expert
+    index, as ``np.argmax`` does.  Returns (ids int32 [T,k], weights f32 [T,k]).
+    With ``renormalize`` the weights are ``p_i / sum_topk p`` computed in f32
+    by a left-to-right sum over the k selected probabilities.
+    """
+    probs = softmax_f32(np.atleast_2d(logits))
+    sel = probs if bias is None else (probs + np.asarray(bias, np.float32)).astype(np.float32)
+    # stable descending sort: lexsort on (index, -value)
+    order = np.argsort(-sel, axis=-1, kind='stable')[:, :k].astype(np.int32)
+    w = np.take_along_axis(probs, order, axis=-1).astype(np.float32)
+    if renormalize:
+        total = np.zeros(w.shape[0], np.float32)
+        for j in range(k):
+            total = (total + w[:, j]).astype(np.float32)
+        w = (w / total[:, None]).astype(np.float32)
+    return order, w
+
+
+def expert_ffn_f64(gate_up_raw, down_raw, t_gu, t_dn, d_model, d_ff, d_ff_padded, h):
+    """One expert on a batch: down(silu(gate h) * up h) -- engine/zaya.py:303-306.
+
+    ``gate_up_raw`` is the packed [2F, D] matrix (gate rows first, then up
+    rows, as np.split(packed, 2) reads them); ``down_raw`` is [D, F_padded].
+    Returns float64 [tokens, D].
+    """
+    h = np.atleast_2d(np.asarray(h, np.float64))
+    gu = matmul_f64(gate_up_raw, t_gu, 2 * d_ff, d_model, h)
+    gate, up = gu[:, :d_ff], gu[:, d_ff:]
+    act = np.zeros((h.shape[0], d_ff_padded), np.float64)
+    act[:, :d_ff] = silu(gate) * up
+    return matmul_f64(down_raw, t_dn, d_model, d_ff_padded, act)
+
+
+def moe_forward_f64(h, ids, weights, experts, t_gu, t_dn, d_model, d_ff, d_ff_padded):
+    """Weighted combine over the selected experts, in fixed k order.
+
+    ``experts[e] = (gate_up_raw, down_raw)``.  Tokens are grouped per expert
+    (each expert's product runs once over its tokens), then
+    ``y[t] = sum_j w[t,j] * out_e(t)`` with j ascending.
+    """
+    h = np.atleast_2d(np.asarray(h, np.float32))
+    T, k = ids.shape
+    y = np.zeros((T, d_model), np.float64)
+    for e in np.unique(ids):
+        # a token selects an expert at most once, so ``rows`` is duplicate-free
+        rows, slots = np.nonzero(ids == e)
+        out = expert_ffn_f64(experts[e][0], experts[e][1], t_gu, t_dn,
+                             d_model, d_ff, d_ff_padded, h[rows])
+        y[rows] += out * weights[rows, slots].astype(np.float64)[:, None]
+    return y
