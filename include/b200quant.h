@@ -94,7 +94,10 @@ int b200q_dequant_bf16_dev(int ggml_type, const void *w, void *out_bf16, long lo
 /* y[t*ys_t + r*ys_r] = sum_c W[r][c] * x[t*cols + c], f32 accumulate.
  * W: raw GGUF bytes of a [rows, cols] matrix (2-byte aligned);
  * x: f32 [tokens][cols], 16-byte aligned.  Replaces the math of
- * localai_*_matvec/matmul (engine/native_quant.cpp:126-337, :620-681). */
+ * localai_*_matvec/matmul (engine/native_quant.cpp:126-337, :620-681).
+ * Allocates nothing; launched with programmatic dependent launch, so the
+ * weight stream may start before the previous kernel of ``stream`` ends
+ * (W must not be written by that kernel). */
 int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int rows, int cols, int tokens,
                    long long ys_t, long long ys_r, void *stream);
 
@@ -102,9 +105,11 @@ int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int r
  * current device (0 if none).  Synchronises the device. */
 int b200q_check_device_error(void);
 
-/* Tuning knobs of the GEMV (bytes of weights per pipeline stage, stage
- * count); 0 keeps the current value. */
-void b200q_gemv_tuning(int stage_bytes, int stages);
+/* Tuning knobs of the GEMV: bytes of weights per pipeline stage, stage
+ * count, the most rows one consumer group handles per stage (1, 2 or 4),
+ * and the most CTAs per SM in the grid (0 = as many as fit); 0 (-1 for the
+ * last) keeps the current value. */
+void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas_per_sm);
 
 /* Number of kernel launches made by this library since load. */
 long long b200q_launch_count(void);

@@ -19,7 +19,7 @@ cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, l
                                 cudaStream_t st);
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st);
-void gemv_set_tuning(int stage_target_bytes, int stages);
+void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm);
 
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
@@ -115,7 +115,8 @@ static int host_init(int device)
     return B200Q_OK;
 }
 
-static int grow(void **p, size_t *cap, size_t need)
+int grow(void **p, size_t *cap, size_t need);
+int grow(void **p, size_t *cap, size_t need)
 {
     if (need <= *cap) return B200Q_OK;
     if (*p) cudaFree(*p);
@@ -356,10 +357,10 @@ B200Q_API int b200q_check_device_error(void)
     return v;
 }
 
-B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages)
+B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas_per_sm)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
-    gemv_set_tuning(stage_bytes, stages);
+    gemv_set_tuning(stage_bytes, stages, rows_per_group, ctas_per_sm);
 }
 
 B200Q_API long long b200q_launch_count(void) { return g_launches; }

@@ -127,6 +127,13 @@ __device__ __forceinline__ uint64_t policy_evict_last()
     return p;
 }
 
+// Programmatic dependent launch (kernels launched with the
+// programmatic-stream-serialization attribute): let the next kernel of the
+// stream start launching, and wait for the previous kernel's completion (and
+// memory flush) before touching anything it may write.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

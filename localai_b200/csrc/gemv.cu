@@ -3,8 +3,7 @@
 // y[t, r] = sum_c W[r, c] * x[t, c] for W stored as the raw GGUF bytes of a
 // [rows, cols] Q4_0/Q8_0/Q4_K/Q5_K/Q6_K matrix -- the computation of
 // localai_*_matvec / localai_*_matmul in the reference
-// (engine/native_quant.cpp:126-337 row kernels, :705-768 exports), with the
-// activation kept in f32 (the reference quantises it to int8/int16).
+// (engine/native_quant.cpp:126-337 row kernels, :705-768 exports).
 //
 // Design (HBM-bound; ~0.56 B of weight per value for Q4_K):
 // * One producer thread per CTA streams contiguous row tiles of the raw bytes
@@ -12,15 +11,21 @@
 //   (cp.async.bulk, mbarrier complete_tx).  Any sub-16-byte tail is copied by
 //   the producer with plain loads before it arrives on the stage barrier.
 // * Consumer threads are "column stationary": a group of threads covers one
-//   full row, each thread owning CPT fixed 32-value units of the row; the
-//   x values of its units stay in registers for the whole kernel.  Groups
-//   take different rows of a stage.  x is therefore read once per CTA and the
-//   only shared-memory traffic is the weight stream itself.
-// * A 4/5/6-bit quant q becomes the float 32768 + 256*q with one byte
-//   permute (the byte lands in mantissa bits 16..23 under exponent 2^15), so
-//   sum(q*x) = S/256 - 128*sum(x) with S accumulated by plain f32 FMAs.  The
-//   per-unit sums of x are precomputed once.  Q8_0 uses the exact product
-//   256*q*x.  Scales are applied once per 16-value run, in f32.
+//   full row, each thread owning CPT fixed units (64 values of a K-quant
+//   super-block, or one 32-value Q8_0/Q4_0 block); the activation values of
+//   its units stay in registers for the whole kernel.  Groups take different
+//   rows of a stage.  x is read once per CTA; the only shared-memory traffic
+//   is the weight stream itself.
+// * Integer dot products.  Each thread converts its x values once to 24-bit
+//   fixed point, xq = rint(x / s) with s = max|x_unit| / (2^23 - 1), held as
+//   three byte planes (xq = 65536*b2 + 256*b1 + b0; b2 signed, b1/b0
+//   unsigned).  The unpacked 4/5/6/8-bit quants are multiplied against the
+//   planes with dp4a (4 products per instruction, exact int32 sums) and every
+//   sub-block sum is scaled and accumulated in f32.  The activation grid step
+//   is 2^-24 of the unit's max |x| -- the same order as f32 rounding -- so
+//   results agree with the f32 dot product to f32 accuracy (the reference
+//   itself quantises x to int8 for Q4_K/Q5_K and int16 for Q6_K,
+//   engine/native_quant.cpp:53-109).
 // * Per-stage partial sums are reduced with warp shuffles, then across the
 //   group's warps through shared memory in a fixed order (deterministic).
 #include "common.cuh"
@@ -35,7 +40,7 @@ struct GemvArgs {
     long long ys_t, ys_r;
     int rows, cols, tokens;
     int rb;               // bytes per row
-    int units;            // 32-value units per row
+    int units;            // units per row
     int nct;              // consumer threads per group (multiple of 32)
     int groups;           // row groups per CTA
     int stage_rows;       // groups * RPG
@@ -44,32 +49,76 @@ struct GemvArgs {
     int *err;
 };
 
-constexpr uint32_t MAGIC_B2 = 0x47000000u;   // exponent 2^15; byte 2 = q -> 32768 + 256 q
+// Unit geometry per type: values per unit, units per block, x words per unit.
+template <int T> struct Unit;
+template <> struct Unit<T_Q4_K> { static constexpr int UV = 64, UPB = 4, NW = 16; };
+template <> struct Unit<T_Q5_K> { static constexpr int UV = 64, UPB = 4, NW = 16; };
+template <> struct Unit<T_Q6_K> { static constexpr int UV = 64, UPB = 4, NW = 16; };
+template <> struct Unit<T_Q8_0> { static constexpr int UV = 32, UPB = 1, NW = 8; };
+template <> struct Unit<T_Q4_0> { static constexpr int UV = 32, UPB = 1, NW = 8; };
 
-__device__ __forceinline__ float qf(uint32_t bytes4, int b)
+// Activation slice of one unit in 24-bit fixed point (three byte planes).
+template <int NW>
+struct XU {
+    uint32_t b2[NW];    // signed top bytes of xq, 4 per word
+    uint32_t b1[NW];    // unsigned middle bytes
+    uint32_t b0[NW];    // unsigned low bytes
+    float s;            // x ~= s * xq
+    float sum[2];       // exact f32 sums of x over the two 32-value runs
+    float qsum[4];      // sums of xq over the four 16-value runs (as f32)
+};
+
+// Sum of q*xq for one 32-value run from the three plane sums:
+// 65536*a2 + 256*a1 + a0 (the two low planes combine exactly in int32).
+__device__ __forceinline__ float planes_f(int a2, int a1, int a0)
 {
-    return __uint_as_float(__byte_perm(bytes4, MAGIC_B2, 0x7044u | (uint32_t)(b << 8)));
+    return fmaf((float)a2, 65536.0f, (float)(a1 * 256 + a0));
 }
 
-// Column start of the low and high 16-value runs of unit u.
+// Column of the first value of the two 32-value runs of unit u.
 template <int T>
-__device__ __forceinline__ void unit_cols(int u, int &lo, int &hi)
+__device__ __forceinline__ void unit_cols(int u, int &c0, int &c1)
 {
     if constexpr (T == T_Q4_K || T == T_Q5_K) {
-        const int blk = u >> 3, c = u & 7;
-        lo = blk * 256 + 64 * (c >> 1) + 16 * (c & 1);
-        hi = lo + 32;
+        const int blk = u >> 2, p = u & 3;
+        c0 = blk * 256 + 64 * p;
+        c1 = c0 + 32;
     } else if constexpr (T == T_Q6_K) {
-        const int blk = u >> 3, c = u & 7;
-        lo = blk * 256 + 128 * (c >> 2) + 32 * ((c >> 1) & 1) + 16 * (c & 1);
-        hi = lo + 64;
+        const int blk = u >> 2, h = (u >> 1) & 1, a = u & 1;
+        c0 = blk * 256 + 128 * h + 32 * a;
+        c1 = c0 + 64;
     } else {
-        lo = u * 32;
-        hi = lo + 16;
+        c0 = u * 32;
+        c1 = c0;
     }
 }
 
-// 32 bytes from any shared address (9 aligned words + funnel shifts).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)   // u8 x s8
+{
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c)   // u8 x u8
+{
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)   // s8 x s8
+{
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c)   // s8 x u8
+{
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 32 bytes from a shared address that is at least 2-byte aligned.
 __device__ __forceinline__ void lds256_any(uint32_t a, uint32_t o[8])
 {
     const uint32_t base = a & ~3u, sh = (a & 3u) * 8u;
@@ -79,229 +128,346 @@ __device__ __forceinline__ void lds256_any(uint32_t a, uint32_t o[8])
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
+__device__ __forceinline__ void lds128x2(uint32_t a, uint32_t o[8], bool aligned16)
+{
+    if (aligned16) {
+        const uint4 v0 = lds128(a), v1 = lds128(a + 16);
+        o[0] = v0.x; o[1] = v0.y; o[2] = v0.z; o[3] = v0.w;
+        o[4] = v1.x; o[5] = v1.y; o[6] = v1.z; o[7] = v1.w;
+    } else {
+        lds256_any(a, o);
+    }
+}
+
+__device__ __forceinline__ float ubyte_f(uint32_t v, int k) { return (float)((v >> (8 * k)) & 0xffu); }
+
+// Q4_K/Q5_K: the four 6-bit fields (scale, scale, min, min) of sub-blocks
+// 2p and 2p+1 packed into bytes (engine/dequant.py:108-113).
+__device__ __forceinline__ uint32_t k_scales_packed(const uint4 hdr, int p)
+{
+    const bool hk = p >= 2;
+    const uint32_t i0 = (2 * p) & 3;
+    const uint32_t sel = i0 | ((i0 + 1) << 4) | ((i0 + 4) << 8) | ((i0 + 5) << 12);
+    const uint32_t lowsrc = __byte_perm(hk ? hdr.w : hdr.y, hk ? hdr.w : hdr.z, sel);
+    const uint32_t lo4 = (lowsrc & 0x00000F0Fu) | ((lowsrc >> (hk ? 4 : 0)) & 0x0F0F0000u);
+    const uint32_t top = __byte_perm(hdr.y, hdr.z, sel);
+    return lo4 | ((top >> (hk ? 2 : 0)) & 0x30303030u);
+}
 
 // ---------------------------------------------------------------- unit dots
 // Each adds the unit's contribution for NTOK tokens into acc[].
-// blk: shared address of the block start; c: unit index inside the block.
+// blk: shared address of the block start; p: unit index inside the block.
+
+// Accumulate one 4-byte word of unsigned quants against word k of the planes.
+#define B200Q_DOT_U(Q, XX, K, A2, A1, A0)       \
+    A2 = dp4a_us((Q), (XX).b2[K], A2);          \
+    A1 = dp4a_uu((Q), (XX).b1[K], A1);          \
+    A0 = dp4a_uu((Q), (XX).b0[K], A0);
 
 template <int NTOK, bool AL>
-__device__ __forceinline__ void dot_q4k(uint32_t blk, int c, const float (&x)[NTOK][32],
-                                        const float (&xs)[NTOK][2], float (&acc)[NTOK])
+__device__ __forceinline__ void dot_q4k(uint32_t blk, int p, const XU<16> (&X)[NTOK], float (&acc)[NTOK])
 {
     const uint4 hdr = lds128_any<AL>(blk);
-    const uint4 q = lds128_any<AL>(blk + 16 + 16 * c);
+    uint32_t w[8];
+    lds128x2(blk + 16 + 32 * p, w, AL);
+    const uint32_t sp = k_scales_packed(hdr, p);
     const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
-    // 6-bit scale/min of sub-blocks k0 = 2*(c>>1) and k0+1 (engine/dequant.py:108-113)
-    const bool hk = c >= 4;
-    const int k0 = 2 * (c >> 1);
-    const int o0 = 8 * (k0 & 3), o1 = o0 + 8;
-    const uint32_t as = hk ? hdr.w : hdr.y, am = hk ? hdr.w : hdr.z;
-    const int mo = hk ? 4 : 0, ho = hk ? 6 : 4;
-    const uint32_t sc0 = ((as >> o0) & 15u) | (((hdr.y >> (o0 + ho)) & 3u) << 4);
-    const uint32_t sc1 = ((as >> o1) & 15u) | (((hdr.y >> (o1 + ho)) & 3u) << 4);
-    const uint32_t mn0 = ((am >> (o0 + mo)) & 15u) | (((hdr.z >> (o0 + ho)) & 3u) << 4);
-    const uint32_t mn1 = ((am >> (o1 + mo)) & 15u) | (((hdr.z >> (o1 + ho)) & 3u) << 4);
-    const float ds0 = d * (float)sc0, ds1 = d * (float)sc1;
-    const float dm0 = dmin * (float)mn0, dm1 = dmin * (float)mn1;
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    float s0[NTOK], s1[NTOK];
+    const float sc0 = ubyte_f(sp, 0), sc1 = ubyte_f(sp, 1), mn0 = ubyte_f(sp, 2), mn1 = ubyte_f(sp, 3);
+    int a[NTOK][6];
 #pragma unroll
-    for (int t = 0; t < NTOK; ++t) s0[t] = s1[t] = 0.f;
+    for (int t = 0; t < NTOK; ++t)
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const uint32_t lo = qw[w] & 0x0F0F0F0Fu, hi = (qw[w] >> 4) & 0x0F0F0F0Fu;
+        for (int i = 0; i < 6; ++i) a[t][i] = 0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float flo = qf(lo, b), fhi = qf(hi, b);
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t L = w[k] & 0x0F0F0F0Fu, H = (w[k] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-            for (int t = 0; t < NTOK; ++t) {
-                s0[t] = fmaf(flo, x[t][4 * w + b], s0[t]);
-                s1[t] = fmaf(fhi, x[t][16 + 4 * w + b], s1[t]);
-            }
+        for (int t = 0; t < NTOK; ++t) {
+            B200Q_DOT_U(L, X[t], k, a[t][0], a[t][1], a[t][2]);
+            B200Q_DOT_U(H, X[t], 8 + k, a[t][3], a[t][4], a[t][5]);
         }
     }
 #pragma unroll
     for (int t = 0; t < NTOK; ++t) {
-        const float a0 = fmaf(s0[t], 1.0f / 256.0f, -128.0f * xs[t][0]);   // sum q*x, low run
-        const float a1 = fmaf(s1[t], 1.0f / 256.0f, -128.0f * xs[t][1]);
-        acc[t] += (ds0 * a0 + ds1 * a1) - (dm0 * xs[t][0] + dm1 * xs[t][1]);
+        const float i0 = planes_f(a[t][0], a[t][1], a[t][2]);
+        const float i1 = planes_f(a[t][3], a[t][4], a[t][5]);
+        acc[t] += (d * X[t].s) * fmaf(sc0, i0, sc1 * i1) - dmin * fmaf(mn0, X[t].sum[0], mn1 * X[t].sum[1]);
     }
 }
 
 template <int NTOK, bool AL>
-__device__ __forceinline__ void dot_q5k(uint32_t blk, int c, const float (&x)[NTOK][32],
-                                        const float (&xs)[NTOK][2], float (&acc)[NTOK])
+__device__ __forceinline__ void dot_q5k(uint32_t blk, int p, const XU<16> (&X)[NTOK], float (&acc)[NTOK])
 {
     const uint4 hdr = lds128_any<AL>(blk);
-    const uint4 qh = lds128_any<AL>(blk + 16 + 16 * (c & 1));
-    const uint4 q = lds128_any<AL>(blk + 48 + 16 * c);
+    uint32_t w[8], h[8];
+    lds128x2(blk + 16, h, AL);
+    lds128x2(blk + 48 + 32 * p, w, AL);
+    const uint32_t sp = k_scales_packed(hdr, p);
     const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
-    const bool hk = c >= 4;
-    const int k0 = 2 * (c >> 1);
-    const int o0 = 8 * (k0 & 3), o1 = o0 + 8;
-    const uint32_t as = hk ? hdr.w : hdr.y, am = hk ? hdr.w : hdr.z;
-    const int mo = hk ? 4 : 0, ho = hk ? 6 : 4;
-    const uint32_t sc0 = ((as >> o0) & 15u) | (((hdr.y >> (o0 + ho)) & 3u) << 4);
-    const uint32_t sc1 = ((as >> o1) & 15u) | (((hdr.y >> (o1 + ho)) & 3u) << 4);
-    const uint32_t mn0 = ((am >> (o0 + mo)) & 15u) | (((hdr.z >> (o0 + ho)) & 3u) << 4);
-    const uint32_t mn1 = ((am >> (o1 + mo)) & 15u) | (((hdr.z >> (o1 + ho)) & 3u) << 4);
-    const float ds0 = d * (float)sc0, ds1 = d * (float)sc1;
-    const float dm0 = dmin * (float)mn0, dm1 = dmin * (float)mn1;
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
-    float s0[NTOK], s1[NTOK];
+    const float sc0 = ubyte_f(sp, 0), sc1 = ubyte_f(sp, 1), mn0 = ubyte_f(sp, 2), mn1 = ubyte_f(sp, 3);
+    const int k0 = 2 * p;
+    int a[NTOK][6];
 #pragma unroll
-    for (int t = 0; t < NTOK; ++t) s0[t] = s1[t] = 0.f;
+    for (int t = 0; t < NTOK; ++t)
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const uint32_t lo = (qw[w] & 0x0F0F0F0Fu) | (((hw[w] >> k0) & 0x01010101u) << 4);
-        const uint32_t hi = ((qw[w] >> 4) & 0x0F0F0F0Fu) | (((hw[w] >> (k0 + 1)) & 0x01010101u) << 4);
+        for (int i = 0; i < 6; ++i) a[t][i] = 0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float flo = qf(lo, b), fhi = qf(hi, b);
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t L = (w[k] & 0x0F0F0F0Fu) | (((h[k] >> k0) & 0x01010101u) << 4);
+        const uint32_t H = ((w[k] >> 4) & 0x0F0F0F0Fu) | (((h[k] >> (k0 + 1)) & 0x01010101u) << 4);
 #pragma unroll
-            for (int t = 0; t < NTOK; ++t) {
-                s0[t] = fmaf(flo, x[t][4 * w + b], s0[t]);
-                s1[t] = fmaf(fhi, x[t][16 + 4 * w + b], s1[t]);
-            }
+        for (int t = 0; t < NTOK; ++t) {
+            B200Q_DOT_U(L, X[t], k, a[t][0], a[t][1], a[t][2]);
+            B200Q_DOT_U(H, X[t], 8 + k, a[t][3], a[t][4], a[t][5]);
         }
     }
 #pragma unroll
     for (int t = 0; t < NTOK; ++t) {
-        const float a0 = fmaf(s0[t], 1.0f / 256.0f, -128.0f * xs[t][0]);
-        const float a1 = fmaf(s1[t], 1.0f / 256.0f, -128.0f * xs[t][1]);
-        acc[t] += (ds0 * a0 + ds1 * a1) - (dm0 * xs[t][0] + dm1 * xs[t][1]);
+        const float i0 = planes_f(a[t][0], a[t][1], a[t][2]);
+        const float i1 = planes_f(a[t][3], a[t][4], a[t][5]);
+        acc[t] += (d * X[t].s) * fmaf(sc0, i0, sc1 * i1) - dmin * fmaf(mn0, X[t].sum[0], mn1 * X[t].sum[1]);
     }
 }
 
 template <int NTOK>
-__device__ __forceinline__ void dot_q6k(uint32_t blk, int c, const float (&x)[NTOK][32],
-                                        const float (&xs)[NTOK][2], float (&acc)[NTOK])
+__device__ __forceinline__ void dot_q6k(uint32_t blk, int u, const XU<16> (&X)[NTOK], float (&acc)[NTOK])
 {
-    const int h = c >> 2, a = (c >> 1) & 1, jh = c & 1;
-    const uint4 ql = lds128_any<false>(blk + 64 * h + 32 * a + 16 * jh);
-    const uint4 qh = lds128_any<false>(blk + 128 + 32 * h + 16 * jh);
-    const uint32_t sb = blk + 192 + 8 * h + 2 * a + jh;
-    const float sc0 = (float)(int8_t)lds_u8(sb), sc1 = (float)(int8_t)lds_u8(sb + 4);
+    const int h = (u >> 1) & 1, a = u & 1;
+    uint32_t ql[8], qh[8];
+    lds256_any(blk + 64 * h + 32 * a, ql);
+    lds256_any(blk + 128 + 32 * h, qh);
+    const uint32_t sb = blk + 192 + 8 * h + 2 * a;
+    const uint32_t s01 = lds_u16(sb), s45 = lds_u16(sb + 4);
+    const float sc[4] = {(float)(int8_t)(s01 & 0xff), (float)(int8_t)(s01 >> 8), (float)(int8_t)(s45 & 0xff),
+                         (float)(int8_t)(s45 >> 8)};
     const float d = h2f(lds_u16(blk + 208));
     const int shl = 4 - 2 * a, shr = 2 * a;
-    const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
-    const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
-    float s0[NTOK], s1[NTOK];
+    int acc3[NTOK][4][3];
 #pragma unroll
-    for (int t = 0; t < NTOK; ++t) s0[t] = s1[t] = 0.f;
+    for (int t = 0; t < NTOK; ++t)
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const uint32_t lo = (lw[w] & 0x0F0F0F0Fu) | ((hw[w] << shl) & 0x30303030u);
-        const uint32_t hi = ((lw[w] >> 4) & 0x0F0F0F0Fu) | ((hw[w] >> shr) & 0x30303030u);
+        for (int r = 0; r < 4; ++r) acc3[t][r][0] = acc3[t][r][1] = acc3[t][r][2] = 0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float flo = qf(lo, b), fhi = qf(hi, b);
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t L = (ql[k] & 0x0F0F0F0Fu) | ((qh[k] << shl) & 0x30303030u);
+        const uint32_t H = ((ql[k] >> 4) & 0x0F0F0F0Fu) | ((qh[k] >> shr) & 0x30303030u);
+        const int r0 = k >> 2, r1 = 2 + (k >> 2);
 #pragma unroll
-            for (int t = 0; t < NTOK; ++t) {
-                s0[t] = fmaf(flo, x[t][4 * w + b], s0[t]);
-                s1[t] = fmaf(fhi, x[t][16 + 4 * w + b], s1[t]);
-            }
-        }
-    }
-    const float ds0 = d * sc0, ds1 = d * sc1;
-#pragma unroll
-    for (int t = 0; t < NTOK; ++t) {
-        // sum (q-32)*x = S/256 - 128*X - 32*X
-        const float a0 = fmaf(s0[t], 1.0f / 256.0f, -160.0f * xs[t][0]);
-        const float a1 = fmaf(s1[t], 1.0f / 256.0f, -160.0f * xs[t][1]);
-        acc[t] += ds0 * a0 + ds1 * a1;
-    }
-}
-
-template <int NTOK>
-__device__ __forceinline__ void dot_q8_0(uint32_t blk, const float (&x)[NTOK][32], float (&acc)[NTOK])
-{
-    const float d = h2f(lds_u16(blk));
-    uint32_t qw[8];
-    lds256_any(blk + 2, qw);
-    float s[NTOK];
-#pragma unroll
-    for (int t = 0; t < NTOK; ++t) s[t] = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-        const uint32_t v = qw[w] ^ 0x80808080u;     // q + 128 as unsigned bytes
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            // 2^23 + 256*(q+128), minus 2^23 + 32768 -> exactly 256*q
-            const float f = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7404u | (uint32_t)(b << 4))) - 8421376.0f;
-#pragma unroll
-            for (int t = 0; t < NTOK; ++t) s[t] = fmaf(f, x[t][4 * w + b], s[t]);
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < NTOK; ++t) acc[t] = fmaf(d * (1.0f / 256.0f), s[t], acc[t]);
-}
-
-template <int NTOK>
-__device__ __forceinline__ void dot_q4_0(uint32_t blk, const float (&x)[NTOK][32], const float (&xs)[NTOK][2],
-                                         float (&acc)[NTOK])
-{
-    const float d = h2f(lds_u16(blk));
-    const uint4 q = lds128_any<false>(blk + 2);
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    float s0[NTOK], s1[NTOK];
-#pragma unroll
-    for (int t = 0; t < NTOK; ++t) s0[t] = s1[t] = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const uint32_t lo = qw[w] & 0x0F0F0F0Fu, hi = (qw[w] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float flo = qf(lo, b), fhi = qf(hi, b);
-#pragma unroll
-            for (int t = 0; t < NTOK; ++t) {
-                s0[t] = fmaf(flo, x[t][4 * w + b], s0[t]);
-                s1[t] = fmaf(fhi, x[t][16 + 4 * w + b], s1[t]);
-            }
+        for (int t = 0; t < NTOK; ++t) {
+            B200Q_DOT_U(L, X[t], k, acc3[t][r0][0], acc3[t][r0][1], acc3[t][r0][2]);
+            B200Q_DOT_U(H, X[t], 8 + k, acc3[t][r1][0], acc3[t][r1][1], acc3[t][r1][2]);
         }
     }
 #pragma unroll
     for (int t = 0; t < NTOK; ++t) {
-        // sum (q-8)*x = S/256 - 128*X - 8*X
-        const float a0 = fmaf(s0[t], 1.0f / 256.0f, -136.0f * xs[t][0]);
-        const float a1 = fmaf(s1[t], 1.0f / 256.0f, -136.0f * xs[t][1]);
-        acc[t] = fmaf(d, a0 + a1, acc[t]);
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < 4; ++r)   // sum (q-32)*xq over a 16-value run
+            v = fmaf(sc[r], fmaf(-32.0f, X[t].qsum[r], planes_f(acc3[t][r][0], acc3[t][r][1], acc3[t][r][2])), v);
+        acc[t] = fmaf(d * X[t].s, v, acc[t]);
+    }
+}
+
+template <int NTOK>
+__device__ __forceinline__ void dot_q8_0(uint32_t blk, const XU<8> (&X)[NTOK], float (&acc)[NTOK])
+{
+    const float d = h2f(lds_u16(blk));
+    uint32_t q[8];
+    lds256_any(blk + 2, q);
+    int a2[NTOK], a1[NTOK], a0[NTOK];
+#pragma unroll
+    for (int t = 0; t < NTOK; ++t) a2[t] = a1[t] = a0[t] = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int t = 0; t < NTOK; ++t) {
+            a2[t] = dp4a_ss(q[k], X[t].b2[k], a2[t]);
+            a1[t] = dp4a_su(q[k], X[t].b1[k], a1[t]);
+            a0[t] = dp4a_su(q[k], X[t].b0[k], a0[t]);
+        }
+#pragma unroll
+    for (int t = 0; t < NTOK; ++t) acc[t] = fmaf(d * X[t].s, planes_f(a2[t], a1[t], a0[t]), acc[t]);
+}
+
+template <int NTOK>
+__device__ __forceinline__ void dot_q4_0(uint32_t blk, const XU<8> (&X)[NTOK], float (&acc)[NTOK])
+{
+    const float d = h2f(lds_u16(blk));
+    const uint4 q4 = lds128_any<false>(blk + 2);
+    const uint32_t w[4] = {q4.x, q4.y, q4.z, q4.w};
+    int a2[NTOK], a1[NTOK], a0[NTOK];
+#pragma unroll
+    for (int t = 0; t < NTOK; ++t) a2[t] = a1[t] = a0[t] = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t L = w[k] & 0x0F0F0F0Fu, H = (w[k] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int t = 0; t < NTOK; ++t) {
+            B200Q_DOT_U(L, X[t], k, a2[t], a1[t], a0[t]);
+            B200Q_DOT_U(H, X[t], 4 + k, a2[t], a1[t], a0[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NTOK; ++t) {
+        const float qs = X[t].qsum[0] + X[t].qsum[1];
+        acc[t] = fmaf(d * X[t].s, fmaf(-8.0f, qs, planes_f(a2[t], a1[t], a0[t])), acc[t]);
     }
 }
 
 template <int T, int NTOK, bool AL>
-__device__ __forceinline__ void unit_dot(uint32_t blk, int c, const float (&x)[NTOK][32], const float (&xs)[NTOK][2],
-                                         float (&acc)[NTOK])
+__device__ __forceinline__ void unit_dot(uint32_t blk, int c, const XU<Unit<T>::NW> (&X)[NTOK], float (&acc)[NTOK])
 {
-    if constexpr (T == T_Q4_K) dot_q4k<NTOK, AL>(blk, c, x, xs, acc);
-    else if constexpr (T == T_Q5_K) dot_q5k<NTOK, AL>(blk, c, x, xs, acc);
-    else if constexpr (T == T_Q6_K) dot_q6k<NTOK>(blk, c, x, xs, acc);
-    else if constexpr (T == T_Q8_0) dot_q8_0<NTOK>(blk, x, acc);
-    else dot_q4_0<NTOK>(blk, x, xs, acc);
+    if constexpr (T == T_Q4_K) dot_q4k<NTOK, AL>(blk, c, X, acc);
+    else if constexpr (T == T_Q5_K) dot_q5k<NTOK, AL>(blk, c, X, acc);
+    else if constexpr (T == T_Q6_K) dot_q6k<NTOK>(blk, c, X, acc);
+    else if constexpr (T == T_Q8_0) dot_q8_0<NTOK>(blk, X, acc);
+    else dot_q4_0<NTOK>(blk, X, acc);
+}
+
+// Packed activation of one (token, unit): the XU fields laid out as
+// 3*NW plane words, then s, sum[2], qsum[4], padded to a multiple of 4 words.
+template <int NW> struct XPackWords { static constexpr int N = ((3 * NW + 7) + 3) / 4 * 4; };
+
+// Cooperative quantisation of x [ntok, cols] into packed per-unit words in
+// shared memory (xs[(t * units + u) * N ...]).  NW consecutive lanes handle one
+// (token, unit), one 4-value word each; max/sums use shuffles inside the
+// NW-lane segment.  Every lane of the calling warps must execute this.
+template <int T>
+__device__ __forceinline__ void quantize_x_smem(const float *__restrict__ x, int cols, int units, int ntok,
+                                                uint32_t xs, int tid, int nthreads)
+{
+    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
+    const int tasks = ntok * units * NW;
+    for (int base = 0; base < tasks; base += nthreads) {
+        const int task = base + tid;
+        const bool valid = task < tasks;
+        const int k = task % NW, tu = task / NW;
+        const int u = tu % units, t = tu / units;
+        int c0 = 0, c1 = 0;
+        if (valid) unit_cols<T>(u, c0, c1);
+        const float4 f = valid ? __ldg(reinterpret_cast<const float4 *>(x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7)))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
+#pragma unroll
+        for (int o = 1; o < NW; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float inv = m > 0.f ? 8388607.0f / m : 0.f;
+        const float v[4] = {f.x, f.y, f.z, f.w};
+        uint32_t p2 = 0, p1 = 0, p0 = 0;
+        int qs = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int q = __float2int_rn(v[e] * inv);
+            q = max(-8388607, min(8388607, q));
+            p2 |= (uint32_t)((q >> 16) & 0xff) << (8 * e);
+            p1 |= (uint32_t)((q >> 8) & 0xff) << (8 * e);
+            p0 |= (uint32_t)(q & 0xff) << (8 * e);
+            qs += q;
+        }
+        float sm = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);      // 16-value runs
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);      // 32-value runs
+        if (valid) {
+            const uint32_t o = xs + (uint32_t)tu * N * 4;
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(p2) : "memory");
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(p1) : "memory");
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(p0) : "memory");
+            if (k == 0)
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(m > 0.f ? m / 8388607.0f : 0.f)) : "memory");
+            if ((k & 7) == 0)
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(sm)) : "memory");
+            if ((k & 3) == 0)
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)qs)) : "memory");
+        }
+    }
+}
+
+// Load one unit's packed activation from shared memory.
+template <int T>
+__device__ __forceinline__ void load_unit_x(uint32_t xsu, bool valid, XU<Unit<T>::NW> &X)
+{
+    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
+    uint32_t w[N];
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) {
+        const uint4 v = valid ? lds128(xsu + 16 * k) : make_uint4(0, 0, 0, 0);
+        w[4 * k] = v.x; w[4 * k + 1] = v.y; w[4 * k + 2] = v.z; w[4 * k + 3] = v.w;
+    }
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        X.b2[k] = w[k];
+        X.b1[k] = w[NW + k];
+        X.b0[k] = w[2 * NW + k];
+    }
+    X.s = __uint_as_float(w[3 * NW]);
+    X.sum[0] = __uint_as_float(w[3 * NW + 1]);
+    X.sum[1] = __uint_as_float(w[3 * NW + 2]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) X.qsum[r] = __uint_as_float(w[3 * NW + 3 + r]);
 }
 
 // ---------------------------------------------------------------- kernel
-// Shared layout: [full mbarriers][empty mbarriers] (128 B) | reduction
-// buffers | stage buffers (128-B aligned).
-// Thread cap per configuration so that the stationary x registers
-// (32 * CPT * NTOK floats) fit without spilling.
+// Shared layout: [full mbarriers][empty mbarriers] (128 B) | per-stage
+// partial-sum slots | quantised activations | stage buffers (128-B aligned).
+//
+// Roles.  Consumer warps: wait for a stage, add their units' dot products
+// for each of their rows, reduce the per-row values across the warp with a
+// butterfly (each lane ends with one finished row value), store them in the
+// stage's partial-sum slot and arrive on the stage's "empty" barrier.  The
+// producer warp: once a stage is empty it sums the per-warp partials of every
+// row in a fixed order, writes y, and refills the stage with the next row
+// tile.  Consumers never wait on each other.
+
+// Thread cap per configuration so that the stationary x registers fit.
 template <int CPT, int NTOK>
-struct GemvCap { static constexpr int THREADS = (CPT * NTOK >= 4) ? 256 : (CPT * NTOK == 2 ? 384 : 544); };
+struct GemvCap { static constexpr int THREADS = (CPT * NTOK >= 4) ? 256 : 384; };
+
+// Butterfly transpose-reduction of V values per lane (V a power of two <= 32):
+// afterwards every lane holds the warp-wide sum of value (lane >> (5 - log2 V)).
+template <int V>
+__device__ __forceinline__ float warp_transpose_reduce(float (&v)[V], int lane)
+{
+    int n = V;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (n > 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                if (i < n / 2) {
+                    const float send = up ? v[i] : v[i + n / 2];
+                    const float keep = up ? v[i + n / 2] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            n >>= 1;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+    return v[0];
+}
 
 template <int T, int CPT, int NTOK, int RPG, bool AL>
 __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const GemvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int UPB = Fmt<T>::UPB, BYTES = Fmt<T>::BYTES;
+    constexpr int BYTES = Fmt<T>::BYTES;
+    constexpr int V = RPG * NTOK;                                 // values per lane per pass
+    constexpr int LOGV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : 4;
     const int tid = threadIdx.x;
     const int ncons = a.groups * a.nct;
+    const int nwarps_c = ncons >> 5;
+    const int nwg = a.nct >> 5;                                   // warps per group
+    const int npass = (a.tokens + NTOK - 1) / NTOK;
+    const int slot_floats = npass * nwarps_c * V;                  // partials of one stage
     const uint32_t sbase = smem_addr(smem);
     const uint32_t full0 = sbase, empty0 = sbase + 8 * a.stages;
     float *red = reinterpret_cast<float *>(smem + 128);
-    const int nwg = a.nct >> 5;                                  // warps per group
-    const int red_per_buf = a.groups * nwg * RPG * NTOK;
-    const uint32_t stage0 = (sbase + 128 + 2 * red_per_buf * 4 + 127) & ~127u;
+    constexpr int NWX = Unit<T>::NW, NX = XPackWords<NWX>::N;
+    const uint32_t xbuf = (sbase + 128 + (uint32_t)a.stages * slot_floats * 4 + 15) & ~15u;
+    const uint32_t stage0 = (xbuf + (uint32_t)(a.tokens * a.units * NX * 4) + 127) & ~127u;
 
     const long long r_begin = (long long)blockIdx.x * a.rows / gridDim.x;
     const long long r_end = (long long)(blockIdx.x + 1) * a.rows / gridDim.x;
@@ -310,65 +476,93 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, ncons / 32);
+            mbar_init(empty0 + 8 * s, nwarps_c);
         }
         mbar_fence_init();
     }
     __syncthreads();
+    // Weights are read-only for the whole stream, so the weight stream starts
+    // before the dependency wait; x and y are touched only after pdl_wait().
+    pdl_launch_dependents();
 
-    if (tid >= ncons) {                        // ---- producer warp
-        if (tid != ncons) return;
+    if (tid >= ncons) {                        // ---- producer / reducer warp
+        const int lane = tid - ncons;
         const uint64_t pol = policy_evict_first();
-        int it = 0;
         bool ok = true;
-        for (; it < n_it && ok; ++it) {
+        int issued = 0;
+        for (int it = 0; it < n_it + a.stages && ok; ++it) {
             const int s = it % a.stages;
-            if (it >= a.stages && !mbar_wait(empty0 + 8 * s, ((it / a.stages) + 1) & 1, a.err)) {
-                ok = false;
-                break;
+            if (it >= a.stages) {              // stage j = it - S is consumed: reduce it
+                const int j = it - a.stages;
+                if (j == 0) pdl_wait();
+                if (!mbar_wait(empty0 + 8 * s, (j / a.stages) & 1, a.err)) { ok = false; break; }
+                const long long row0 = r_begin + (long long)j * a.stage_rows;
+                const int nr = (int)min((long long)a.stage_rows, r_end - row0);
+                const float *slot = red + s * slot_floats;
+                // value index: ((pass * groups + g) * V + rr * NTOK + t); warp partials
+                // of group g live at slot[(pass * nwarps_c + g * nwg + wig) * V + vi].
+                const int total = npass * a.groups * V;
+                for (int idx = lane; idx < total; idx += 32) {
+                    const int vi = idx % V, pg = idx / V;
+                    const int g = pg % a.groups, pass = pg / a.groups;
+                    const int rr = vi / NTOK, t = vi % NTOK;
+                    const int lr = g + rr * a.groups, tok = pass * NTOK + t;
+                    if (lr < nr && tok < a.tokens) {
+                        const float *pp = slot + (pass * nwarps_c + g * nwg) * V + vi;
+                        float v = 0.f;
+                        for (int w = 0; w < nwg; ++w) v += pp[w * V];
+                        a.y[tok * a.ys_t + (row0 + lr) * a.ys_r] = v;
+                    }
+                }
+                __syncwarp();
             }
-            const long long row0 = r_begin + (long long)it * a.stage_rows;
-            const int nr = (int)min((long long)a.stage_rows, r_end - row0);
-            const uint8_t *gs = a.w + row0 * a.rb;
-            const uint8_t *ge = gs + (long long)nr * a.rb;
-            const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~(uintptr_t)15);
-            const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(ge) & ~(uintptr_t)15);
-            const uint32_t dst = stage0 + (uint32_t)s * a.stage_bytes;
-            for (const uint8_t *p = a1; p < ge; ++p)              // < 16 tail bytes
-                asm volatile("st.shared.u8 [%0], %1;" ::"r"(dst + (uint32_t)(p - a0)), "h"((unsigned short)__ldg(p)));
-            const uint32_t nbytes = (uint32_t)(a1 - a0);
-            if (nbytes) {
-                mbar_arrive_expect_tx(full0 + 8 * s, nbytes);
-                bulk_g2s(dst, a0, nbytes, full0 + 8 * s, pol);
-            } else {
-                mbar_arrive(full0 + 8 * s);
+            if (it < n_it && lane == 0) {
+                const long long row0 = r_begin + (long long)it * a.stage_rows;
+                const int nr = (int)min((long long)a.stage_rows, r_end - row0);
+                const uint8_t *gs = a.w + row0 * a.rb;
+                const uint8_t *ge = gs + (long long)nr * a.rb;
+                const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~(uintptr_t)15);
+                const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(ge) & ~(uintptr_t)15);
+                const uint32_t dst = stage0 + (uint32_t)s * a.stage_bytes;
+                for (const uint8_t *p = a1; p < ge; ++p)           // < 16 tail bytes
+                    asm volatile("st.shared.u8 [%0], %1;" ::"r"(dst + (uint32_t)(p - a0)), "h"((unsigned short)__ldg(p)));
+                const uint32_t nbytes = (uint32_t)(a1 - a0);
+                if (nbytes) {
+                    mbar_arrive_expect_tx(full0 + 8 * s, nbytes);
+                    bulk_g2s(dst, a0, nbytes, full0 + 8 * s, pol);
+                } else {
+                    mbar_arrive(full0 + 8 * s);
+                }
+                issued = it + 1;
             }
+            __syncwarp();
         }
-        if (!ok) {                                // drain copies already issued
-            for (int j = max(0, it - a.stages); j < it; ++j)
+        if (!ok && lane == 0) {                // drain copies that may still be in flight
+            for (int j = max(0, issued - a.stages); j < issued; ++j)
                 mbar_wait(full0 + 8 * (j % a.stages), (j / a.stages) & 1, a.err);
         }
         return;
     }
 
     // ---- consumers
+    constexpr int UPB = Unit<T>::UPB, NW = Unit<T>::NW;
     const int g = tid / a.nct, lt = tid % a.nct;
     const int wig = lt >> 5, lane = tid & 31;
-    int ucol_lo[CPT], ucol_hi[CPT], uoff[CPT], uc[CPT];
+    const int cw = g * nwg + wig;                                  // consumer warp index
+    int uoff[CPT], uc[CPT], uidx[CPT];
     bool uval[CPT];
 #pragma unroll
     for (int i = 0; i < CPT; ++i) {
         const int u = lt + i * a.nct;
         uval[i] = u < a.units;
-        const int uu = uval[i] ? u : 0;
-        unit_cols<T>(uu, ucol_lo[i], ucol_hi[i]);
-        uoff[i] = (uu / UPB) * BYTES;
-        uc[i] = uu % UPB;
+        uidx[i] = uval[i] ? u : 0;
+        uoff[i] = (uidx[i] / UPB) * BYTES;
+        uc[i] = uidx[i] % UPB;
     }
-    float x[CPT][NTOK][32];
-    float xs[CPT][NTOK][2];
-    const int npass = (a.tokens + NTOK - 1) / NTOK;
-
+    XU<NW> X[CPT][NTOK];
+    pdl_wait();                                          // x may come from the previous kernel
+    quantize_x_smem<T>(a.x, a.cols, a.units, a.tokens, xbuf, tid, ncons);
+    named_bar_sync(1, ncons);
     auto load_x = [&](int pass) {
 #pragma unroll
         for (int i = 0; i < CPT; ++i)
@@ -376,25 +570,11 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
             for (int t = 0; t < NTOK; ++t) {
                 const int tok = pass * NTOK + t;
                 const bool v = uval[i] && tok < a.tokens;
-                const float *xl = a.x + (long long)(v ? tok : 0) * a.cols;
-                float slo = 0.f, shi = 0.f;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float4 l = v ? __ldg(reinterpret_cast<const float4 *>(xl + ucol_lo[i]) + q) : make_float4(0, 0, 0, 0);
-                    float4 h = v ? __ldg(reinterpret_cast<const float4 *>(xl + ucol_hi[i]) + q) : make_float4(0, 0, 0, 0);
-                    x[i][t][4 * q + 0] = l.x; x[i][t][4 * q + 1] = l.y; x[i][t][4 * q + 2] = l.z; x[i][t][4 * q + 3] = l.w;
-                    x[i][t][16 + 4 * q + 0] = h.x; x[i][t][16 + 4 * q + 1] = h.y;
-                    x[i][t][16 + 4 * q + 2] = h.z; x[i][t][16 + 4 * q + 3] = h.w;
-                    slo += (l.x + l.y) + (l.z + l.w);
-                    shi += (h.x + h.y) + (h.z + h.w);
-                }
-                xs[i][t][0] = slo;
-                xs[i][t][1] = shi;
+                load_unit_x<T>(xbuf + (uint32_t)(((v ? tok : 0) * a.units + uidx[i]) * NX * 4), v, X[i][t]);
             }
     };
     if (npass == 1) load_x(0);
 
-    int rbuf = 0;
     for (int it = 0; it < n_it; ++it) {
         const int s = it % a.stages;
         if (!mbar_wait(full0 + 8 * s, (it / a.stages) & 1, a.err)) return;
@@ -402,7 +582,7 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
         const int nr = (int)min((long long)a.stage_rows, r_end - row0);
         const uintptr_t gs = reinterpret_cast<uintptr_t>(a.w + row0 * a.rb);
         const uint32_t base = stage0 + (uint32_t)s * a.stage_bytes + (uint32_t)(gs & 15);
-
+        float *slot = red + s * slot_floats;
         for (int pass = 0; pass < npass; ++pass) {
             if (npass > 1) load_x(pass);
             float acc[RPG][NTOK];
@@ -410,73 +590,70 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
             for (int rr = 0; rr < RPG; ++rr)
 #pragma unroll
                 for (int t = 0; t < NTOK; ++t) acc[rr][t] = 0.f;
+            if (g + (RPG - 1) * a.groups < nr) {                  // full stage: no row checks
 #pragma unroll
-            for (int rr = 0; rr < RPG; ++rr) {
-                const int lr = g + rr * a.groups;
-                if (lr < nr) {
-                    const uint32_t rbase = base + (uint32_t)(lr * a.rb);
+                for (int rr = 0; rr < RPG; ++rr) {
+                    const uint32_t rbase = base + (uint32_t)((g + rr * a.groups) * a.rb);
 #pragma unroll
                     for (int i = 0; i < CPT; ++i)
-                        if (uval[i]) unit_dot<T, NTOK, AL>(rbase + uoff[i], uc[i], x[i], xs[i], acc[rr]);
+                        if (uval[i]) unit_dot<T, NTOK, AL>(rbase + uoff[i], uc[i], X[i], acc[rr]);
+                }
+            } else {
+#pragma unroll
+                for (int rr = 0; rr < RPG; ++rr) {
+                    const int lr = g + rr * a.groups;
+                    if (lr < nr) {
+                        const uint32_t rbase = base + (uint32_t)(lr * a.rb);
+#pragma unroll
+                        for (int i = 0; i < CPT; ++i)
+                            if (uval[i]) unit_dot<T, NTOK, AL>(rbase + uoff[i], uc[i], X[i], acc[rr]);
+                    }
                 }
             }
-            if (pass == npass - 1) {              // stage fully read by this warp
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty0 + 8 * s);
-            }
-            // warp reduction
+            float v[V];
 #pragma unroll
             for (int rr = 0; rr < RPG; ++rr)
 #pragma unroll
-                for (int t = 0; t < NTOK; ++t) {
-                    float v = acc[rr][t];
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    acc[rr][t] = v;
-                }
-            if (nwg == 1) {
-                if (lane == 0) {
-#pragma unroll
-                    for (int rr = 0; rr < RPG; ++rr) {
-                        const int lr = g + rr * a.groups;
-#pragma unroll
-                        for (int t = 0; t < NTOK; ++t) {
-                            const int tok = pass * NTOK + t;
-                            if (lr < nr && tok < a.tokens) a.y[tok * a.ys_t + (row0 + lr) * a.ys_r] = acc[rr][t];
-                        }
-                    }
-                }
-            } else {
-                float *rb = red + rbuf * red_per_buf + ((g * nwg + wig) * RPG) * NTOK;
-                if (lane == 0) {
-#pragma unroll
-                    for (int rr = 0; rr < RPG; ++rr)
-#pragma unroll
-                        for (int t = 0; t < NTOK; ++t) rb[rr * NTOK + t] = acc[rr][t];
-                }
-                named_bar_sync(1 + g, a.nct);
-                if (lt < RPG * NTOK) {
-                    const int rr = lt / NTOK, t = lt % NTOK;
-                    const int lr = g + rr * a.groups;
-                    const int tok = pass * NTOK + t;
-                    const float *gb = red + rbuf * red_per_buf + (g * nwg) * RPG * NTOK;
-                    float v = 0.f;
-                    for (int wv = 0; wv < nwg; ++wv) v += gb[wv * RPG * NTOK + lt];
-                    if (lr < nr && tok < a.tokens) a.y[tok * a.ys_t + (row0 + lr) * a.ys_r] = v;
-                }
-                rbuf ^= 1;
-            }
+                for (int t = 0; t < NTOK; ++t) v[rr * NTOK + t] = acc[rr][t];
+            const float r = warp_transpose_reduce<V>(v, lane);
+            if ((lane & ((32 >> LOGV) - 1)) == 0) slot[(pass * nwarps_c + cw) * V + (lane >> (5 - LOGV))] = r;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
     }
 }
 
 // ---------------------------------------------------------------- host side
-struct GemvPlan {
-    int cpt, ntok, rpg;
-    GemvArgs a;
-    size_t smem;
-    int threads;
-};
+// Launch with programmatic stream serialization (PDL).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Tuning knobs (defaults chosen on B200): target bytes of weights per stage
+// and number of stages.
+static int g_stage_target = 48 * 1024;
+static int g_stages = 3;
+static int g_rpg_max = 4;
+static int g_ctas_per_sm = 0;     // 0 = as many as fit
+void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm)
+{
+    if (stage_target_bytes > 0) g_stage_target = stage_target_bytes;
+    if (stages > 0) g_stages = stages;
+    if (rpg_max > 0) g_rpg_max = rpg_max;
+    if (ctas_per_sm >= 0) g_ctas_per_sm = ctas_per_sm;
+}
 
 template <int T, int CPT, int NTOK, int RPG, bool AL>
 static cudaError_t run_cfg(GemvArgs a, int threads, size_t smem, int num_sms, cudaStream_t st)
@@ -500,13 +677,13 @@ static cudaError_t run_cfg(GemvArgs a, int threads, size_t smem, int num_sms, cu
         occ_threads = threads;
         occ_smem = smem;
     }
-    const int per_sm = occ_per_sm;
+    int per_sm = occ_per_sm;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (g_ctas_per_sm > 0 && per_sm > g_ctas_per_sm) per_sm = g_ctas_per_sm;
     const long long tiles = (a.rows + a.stage_rows - 1) / a.stage_rows;
     long long grid = (long long)num_sms * per_sm;
     if (grid > tiles) grid = tiles;
-    kern<<<(int)grid, threads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, st, a);
 }
 
 template <int T, int CPT, int NTOK, int RPG>
@@ -521,11 +698,14 @@ static cudaError_t run_al(GemvArgs a, int threads, size_t smem, int num_sms, cud
 template <int T, int CPT, int NTOK>
 static cudaError_t run_rpg(GemvArgs a, int rpg, int threads, size_t smem, int num_sms, cudaStream_t st, bool al)
 {
-    switch (rpg) {
-    case 1: return run_al<T, CPT, NTOK, 1>(a, threads, smem, num_sms, st, al);
-    case 2: return run_al<T, CPT, NTOK, 2>(a, threads, smem, num_sms, st, al);
-    default: return run_al<T, CPT, NTOK, 4>(a, threads, smem, num_sms, st, al);
+    if constexpr (CPT * NTOK == 1) {
+        switch (rpg) {
+        case 1: return run_al<T, CPT, NTOK, 1>(a, threads, smem, num_sms, st, al);
+        case 2: return run_al<T, CPT, NTOK, 2>(a, threads, smem, num_sms, st, al);
+        default: return run_al<T, CPT, NTOK, 4>(a, threads, smem, num_sms, st, al);
+        }
     }
+    return run_al<T, CPT, NTOK, 1>(a, threads, smem, num_sms, st, al);
 }
 
 template <int T>
@@ -540,25 +720,14 @@ static cudaError_t run_type(GemvArgs a, int cpt, int ntok, int rpg, int threads,
     return run_rpg<T, 4, 1>(a, rpg, threads, smem, num_sms, st, al);
 }
 
-// Tuning knobs (defaults chosen on B200): target bytes of weights per stage
-// and number of stages.
-static int g_stage_target = 24 * 1024;
-static int g_stages = 4;
-void gemv_set_tuning(int stage_target_bytes, int stages)
-{
-    if (stage_target_bytes > 0) g_stage_target = stage_target_bytes;
-    if (stages > 0) g_stages = stages;
-}
-
-// Returns cudaErrorInvalidValue for unsupported shapes (cols not a multiple
-// of the block size, or more than 65536 columns).
-cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
-                        int cols, int tokens, int *err, int num_sms, cudaStream_t st)
+// One launch over tokens [0, tokens) of the given x/y.
+static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r,
+                                     int rows, int cols, int tokens, int *err, int num_sms, cudaStream_t st)
 {
     const int vals = type_vals(type), bytes = type_bytes(type);
-    if (!bytes || rows < 1 || tokens < 1 || cols < vals || cols % vals) return cudaErrorInvalidValue;
-    const int upb = (vals == 256) ? 8 : 1;
+    const int upb = (vals == 256) ? 4 : 1;     // 64-value units in a K-quant block
     const int units = (cols / vals) * upb;
+    const int nx = (vals == 256) ? XPackWords<16>::N : XPackWords<8>::N;
     // Smallest units-per-thread (CPT) whose group fits the thread cap of its
     // register budget; NTOK = tokens held in registers per pass.
     int cpt = 0, ntok = 1, nct = 0, cap = 0;
@@ -566,24 +735,27 @@ cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long 
         int nt = 1;
         if (c == 1) nt = tokens >= 3 ? 4 : tokens;
         else if (c == 2) nt = tokens >= 2 ? 2 : 1;
-        const int cp = (c * nt >= 4) ? 256 : (c * nt == 2 ? 384 : 544);
+        const int cp = (c * nt >= 4) ? 256 : 384;
         const int n = (((units + c - 1) / c) + 31) / 32 * 32;
         if (n + 32 <= cp) { cpt = c; ntok = nt; nct = n; cap = cp; }
     }
     if (!cpt) return cudaErrorInvalidValue;
     const int rb = (cols / vals) * bytes;
     int rpg = 1;
-    if (4 * rb <= g_stage_target / 2) rpg = 4;
-    else if (2 * rb <= g_stage_target / 2) rpg = 2;
+    if (cpt * ntok == 1) {
+        if (g_rpg_max >= 4 && 4 * rb <= g_stage_target / 2) rpg = 4;
+        else if (g_rpg_max >= 2 && 2 * rb <= g_stage_target / 2) rpg = 2;
+    }
     int groups = std::max(1, std::min({(cap - 32) / nct, 15, g_stage_target / (rpg * rb)}));
     const int stage_rows = groups * rpg;
     const int stage_bytes = ((stage_rows * rb + 64) + 127) / 128 * 128;
-    const int nwg = nct / 32;
-    const int red_bytes = 2 * groups * nwg * rpg * ntok * 4;
+    const int npass = (tokens + ntok - 1) / ntok;
+    const int slot_bytes = npass * groups * (nct / 32) * rpg * ntok * 4;
+    const size_t xbytes = (size_t)tokens * units * nx * 4 + 16;
     int stages = g_stages;
-    const size_t fixed = 128 + red_bytes + 128;
-    while (stages > 2 && fixed + (size_t)stages * stage_bytes > 220 * 1024) --stages;
-    const size_t smem = fixed + (size_t)stages * stage_bytes;
+    auto smem_of = [&](int stg) { return 128 + (size_t)stg * slot_bytes + xbytes + 128 + (size_t)stg * stage_bytes; };
+    while (stages > 2 && smem_of(stages) > 220 * 1024) --stages;
+    const size_t smem = smem_of(stages);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
 
     GemvArgs a;
@@ -613,6 +785,28 @@ cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long 
     case T_Q4_0: return run_type<T_Q4_0>(a, cpt, ntok, rpg, threads, smem, num_sms, st, al);
     default: return cudaErrorInvalidValue;
     }
+}
+
+// Returns cudaErrorInvalidValue for unsupported shapes (cols not a multiple
+// of the block size, or rows too wide for the register budget).  Token
+// batches whose quantised activations do not fit in shared memory next to the
+// weight pipeline are processed in chunks of tokens (one launch each).
+cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
+                        int cols, int tokens, int *err, int num_sms, cudaStream_t st)
+{
+    const int vals = type_vals(type), bytes = type_bytes(type);
+    if (!bytes || rows < 1 || tokens < 1 || cols < vals || cols % vals) return cudaErrorInvalidValue;
+    const int units = (cols / vals) * ((vals == 256) ? 4 : 1);
+    const size_t per_tok = (size_t)units * ((vals == 256) ? XPackWords<16>::N : XPackWords<8>::N) * 4;
+    int chunk = (int)std::max<size_t>(1, (96 * 1024) / per_tok);
+    if (chunk > 64) chunk = 64;
+    for (int t0 = 0; t0 < tokens; t0 += chunk) {
+        const int n = std::min(chunk, tokens - t0);
+        cudaError_t e = launch_gemv_chunk(type, w, x + (long long)t0 * cols, y + t0 * ys_t, ys_t, ys_r, rows, cols, n,
+                                          err, num_sms, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 } // namespace b200q
