@@ -101,6 +101,24 @@ int b200q_dequant_bf16_dev(int ggml_type, const void *w, void *out_bf16, long lo
 int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int rows, int cols, int tokens,
                    long long ys_t, long long ys_r, void *stream);
 
+/* Grouped GEMM on the tcgen05 tensor cores with in-kernel Q4_K dequant
+ * (bf16 operands, f32 accumulation; the batched path of
+ * engine/native_quant.cpp:620-703 and the expert products of
+ * engine/zaya.py:303-306).  Group g owns activation rows
+ * [row_off[g], row_off[g+1]) of x_bf16 [x_rows, k] (row_off: device int32
+ * [groups+1]) and weight rows [g*w_rows_per_group, ...) of the raw Q4_K
+ * tensor w (rows of ceil(k/256) super-blocks; k a multiple of 64).
+ *   up_offset <  0: plain mode, out[row*ld_out + n] = x_row . w_n (times
+ *                   row_scale[row] if row_scale != NULL), n < n_feat (multiple
+ *                   of 128);
+ *   up_offset >= 0: gate/up mode over n_feat features (multiple of 64):
+ *                   act[row*ld_act + f] = bf16(SiLU(x.w_f) * (x.w_{f+up_offset})),
+ *                   SiLU as engine/zaya.py:305.
+ * max_ctas limits the persistent grid (0 = one CTA per SM). */
+int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *w, int groups, int w_rows_per_group,
+                       int up_offset, int n_feat, const int *row_off, float *out, long long ld_out,
+                       const float *row_scale, void *act_bf16, long long ld_act, int max_ctas, void *stream);
+
 /* Device error word: returns and clears the sticky kernel error of the
  * current device (0 if none).  Synchronises the device. */
 int b200q_check_device_error(void);

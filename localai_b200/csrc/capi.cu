@@ -20,6 +20,10 @@ cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, l
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st);
 void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm);
+cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
+                               int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
+                               float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
+                               long long ld_act, int *err, int num_sms, int max_ctas, cudaStream_t st);
 
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
@@ -340,6 +344,24 @@ B200Q_API int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float
     return cuda_status(launch_gemv(ggml_type, w, x, y, ys_t, ys_r, rows, cols, tokens, di->err, di->sms,
                                    (cudaStream_t)stream),
                        "gemv");
+}
+
+B200Q_API int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *w, int groups,
+                                 int w_rows_per_group, int up_offset, int n_feat, const int *row_off, float *out,
+                                 long long ld_out, const float *row_scale, void *act_bf16, long long ld_act,
+                                 int max_ctas, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!x_bf16 || !w || !row_off) return set_status(B200Q_EINVAL, "gemm: null pointer");
+    if (up_offset >= 0 ? !act_bf16 : !out) return set_status(B200Q_EINVAL, "gemm: missing output");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(x_bf16), x_rows, k, w, groups,
+                                          w_rows_per_group, up_offset, n_feat, row_off, out, ld_out, row_scale,
+                                          static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
+                                          (cudaStream_t)stream),
+                       "gemm");
 }
 
 B200Q_API int b200q_check_device_error(void)

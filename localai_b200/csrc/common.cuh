@@ -139,6 +139,19 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Q4_K/Q5_K: the four 6-bit fields (scale, scale, min, min) of sub-blocks
+// 2p and 2p+1 packed into bytes (engine/dequant.py:108-113).
+__device__ __forceinline__ uint32_t k_scales_packed(const uint4 hdr, int p)
+{
+    const bool hk = p >= 2;
+    const uint32_t i0 = (2 * p) & 3;
+    const uint32_t sel = i0 | ((i0 + 1) << 4) | ((i0 + 4) << 8) | ((i0 + 5) << 12);
+    const uint32_t lowsrc = __byte_perm(hk ? hdr.w : hdr.y, hk ? hdr.w : hdr.z, sel);
+    const uint32_t lo4 = (lowsrc & 0x00000F0Fu) | ((lowsrc >> (hk ? 4 : 0)) & 0x0F0F0000u);
+    const uint32_t top = __byte_perm(hdr.y, hdr.z, sel);
+    return lo4 | ((top >> (hk ? 2 : 0)) & 0x30303030u);
+}
+
 // ---------------------------------------------------------------- shared loads
 __device__ __forceinline__ uint32_t lds32(uint32_t a)
 {

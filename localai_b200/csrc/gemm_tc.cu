@@ -1,0 +1,522 @@
+// Grouped GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) with the
+// GGML weights dequantised inside the kernel.
+//
+// For every group g (an expert, or the single weight matrix of a dense
+// prefill) and its M_g activation rows [row_off[g], row_off[g+1]) of a bf16
+// matrix X:
+//     C_g[m, n] = sum_k X[row_off[g] + m, k] * W_g[n, k]
+// where W_g is stored as raw GGUF blocks (Q4_K) -- the batched path of the
+// reference (engine/native_quant.cpp:620-703 decoded_matmul_row / MatmulPool,
+// and the per-expert products of engine/zaya.py:303-306).
+//
+// Tile: 128 weight rows (MMA M) x 256 activation rows (MMA N) x the full K, in
+// K-steps of 64 (one 128-byte swizzle atom of bf16).
+//
+// Warp roles (512 threads, one CTA per SM, persistent over tiles):
+//   warp 0        TMA: activation box [64 k x 256 rows] (SWIZZLE_128B) per
+//                 K-step, raw weight boxes [one 256-value block x 64 rows] x 2
+//                 per 256-K chunk;
+//   warp 1        TMEM allocator; lane 0 issues tcgen05.mma (kind::f16, bf16
+//                 in, f32 accumulate in TMEM; two 256-column accumulators so
+//                 the epilogue of one tile overlaps the main loop of the next)
+//                 and tcgen05.commit;
+//   warps 4-7     epilogue: tcgen05.ld of the accumulator, then either
+//                 (gate/up mode) SiLU(gate) * up -> bf16, or (plain mode) a
+//                 per-row scaled f32 store;
+//   warps 8-15    dequantisers: raw Q4_K block bytes (shared memory) -> bf16 A
+//                 tile in the canonical K-major SWIZZLE_128B layout.
+// All waits are bounded (an error word is set and the CTA leaves).
+//
+// Gate/up mode computes, for 64 features f0..f0+63, the 64 gate rows and the 64
+// up rows of the same features in one tile, ordered so that every warp holds
+// 16 gate rows and the 16 matching up rows (lanes l and l+16).
+#include "common.cuh"
+
+#include <cuda.h>
+#include <algorithm>
+#include <mutex>
+
+namespace b200q {
+
+constexpr int TC_BM = 128;              // weight rows per tile (MMA M)
+constexpr int TC_BN = 256;              // activation rows per tile (MMA N)
+constexpr int TC_BK = 64;               // K per stage (bf16, 128 bytes)
+constexpr int TC_STAGES = 3;            // A/B pipeline depth
+constexpr int TC_RAW_STAGES = 2;        // raw weight chunk pipeline depth
+constexpr int TC_THREADS = 512;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;     // 16 KB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;     // 32 KB
+constexpr int TC_MAX_GROUPS = 1024;
+
+struct TcArgs {
+    int n_tiles;            // weight-row tiles per group (N/128, or F/64 in gate/up mode)
+    int k;                  // reduction length (multiple of 64)
+    int groups;
+    const int *row_off;     // [groups + 1] activation row offsets (device)
+    int w_rows_per_group;   // weight rows of one group in the raw tensor map
+    int up_offset;          // gate/up mode: row offset of the up half (F); < 0: plain mode
+    int raw_chunk_bytes;    // bytes of one 256-value block
+    // epilogue
+    float *out;             // plain mode: out[row * ld_out + n]
+    long long ld_out;
+    const float *row_scale; // plain mode, optional: out *= row_scale[row]
+    __nv_bfloat16 *act;     // gate/up mode: act[row * ld_act + f]
+    long long ld_act;
+    int *err;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, f32 accumulation.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive (once) on an mbarrier when every MMA issued so far by this thread completes.
+__device__ __forceinline__ void umma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (stride byte offset), leading byte offset 16 (unused by the
+// swizzled K-major form), descriptor version 1 (sm100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((smem & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16 (K-major), D = f32, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
+{
+    __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&p);
+}
+
+__device__ __forceinline__ float silu_ref(float g)
+{
+    // engine/zaya.py:305: g / (1 + exp(-clip(g, -80, 80)))
+    const float c = fminf(fmaxf(g, -80.f), 80.f);
+    return g / (1.0f + expf(-c));
+}
+
+// ---------------------------------------------------------------- dequant
+// Q4_K: one K-step (pair p of a super-block) of one tile row and one half
+// (h = 0: sub-block 2p, low nibbles -> K columns 0..31; h = 1: sub-block
+// 2p+1, high nibbles -> K columns 32..63) into the SWIZZLE_128B A tile.
+__device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, int p, int h, uint32_t a_row, int r)
+{
+    const uint4 hdr = lds128(raw_row);
+    const uint4 q0 = lds128(raw_row + 16 + 32 * p), q1 = lds128(raw_row + 32 + 32 * p);
+    // bytes [sc(2p), sc(2p+1), mn(2p), mn(2p+1)] (engine/dequant.py:108-113)
+    const uint32_t sp = k_scales_packed(hdr, p);
+    const uint32_t sc = (sp >> (8 * h)) & 0xffu, mn = (sp >> (8 * (2 + h))) & 0xffu;
+    const float s = h2f(hdr.x) * (float)sc;            // exact
+    const float m = h2f(hdr.x >> 16) * (float)mn;      // exact
+    // q -> f = 0.5 + q/256 (byte q placed under exponent 2^-1), value = 256 s f - (128 s + m)
+    const float A = 256.0f * s, B = -(128.0f * s + m);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {                       // 16-byte chunk = 8 K columns
+        uint32_t o[4];
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const uint32_t wd = w[2 * c + ww];
+            const uint32_t nib = h ? ((wd >> 4) & 0x0F0F0F0Fu) : (wd & 0x0F0F0F0Fu);
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                v[b] = fmaf(A, __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7044u | (uint32_t)(b << 8))), B);
+            o[2 * ww] = pack_bf16(v[0], v[1]);
+            o[2 * ww + 1] = pack_bf16(v[2], v[3]);
+        }
+        const uint32_t chunk = (uint32_t)(4 * h + c);
+        const uint32_t dst = a_row + ((chunk ^ (uint32_t)(r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- kernel
+struct TileCoord {
+    int g, nt, m0, rows;    // group, weight-row tile, first activation row (local), valid rows
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int t, const int *tile_pref, const int *row_off, int groups,
+                                                int n_tiles)
+{
+    int lo = 0, hi = groups;                 // largest g with tile_pref[g] <= t
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (tile_pref[mid] <= t) lo = mid; else hi = mid;
+    }
+    TileCoord c;
+    c.g = lo;
+    const int local = t - tile_pref[lo];
+    const int mrows = row_off[lo + 1] - row_off[lo];
+    const int mt = (mrows + TC_BN - 1) / TC_BN;
+    c.nt = local / mt;
+    c.m0 = (local % mt) * TC_BN;
+    c.rows = min(TC_BN, mrows - c.m0);
+    return c;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                       const TcArgs a)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-aligned base for the swizzled tiles
+    const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    const uint32_t sA = base;
+    const uint32_t sB = sA + TC_STAGES * TC_A_BYTES;
+    const uint32_t sRaw = sB + TC_STAGES * TC_B_BYTES;
+    const uint32_t raw_stage_bytes = (uint32_t)(TC_BM * a.raw_chunk_bytes);
+    const uint32_t sBar = (sRaw + TC_RAW_STAGES * raw_stage_bytes + 7u) & ~7u;
+    const uint32_t full = sBar;                               // [STAGES]   8 dequant warps + TMA tx
+    const uint32_t empty = full + 8 * TC_STAGES;              // [STAGES]   MMA commit
+    const uint32_t raw_full = empty + 8 * TC_STAGES;          // [RAW]      TMA tx
+    const uint32_t raw_empty = raw_full + 8 * TC_RAW_STAGES;  // [RAW]      8 dequant warps
+    const uint32_t acc_full = raw_empty + 8 * TC_RAW_STAGES;  // [2]        MMA commit
+    const uint32_t acc_empty = acc_full + 16;                 // [2]        4 epilogue warps
+    const uint32_t tmem_slot = acc_empty + 16;
+    __shared__ int tile_pref[TC_MAX_GROUPS + 1];
+    __shared__ int row_off_s[TC_MAX_GROUPS + 1];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ksteps = a.k / TC_BK;
+
+    if (tid == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            mbar_init(full + 8 * s, 8 + 1);
+            mbar_init(empty + 8 * s, 1);
+        }
+        for (int s = 0; s < TC_RAW_STAGES; ++s) {
+            mbar_init(raw_full + 8 * s, 1);
+            mbar_init(raw_empty + 8 * s, 8);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(acc_full + 8 * s, 1);
+            mbar_init(acc_empty + 8 * s, 4);
+        }
+        mbar_fence_init();
+    }
+    // tile prefix over groups (every CTA computes the same table)
+    if (warp == 2) {
+        for (int g = lane; g <= a.groups; g += 32) row_off_s[g] = a.row_off[g];
+        __syncwarp();
+        if (lane == 0) {
+            int acc = 0;
+            for (int g = 0; g < a.groups; ++g) {
+                tile_pref[g] = acc;
+                const int m = row_off_s[g + 1] - row_off_s[g];
+                acc += (m > 0 ? (m + TC_BN - 1) / TC_BN : 0) * a.n_tiles;
+            }
+            tile_pref[a.groups] = acc;
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = lds32(tmem_slot);
+    const int total_tiles = tile_pref[a.groups];
+    const bool gate_up = a.up_offset >= 0;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int q = 0, rq = 0;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
+                const int wrow0 = c.g * a.w_rows_per_group + (gate_up ? c.nt * 64 : c.nt * TC_BM);
+                const int wrow1 = gate_up ? wrow0 + a.up_offset : wrow0 + 64;
+                const int xrow = row_off_s[c.g] + c.m0;
+                for (int ks = 0; ks < ksteps && ok; ++ks) {
+                    if ((ks & 3) == 0) {
+                        const int rs = rq % TC_RAW_STAGES;
+                        if (rq >= TC_RAW_STAGES && !mbar_wait(raw_empty + 8 * rs, ((rq / TC_RAW_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                        const uint32_t dst = sRaw + rs * raw_stage_bytes;
+                        mbar_arrive_expect_tx(raw_full + 8 * rs, raw_stage_bytes);
+                        const int xb = (ks >> 2) * a.raw_chunk_bytes;
+                        tma_load_2d(dst, &map_w, xb, wrow0, raw_full + 8 * rs);
+                        tma_load_2d(dst + 64 * a.raw_chunk_bytes, &map_w, xb, wrow1, raw_full + 8 * rs);
+                        ++rq;
+                    }
+                    const int s = q % TC_STAGES;
+                    if (q >= TC_STAGES && !mbar_wait(empty + 8 * s, ((q / TC_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full + 8 * s, TC_B_BYTES);
+                    tma_load_2d(sB + s * TC_B_BYTES, &map_x, ks * TC_BK, xrow, full + 8 * s);
+                    ++q;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(TC_BM, TC_BN);
+            int q = 0, acc = 0;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
+                const int ab = acc & 1;
+                if (acc >= 2 && !mbar_wait(acc_empty + 8 * ab, ((acc >> 1) + 1) & 1, a.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ab * TC_BN);
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    const int s = q % TC_STAGES;
+                    if (!mbar_wait(full + 8 * s, (q / TC_STAGES) & 1, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t as = sA + s * TC_A_BYTES, bs = sB + s * TC_B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; ++kk)
+                        umma_bf16(d_tmem, sw128_desc(as + 32 * kk), sw128_desc(bs + 32 * kk), idesc,
+                                  (ks > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(empty + 8 * s);
+                    ++q;
+                }
+                if (!ok) break;
+                umma_commit(acc_full + 8 * ab);
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------ epilogue
+        const int ew = warp - 4;
+        int acc = 0;
+        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
+            const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
+            const int ab = acc & 1;
+            if (!mbar_wait(acc_full + 8 * ab, (acc >> 1) & 1, a.err)) { ok = false; break; }
+            tc_fence_after();
+            const long long row_base = row_off_s[c.g] + c.m0;
+            for (int ch = 0; ch < TC_BN / 32; ++ch) {
+                if (ch * 32 >= c.rows) break;                       // warp-uniform
+                uint32_t v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(32 * ew) << 16) + (uint32_t)(ab * TC_BN + 32 * ch), v);
+                tmem_ld_wait();
+                if (gate_up) {
+                    const int f = c.nt * 64 + 16 * ew + (lane & 15);
+                    const bool lo = lane < 16;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float mine_g = __uint_as_float(v[j]), mine_h = __uint_as_float(v[16 + j]);
+                        const float recv = __shfl_xor_sync(0xffffffffu, lo ? mine_h : mine_g, 16);
+                        const float gv = lo ? mine_g : recv, uv = lo ? recv : mine_h;
+                        const int col = 32 * ch + (lo ? j : 16 + j);
+                        if (col < c.rows)
+                            a.act[(row_base + col) * a.ld_act + f] = __float2bfloat16_rn(silu_ref(gv) * uv);
+                    }
+                } else {
+                    const int n = c.nt * TC_BM + 32 * ew + lane;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = 32 * ch + j;
+                        if (col < c.rows) {
+                            const long long row = row_base + col;
+                            const float sc = a.row_scale ? __ldg(a.row_scale + row) : 1.0f;
+                            a.out[row * a.ld_out + n] = __uint_as_float(v[j]) * sc;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------ dequantisers
+        const int dt = tid - 256;                   // 0..255
+        const int r = dt & 127, h = dt >> 7;
+        const int ew = r >> 5, l = r & 31;
+        // raw row of tile row r
+        const int raw_r = gate_up ? ((l < 16) ? 16 * ew + (l & 15) : 64 + 16 * ew + (l & 15)) : r;
+        int q = 0, rq = 0;
+        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < ksteps && ok; ++ks) {
+                const int rs = rq % TC_RAW_STAGES;
+                if ((ks & 3) == 0 && !mbar_wait(raw_full + 8 * rs, (rq / TC_RAW_STAGES) & 1, a.err)) { ok = false; break; }
+                const int s = q % TC_STAGES;
+                if (q >= TC_STAGES && !mbar_wait(empty + 8 * s, ((q / TC_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                const uint32_t raw_row = sRaw + rs * raw_stage_bytes + (uint32_t)(raw_r * a.raw_chunk_bytes);
+                dequant_q4k_half(raw_row, ks & 3, h, sA + s * TC_A_BYTES + (uint32_t)(r * 128), r);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full + 8 * s);
+                ++q;
+                if ((ks & 3) == 3 || ks == ksteps - 1) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(raw_empty + 8 * rs);
+                    ++rq;
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode()
+{
+    static PFN_encodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+    });
+    return fn;
+}
+
+// bf16 [rows, cols] row-major, box [64 cols x box_rows], 128-byte swizzle.
+static cudaError_t make_map_bf16(CUtensorMap *m, const void *ptr, long long rows, long long cols, int box_rows)
+{
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16) return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// raw bytes [rows, row_bytes], box [chunk_bytes x 64 rows], no swizzle.
+static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows, long long row_bytes, int chunk_bytes)
+{
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || row_bytes % 16 || chunk_bytes % 16 || chunk_bytes > 256)
+        return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)chunk_bytes, 64};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+size_t tc_gemm_smem_bytes(int chunk_bytes)
+{
+    return 1024 + (size_t)TC_STAGES * (TC_A_BYTES + TC_B_BYTES) + (size_t)TC_RAW_STAGES * TC_BM * chunk_bytes + 256;
+}
+
+// Grouped GEMM, Q4_K weights.
+//   x        bf16 [x_rows, k] activations (rows of group g: row_off[g]..row_off[g+1])
+//   w        raw Q4_K bytes of groups*w_rows_per_group rows of k values each
+//   up_offset >= 0: gate/up mode over n_feat features (act bf16 [x_rows, ld_act]);
+//            < 0: plain mode over n_feat output columns (out f32 [x_rows, ld_out]).
+cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
+                               int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
+                               float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
+                               long long ld_act, int *err, int num_sms, int max_ctas, cudaStream_t st)
+{
+    if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
+    if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
+    const bool gu = up_offset >= 0;
+    if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
+    const int chunk = 144;
+    const long long kpad = ((long long)k + 255) / 256 * 256;     // raw rows hold whole super-blocks
+    const long long row_bytes = kpad / 256 * chunk;
+    CUtensorMap mx, mw;
+    cudaError_t e = make_map_bf16(&mx, x, x_rows, k, TC_BN);
+    if (e != cudaSuccess) return e;
+    e = make_map_raw(&mw, w, (long long)groups * w_rows_per_group, row_bytes, chunk);
+    if (e != cudaSuccess) return e;
+    TcArgs a;
+    a.n_tiles = gu ? n_feat / 64 : n_feat / TC_BM;
+    a.k = k;
+    a.groups = groups;
+    a.row_off = row_off;
+    a.w_rows_per_group = w_rows_per_group;
+    a.up_offset = up_offset;
+    a.raw_chunk_bytes = chunk;
+    a.out = out;
+    a.ld_out = ld_out;
+    a.row_scale = row_scale;
+    a.act = act;
+    a.ld_act = ld_act;
+    a.err = err;
+    const size_t smem = tc_gemm_smem_bytes(chunk);
+    static bool attr = false;
+    if (!attr) {
+        e = cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    int grid = num_sms;
+    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+    tc_gemm_q4k_kernel<<<grid, TC_THREADS, smem, st>>>(mx, mw, a);
+    return cudaGetLastError();
+}
+
+} // namespace b200q

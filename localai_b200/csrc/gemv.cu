@@ -141,19 +141,6 @@ __device__ __forceinline__ void lds128x2(uint32_t a, uint32_t o[8], bool aligned
 
 __device__ __forceinline__ float ubyte_f(uint32_t v, int k) { return (float)((v >> (8 * k)) & 0xffu); }
 
-// Q4_K/Q5_K: the four 6-bit fields (scale, scale, min, min) of sub-blocks
-// 2p and 2p+1 packed into bytes (engine/dequant.py:108-113).
-__device__ __forceinline__ uint32_t k_scales_packed(const uint4 hdr, int p)
-{
-    const bool hk = p >= 2;
-    const uint32_t i0 = (2 * p) & 3;
-    const uint32_t sel = i0 | ((i0 + 1) << 4) | ((i0 + 4) << 8) | ((i0 + 5) << 12);
-    const uint32_t lowsrc = __byte_perm(hk ? hdr.w : hdr.y, hk ? hdr.w : hdr.z, sel);
-    const uint32_t lo4 = (lowsrc & 0x00000F0Fu) | ((lowsrc >> (hk ? 4 : 0)) & 0x0F0F0000u);
-    const uint32_t top = __byte_perm(hdr.y, hdr.z, sel);
-    return lo4 | ((top >> (hk ? 2 : 0)) & 0x30303030u);
-}
-
 // ---------------------------------------------------------------- unit dots
 // Each adds the unit's contribution for NTOK tokens into acc[].
 // blk: shared address of the block start; p: unit index inside the block.

@@ -84,3 +84,44 @@ def check_device_error() -> None:
     code = _lib.load().b200q_check_device_error()
     if code:
         raise _lib.B200QError(f'kernel error word {code}')
+
+
+def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k: int, n_feat: int,
+             w_rows_per_group: int, up_offset: int = -1, out: torch.Tensor | None = None,
+             row_scale: torch.Tensor | None = None, act: torch.Tensor | None = None,
+             max_ctas: int = 0) -> torch.Tensor:
+    """Grouped tensor-core GEMM with in-kernel Q4_K dequantisation.
+
+    ``x_bf16`` [rows, k] bf16 activations; group g owns rows
+    ``row_off[g]:row_off[g+1]`` (int32 CUDA tensor, groups+1 entries) and
+    weight rows ``g*w_rows_per_group ...`` of ``w`` (raw Q4_K bytes).
+    Plain mode (``up_offset < 0``) returns f32 [rows, n_feat]; gate/up mode
+    returns bf16 [rows, n_feat] = SiLU(gate) * up with up rows at
+    ``f + up_offset``.
+    """
+    if x_bf16.dtype != torch.bfloat16 or not x_bf16.is_cuda or x_bf16.dim() != 2 or x_bf16.shape[1] != k:
+        raise ValueError('x must be a CUDA bf16 [rows, k] tensor')
+    if row_off.dtype != torch.int32 or not row_off.is_cuda:
+        raise ValueError('row_off must be a CUDA int32 tensor')
+    x_bf16 = x_bf16.contiguous()
+    rows = x_bf16.shape[0]
+    groups = row_off.numel() - 1
+    kpad = (k + 255) // 256 * 256
+    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < groups * w_rows_per_group * (kpad // 256) * 144:
+        raise ValueError('w must hold groups * w_rows_per_group Q4_K rows')
+    lib = _lib.load()
+    if up_offset >= 0:
+        if act is None:
+            act = torch.empty((rows, n_feat), dtype=torch.bfloat16, device=x_bf16.device)
+        st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, up_offset,
+                                    n_feat, row_off.data_ptr(), None, 0, None, act.data_ptr(), act.stride(0),
+                                    max_ctas, _stream())
+        _lib.check(st)
+        return act
+    if out is None:
+        out = torch.empty((rows, n_feat), dtype=torch.float32, device=x_bf16.device)
+    st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, -1, n_feat,
+                                row_off.data_ptr(), out.data_ptr(), out.stride(0),
+                                None if row_scale is None else row_scale.data_ptr(), None, 0, max_ctas, _stream())
+    _lib.check(st)
+    return out
