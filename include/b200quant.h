@@ -119,6 +119,30 @@ int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *
                        int up_offset, int n_feat, const int *row_off, float *out, long long ld_out,
                        const float *row_scale, void *act_bf16, long long ld_act, int max_ctas, void *stream);
 
+/* ---- MoE layer stages (engine/zaya.py:274-307, generalised to top-k) ----
+ * All buffers are device memory owned by the caller; nothing is allocated. */
+/* logits[t*E + e] = h[t] . wr[e] + bias[e] (f32; bias may be NULL). */
+int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
+                         void *stream);
+/* Softmax over each row of logits (f32, max-subtracted, engine/zaya.py:290),
+ * selection on p + sel_bias (sel_bias may be NULL, :295), the k largest with
+ * the lower expert index first on ties (:296 for k = 1); w = p[e], divided by
+ * the sum of the k selected probabilities when renormalize != 0. */
+int b200q_moe_topk_dev(const float *logits, const float *sel_bias, int T, int E, int k, int renormalize, int *ids,
+                       float *w, void *stream);
+/* Scratch rows needed by b200q_moe_dispatch_dev: block_counts and base are
+ * int32 [b200q_moe_num_blocks(T) * E]. */
+int b200q_moe_num_blocks(int T);
+/* Stable counting sort of the T*k routed pairs by expert (slot order inside an
+ * expert follows (token, j) order): offsets int32 [E+1], slot_of int32 [T*k],
+ * token_of int32 [T*k], slot_w f32 [T*k] (routing weight per slot), and, if
+ * xperm_bf16 != NULL, xperm[slot] = bf16(h[token_of[slot]]) (bf16 [T*k, D]). */
+int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
+                           int *block_counts, int *base, int *offsets, int *slot_of, int *token_of, float *slot_w,
+                           void *xperm_bf16, void *stream);
+/* y[t] = sum_{j<k} out[slot_of[t*k + j]] in j order (f32 [T, D]). */
+int b200q_moe_combine_dev(const float *out, const int *slot_of, int T, int k, int D, float *y, void *stream);
+
 /* Device error word: returns and clears the sticky kernel error of the
  * current device (0 if none).  Synchronises the device. */
 int b200q_check_device_error(void);

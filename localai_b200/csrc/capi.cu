@@ -20,6 +20,15 @@ cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, l
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st);
 void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm);
+cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
+                              cudaStream_t st);
+cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, int E, int k, int renorm, int *ids,
+                            float *wts, cudaStream_t st);
+int moe_num_blocks(int T);
+cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
+                                int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
+                                float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
+cudaError_t launch_moe_combine(const float *out, const int *slot_of, int T, int k, int D, float *y, cudaStream_t st);
 cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
@@ -362,6 +371,51 @@ B200Q_API int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, co
                                           static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
                                           (cudaStream_t)stream),
                        "gemm");
+}
+
+B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,
+                                   int D, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h || !wr || !logits) return set_status(B200Q_EINVAL, "router: null pointer");
+    ++g_launches;
+    return cuda_status(launch_moe_router(h, wr, bias, logits, T, E, D, (cudaStream_t)stream), "router");
+}
+
+B200Q_API int b200q_moe_topk_dev(const float *logits, const float *sel_bias, int T, int E, int k, int renormalize,
+                                 int *ids, float *w, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!logits || !ids || !w) return set_status(B200Q_EINVAL, "topk: null pointer");
+    ++g_launches;
+    return cuda_status(launch_moe_topk(logits, sel_bias, T, E, k, renormalize, ids, w, (cudaStream_t)stream), "topk");
+}
+
+B200Q_API int b200q_moe_num_blocks(int T) { return moe_num_blocks(T); }
+
+B200Q_API int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
+                                     int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
+                                     float *slot_w, void *xperm_bf16, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ids || !w || !block_counts || !base || !offsets || !slot_of || !token_of || !slot_w || (xperm_bf16 && !h))
+        return set_status(B200Q_EINVAL, "dispatch: null pointer");
+    if (E > 1024) return set_status(B200Q_EINVAL, "dispatch: at most 1024 experts");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += xperm_bf16 ? 4 : 3;
+    return cuda_status(launch_moe_dispatch(ids, w, T, k, E, h, D, block_counts, base, offsets, slot_of, token_of,
+                                           slot_w, static_cast<__nv_bfloat16 *>(xperm_bf16), di->err,
+                                           (cudaStream_t)stream),
+                       "dispatch");
+}
+
+B200Q_API int b200q_moe_combine_dev(const float *out, const int *slot_of, int T, int k, int D, float *y, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!out || !slot_of || !y) return set_status(B200Q_EINVAL, "combine: null pointer");
+    ++g_launches;
+    return cuda_status(launch_moe_combine(out, slot_of, T, k, D, y, (cudaStream_t)stream), "combine");
 }
 
 B200Q_API int b200q_check_device_error(void)

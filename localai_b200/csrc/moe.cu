@@ -1,0 +1,314 @@
+// Mixture-of-experts routing, dispatch and combine (sm_100a).
+//
+// The reference MoE block (engine/zaya.py:274-307) routes one token at a time:
+// router logits, softmax (f32, max-subtracted, :290), optional additive
+// selection bias (:295), argmax (:296), expert FFN, scale by the unbiased
+// probability (:306).  Here the same steps run batched over T tokens and
+// generalised to top-k:
+//   router   logits[t, e] = h[t] . Wr[e] + bias[e]          (f32, fixed order)
+//   top-k    p = softmax(logits[t]); sel = p + sel_bias; k largest sel, lower
+//            expert index first on ties; weight p[e] or p[e] / sum_topk p
+//   dispatch stable counting sort of the (token, j) pairs by expert: slot
+//            order inside an expert follows token order, so the whole layer is
+//            deterministic; rows are gathered into a bf16 matrix grouped by
+//            expert (the tensor-core GEMM's B operand)
+//   combine  y[t] = sum_j out[slot(t, j)] for j = 0..k-1 in that order (the
+//            expert outputs already carry their routing weight)
+#include "common.cuh"
+
+namespace b200q {
+
+// ---------------------------------------------------------------- router
+// 64 tokens x 64 experts per CTA, K tiles of 32; 256 threads x (4 x 4) outputs.
+__global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ h, const float *__restrict__ wr,
+                                                         const float *__restrict__ bias, float *__restrict__ logits,
+                                                         int T, int E, int D)
+{
+    __shared__ float hs[32][64 + 4];
+    __shared__ float ws[32][64 + 4];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+    const int ty = tid >> 4, tx = tid & 15;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < D; k0 += 32) {
+        for (int i = tid; i < 64 * 32; i += 256) {
+            const int r = i >> 5, c = i & 31;
+            const int t = t0 + r, e = e0 + r, kk = k0 + c;
+            hs[c][r] = (t < T && kk < D) ? h[(long long)t * D + kk] : 0.f;
+            ws[c][r] = (e < E && kk < D) ? wr[(long long)e * D + kk] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int c = 0; c < 32; ++c) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a[i] = hs[c][ty * 4 + i];
+                b[i] = ws[c][tx * 4 + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
+            if (t < T && e < E) logits[(long long)t * E + e] = acc[i][j] + (bias ? bias[e] : 0.f);
+        }
+}
+
+// ---------------------------------------------------------------- top-k
+// One warp per token; E <= 32 * EPL.
+template <int EPL>
+__global__ void moe_topk_kernel(const float *__restrict__ logits, const float *__restrict__ sel_bias, int T, int E,
+                                int k, int renorm, int *__restrict__ ids, float *__restrict__ wts)
+{
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float *lr = logits + (long long)warp * E;
+    float p[EPL], sel[EPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? lr[e] : -INFINITY;
+        m = fmaxf(m, p[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = e < E ? expf(p[i] - m) : 0.f;
+        s += p[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        p[i] = p[i] / s;
+        sel[i] = e < E ? (sel_bias ? p[i] + sel_bias[e] : p[i]) : -INFINITY;
+    }
+    float total = 0.f, chosen_p = 0.f;
+    int chosen_e = -1;
+    for (int j = 0; j < k; ++j) {
+        float bv = -INFINITY;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && (sel[i] > bv || (sel[i] == bv && e < be))) { bv = sel[i]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        float pv = 0.f;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+            if (lane + 32 * i == be) { pv = p[i]; sel[i] = -INFINITY; }
+        pv = __shfl_sync(0xffffffffu, pv, be & 31);
+        total += pv;
+        if (lane == j) { chosen_e = be; chosen_p = pv; }
+    }
+    if (lane < k) {
+        ids[(long long)warp * k + lane] = chosen_e;
+        wts[(long long)warp * k + lane] = renorm ? chosen_p / total : chosen_p;
+    }
+}
+
+// ---------------------------------------------------------------- dispatch
+constexpr int MOE_TB = 256;       // tokens per dispatch block
+
+__global__ void moe_count_kernel(const int *__restrict__ ids, int T, int k, int E, int *__restrict__ block_counts,
+                                 int *err)
+{
+    extern __shared__ int cnt[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const long long i0 = (long long)blockIdx.x * MOE_TB * k;
+    const long long n = min((long long)MOE_TB * k, (long long)T * k - i0);
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = ids[i0 + i];
+        if (e < 0 || e >= E) { atomicExch(err, ERR_BAD_INDEX); continue; }
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) block_counts[(long long)blockIdx.x * E + e] = cnt[e];
+}
+
+// offsets[e] = rows of experts < e; base[b][e] = offsets[e] + rows of expert e in blocks < b.
+__global__ void moe_scan_kernel(const int *__restrict__ block_counts, int nblk, int E, int *__restrict__ base,
+                                int *__restrict__ offsets)
+{
+    extern __shared__ int tot[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int s = 0;
+        for (int b = 0; b < nblk; ++b) s += block_counts[(long long)b * E + e];
+        tot[e] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int e = 0; e < E; ++e) {
+            const int c = tot[e];
+            tot[e] = run;
+            offsets[e] = run;
+            run += c;
+        }
+        offsets[E] = run;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = tot[e];
+        for (int b = 0; b < nblk; ++b) {
+            base[(long long)b * E + e] = run;
+            run += block_counts[(long long)b * E + e];
+        }
+    }
+}
+
+// Slot of every (token, j) pair, stable in (token, j) order inside each expert.
+__global__ void __launch_bounds__(256) moe_assign_kernel(const int *__restrict__ ids, const float *__restrict__ wts,
+                                                         int T, int k, int E, const int *__restrict__ base,
+                                                         int *__restrict__ slot_of, int *__restrict__ token_of,
+                                                         float *__restrict__ slot_w)
+{
+    extern __shared__ int sm[];
+    int *running = sm;                 // [E]
+    int *wcnt = sm + E;                // [8][E]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int e = tid; e < E; e += 256) running[e] = 0;
+    for (int i = tid; i < 8 * E; i += 256) wcnt[i] = 0;
+    __syncthreads();
+    const long long i0 = (long long)blockIdx.x * MOE_TB * k;
+    const int n = (int)min((long long)MOE_TB * k, (long long)T * k - i0);
+    for (int r0 = 0; r0 < n; r0 += 256) {
+        const int item = r0 + tid;
+        const bool valid = item < n;
+        int e = valid ? ids[i0 + item] : E + lane;
+        if (valid && (e < 0 || e >= E)) e = E + lane;     // reported by moe_count_kernel
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const bool real = e < E;
+        if (real && rank == 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        for (int ee = tid; ee < E; ee += 256) {
+            int run = running[ee];
+            for (int w = 0; w < 8; ++w) {
+                const int c = wcnt[w * E + ee];
+                wcnt[w * E + ee] = run;          // becomes the warp's exclusive prefix
+                run += c;
+            }
+            running[ee] = run;
+        }
+        __syncthreads();
+        if (real) {
+            const int slot = base[(long long)blockIdx.x * E + e] + wcnt[warp * E + e] + rank;
+            const long long gi = i0 + item;
+            slot_of[gi] = slot;
+            token_of[slot] = (int)(gi / k);
+            slot_w[slot] = wts[gi];
+        }
+        __syncthreads();
+        for (int i = tid; i < 8 * E; i += 256) wcnt[i] = 0;
+        __syncthreads();
+    }
+}
+
+// xperm[slot, :] = bf16(h[token_of[slot], :]); one warp per slot row.
+__global__ void moe_gather_kernel(const float *__restrict__ h, const int *__restrict__ token_of, long long S, int D,
+                                  __nv_bfloat16 *__restrict__ xperm)
+{
+    const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= S) return;
+    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)token_of[row] * D);
+    uint2 *dst = reinterpret_cast<uint2 *>(xperm + row * D);
+    for (int c = lane; c < D / 4; c += 32) {
+        const float4 v = __ldg(src + c);
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t *>(&a);
+        o.y = *reinterpret_cast<uint32_t *>(&b);
+        dst[c] = o;
+    }
+}
+
+// y[t, :] = sum_j out[slot_of[t, j], :]   (j ascending)
+__global__ void moe_combine_kernel(const float *__restrict__ out, const int *__restrict__ slot_of, int T, int k, int D,
+                                   float *__restrict__ y)
+{
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    for (int c = threadIdx.x; c < D / 4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < k; ++j) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(out + (long long)slot_of[(long long)t * k + j] * D) + c);
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        reinterpret_cast<float4 *>(y + (long long)t * D)[c] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
+                              cudaStream_t st)
+{
+    if (T < 1 || E < 1 || D < 1) return cudaErrorInvalidValue;
+    dim3 grid((T + 63) / 64, (E + 63) / 64);
+    moe_router_kernel<<<grid, 256, 0, st>>>(h, wr, bias, logits, T, E, D);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, int E, int k, int renorm, int *ids,
+                            float *wts, cudaStream_t st)
+{
+    if (T < 1 || E < 1 || E > 256 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
+    const int threads = 256, grid = (int)(((long long)T * 32 + threads - 1) / threads);
+    if (E <= 32) moe_topk_kernel<1><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
+    else if (E <= 64) moe_topk_kernel<2><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
+    else if (E <= 128) moe_topk_kernel<4><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
+    else moe_topk_kernel<8><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
+    return cudaGetLastError();
+}
+
+int moe_num_blocks(int T) { return (T + MOE_TB - 1) / MOE_TB; }
+
+// Counting sort of the routed pairs and the bf16 gather.
+//   block_counts, base: int32 [moe_num_blocks(T) * E] scratch
+//   offsets: int32 [E + 1]; slot_of: int32 [T * k]; token_of: int32 [T * k];
+//   slot_w: f32 [T * k]; xperm: bf16 [T * k, D] (may be null: no gather)
+cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
+                                int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
+                                float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st)
+{
+    if (T < 1 || k < 1 || E < 1 || E > 4096 || (xperm && D % 4)) return cudaErrorInvalidValue;
+    const int nblk = moe_num_blocks(T);
+    moe_count_kernel<<<nblk, 256, E * sizeof(int), st>>>(ids, T, k, E, block_counts, err);
+    moe_scan_kernel<<<1, 256, E * sizeof(int), st>>>(block_counts, nblk, E, base, offsets);
+    moe_assign_kernel<<<nblk, 256, 9 * E * sizeof(int), st>>>(ids, wts, T, k, E, base, slot_of, token_of, slot_w);
+    if (xperm) {
+        const long long S = (long long)T * k;
+        moe_gather_kernel<<<(unsigned)((S * 32 + 255) / 256), 256, 0, st>>>(h, token_of, S, D, xperm);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_combine(const float *out, const int *slot_of, int T, int k, int D, float *y, cudaStream_t st)
+{
+    if (T < 1 || k < 1 || D % 4) return cudaErrorInvalidValue;
+    moe_combine_kernel<<<T, 256, 0, st>>>(out, slot_of, T, k, D, y);
+    return cudaGetLastError();
+}
+
+} // namespace b200q

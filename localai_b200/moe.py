@@ -1,0 +1,121 @@
+"""Quantised mixture-of-experts FFN on the GPU.
+
+The reference block (engine/zaya.py:274-307, ``ZayaModel._moe``) routes one
+token at a time to one expert and runs two GEMVs on it.  ``QuantMoE`` runs the
+same block batched over T tokens and generalised to top-k:
+
+    logits = h @ Wr^T (+ router bias)             b200q_moe_router_dev
+    p = softmax(logits); top-k of p (+ sel bias)  b200q_moe_topk_dev
+    stable counting sort of (token, j) by expert  b200q_moe_dispatch_dev
+    act = SiLU(gate x) * (up x)  per expert       b200q_gemm_q4k_dev (gate/up mode, tcgen05)
+    out = w_slot * (down act)    per expert       b200q_gemm_q4k_dev (plain mode, tcgen05)
+    y[t] = sum_j out[slot(t, j)]                  b200q_moe_combine_dev
+
+Expert weights are the raw GGUF Q4_K tensors in ZAYA's layout: ``gate_up``
+[E, 2F, D] (gate rows first, then up rows, as ``np.split(packed, 2)`` reads
+them, engine/zaya.py:304) and ``down`` [E, D, F_pad] with F_pad the next
+multiple of 256 (padded sub-blocks decode to zero).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+Q4_K = 12
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+class QuantMoE:
+    def __init__(self, router_w: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *, d_model: int,
+                 d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
+                 sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K):
+        if ggml_type != Q4_K:
+            raise NotImplementedError('the tensor-core expert path supports Q4_K expert weights')
+        if d_ff % 64 or d_model % 128:
+            raise ValueError('d_ff must be a multiple of 64 and d_model of 128')
+        self.E = router_w.shape[0]
+        self.D, self.F, self.k = d_model, d_ff, top_k
+        self.F_pad = (d_ff + 255) // 256 * 256
+        self.router_w = router_w.contiguous().float()
+        self.router_bias = None if router_bias is None else router_bias.contiguous().float()
+        self.sel_bias = None if sel_bias is None else sel_bias.contiguous().float()
+        self.renorm = 1 if renormalize else 0
+        self.gate_up = gate_up.contiguous()
+        self.down = down.contiguous()
+        gu_bytes = self.E * 2 * d_ff * (d_model // 256) * 144
+        dn_bytes = self.E * d_model * (self.F_pad // 256) * 144
+        if self.gate_up.numel() != gu_bytes or self.down.numel() != dn_bytes:
+            raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of Q4_K')
+        self.lib = _lib.load()
+
+    # -- stages ---------------------------------------------------------------
+    def route(self, h: torch.Tensor):
+        T = h.shape[0]
+        dev = h.device
+        logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
+        _lib.check(self.lib.b200q_moe_router_dev(
+            h.data_ptr(), self.router_w.data_ptr(),
+            None if self.router_bias is None else self.router_bias.data_ptr(),
+            logits.data_ptr(), T, self.E, self.D, _stream()))
+        ids, w = self.topk(logits)
+        return logits, ids, w
+
+    def topk(self, logits: torch.Tensor):
+        T = logits.shape[0]
+        ids = torch.empty((T, self.k), dtype=torch.int32, device=logits.device)
+        w = torch.empty((T, self.k), dtype=torch.float32, device=logits.device)
+        _lib.check(self.lib.b200q_moe_topk_dev(
+            logits.data_ptr(), None if self.sel_bias is None else self.sel_bias.data_ptr(),
+            T, self.E, self.k, self.renorm, ids.data_ptr(), w.data_ptr(), _stream()))
+        return ids, w
+
+    def dispatch(self, h: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, gather: bool = True):
+        T, dev = ids.shape[0], ids.device
+        S = T * self.k
+        nblk = self.lib.b200q_moe_num_blocks(T)
+        scratch = torch.empty((2, nblk * self.E), dtype=torch.int32, device=dev)
+        offsets = torch.empty(self.E + 1, dtype=torch.int32, device=dev)
+        slot_of = torch.empty(S, dtype=torch.int32, device=dev)
+        token_of = torch.empty(S, dtype=torch.int32, device=dev)
+        slot_w = torch.empty(S, dtype=torch.float32, device=dev)
+        xperm = torch.empty((S, self.D), dtype=torch.bfloat16, device=dev) if gather else None
+        _lib.check(self.lib.b200q_moe_dispatch_dev(
+            ids.data_ptr(), w.data_ptr(), T, self.k, self.E, h.data_ptr() if gather else None, self.D,
+            scratch[0].data_ptr(), scratch[1].data_ptr(), offsets.data_ptr(), slot_of.data_ptr(),
+            token_of.data_ptr(), slot_w.data_ptr(), None if xperm is None else xperm.data_ptr(), _stream()))
+        return offsets, slot_of, token_of, slot_w, xperm
+
+    def experts(self, xperm: torch.Tensor, offsets: torch.Tensor, slot_w: torch.Tensor, *, max_ctas: int = 0):
+        """Grouped gate/up (fused SiLU*up) then grouped down, on the tensor cores."""
+        S, dev = xperm.shape[0], xperm.device
+        act = torch.empty((S, self.F), dtype=torch.bfloat16, device=dev)
+        _lib.check(self.lib.b200q_gemm_q4k_dev(
+            xperm.data_ptr(), S, self.D, self.gate_up.data_ptr(), self.E, 2 * self.F, self.F, self.F,
+            offsets.data_ptr(), None, 0, None, act.data_ptr(), self.F, max_ctas, _stream()))
+        out = torch.empty((S, self.D), dtype=torch.float32, device=dev)
+        _lib.check(self.lib.b200q_gemm_q4k_dev(
+            act.data_ptr(), S, self.F, self.down.data_ptr(), self.E, self.D, -1, self.D,
+            offsets.data_ptr(), out.data_ptr(), self.D, slot_w.data_ptr(), None, 0, max_ctas, _stream()))
+        return out
+
+    def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int):
+        y = torch.empty((T, self.D), dtype=torch.float32, device=out.device)
+        _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), slot_of.data_ptr(), T, self.k, self.D,
+                                                  y.data_ptr(), _stream()))
+        return y
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        """y[T, D] for hidden states h[T, D] (f32)."""
+        if h.dtype != torch.float32 or not h.is_cuda or h.dim() != 2 or h.shape[1] != self.D:
+            raise ValueError('h must be a CUDA f32 [T, d_model] tensor')
+        h = h.contiguous()
+        _, ids, w = self.route(h)
+        offsets, slot_of, _, slot_w, xperm = self.dispatch(h, ids, w)
+        out = self.experts(xperm, offsets, slot_w)
+        return self.combine(out, slot_of, h.shape[0])
+
+    __call__ = forward

@@ -1,0 +1,106 @@
+"""GPU tests of the MoE layer: routing, dispatch, expert products, combine.
+
+* top-k: bit-exact expert ids against the oracle on the same logits
+  (engine/zaya.py:290-296 generalised to top-k), weights to 1e-6;
+* router logits against float64;
+* dispatch: stable counting sort (slot order follows token order inside an
+  expert), gathered rows equal bf16(h[token]);
+* the whole layer against ``moe_forward_f64`` run with the GPU's routing
+  decisions: normwise max relative error <= 1e-2 (bf16 tensor-core path).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant_oracle as o
+from localai_b200 import synth
+from localai_b200.moe import QuantMoE
+
+pytestmark = pytest.mark.gpu
+
+
+def make_layer(rng, E, D, F, k, renorm=True, router_bias=None, sel_bias=None):
+    F_pad = (F + 255) // 256 * 256
+    gate_up = [synth.q4_k(rng, 2 * F, D) for _ in range(E)]
+    down = [synth.q4_k(rng, D, F_pad, zero_tail_cols=F_pad - F) for _ in range(E)]
+    wr = rng.normal(0, 1 / np.sqrt(D), size=(E, D)).astype(np.float32)
+    cat = lambda parts: torch.frombuffer(bytearray(b''.join(parts)), dtype=torch.uint8).cuda()
+    layer = QuantMoE(torch.from_numpy(wr).cuda(), cat(gate_up), cat(down), d_model=D, d_ff=F, top_k=k,
+                     router_bias=None if router_bias is None else torch.from_numpy(router_bias).cuda(),
+                     sel_bias=None if sel_bias is None else torch.from_numpy(sel_bias).cuda(), renormalize=renorm)
+    return layer, wr, gate_up, down, F_pad
+
+
+@pytest.mark.parametrize('E,k,renorm,bias', [(64, 8, True, False), (16, 2, True, False), (17, 1, False, True),
+                                             (128, 4, True, True), (8, 8, True, False)])
+def test_topk_bit_exact_on_oracle_logits(E, k, renorm, bias):
+    rng = np.random.default_rng(E * 10 + k)
+    T = 700
+    logits = rng.normal(size=(T, E)).astype(np.float32)
+    logits[5, :] = 0.0                        # all-tie row: lower indices win
+    logits[6, 1] = logits[6, E - 1] = 5.0     # a two-way tie at the top
+    sel_bias = rng.normal(scale=0.05, size=E).astype(np.float32) if bias else None
+    ref_ids, ref_w = o.route_topk(logits, k, bias=sel_bias, renormalize=renorm)
+    layer = QuantMoE.__new__(QuantMoE)
+    layer.E, layer.k, layer.renorm = E, k, 1 if renorm else 0
+    layer.sel_bias = None if sel_bias is None else torch.from_numpy(sel_bias).cuda()
+    from localai_b200 import _lib
+    layer.lib = _lib.load()
+    ids, w = layer.topk(torch.from_numpy(logits).cuda())
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    np.testing.assert_allclose(w.cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
+
+
+def test_router_logits_and_dispatch():
+    rng = np.random.default_rng(3)
+    E, D, F, k, T = 16, 512, 128, 4, 1000
+    bias = np.log(np.arange(1, E + 1, dtype=np.float64) ** -1.1 / np.sum(np.arange(1, E + 1) ** -1.1)).astype(np.float32)
+    layer, wr, *_ = make_layer(rng, E, D, F, k, router_bias=bias)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    hd = torch.from_numpy(h).cuda()
+    logits, ids, w = layer.route(hd)
+    ref = h.astype(np.float64) @ wr.T.astype(np.float64) + bias
+    assert np.max(np.abs(logits.cpu().numpy() - ref)) / np.max(np.abs(ref)) < 1e-5
+    offsets, slot_of, token_of, slot_w, xperm = layer.dispatch(hd, ids, w)
+    torch.cuda.synchronize()
+    ids_n, off, so, to = ids.cpu().numpy(), offsets.cpu().numpy(), slot_of.cpu().numpy(), token_of.cpu().numpy()
+    counts = np.bincount(ids_n.reshape(-1), minlength=E)
+    assert np.array_equal(off, np.concatenate([[0], np.cumsum(counts)]))
+    # every (token, j) owns one slot inside its expert's range, in token order
+    for e in range(E):
+        seg = to[off[e]:off[e + 1]]
+        assert np.all(np.diff(seg) > 0)
+    flat_e = ids_n.reshape(-1)
+    assert np.all((so >= off[flat_e]) & (so < off[flat_e + 1]))
+    assert np.array_equal(to[so], np.repeat(np.arange(T), k))
+    np.testing.assert_array_equal(slot_w.cpu().numpy()[so], w.cpu().numpy().reshape(-1))
+    np.testing.assert_array_equal(xperm.float().cpu().numpy(), hd.to(torch.bfloat16).float().cpu().numpy()[to])
+
+
+@pytest.mark.parametrize('E,D,F,k,T', [(8, 512, 128, 2, 300), (16, 1024, 192, 4, 600), (32, 512, 64, 8, 257)])
+def test_layer_matches_oracle(E, D, F, k, T):
+    rng = np.random.default_rng(E + D + F + k + T)
+    layer, wr, gate_up, down, F_pad = make_layer(rng, E, D, F, k)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    y = layer(torch.from_numpy(h).cuda())
+    torch.cuda.synchronize()
+    from localai_b200 import ops
+    ops.check_device_error()
+    logits, ids, w = layer.route(torch.from_numpy(h).cuda())
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    # the GPU routing agrees with the oracle on float64 logits except at near-ties
+    ref_ids, _ = o.route_topk((h.astype(np.float64) @ wr.T.astype(np.float64)).astype(np.float32), k)
+    assert np.mean(np.all(np.sort(ids, 1) == np.sort(ref_ids, 1), axis=1)) > 0.97
+    experts = [(gate_up[e], down[e]) for e in range(E)]
+    ref = o.moe_forward_f64(h, ids, w, experts, 12, 12, D, F, F_pad)
+    assert o.normwise_rel_err(y.cpu().numpy(), ref) < 1e-2
+
+
+def test_layer_deterministic():
+    rng = np.random.default_rng(5)
+    layer, *_ = make_layer(rng, 16, 512, 128, 4)
+    h = torch.from_numpy(rng.normal(size=(333, 512)).astype(np.float32)).cuda()
+    a = layer(h)
+    b = layer(h)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
