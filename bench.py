@@ -1,0 +1,413 @@
+"""Benchmark: expert-parallel MoE layer tokens/s (+ quantised GEMV HBM GB/s).
+
+Workload (the headline configuration): one MoE FFN layer with hidden 4096,
+64 experts of intermediate 1408 (down weights padded to 1536), top-8 routing
+with renormalised weights, Q4_K expert weights, 16384 tokens of f32 N(0,1)
+hidden states, and a router bias log(p_e), p_e ~ (e+1)^-1.1 (Zipf s = 1.1).
+All inputs are seeded synthetic data; the token count is fixed across GPU
+counts (strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs one process per GPU (torchrun); experts are placed by greedy LPT on
+the routing loads and exchanged with NCCL all-to-all.  ``--impl reference``
+times the reference engine's own CPU kernels (the reference's native_quant.cpp,
+compiled from its sources into oracle/_ref/) on a bounded token sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+E, D, F, K_TOP, T_TOTAL = 64, 4096, 1408, 8, 16384
+F_PAD = 1536
+Q4K_BLOCK = 144
+WORKLOAD = 'moe_q4k_d4096_e64_f1408_top8_t16384_zipf1.1'
+METRIC = 'MoE-layer tokens/s (expert-parallel, 1/2/4/8 GPU); quant GEMV HBM GB/s'
+PROFILE_TRAFFIC = ROOT / 'profiles' / 'gemm_q4k_gate_up_moe_config5.txt'
+
+
+# ----------------------------------------------------------------- workload
+def zipf_bias():
+    p = np.arange(1, E + 1, dtype=np.float64) ** -1.1
+    return np.log(p / p.sum()).astype(np.float32)
+
+
+def router_weights():
+    return np.random.default_rng(1000).normal(0, 1 / np.sqrt(D), size=(E, D)).astype(np.float32)
+
+
+def expert_weights(e):
+    from localai_b200 import synth
+    rng = np.random.default_rng(2000 + e)
+    return synth.q4_k(rng, 2 * F, D), synth.q4_k(rng, D, F_PAD, zero_tail_cols=F_PAD - F)
+
+
+def hidden_states(torch, device, t0, t1):
+    g = torch.Generator(device=device)
+    g.manual_seed(1001)
+    h = torch.randn((T_TOTAL, D), generator=g, device=device, dtype=torch.float32)
+    return h[t0:t1].contiguous()
+
+
+def algorithmic_flops(slots):
+    return 2.0 * slots * (2 * F * D + D * F)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.gpu_index = str(gpu_index)
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
+                                          '-lms', '200'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9 or f[0] != self.gpu_index:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx), 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ----------------------------------------------------------------- CPU (reference kernels)
+def cpu_reference_moe(tokens, threads=8):
+    """Time the reference engine's CPU path on ``tokens`` tokens.
+
+    Router + softmax/top-8 in NumPy, then per expert the reference's own
+    batched Q4_K kernel (localai_q4k_matmul, engine/native_quant.cpp:754-758,
+    built from the reference sources into oracle/_ref/) for gate/up and
+    down, SiLU in NumPy (engine/zaya.py:304-306), weighted combine.  Falls back
+    to the NumPy oracle port when the compiled reference is unavailable.
+    Returns (tokens/s, kind, cores).
+    """
+    from oracle import quant_oracle as o
+    so = ROOT / 'oracle' / '_ref' / 'libnative_quant_ref.so'
+    lib = ctypes.CDLL(str(so)) if so.exists() else None
+    cores = min(threads, os.cpu_count() or 1)
+    wr = router_weights()
+    bias = zipf_bias()
+    h = np.random.default_rng(1002).normal(size=(tokens, D)).astype(np.float32)
+    ids, w = o.route_topk(h @ wr.T + bias, K_TOP)          # the routing of the sample (untimed below)
+    experts = {int(e): expert_weights(int(e)) for e in np.unique(ids)}
+
+    def matmul(raw, x, rows, cols):
+        if lib is None:
+            return (o.dequantize(raw, 12, (rows, cols)) @ x.T.astype(np.float32)).astype(np.float32)
+        out = np.empty((rows, x.shape[0]), np.float32)
+        xb = np.ascontiguousarray(x, np.float32)
+        rb = np.frombuffer(raw, np.uint8)
+        lib.localai_q4k_matmul(rb.ctypes.data_as(ctypes.c_void_p), xb.ctypes.data_as(ctypes.c_void_p),
+                               out.ctypes.data_as(ctypes.c_void_p), rows, cols, x.shape[0], cores)
+        return out
+
+    t0 = time.perf_counter()
+    logits = h @ wr.T + bias
+    ids, w = o.route_topk(logits, K_TOP)
+    y = np.zeros((tokens, D), np.float32)
+    for e in np.unique(ids):
+        rows, slots = np.nonzero(ids == e)
+        gu_raw, dn_raw = experts[int(e)]
+        gu = matmul(gu_raw, h[rows], 2 * F, D)               # [2F, n]
+        gate, up = gu[:F], gu[F:]
+        act = np.zeros((rows.size, F_PAD), np.float32)
+        act[:, :F] = (gate / (1.0 + np.exp(-np.clip(gate, -80, 80))) * up).T
+        out = matmul(dn_raw, act, D, F_PAD)                  # [D, n]
+        y[rows] += (out * w[rows, slots][None, :]).T
+    dt = time.perf_counter() - t0
+    return tokens / dt, ('reference' if lib is not None else 'port'), cores, dt
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    tokens = args.cpu_tokens
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, kind, cores, dt = cpu_reference_moe(tokens)
+        if i >= args.warmup:
+            vals.append(v)
+    value = float(np.mean(vals))
+    line = {'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': args.gpus,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': tokens / value * 1e3,
+            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic',
+            'config': {'workload': WORKLOAD, 'sample_tokens': tokens},
+            'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': cores, 'kind': kind,
+                             'sample': f'{tokens} of {T_TOTAL} tokens per step, all experts they route to'},
+            'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arm
+def gemv_probe(torch, ops, synth, hbm_peak):
+    """Config-1 Q4_K GEMV (4096 x 4096, batch 1) and a 14336 x 4096 one, in a
+    CUDA graph over weight copies that together exceed twice the L2."""
+    res = {}
+    for rows, cols in ((4096, 4096), (14336, 4096)):
+        raw = synth.q4_k(np.random.default_rng(1), rows, cols)
+        w0 = torch.frombuffer(bytearray(raw), dtype=torch.uint8).cuda()
+        ncopy = max(2, int(300e6 // len(raw)) + 1)
+        ws = [w0.clone() for _ in range(ncopy)]
+        x = torch.randn(1, cols, device='cuda')
+        y = torch.empty(1, rows, device='cuda')
+        reps = 60
+        for i in range(3):
+            ops.gemv(ws[i % ncopy], x, 12, rows, cols, out=y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    ops.gemv(ws[i % ncopy], x, 12, rows, cols, out=y)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (5 * reps)
+        nbytes = len(raw) + 4 * cols + 4 * rows
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[f'{rows}x{cols}'] = {'us_per_call': round(us, 2), 'GB_s': round(gbs, 1),
+                                 'frac_of_measured_hbm': round(gbs / hbm_peak, 3), 'bytes_per_call': nbytes}
+        del ws, g
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--cpu-tokens', type=int, default=2048, help='token sample of the CPU baseline')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-gemv', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == 'reference':
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from localai_b200 import _lib, ops, synth
+    from localai_b200.moe import QuantMoE
+    from localai_b200.ep import EPMoE, lpt_placement
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device('cuda', local_rank)
+    if world > 1:
+        dist.init_process_group('nccl', timeout=timedelta(seconds=300), device_id=dev)
+    lib = _lib.load()
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    hbm_peak = float(peaks.get('hbm_gbs', 6650.0))
+    tc_burst = float(peaks.get('bf16_tflops', 1590.0))
+    peak_src = 'measured' if peaks else 'fallback'
+
+    wr = torch.from_numpy(router_weights()).to(dev)
+    bias = torch.from_numpy(zipf_bias()).to(dev)
+    T_loc = T_TOTAL // world
+    t0, t1 = rank * T_loc, (rank + 1) * T_loc
+    h = hidden_states(torch, dev, t0, t1)
+
+    # expert placement: LPT on the routing loads of the full token set (setup, untimed)
+    if world > 1:
+        probe = QuantMoE.__new__(QuantMoE)
+        probe.E, probe.D, probe.k, probe.renorm, probe.sel_bias = E, D, K_TOP, 1, None
+        probe.router_w, probe.router_bias, probe.lib = wr, bias, lib
+        _, ids_all, _ = probe.route(hidden_states(torch, dev, 0, T_TOTAL))
+        loads = torch.bincount(ids_all.reshape(-1).long(), minlength=E).cpu().numpy()
+        owner, local = lpt_placement(loads, world)
+        mine = [int(e) for e in np.nonzero(owner == rank)[0]]
+    else:
+        owner = local = None
+        mine = list(range(E))
+    parts = [expert_weights(e) for e in mine]
+    gate_up = torch.frombuffer(bytearray(b''.join(p[0] for p in parts)), dtype=torch.uint8).to(dev)
+    down = torch.frombuffer(bytearray(b''.join(p[1] for p in parts)), dtype=torch.uint8).to(dev)
+    del parts
+    layer = QuantMoE(wr, gate_up, down, d_model=D, d_ff=F, top_k=K_TOP, router_bias=bias, renormalize=True,
+                     local_experts=len(mine))
+    step = EPMoE(layer, owner, local) if world > 1 else layer
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step(h)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+
+    # ---- timed region (device-resident inputs)
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    n0 = lib.b200q_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        y = step(h)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = lib.b200q_launch_count() - n0
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    value = T_TOTAL / (ms * 1e-3)
+
+    # ---- end to end through the public API: host (pinned) input and output
+    h_host = h.cpu().pin_memory()
+    y_host = torch.empty((T_loc, D), dtype=torch.float32).pin_memory()
+    h_dev = torch.empty_like(h)
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(e2e_steps):
+        h_dev.copy_(h_host, non_blocking=True)
+        yy = step(h_dev)
+        y_host.copy_(yy, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = torch.tensor([e2.elapsed_time(e3) / e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+    e2e_value = T_TOTAL / (float(ms_e2e.item()) * 1e-3)
+
+    # ---- dominant kernel: the gate/up grouped GEMM, timed alone on this rank's experts
+    _, ids, w = layer.route(h)
+    if world > 1:
+        ids = step.virt[ids.long()]
+    offsets, slot_of, _, slot_w, xperm = layer.dispatch(h, ids, w)
+    slots = xperm.shape[0]
+    act = torch.empty((slots, F), dtype=torch.bfloat16, device=dev)
+    gemm_reps = 5
+    n_groups = E if world == 1 else E    # virtual-expert grouping of this rank's own tokens
+    gu_all = gate_up if world == 1 else None
+    roof = None
+    if world == 1:
+        for _ in range(2):
+            ops.gemm_q4k(xperm, gu_all, offsets, k=D, n_feat=F, w_rows_per_group=2 * F, up_offset=F, act=act)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(gemm_reps):
+            ops.gemm_q4k(xperm, gu_all, offsets, k=D, n_feat=F, w_rows_per_group=2 * F, up_offset=F, act=act)
+        g1.record()
+        torch.cuda.synchronize()
+        gemm_ms = g0.elapsed_time(g1) / gemm_reps
+        flops = 2.0 * slots * (2 * F) * D
+        achieved = flops / (gemm_ms * 1e-3) / 1e12
+        traffic = None
+        if PROFILE_TRAFFIC.exists():
+            for line in PROFILE_TRAFFIC.read_text().splitlines():
+                if line.startswith('traffic_bytes_per_launch:'):
+                    traffic = float(line.split(':', 1)[1].split()[0])
+        roof = {'kernel': 'tc_gemm_q4k_kernel (gate/up, fused SiLU*up)', 'bound': 'tensor',
+                'achieved': round(achieved, 1), 'peak': tc_burst, 'unit': 'TFLOP/s',
+                'frac': round(achieved / tc_burst, 3), 'traffic': traffic,
+                'peak_source': f'{peak_src} bf16 (burst; kernel timed alone)',
+                'flops_per_launch': flops, 'ms_per_launch': round(gemm_ms, 4)}
+
+    gemv = None
+    if rank == 0 and not args.no_gemv and world == 1:
+        gemv = gemv_probe(torch, ops, synth, hbm_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, kind, cores, dt = cpu_reference_moe(args.cpu_tokens)
+        cpu = {'value': v, 'unit': 'tokens/s', 'cores': cores, 'kind': kind,
+               'sample': f'{args.cpu_tokens} of {T_TOTAL} tokens (same layer shapes and routing), {dt:.1f} s'}
+
+    if rank == 0:
+        line = {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
+                'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'strong',
+                'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+                'config': {'workload': WORKLOAD, 'hidden': D, 'experts': E, 'intermediate': F, 'top_k': K_TOP,
+                           'tokens': T_TOTAL, 'weights': 'Q4_K', 'router': 'f32 + Zipf(1.1) bias',
+                           'parallelism': f'ep{world}' if world > 1 else 'single',
+                           'l2': 'inputs larger than L2 (641 MB expert weights, 256 MB hidden states)'},
+                'roofline': roof, 'cpu_baseline': cpu,
+                'e2e': {'value': e2e_value, 'unit': 'tokens/s', 'h2d_bytes_per_step': T_TOTAL * D * 4,
+                        'd2h_bytes_per_step': T_TOTAL * D * 4},
+                'gpu_launches': int(launches), 'clocks': clocks, 'gemv': gemv,
+                'flops_per_step': algorithmic_flops(T_TOTAL * K_TOP)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -140,8 +140,10 @@ int b200q_moe_num_blocks(int T);
 int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
                            int *block_counts, int *base, int *offsets, int *slot_of, int *token_of, float *slot_w,
                            void *xperm_bf16, void *stream);
-/* y[t] = sum_{j<k} out[slot_of[t*k + j]] in j order (f32 [T, D]). */
-int b200q_moe_combine_dev(const float *out, const int *slot_of, int T, int k, int D, float *y, void *stream);
+/* y[t] = sum_{j<k} w_j * out[slot_of[t*k + j]] in j order (f32 [T, D]), with
+ * w_j = slot_w[slot] if slot_w != NULL, else 1 (rows already weighted). */
+int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
+                          void *stream);
 
 /* Device error word: returns and clears the sticky kernel error of the
  * current device (0 if none).  Synchronises the device. */

@@ -28,7 +28,8 @@ int moe_num_blocks(int T);
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
-cudaError_t launch_moe_combine(const float *out, const int *slot_of, int T, int k, int D, float *y, cudaStream_t st);
+cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
+                               cudaStream_t st);
 cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
@@ -410,12 +411,13 @@ B200Q_API int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int 
                        "dispatch");
 }
 
-B200Q_API int b200q_moe_combine_dev(const float *out, const int *slot_of, int T, int k, int D, float *y, void *stream)
+B200Q_API int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D,
+                                    float *y, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!out || !slot_of || !y) return set_status(B200Q_EINVAL, "combine: null pointer");
     ++g_launches;
-    return cuda_status(launch_moe_combine(out, slot_of, T, k, D, y, (cudaStream_t)stream), "combine");
+    return cuda_status(launch_moe_combine(out, slot_of, slot_w, T, k, D, y, (cudaStream_t)stream), "combine");
 }
 
 B200Q_API int b200q_check_device_error(void)

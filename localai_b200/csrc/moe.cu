@@ -244,17 +244,21 @@ __global__ void moe_gather_kernel(const float *__restrict__ h, const int *__rest
     }
 }
 
-// y[t, :] = sum_j out[slot_of[t, j], :]   (j ascending)
-__global__ void moe_combine_kernel(const float *__restrict__ out, const int *__restrict__ slot_of, int T, int k, int D,
-                                   float *__restrict__ y)
+// y[t, :] = sum_j w_j * out[slot_of[t, j], :]   (j ascending; w_j = slot_w[slot]
+// when slot_w is given, else 1 because the rows already carry their weight)
+__global__ void moe_combine_kernel(const float *__restrict__ out, const int *__restrict__ slot_of,
+                                   const float *__restrict__ slot_w, int T, int k, int D, float *__restrict__ y)
 {
     const int t = blockIdx.x;
     if (t >= T) return;
     for (int c = threadIdx.x; c < D / 4; c += blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; ++j) {
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(out + (long long)slot_of[(long long)t * k + j] * D) + c);
-            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            const int slot = slot_of[(long long)t * k + j];
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(out + (long long)slot * D) + c);
+            const float wj = slot_w ? __ldg(slot_w + slot) : 1.0f;
+            acc.x = fmaf(wj, v.x, acc.x); acc.y = fmaf(wj, v.y, acc.y);
+            acc.z = fmaf(wj, v.z, acc.z); acc.w = fmaf(wj, v.w, acc.w);
         }
         reinterpret_cast<float4 *>(y + (long long)t * D)[c] = acc;
     }
@@ -304,10 +308,11 @@ cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_combine(const float *out, const int *slot_of, int T, int k, int D, float *y, cudaStream_t st)
+cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
+                               cudaStream_t st)
 {
     if (T < 1 || k < 1 || D % 4) return cudaErrorInvalidValue;
-    moe_combine_kernel<<<T, 256, 0, st>>>(out, slot_of, T, k, D, y);
+    moe_combine_kernel<<<T, 256, 0, st>>>(out, slot_of, slot_w, T, k, D, y);
     return cudaGetLastError();
 }
 

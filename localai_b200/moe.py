@@ -32,7 +32,8 @@ def _stream():
 class QuantMoE:
     def __init__(self, router_w: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *, d_model: int,
                  d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
-                 sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K):
+                 sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K,
+                 local_experts: int | None = None):
         if ggml_type != Q4_K:
             raise NotImplementedError('the tensor-core expert path supports Q4_K expert weights')
         if d_ff % 64 or d_model % 128:
@@ -46,8 +47,10 @@ class QuantMoE:
         self.renorm = 1 if renormalize else 0
         self.gate_up = gate_up.contiguous()
         self.down = down.contiguous()
-        gu_bytes = self.E * 2 * d_ff * (d_model // 256) * 144
-        dn_bytes = self.E * d_model * (self.F_pad // 256) * 144
+        # expert tensors may hold a subset of the experts (expert parallelism)
+        self.E_held = self.E if local_experts is None else local_experts
+        gu_bytes = self.E_held * 2 * d_ff * (d_model // 256) * 144
+        dn_bytes = self.E_held * d_model * (self.F_pad // 256) * 144
         if self.gate_up.numel() != gu_bytes or self.down.numel() != dn_bytes:
             raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of Q4_K')
         self.lib = _lib.load()
@@ -89,23 +92,35 @@ class QuantMoE:
             token_of.data_ptr(), slot_w.data_ptr(), None if xperm is None else xperm.data_ptr(), _stream()))
         return offsets, slot_of, token_of, slot_w, xperm
 
-    def experts(self, xperm: torch.Tensor, offsets: torch.Tensor, slot_w: torch.Tensor, *, max_ctas: int = 0):
-        """Grouped gate/up (fused SiLU*up) then grouped down, on the tensor cores."""
+    def experts(self, xperm: torch.Tensor, offsets: torch.Tensor, slot_w: torch.Tensor | None, *,
+                max_ctas: int = 0, gate_up: torch.Tensor | None = None, down: torch.Tensor | None = None,
+                n_experts: int | None = None):
+        """Grouped gate/up (fused SiLU*up) then grouped down, on the tensor cores.
+
+        ``slot_w`` scales each output row (None: unscaled).  ``gate_up``/``down``/
+        ``n_experts`` override the layer's expert set (expert parallelism runs a
+        rank's local experts)."""
         S, dev = xperm.shape[0], xperm.device
+        gu = self.gate_up if gate_up is None else gate_up
+        dn = self.down if down is None else down
+        ne = self.E_held if n_experts is None else n_experts
         act = torch.empty((S, self.F), dtype=torch.bfloat16, device=dev)
         _lib.check(self.lib.b200q_gemm_q4k_dev(
-            xperm.data_ptr(), S, self.D, self.gate_up.data_ptr(), self.E, 2 * self.F, self.F, self.F,
+            xperm.data_ptr(), S, self.D, gu.data_ptr(), ne, 2 * self.F, self.F, self.F,
             offsets.data_ptr(), None, 0, None, act.data_ptr(), self.F, max_ctas, _stream()))
         out = torch.empty((S, self.D), dtype=torch.float32, device=dev)
         _lib.check(self.lib.b200q_gemm_q4k_dev(
-            act.data_ptr(), S, self.F, self.down.data_ptr(), self.E, self.D, -1, self.D,
-            offsets.data_ptr(), out.data_ptr(), self.D, slot_w.data_ptr(), None, 0, max_ctas, _stream()))
+            act.data_ptr(), S, self.F, dn.data_ptr(), ne, self.D, -1, self.D,
+            offsets.data_ptr(), out.data_ptr(), self.D, None if slot_w is None else slot_w.data_ptr(), None, 0,
+            max_ctas, _stream()))
         return out
 
-    def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int):
+    def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int, slot_w: torch.Tensor | None = None):
+        """y[t] = sum_j (slot_w) * out[slot(t, j)]; pass slot_w when out is unweighted."""
         y = torch.empty((T, self.D), dtype=torch.float32, device=out.device)
-        _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), slot_of.data_ptr(), T, self.k, self.D,
-                                                  y.data_ptr(), _stream()))
+        _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), slot_of.data_ptr(),
+                                                  None if slot_w is None else slot_w.data_ptr(), T, self.k,
+                                                  self.D, y.data_ptr(), _stream()))
         return y
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
