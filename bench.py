@@ -57,6 +57,12 @@ def expert_weights(e):
     return synth.q4_k(rng, 2 * F, D), synth.q4_k(rng, D, F_PAD, zero_tail_cols=F_PAD - F)
 
 
+def set_tokens(n):
+    global T_TOTAL, WORKLOAD
+    T_TOTAL = n
+    WORKLOAD = f'moe_q4k_d4096_e64_f1408_top8_t{n}_zipf1.1'
+
+
 def hidden_states(torch, device, t0, t1):
     g = torch.Generator(device=device)
     g.manual_seed(1001)
@@ -240,7 +246,10 @@ def main():
     ap.add_argument('--cpu-tokens', type=int, default=2048, help='token sample of the CPU baseline')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-gemv', action='store_true')
+    ap.add_argument('--tokens', type=int, default=T_TOTAL,
+                    help='tokens per layer call (16384 = the headline configuration; smaller for profiling)')
     args = ap.parse_args()
+    set_tokens(args.tokens)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == 'reference':
