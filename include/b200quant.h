@@ -140,6 +140,22 @@ int b200q_moe_num_blocks(int T);
 int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
                            int *block_counts, int *base, int *offsets, int *slot_of, int *token_of, float *slot_w,
                            void *xperm_bf16, void *stream);
+/* Allocation-free variant of b200q_moe_dispatch_dev, with no counterpart in
+ * the reference.  For callers that must not allocate device memory (a plugin
+ * inside a host framework whose memory pool owns the device budget, or a
+ * latency-critical loop that cannot take cudaMalloc's implicit
+ * synchronisation): the counting-sort scratch lives in a file-scope device
+ * array of 256 KB that every GPU loading the library keeps until exit, so the
+ * call needs no block_counts/base buffers and calls no cudaMalloc, cudaFree or
+ * allocating library routine.  Limit: b200q_moe_num_blocks(T) * E <= 32768
+ * (larger calls return B200Q_EINVAL with a message).  The first call on a
+ * device looks up the array's device address; make that first call before
+ * any stream capture.  All calls share the array (it keeps the last call's
+ * contents; nothing in it must start at zero because each call writes every
+ * entry it reads), so calls that overlap on the GPU race. */
+int b200q_moe_dispatch_noalloc_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
+                                   int *offsets, int *slot_of, int *token_of, float *slot_w, void *xperm_bf16,
+                                   void *stream);
 /* y[t] = sum_{j<k} w_j * out[slot_of[t*k + j]] in j order (f32 [T, D]), with
  * w_j = slot_w[slot] if slot_w != NULL, else 1 (rows already weighted). */
 int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,

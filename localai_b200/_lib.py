@@ -47,6 +47,7 @@ SIGNATURES = {
     'b200q_moe_topk_dev': (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_moe_num_blocks': (_i, [_i]),
     'b200q_moe_dispatch_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    'b200q_moe_dispatch_noalloc_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_combine_dev': (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     'b200q_check_device_error': (_i, []),
     'b200q_gemv_tuning': (None, [_i, _i, _i, _i]),

@@ -30,6 +30,10 @@ cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, 
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
 cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
                                cudaStream_t st);
+cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
+                                        int *offsets, int *slot_of, int *token_of, float *slot_w,
+                                        __nv_bfloat16 *xperm, cudaStream_t st);
+int noalloc_dispatch_max();
 cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
@@ -409,6 +413,27 @@ B200Q_API int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int 
                                            slot_w, static_cast<__nv_bfloat16 *>(xperm_bf16), di->err,
                                            (cudaStream_t)stream),
                        "dispatch");
+}
+
+// Allocation-free variant of b200q_moe_dispatch_dev: scratch in a file-scope
+// device array (see moe.cu); no cudaMalloc, cudaFree or allocating library call.
+B200Q_API int b200q_moe_dispatch_noalloc_dev(const int *ids, const float *w, int T, int k, int E, const float *h,
+                                             int D, int *offsets, int *slot_of, int *token_of, float *slot_w,
+                                             void *xperm_bf16, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ids || !w || !offsets || !slot_of || !token_of || !slot_w || (xperm_bf16 && !h))
+        return set_status(B200Q_EINVAL, "dispatch_noalloc: null pointer");
+    if (T < 1 || k < 1 || E < 1 || E > 1024)
+        return set_status(B200Q_EINVAL, "dispatch_noalloc: invalid T=%d k=%d E=%d", T, k, E);
+    if ((long long)moe_num_blocks(T) * E > noalloc_dispatch_max())
+        return set_status(B200Q_EINVAL,
+                          "dispatch_noalloc: ceil(T/256)*E = %lld exceeds the static scratch limit of %d entries",
+                          (long long)moe_num_blocks(T) * E, noalloc_dispatch_max());
+    g_launches += xperm_bf16 ? 4 : 3;
+    return cuda_status(launch_moe_dispatch_noalloc(ids, w, T, k, E, h, D, offsets, slot_of, token_of, slot_w,
+                                                   static_cast<__nv_bfloat16 *>(xperm_bf16), (cudaStream_t)stream),
+                       "dispatch_noalloc");
 }
 
 B200Q_API int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D,

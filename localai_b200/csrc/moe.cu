@@ -308,6 +308,61 @@ cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- allocation-free dispatch
+// Callers that cannot allocate device memory -- for example a plugin running
+// inside a host framework whose memory pool owns the whole device budget, or a
+// latency-critical loop that must not take the implicit synchronisation of
+// cudaMalloc/cudaFree -- use this variant of the dispatch.  Its scratch (the
+// per-block expert counts and bases of the counting sort, and the error word)
+// is a file-scope device array instead of caller or library allocations.
+//
+// Limit: moe_num_blocks(T) * E <= NOALLOC_DISPATCH_MAX (32768), e.g. 16384
+// tokens x 512 experts or 131072 tokens x 64 experts; larger calls are
+// rejected on the host.  The array occupies 256 KB + 256 B on every GPU that
+// loads the library until the process exits.  Every call shares it and it
+// keeps the previous call's contents; nothing in it has to start at zero,
+// because each call writes every count and base entry it later reads (the
+// error word is the only cumulative field, set on a bad expert id).  Calls
+// that overlap on the GPU (different streams, or different host threads
+// without ordering) race on the array.
+constexpr int NOALLOC_DISPATCH_MAX = 32768;
+static __device__ __align__(256) int g_noalloc_dispatch_scratch[2 * NOALLOC_DISPATCH_MAX + 64];
+
+// Device address of the array, looked up once per device (with that device
+// current) on the first call made on it.
+cudaError_t noalloc_dispatch_scratch(int **ptr)
+{
+    static int *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_dispatch_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = static_cast<int *>(p);
+    }
+    *ptr = addr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
+                                        int *offsets, int *slot_of, int *token_of, float *slot_w,
+                                        __nv_bfloat16 *xperm, cudaStream_t st)
+{
+    if (T < 1 || E < 1 || (long long)moe_num_blocks(T) * E > NOALLOC_DISPATCH_MAX) return cudaErrorInvalidValue;
+    int *scratch = nullptr;
+    cudaError_t e = noalloc_dispatch_scratch(&scratch);
+    if (e != cudaSuccess) return e;
+    int *block_counts = scratch, *base = scratch + NOALLOC_DISPATCH_MAX;
+    int *err = scratch + 2 * NOALLOC_DISPATCH_MAX;
+    return launch_moe_dispatch(ids, wts, T, k, E, h, D, block_counts, base, offsets, slot_of, token_of, slot_w, xperm,
+                               err, st);
+}
+
+int noalloc_dispatch_max() { return NOALLOC_DISPATCH_MAX; }
+
 cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
                                cudaStream_t st)
 {
