@@ -88,7 +88,7 @@ class EPMoE:
         counts = torch.stack([cnt_send.sum(1), cnt_recv.sum(1)]).cpu()      # one host sync per call
         send_splits, recv_splits = counts[0].tolist(), counts[1].tolist()
         R = int(sum(recv_splits))
-        xrecv = torch.empty((R, L.D), dtype=torch.bfloat16, device=dev)
+        xrecv = torch.empty((R, L.D), dtype=xsend.dtype, device=dev)
         dist.all_to_all_single(xrecv, xsend, recv_splits, send_splits, group=self.group)
         # received rows are ordered (source rank, local expert); group them by local expert
         le = torch.arange(self.E_loc, device=dev, dtype=torch.int32).repeat(self.G)
@@ -103,7 +103,7 @@ class EPMoE:
             out_g = torch.empty((0, L.D), dtype=torch.float32, device=dev)
         out_recv = torch.empty_like(out_g)
         out_recv[order] = out_g
-        back = torch.empty((xsend.shape[0], L.D), dtype=torch.float32, device=dev)
+        back = torch.empty((xsend.shape[0], L.D), dtype=out_g.dtype, device=dev)
         dist.all_to_all_single(back, out_recv, send_splits, recv_splits, group=self.group)
         return L.combine(back, slot_of, T, slot_w)
 

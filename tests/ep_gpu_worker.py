@@ -1,0 +1,57 @@
+"""Worker for tests/test_ep_gpu.py: one process per GPU (launched by torchrun).
+
+Every rank builds the same small MoE layer, runs its token shard through the
+expert-parallel layer (its E/G experts, NCCL all-to-all) and through a full
+single-GPU QuantMoE, and exits non-zero if they differ.
+"""
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+from localai_b200 import synth                       # noqa: E402
+from localai_b200.ep import EPMoE, lpt_placement     # noqa: E402
+from localai_b200.moe import QuantMoE                # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ['RANK']), int(os.environ['WORLD_SIZE'])
+    dev = torch.device('cuda', int(os.environ['LOCAL_RANK']))
+    torch.cuda.set_device(dev)
+    dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=dev)
+    E, D, F, k, T = 16, 512, 128, 4, 1024
+    rng = np.random.default_rng(0)
+    gate_up = [synth.q4_k(rng, 2 * F, D) for _ in range(E)]
+    down = [synth.q4_k(rng, D, 256, zero_tail_cols=256 - F) for _ in range(E)]
+    wr = torch.from_numpy(rng.normal(0, D ** -0.5, size=(E, D)).astype(np.float32)).to(dev)
+    bias = torch.from_numpy(np.log(np.arange(1, E + 1) ** -1.1).astype(np.float32)).to(dev)
+    h = torch.from_numpy(rng.normal(size=(T, D)).astype(np.float32)).to(dev)
+    cat = lambda parts: torch.frombuffer(bytearray(b''.join(parts)), dtype=torch.uint8).to(dev)
+    full = QuantMoE(wr, cat(gate_up), cat(down), d_model=D, d_ff=F, top_k=k, router_bias=bias)
+    _, ids, _ = full.route(h)
+    loads = torch.bincount(ids.reshape(-1).long(), minlength=E).cpu().numpy()
+    owner, local = lpt_placement(loads, world)
+    mine = [int(e) for e in np.nonzero(owner == rank)[0]]
+    part = QuantMoE(wr, cat([gate_up[e] for e in mine]), cat([down[e] for e in mine]), d_model=D, d_ff=F,
+                    top_k=k, router_bias=bias, local_experts=len(mine))
+    ep = EPMoE(part, owner, local)
+    n = T // world
+    shard = h[rank * n:(rank + 1) * n]
+    y_ep = ep(shard)
+    y_ref = full(shard)
+    torch.cuda.synchronize()
+    err = float((y_ep - y_ref).abs().max() / y_ref.abs().max())
+    ok = torch.tensor([1 if err < 1e-5 else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    print(f'rank {rank}: ep vs single-GPU max rel err {err:.3e}', flush=True)
+    dist.destroy_process_group()
+    sys.exit(0 if int(ok.item()) == 1 else 1)
+
+
+if __name__ == '__main__':
+    main()

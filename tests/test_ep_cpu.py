@@ -1,0 +1,136 @@
+"""Expert-parallel exchange logic on CPU: 2 gloo ranks vs one process.
+
+The GPU stages (router, top-k, dispatch, expert GEMMs, combine) are replaced
+by plain torch CPU stand-ins with the same interfaces, so these tests check the
+parts of ``EPMoE`` that are host logic: virtual expert numbering, split sizes,
+the count and row all-to-alls, regrouping by local expert, the return
+exchange and the weighted combine -- plus LPT placement.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from localai_b200.ep import EPMoE, lpt_placement
+
+
+class StandInLayer:
+    """torch CPU implementation of the QuantMoE stage interface (dense f32 experts)."""
+
+    def __init__(self, router_w, bias, gate_up, down, k, held_experts):
+        self.router_w, self.bias = router_w, bias
+        self.gate_up, self.down = gate_up, down          # [held, 2F, D], [held, D, F]
+        self.E, self.D = router_w.shape
+        self.F = down.shape[2]
+        self.k = k
+        self.E_held = held_experts
+
+    def route(self, h):
+        logits = h @ self.router_w.T + self.bias
+        p = torch.softmax(logits, dim=1)
+        order = torch.sort(-p, dim=1, stable=True).indices[:, :self.k].to(torch.int32)
+        w = torch.gather(p, 1, order.long())
+        return logits, order, w / w.sum(1, keepdim=True)
+
+    def dispatch(self, h, ids, w):
+        T = ids.shape[0]
+        flat = ids.reshape(-1).long()
+        order = torch.sort(flat, stable=True).indices
+        slot_of = torch.empty_like(order)
+        slot_of[order] = torch.arange(order.numel())
+        token_of = order // self.k
+        offsets = torch.zeros(self.E + 1, dtype=torch.int32)
+        offsets[1:] = torch.cumsum(torch.bincount(flat, minlength=self.E), 0)
+        return offsets, slot_of.to(torch.int32), token_of.to(torch.int32), w.reshape(-1)[order], h[token_of]
+
+    def experts(self, x, offsets, slot_w, n_experts=None):
+        out = torch.zeros((x.shape[0], self.D))
+        for e in range(n_experts or self.E_held):
+            a, b = int(offsets[e]), int(offsets[e + 1])
+            if a == b:
+                continue
+            gu = x[a:b] @ self.gate_up[e].T
+            g, u = gu[:, :self.F], gu[:, self.F:]
+            out[a:b] = (g / (1 + torch.exp(-g.clamp(-80, 80))) * u) @ self.down[e].T
+        if slot_w is not None:
+            out = out * slot_w[:, None]
+        return out
+
+    def combine(self, out, slot_of, T, slot_w=None):
+        rows = out[slot_of.long()]
+        if slot_w is not None:
+            rows = rows * slot_w[slot_of.long()][:, None]
+        return rows.view(T, self.k, self.D).sum(1)
+
+
+def make_problem(seed=0, E=8, D=32, F=16, T=96):
+    g = torch.Generator().manual_seed(seed)
+    router_w = torch.randn((E, D), generator=g) / D ** 0.5
+    bias = torch.log(torch.arange(1, E + 1, dtype=torch.float64) ** -1.1).float()
+    gate_up = torch.randn((E, 2 * F, D), generator=g) / D ** 0.5
+    down = torch.randn((E, D, F), generator=g) / F ** 0.5
+    h = torch.randn((T, D), generator=g)
+    return router_w, bias, gate_up, down, h
+
+
+def single_process(router_w, bias, gate_up, down, h, k):
+    L = StandInLayer(router_w, bias, gate_up, down, k, gate_up.shape[0])
+    _, ids, w = L.route(h)
+    offsets, slot_of, _, slot_w, x = L.dispatch(h, ids, w)
+    return L.combine(L.experts(x, offsets, slot_w), slot_of, h.shape[0]), ids
+
+
+def _worker(rank, world, port, k, result):
+    dist.init_process_group('gloo', init_method=f'tcp://127.0.0.1:{port}', rank=rank, world_size=world)
+    try:
+        router_w, bias, gate_up, down, h = make_problem()
+        ref, ids = single_process(router_w, bias, gate_up, down, h, k)
+        loads = torch.bincount(ids.reshape(-1).long(), minlength=router_w.shape[0]).numpy()
+        owner, local = lpt_placement(loads, world)
+        mine = np.nonzero(owner == rank)[0]
+        L = StandInLayer(router_w, bias, gate_up[mine], down[mine], k, len(mine))
+        T = h.shape[0] // world
+        y = EPMoE(L, owner, local).forward(h[rank * T:(rank + 1) * T])
+        result[rank] = float((y - ref[rank * T:(rank + 1) * T]).abs().max() / ref.abs().max())
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize('world,k', [(2, 2), (2, 3), (4, 2)])
+def test_ep_matches_single_process(world, k):
+    ctx = mp.get_context('spawn')
+    with ctx.Manager() as m:
+        result = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, k, result)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert len(result) == world
+        assert max(result.values()) < 1e-5, dict(result)
+
+
+def test_lpt_placement_balances_zipf_loads():
+    E = 64
+    loads = (np.arange(1, E + 1) ** -1.1) * 1e6
+    for G in (2, 4, 8):
+        owner, local = lpt_placement(loads, G)
+        assert np.all(np.bincount(owner, minlength=G) == E // G)
+        for r in range(G):
+            assert sorted(local[owner == r]) == list(range(E // G))
+        per = np.bincount(owner, weights=loads, minlength=G)
+        # no placement beats the largest expert plus the E/G-1 smallest ones
+        floor = loads.max() + np.sort(loads)[:E // G - 1].sum()
+        assert per.max() <= max(floor, 1.25 * per.mean())
