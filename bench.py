@@ -97,9 +97,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
+        """Stop sampling; summarise the samples taken in [t0, t1] (the timed
+        region).  If the region was shorter than the sampling period, the
+        samples of the whole loaded period (warm-up + timed) are used and the
+        summary says so."""
         if self.proc is None:
             return None
         time.sleep(0.25)
@@ -108,9 +112,14 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        window = 'timed region'
+        lines = [l for (t, l) in self.lines if t0 is None or (t0 <= t <= t1 + 0.2)]
+        if not lines:
+            window = 'warm-up and timed region (timed region shorter than the 200 ms sampling period)'
+            lines = [l for (_, l) in self.lines]
         sm, mx, reasons = [], [], set()
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for line in self.lines:
+        for line in lines:
             f = [x.strip() for x in line.split(',')]
             if len(f) < 9 or f[0] != self.gpu_index:
                 continue
@@ -125,7 +134,7 @@ class ClockSampler:
         if not sm:
             return None
         return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx), 'reasons': sorted(reasons),
-                'samples': len(sm)}
+                'samples': len(sm), 'window': window}
 
 
 # ----------------------------------------------------------------- CPU (reference kernels)
@@ -305,28 +314,32 @@ def main():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    # clock sampling starts before the warm-up so that nvidia-smi's own start-up
+    # does not fall into the timed region
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(1.0)
     for _ in range(args.warmup):
         step(h)
     torch.cuda.synchronize()
     ops.check_device_error()
 
     # ---- timed region (device-resident inputs)
-    sampler = ClockSampler(local_rank) if rank == 0 else None
     barrier()
     torch.cuda.synchronize()
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
     n0 = lib.b200q_launch_count()
+    t_start = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         y = step(h)
     e1.record()
     torch.cuda.synchronize()
+    t_end = time.time()
     launches = lib.b200q_launch_count() - n0
     barrier()
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop(t_start, t_end) if sampler else None
     ms = e0.elapsed_time(e1) / args.steps
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:

@@ -106,18 +106,22 @@ int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float *y, int r
  * engine/native_quant.cpp:620-703 and the expert products of
  * engine/zaya.py:303-306).  Group g owns activation rows
  * [row_off[g], row_off[g+1]) of x_bf16 [x_rows, k] (row_off: device int32
- * [groups+1]) and weight rows [g*w_rows_per_group, ...) of the raw Q4_K
- * tensor w (rows of ceil(k/256) super-blocks; k a multiple of 64).
+ * [groups+1]) and the weight rows [wg*w_rows_per_group, ...) of the raw Q4_K
+ * tensor w (rows of ceil(k/256) super-blocks; k a multiple of 64), where
+ * wg = group_w[g] if group_w (device int32 [groups]) is given, else g;
+ * n_weight_groups is the number of weight groups w holds (needed with
+ * group_w).
  *   up_offset <  0: plain mode, out[row*ld_out + n] = x_row . w_n (times
  *                   row_scale[row] if row_scale != NULL), n < n_feat (multiple
- *                   of 128);
+ *                   of 128); out is f32, or bf16 when out_is_bf16 != 0;
  *   up_offset >= 0: gate/up mode over n_feat features (multiple of 64):
  *                   act[row*ld_act + f] = bf16(SiLU(x.w_f) * (x.w_{f+up_offset})),
  *                   SiLU as engine/zaya.py:305.
  * max_ctas limits the persistent grid (0 = one CTA per SM). */
 int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *w, int groups, int w_rows_per_group,
-                       int up_offset, int n_feat, const int *row_off, float *out, long long ld_out,
-                       const float *row_scale, void *act_bf16, long long ld_act, int max_ctas, void *stream);
+                       int up_offset, int n_feat, const int *row_off, const int *group_w, int n_weight_groups,
+                       void *out, int out_is_bf16, long long ld_out, const float *row_scale, void *act_bf16,
+                       long long ld_act, int max_ctas, void *stream);
 
 /* ---- MoE layer stages (engine/zaya.py:274-307, generalised to top-k) ----
  * All buffers are device memory owned by the caller; nothing is allocated. */
@@ -157,9 +161,10 @@ int b200q_moe_dispatch_noalloc_dev(const int *ids, const float *w, int T, int k,
                                    int *offsets, int *slot_of, int *token_of, float *slot_w, void *xperm_bf16,
                                    void *stream);
 /* y[t] = sum_{j<k} w_j * out[slot_of[t*k + j]] in j order (f32 [T, D]), with
- * w_j = slot_w[slot] if slot_w != NULL, else 1 (rows already weighted). */
-int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
-                          void *stream);
+ * w_j = slot_w[slot] if slot_w != NULL, else 1 (rows already weighted); the
+ * rows of out are f32, or bf16 when out_is_bf16 != 0. */
+int b200q_moe_combine_dev(const void *out, int out_is_bf16, const int *slot_of, const float *slot_w, int T, int k,
+                          int D, float *y, void *stream);
 
 /* Device error word: returns and clears the sticky kernel error of the
  * current device (0 if none).  Synchronises the device. */

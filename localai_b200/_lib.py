@@ -42,13 +42,13 @@ SIGNATURES = {
     'b200q_dequant_f32_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
     'b200q_dequant_bf16_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
     'b200q_gemv_dev': (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _ll, _ll, _vp]),
-    'b200q_gemm_q4k_dev': (_i, [_vp, _ll, _i, _vp, _i, _i, _i, _i, _vp, _vp, _ll, _vp, _vp, _ll, _i, _vp]),
+    'b200q_gemm_q4k_dev': (_i, [_vp, _ll, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll, _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     'b200q_moe_topk_dev': (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_moe_num_blocks': (_i, [_i]),
     'b200q_moe_dispatch_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_dispatch_noalloc_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
-    'b200q_moe_combine_dev': (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    'b200q_moe_combine_dev': (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     'b200q_check_device_error': (_i, []),
     'b200q_gemv_tuning': (None, [_i, _i, _i, _i]),
     'b200q_launch_count': (_ll, []),

@@ -28,16 +28,17 @@ int moe_num_blocks(int T);
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
-cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
-                               cudaStream_t st);
+cudaError_t launch_moe_combine(const void *out, bool out_bf16, const int *slot_of, const float *slot_w, int T, int k,
+                               int D, float *y, cudaStream_t st);
 cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                         int *offsets, int *slot_of, int *token_of, float *slot_w,
                                         __nv_bfloat16 *xperm, cudaStream_t st);
 int noalloc_dispatch_max();
 cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
-                               float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
-                               long long ld_act, int *err, int num_sms, int max_ctas, cudaStream_t st);
+                               const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
+                               long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
+                               int *err, int num_sms, int max_ctas, cudaStream_t st);
 
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
@@ -361,20 +362,24 @@ B200Q_API int b200q_gemv_dev(int ggml_type, const void *w, const float *x, float
 }
 
 B200Q_API int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *w, int groups,
-                                 int w_rows_per_group, int up_offset, int n_feat, const int *row_off, float *out,
+                                 int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
+                                 const int *group_w, int n_weight_groups, void *out, int out_is_bf16,
                                  long long ld_out, const float *row_scale, void *act_bf16, long long ld_act,
                                  int max_ctas, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!x_bf16 || !w || !row_off) return set_status(B200Q_EINVAL, "gemm: null pointer");
     if (up_offset >= 0 ? !act_bf16 : !out) return set_status(B200Q_EINVAL, "gemm: missing output");
+    if (group_w && n_weight_groups < 1) return set_status(B200Q_EINVAL, "gemm: n_weight_groups must be >= 1");
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
     return cuda_status(launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(x_bf16), x_rows, k, w, groups,
-                                          w_rows_per_group, up_offset, n_feat, row_off, out, ld_out, row_scale,
-                                          static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
-                                          (cudaStream_t)stream),
+                                          w_rows_per_group, up_offset, n_feat, row_off, group_w, n_weight_groups,
+                                          out_is_bf16 ? nullptr : static_cast<float *>(out),
+                                          out_is_bf16 ? static_cast<__nv_bfloat16 *>(out) : nullptr, ld_out,
+                                          row_scale, static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err,
+                                          di->sms, max_ctas, (cudaStream_t)stream),
                        "gemm");
 }
 
@@ -436,13 +441,14 @@ B200Q_API int b200q_moe_dispatch_noalloc_dev(const int *ids, const float *w, int
                        "dispatch_noalloc");
 }
 
-B200Q_API int b200q_moe_combine_dev(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D,
-                                    float *y, void *stream)
+B200Q_API int b200q_moe_combine_dev(const void *out, int out_is_bf16, const int *slot_of, const float *slot_w, int T,
+                                    int k, int D, float *y, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!out || !slot_of || !y) return set_status(B200Q_EINVAL, "combine: null pointer");
     ++g_launches;
-    return cuda_status(launch_moe_combine(out, slot_of, slot_w, T, k, D, y, (cudaStream_t)stream), "combine");
+    return cuda_status(launch_moe_combine(out, out_is_bf16 != 0, slot_of, slot_w, T, k, D, y, (cudaStream_t)stream),
+                       "combine");
 }
 
 B200Q_API int b200q_check_device_error(void)

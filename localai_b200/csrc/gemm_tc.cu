@@ -53,11 +53,13 @@ struct TcArgs {
     int k;                  // reduction length (multiple of 64)
     int groups;
     const int *row_off;     // [groups + 1] activation row offsets (device)
+    const int *group_w;     // optional [groups]: weight index of each group (default: g)
     int w_rows_per_group;   // weight rows of one group in the raw tensor map
     int up_offset;          // gate/up mode: row offset of the up half (F); < 0: plain mode
     int raw_chunk_bytes;    // bytes of one 256-value block
     // epilogue
-    float *out;             // plain mode: out[row * ld_out + n]
+    float *out;             // plain mode: out[row * ld_out + n] (f32), or
+    __nv_bfloat16 *out_bf16;//             out_bf16[row * ld_out + n]
     long long ld_out;
     const float *row_scale; // plain mode, optional: out *= row_scale[row]
     __nv_bfloat16 *act;     // gate/up mode: act[row * ld_act + f]
@@ -234,6 +236,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t tmem_slot = acc_empty + 16;
     __shared__ int tile_pref[TC_MAX_GROUPS + 1];
     __shared__ int row_off_s[TC_MAX_GROUPS + 1];
+    __shared__ int group_w_s[TC_MAX_GROUPS];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ksteps = a.k / TC_BK;
@@ -256,6 +259,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // tile prefix over groups (every CTA computes the same table)
     if (warp == 2) {
         for (int g = lane; g <= a.groups; g += 32) row_off_s[g] = a.row_off[g];
+        for (int g = lane; g < a.groups; g += 32) group_w_s[g] = a.group_w ? a.group_w[g] : g;
         __syncwarp();
         if (lane == 0) {
             int acc = 0;
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int q = 0, rq = 0;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
                 const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
-                const int wrow0 = c.g * a.w_rows_per_group + (gate_up ? c.nt * 64 : c.nt * TC_BM);
+                const int wrow0 = group_w_s[c.g] * a.w_rows_per_group + (gate_up ? c.nt * 64 : c.nt * TC_BM);
                 const int wrow1 = gate_up ? wrow0 + a.up_offset : wrow0 + 64;
                 const int xrow = row_off_s[c.g] + c.m0;
                 for (int ks = 0; ks < ksteps && ok; ++ks) {
@@ -368,7 +372,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (col < c.rows) {
                             const long long row = row_base + col;
                             const float sc = a.row_scale ? __ldg(a.row_scale + row) : 1.0f;
-                            a.out[row * a.ld_out + n] = __uint_as_float(v[j]) * sc;
+                            const float val = __uint_as_float(v[j]) * sc;
+                            if (a.out_bf16) a.out_bf16[row * a.ld_out + n] = __float2bfloat16_rn(val);
+                            else a.out[row * a.ld_out + n] = val;
                         }
                     }
                 }
@@ -477,8 +483,9 @@ size_t tc_gemm_smem_bytes(int chunk_bytes)
 //            < 0: plain mode over n_feat output columns (out f32 [x_rows, ld_out]).
 cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
-                               float *out, long long ld_out, const float *row_scale, __nv_bfloat16 *act,
-                               long long ld_act, int *err, int num_sms, int max_ctas, cudaStream_t st)
+                               const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
+                               long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
+                               int *err, int num_sms, int max_ctas, cudaStream_t st)
 {
     if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
@@ -490,17 +497,19 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
     CUtensorMap mx, mw;
     cudaError_t e = make_map_bf16(&mx, x, x_rows, k, TC_BN);
     if (e != cudaSuccess) return e;
-    e = make_map_raw(&mw, w, (long long)groups * w_rows_per_group, row_bytes, chunk);
+    e = make_map_raw(&mw, w, (long long)(group_w ? n_weight_groups : groups) * w_rows_per_group, row_bytes, chunk);
     if (e != cudaSuccess) return e;
     TcArgs a;
     a.n_tiles = gu ? n_feat / 64 : n_feat / TC_BM;
     a.k = k;
     a.groups = groups;
     a.row_off = row_off;
+    a.group_w = group_w;
     a.w_rows_per_group = w_rows_per_group;
     a.up_offset = up_offset;
     a.raw_chunk_bytes = chunk;
     a.out = out;
+    a.out_bf16 = out_bf16;
     a.ld_out = ld_out;
     a.row_scale = row_scale;
     a.act = act;

@@ -246,7 +246,16 @@ __global__ void moe_gather_kernel(const float *__restrict__ h, const int *__rest
 
 // y[t, :] = sum_j w_j * out[slot_of[t, j], :]   (j ascending; w_j = slot_w[slot]
 // when slot_w is given, else 1 because the rows already carry their weight)
-__global__ void moe_combine_kernel(const float *__restrict__ out, const int *__restrict__ slot_of,
+__device__ __forceinline__ float4 load4(const float *p, long long i) { return __ldg(reinterpret_cast<const float4 *>(p) + i); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16 *p, long long i)
+{
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p) + i);
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+}
+
+template <typename RowT>
+__global__ void moe_combine_kernel(const RowT *__restrict__ out, const int *__restrict__ slot_of,
                                    const float *__restrict__ slot_w, int T, int k, int D, float *__restrict__ y)
 {
     const int t = blockIdx.x;
@@ -255,7 +264,7 @@ __global__ void moe_combine_kernel(const float *__restrict__ out, const int *__r
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; ++j) {
             const int slot = slot_of[(long long)t * k + j];
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(out + (long long)slot * D) + c);
+            const float4 v = load4(out, (long long)slot * (D / 4) + c);
             const float wj = slot_w ? __ldg(slot_w + slot) : 1.0f;
             acc.x = fmaf(wj, v.x, acc.x); acc.y = fmaf(wj, v.y, acc.y);
             acc.z = fmaf(wj, v.z, acc.z); acc.w = fmaf(wj, v.w, acc.w);
@@ -363,11 +372,15 @@ cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T,
 
 int noalloc_dispatch_max() { return NOALLOC_DISPATCH_MAX; }
 
-cudaError_t launch_moe_combine(const float *out, const int *slot_of, const float *slot_w, int T, int k, int D, float *y,
-                               cudaStream_t st)
+cudaError_t launch_moe_combine(const void *out, bool out_bf16, const int *slot_of, const float *slot_w, int T, int k,
+                               int D, float *y, cudaStream_t st)
 {
     if (T < 1 || k < 1 || D % 4) return cudaErrorInvalidValue;
-    moe_combine_kernel<<<T, 256, 0, st>>>(out, slot_of, slot_w, T, k, D, y);
+    if (out_bf16)
+        moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(out), slot_of, slot_w,
+                                                             T, k, D, y);
+    else
+        moe_combine_kernel<float><<<T, 256, 0, st>>>(static_cast<const float *>(out), slot_of, slot_w, T, k, D, y);
     return cudaGetLastError();
 }
 

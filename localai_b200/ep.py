@@ -9,9 +9,10 @@ NVLink/NVSwitch) and the T tokens are sharded evenly; per layer call:
        stable counting sort, rows gathered as bf16;
     3. all-to-all of the per-(rank, expert) row counts, then all-to-all of the
        rows (variable splits);
-    4. received rows are grouped by local expert and run through the grouped
-       tensor-core GEMMs (gate/up with fused SiLU*up, then down);
-    5. all-to-all of the expert outputs back to the source ranks;
+    4. the received rows, ordered (source rank, local expert), run in place
+       through the grouped tensor-core GEMMs (gate/up with fused SiLU*up,
+       then down, bf16 rows), one GEMM group per (source, expert) run;
+    5. all-to-all of the expert outputs (bf16) back to the source ranks;
     6. weighted combine in fixed j order.
 
 Expert placement is greedy LPT on expected per-expert loads with E/G experts
@@ -74,6 +75,8 @@ class EPMoE:
         dev = layer.router_w.device
         # virtual expert index: experts ordered by (owner rank, local index)
         self.virt = torch.from_numpy((owner * self.E_loc + local).astype(np.int32)).to(dev)
+        # GEMM group (source rank, local expert) -> local expert
+        self.group_w = torch.arange(self.E_loc, dtype=torch.int32, device=dev).repeat(self.G)
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         L = self.layer
@@ -90,20 +93,15 @@ class EPMoE:
         R = int(sum(recv_splits))
         xrecv = torch.empty((R, L.D), dtype=xsend.dtype, device=dev)
         dist.all_to_all_single(xrecv, xsend, recv_splits, send_splits, group=self.group)
-        # received rows are ordered (source rank, local expert); group them by local expert
-        le = torch.arange(self.E_loc, device=dev, dtype=torch.int32).repeat(self.G)
-        row_e = torch.repeat_interleave(le, cnt_recv.reshape(-1).to(torch.int64), output_size=R)
-        order = torch.sort(row_e, stable=True).indices
-        xg = xrecv[order]
-        loc_off = torch.zeros(self.E_loc + 1, dtype=torch.int32, device=dev)
-        loc_off[1:] = torch.cumsum(cnt_recv.sum(0), 0).to(torch.int32)
+        # Received rows are ordered (source rank, local expert); each such run is
+        # one GEMM group whose weights are its local expert -- no regrouping copy.
+        grp_off = torch.zeros(self.G * self.E_loc + 1, dtype=torch.int32, device=dev)
+        grp_off[1:] = torch.cumsum(cnt_recv.reshape(-1), 0).to(torch.int32)
         if R > 0:
-            out_g = L.experts(xg, loc_off, None, n_experts=self.E_loc)
+            out_recv = L.experts(xrecv, grp_off, None, group_w=self.group_w)
         else:
-            out_g = torch.empty((0, L.D), dtype=torch.float32, device=dev)
-        out_recv = torch.empty_like(out_g)
-        out_recv[order] = out_g
-        back = torch.empty((xsend.shape[0], L.D), dtype=out_g.dtype, device=dev)
+            out_recv = torch.empty((0, L.D), dtype=torch.bfloat16, device=dev)
+        back = torch.empty((xsend.shape[0], L.D), dtype=out_recv.dtype, device=dev)
         dist.all_to_all_single(back, out_recv, send_splits, recv_splits, group=self.group)
         return L.combine(back, slot_of, T, slot_w)
 

@@ -8,7 +8,7 @@ same block batched over T tokens and generalised to top-k:
     p = softmax(logits); top-k of p (+ sel bias)  b200q_moe_topk_dev
     stable counting sort of (token, j) by expert  b200q_moe_dispatch_dev
     act = SiLU(gate x) * (up x)  per expert       b200q_gemm_q4k_dev (gate/up mode, tcgen05)
-    out = w_slot * (down act)    per expert       b200q_gemm_q4k_dev (plain mode, tcgen05)
+    out = w_slot * (down act)    per expert       b200q_gemm_q4k_dev (plain mode, tcgen05; bf16 rows)
     y[t] = sum_j out[slot(t, j)]                  b200q_moe_combine_dev
 
 Expert weights are the raw GGUF Q4_K tensors in ZAYA's layout: ``gate_up``
@@ -93,34 +93,33 @@ class QuantMoE:
         return offsets, slot_of, token_of, slot_w, xperm
 
     def experts(self, xperm: torch.Tensor, offsets: torch.Tensor, slot_w: torch.Tensor | None, *,
-                max_ctas: int = 0, gate_up: torch.Tensor | None = None, down: torch.Tensor | None = None,
-                n_experts: int | None = None):
+                group_w: torch.Tensor | None = None, out_dtype=torch.bfloat16, max_ctas: int = 0):
         """Grouped gate/up (fused SiLU*up) then grouped down, on the tensor cores.
 
-        ``slot_w`` scales each output row (None: unscaled).  ``gate_up``/``down``/
-        ``n_experts`` override the layer's expert set (expert parallelism runs a
-        rank's local experts)."""
+        ``slot_w`` scales each output row (None: unscaled).  With ``group_w``
+        the rows form ``len(group_w)`` groups whose experts are
+        ``group_w[g]`` among the experts this layer holds (expert parallelism
+        feeds the rows received from every rank this way, in place)."""
         S, dev = xperm.shape[0], xperm.device
-        gu = self.gate_up if gate_up is None else gate_up
-        dn = self.down if down is None else down
-        ne = self.E_held if n_experts is None else n_experts
+        groups = offsets.numel() - 1
+        gw = None if group_w is None else group_w.data_ptr()
         act = torch.empty((S, self.F), dtype=torch.bfloat16, device=dev)
         _lib.check(self.lib.b200q_gemm_q4k_dev(
-            xperm.data_ptr(), S, self.D, gu.data_ptr(), ne, 2 * self.F, self.F, self.F,
-            offsets.data_ptr(), None, 0, None, act.data_ptr(), self.F, max_ctas, _stream()))
-        out = torch.empty((S, self.D), dtype=torch.float32, device=dev)
+            xperm.data_ptr(), S, self.D, self.gate_up.data_ptr(), groups, 2 * self.F, self.F, self.F,
+            offsets.data_ptr(), gw, self.E_held, None, 0, 0, None, act.data_ptr(), self.F, max_ctas, _stream()))
+        out = torch.empty((S, self.D), dtype=out_dtype, device=dev)
         _lib.check(self.lib.b200q_gemm_q4k_dev(
-            act.data_ptr(), S, self.F, dn.data_ptr(), ne, self.D, -1, self.D,
-            offsets.data_ptr(), out.data_ptr(), self.D, None if slot_w is None else slot_w.data_ptr(), None, 0,
-            max_ctas, _stream()))
+            act.data_ptr(), S, self.F, self.down.data_ptr(), groups, self.D, -1, self.D,
+            offsets.data_ptr(), gw, self.E_held, out.data_ptr(), 1 if out_dtype == torch.bfloat16 else 0, self.D,
+            None if slot_w is None else slot_w.data_ptr(), None, 0, max_ctas, _stream()))
         return out
 
     def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int, slot_w: torch.Tensor | None = None):
         """y[t] = sum_j (slot_w) * out[slot(t, j)]; pass slot_w when out is unweighted."""
         y = torch.empty((T, self.D), dtype=torch.float32, device=out.device)
-        _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), slot_of.data_ptr(),
-                                                  None if slot_w is None else slot_w.data_ptr(), T, self.k,
-                                                  self.D, y.data_ptr(), _stream()))
+        _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), 1 if out.dtype == torch.bfloat16 else 0,
+                                                  slot_of.data_ptr(), None if slot_w is None else slot_w.data_ptr(),
+                                                  T, self.k, self.D, y.data_ptr(), _stream()))
         return y
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:

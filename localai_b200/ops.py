@@ -89,14 +89,17 @@ def check_device_error() -> None:
 def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k: int, n_feat: int,
              w_rows_per_group: int, up_offset: int = -1, out: torch.Tensor | None = None,
              row_scale: torch.Tensor | None = None, act: torch.Tensor | None = None,
+             group_w: torch.Tensor | None = None, n_weight_groups: int = 0, out_dtype=torch.float32,
              max_ctas: int = 0) -> torch.Tensor:
     """Grouped tensor-core GEMM with in-kernel Q4_K dequantisation.
 
     ``x_bf16`` [rows, k] bf16 activations; group g owns rows
-    ``row_off[g]:row_off[g+1]`` (int32 CUDA tensor, groups+1 entries) and
-    weight rows ``g*w_rows_per_group ...`` of ``w`` (raw Q4_K bytes).
-    Plain mode (``up_offset < 0``) returns f32 [rows, n_feat]; gate/up mode
-    returns bf16 [rows, n_feat] = SiLU(gate) * up with up rows at
+    ``row_off[g]:row_off[g+1]`` (int32 CUDA tensor, groups+1 entries) and the
+    weight rows ``wg*w_rows_per_group ...`` of ``w`` (raw Q4_K bytes), with
+    ``wg = group_w[g]`` when ``group_w`` is given (then ``w`` holds
+    ``n_weight_groups`` weight groups), else ``wg = g``.  Plain mode
+    (``up_offset < 0``) returns [rows, n_feat] in ``out_dtype`` (f32 or bf16);
+    gate/up mode returns bf16 [rows, n_feat] = SiLU(gate) * up with up rows at
     ``f + up_offset``.
     """
     if x_bf16.dtype != torch.bfloat16 or not x_bf16.is_cuda or x_bf16.dim() != 2 or x_bf16.shape[1] != k:
@@ -106,22 +109,29 @@ def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k:
     x_bf16 = x_bf16.contiguous()
     rows = x_bf16.shape[0]
     groups = row_off.numel() - 1
+    wgroups = n_weight_groups if group_w is not None else groups
+    if group_w is not None and (group_w.dtype != torch.int32 or group_w.numel() != groups):
+        raise ValueError('group_w must be an int32 tensor with one entry per group')
     kpad = (k + 255) // 256 * 256
-    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < groups * w_rows_per_group * (kpad // 256) * 144:
-        raise ValueError('w must hold groups * w_rows_per_group Q4_K rows')
+    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < wgroups * w_rows_per_group * (kpad // 256) * 144:
+        raise ValueError('w must hold the weight groups as Q4_K rows')
     lib = _lib.load()
+    gw = None if group_w is None else group_w.data_ptr()
     if up_offset >= 0:
         if act is None:
             act = torch.empty((rows, n_feat), dtype=torch.bfloat16, device=x_bf16.device)
         st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, up_offset,
-                                    n_feat, row_off.data_ptr(), None, 0, None, act.data_ptr(), act.stride(0),
-                                    max_ctas, _stream())
+                                    n_feat, row_off.data_ptr(), gw, wgroups, None, 0, 0, None, act.data_ptr(),
+                                    act.stride(0), max_ctas, _stream())
         _lib.check(st)
         return act
     if out is None:
-        out = torch.empty((rows, n_feat), dtype=torch.float32, device=x_bf16.device)
+        out = torch.empty((rows, n_feat), dtype=out_dtype, device=x_bf16.device)
+    if out.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError('out must be f32 or bf16')
     st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, -1, n_feat,
-                                row_off.data_ptr(), out.data_ptr(), out.stride(0),
+                                row_off.data_ptr(), gw, wgroups, out.data_ptr(),
+                                1 if out.dtype == torch.bfloat16 else 0, out.stride(0),
                                 None if row_scale is None else row_scale.data_ptr(), None, 0, max_ctas, _stream())
     _lib.check(st)
     return out

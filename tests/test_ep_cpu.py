@@ -47,10 +47,11 @@ class StandInLayer:
         offsets[1:] = torch.cumsum(torch.bincount(flat, minlength=self.E), 0)
         return offsets, slot_of.to(torch.int32), token_of.to(torch.int32), w.reshape(-1)[order], h[token_of]
 
-    def experts(self, x, offsets, slot_w, n_experts=None):
+    def experts(self, x, offsets, slot_w, group_w=None):
         out = torch.zeros((x.shape[0], self.D))
-        for e in range(n_experts or self.E_held):
-            a, b = int(offsets[e]), int(offsets[e + 1])
+        for g in range(offsets.numel() - 1):
+            e = g if group_w is None else int(group_w[g])
+            a, b = int(offsets[g]), int(offsets[g + 1])
             if a == b:
                 continue
             gu = x[a:b] @ self.gate_up[e].T

@@ -111,3 +111,33 @@ def test_large_k_many_tiles():
     ops.check_device_error()
     ref = ref_bf16(raw, n, kpad, k, xb)
     assert ((out - ref).abs().max() / ref.abs().max()).item() < 5e-4
+
+
+def test_group_weight_map_and_bf16_output():
+    """Groups that reuse weight groups out of order (the expert-parallel
+    layout: one group per (source rank, local expert)), bf16 rows out."""
+    rng = np.random.default_rng(13)
+    k, n = 512, 128
+    n_w = 3
+    raw, w, kpad = q4k_weights(rng, n_w * n, k)
+    sizes = [100, 0, 300, 17, 256]
+    gmap = [2, 0, 2, 1, 0]
+    rows = sum(sizes)
+    xb = torch.from_numpy(rng.normal(size=(rows, k)).astype(np.float32)).cuda().to(torch.bfloat16)
+    off = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]), dtype=torch.int32, device='cuda')
+    gw = torch.tensor(gmap, dtype=torch.int32, device='cuda')
+    scale = torch.from_numpy(rng.uniform(0.5, 1.5, size=rows).astype(np.float32)).cuda()
+    out = ops.gemm_q4k(xb, w, off, k=k, n_feat=n, w_rows_per_group=n, row_scale=scale, group_w=gw,
+                       n_weight_groups=n_w, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    rawb = np.frombuffer(raw, np.uint8)
+    rb = (kpad // 256) * 144
+    for g, wg in enumerate(gmap):
+        a, b = int(off[g]), int(off[g + 1])
+        if a == b:
+            continue
+        graw = rawb[wg * n * rb:(wg + 1) * n * rb].tobytes()
+        ref = ref_bf16(graw, n, kpad, k, xb[a:b]) * scale[a:b, None]
+        err = ((out[a:b].float() - ref).abs().max() / ref.abs().max()).item()
+        assert err < 1e-2, (g, err)
