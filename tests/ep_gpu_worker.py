@@ -43,12 +43,20 @@ def main():
     n = T // world
     shard = h[rank * n:(rank + 1) * n]
     y_ep = ep(shard)
-    y_ref = full(shard)
+    # single-GPU reference with the same arithmetic as the expert-parallel
+    # path (unweighted bf16 expert rows, routing weight applied in the combine):
+    # every GEMM row is independent of how rows are grouped, so the two must
+    # agree bit for bit
+    _, ids_s, w_s = full.route(shard)
+    off, slot_of, _, slot_w, xperm = full.dispatch(shard, ids_s, w_s)
+    y_same = full.combine(full.experts(xperm, off, None), slot_of, n, slot_w)
+    y_fwd = full(shard)
     torch.cuda.synchronize()
-    err = float((y_ep - y_ref).abs().max() / y_ref.abs().max())
-    ok = torch.tensor([1 if err < 1e-5 else 0], device=dev)
+    err = float((y_ep - y_same).abs().max() / y_same.abs().max())
+    err_fwd = float((y_ep - y_fwd).abs().max() / y_fwd.abs().max())
+    ok = torch.tensor([1 if (err == 0.0 and err_fwd < 1e-2) else 0], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    print(f'rank {rank}: ep vs single-GPU max rel err {err:.3e}', flush=True)
+    print(f'rank {rank}: ep vs single-GPU (same rounding) {err:.3e}, vs forward {err_fwd:.3e}', flush=True)
     dist.destroy_process_group()
     sys.exit(0 if int(ok.item()) == 1 else 1)
 
