@@ -10,7 +10,9 @@
 // and the per-expert products of engine/zaya.py:303-306).
 //
 // Tile: 128 weight rows (MMA M) x 256 activation rows (MMA N) x the full K, in
-// K-steps of 64 (one 128-byte swizzle atom of bf16).
+// K-steps of 64 (one 128-byte swizzle atom of bf16).  The last tile of a group
+// issues its MMAs with N = its valid rows rounded up to 16, so skewed expert
+// loads do not pay for empty columns.
 //
 // Warp roles (512 threads, one CTA per SM, persistent over tiles):
 //   warp 0        TMA: activation box [64 k x 256 rows] (SWIZZLE_128B) per
@@ -314,9 +316,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(TC_BM, TC_BN);
             int q = 0, acc = 0;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
+                // N of this tile's MMAs: its valid activation rows rounded up to 16
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
+                const uint32_t idesc = idesc_bf16(TC_BM, min(TC_BN, (c.rows + 15) & ~15));
                 const int ab = acc & 1;
                 if (acc >= 2 && !mbar_wait(acc_empty + 8 * ab, ((acc >> 1) + 1) & 1, a.err)) { ok = false; break; }
                 tc_fence_after();

@@ -19,47 +19,75 @@
 namespace b200q {
 
 // ---------------------------------------------------------------- router
-// 64 tokens x 64 experts per CTA, K tiles of 32; 256 threads x (4 x 4) outputs.
+// f32, deterministic.  One CTA computes 16 tokens x 64 experts; its 256 threads
+// form two halves that each sweep half of every 128-wide K tile (thread:
+// 2 tokens x 4 experts, 128-bit shared loads along K), and the two halves'
+// sums are added in a fixed order at the end.  T/16 CTAs keep the GPU busy
+// even for a few thousand tokens.  Thread (tp, eq) owns tokens 2tp, 2tp+1 and
+// experts eq + 16j, so the 16 lanes of a half-warp read 16 consecutive rows of
+// the padded W tile (8 distinct 16-byte bank groups).
+constexpr int RT_TOK = 16, RT_EXP = 64, RT_BK = 128, RT_PAD = 4;
+
 __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ h, const float *__restrict__ wr,
                                                          const float *__restrict__ bias, float *__restrict__ logits,
                                                          int T, int E, int D)
 {
-    __shared__ float hs[32][64 + 4];
-    __shared__ float ws[32][64 + 4];
+    __shared__ __align__(16) float hs[RT_TOK][RT_BK + RT_PAD];
+    __shared__ __align__(16) float ws[RT_EXP][RT_BK + RT_PAD];
+    __shared__ float part[RT_TOK][RT_EXP];
     const int tid = threadIdx.x;
-    const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-    const int ty = tid >> 4, tx = tid & 15;
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < D; k0 += 32) {
-        for (int i = tid; i < 64 * 32; i += 256) {
-            const int r = i >> 5, c = i & 31;
-            const int t = t0 + r, e = e0 + r, kk = k0 + c;
-            hs[c][r] = (t < T && kk < D) ? h[(long long)t * D + kk] : 0.f;
-            ws[c][r] = (e < E && kk < D) ? wr[(long long)e * D + kk] : 0.f;
+    const int t0 = blockIdx.x * RT_TOK, e0 = blockIdx.y * RT_EXP;
+    const int half = tid >> 7, lt = tid & 127;
+    const int tp = lt >> 4, eq = lt & 15;             // token pair 0..7, expert quad 0..15
+    float acc[2][4] = {};
+    for (int k0 = 0; k0 < D; k0 += RT_BK) {
+        // h tile: 16 x 128 floats = 512 float4; W tile: 64 x 128 = 2048 float4
+        for (int i = tid; i < RT_TOK * RT_BK / 4; i += 256) {
+            const int r = i / (RT_BK / 4), c = (i % (RT_BK / 4)) * 4;
+            const int t = t0 + r, kk = k0 + c;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < T && kk + 3 < D) v = __ldg(reinterpret_cast<const float4 *>(h + (long long)t * D + kk));
+            *reinterpret_cast<float4 *>(&hs[r][c]) = v;
+        }
+        for (int i = tid; i < RT_EXP * RT_BK / 4; i += 256) {
+            const int r = i / (RT_BK / 4), c = (i % (RT_BK / 4)) * 4;
+            const int e = e0 + r, kk = k0 + c;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < E && kk + 3 < D) v = __ldg(reinterpret_cast<const float4 *>(wr + (long long)e * D + kk));
+            *reinterpret_cast<float4 *>(&ws[r][c]) = v;
         }
         __syncthreads();
-#pragma unroll 8
-        for (int c = 0; c < 32; ++c) {
-            float a[4], b[4];
+        const int kb = half * (RT_BK / 2);
+#pragma unroll 4
+        for (int c = kb; c < kb + RT_BK / 2; c += 4) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&hs[2 * tp][c]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&hs[2 * tp + 1][c]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i] = hs[c][ty * 4 + i];
-                b[i] = ws[c][tx * 4 + i];
+            for (int j = 0; j < 4; ++j) {
+                const float4 b = *reinterpret_cast<const float4 *>(&ws[eq + 16 * j][c]);
+                acc[0][j] = fmaf(a0.x, b.x, fmaf(a0.y, b.y, fmaf(a0.z, b.z, fmaf(a0.w, b.w, acc[0][j]))));
+                acc[1][j] = fmaf(a1.x, b.x, fmaf(a1.y, b.y, fmaf(a1.z, b.z, fmaf(a1.w, b.w, acc[1][j]))));
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
         }
         __syncthreads();
     }
+    if (half == 1) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int t = t0 + ty * 4 + i, e = e0 + tx * 4 + j;
-            if (t < T && e < E) logits[(long long)t * E + e] = acc[i][j] + (bias ? bias[e] : 0.f);
-        }
+            for (int j = 0; j < 4; ++j) part[2 * tp + i][eq + 16 * j] = acc[i][j];
+    }
+    __syncthreads();
+    if (half == 0) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int t = t0 + 2 * tp + i, e = e0 + eq + 16 * j;
+                if (t < T && e < E)
+                    logits[(long long)t * E + e] = (acc[i][j] + part[2 * tp + i][eq + 16 * j]) + (bias ? bias[e] : 0.f);
+            }
+    }
 }
 
 // ---------------------------------------------------------------- top-k
@@ -277,8 +305,10 @@ __global__ void moe_combine_kernel(const RowT *__restrict__ out, const int *__re
 cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
                               cudaStream_t st)
 {
-    if (T < 1 || E < 1 || D < 1) return cudaErrorInvalidValue;
-    dim3 grid((T + 63) / 64, (E + 63) / 64);
+    if (T < 1 || E < 1 || D < 1 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) ||
+        (reinterpret_cast<uintptr_t>(wr) & 15))
+        return cudaErrorInvalidValue;
+    dim3 grid((T + RT_TOK - 1) / RT_TOK, (E + RT_EXP - 1) / RT_EXP);
     moe_router_kernel<<<grid, 256, 0, st>>>(h, wr, bias, logits, T, E, D);
     return cudaGetLastError();
 }
