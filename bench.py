@@ -255,6 +255,8 @@ def main():
     ap.add_argument('--cpu-tokens', type=int, default=2048, help='token sample of the CPU baseline')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-gemv', action='store_true')
+    ap.add_argument('--transport', default='p2p', choices=['p2p', 'nccl'],
+                    help='expert-parallel exchange (N > 1): NVLink peer memory or NCCL all-to-all')
     ap.add_argument('--tokens', type=int, default=T_TOTAL,
                     help='tokens per layer call (16384 = the headline configuration; smaller for profiling)')
     args = ap.parse_args()
@@ -308,7 +310,7 @@ def main():
     del parts
     layer = QuantMoE(wr, gate_up, down, d_model=D, d_ff=F, top_k=K_TOP, router_bias=bias, renormalize=True,
                      local_experts=len(mine))
-    step = EPMoE(layer, owner, local) if world > 1 else layer
+    step = EPMoE(layer, owner, local, transport=args.transport, max_tokens=T_loc) if world > 1 else layer
 
     def barrier():
         if world > 1:
@@ -320,6 +322,7 @@ def main():
     if sampler:
         sampler.start()
         time.sleep(1.0)
+    barrier()
     for _ in range(args.warmup):
         step(h)
     torch.cuda.synchronize()
@@ -419,6 +422,7 @@ def main():
                 'config': {'workload': WORKLOAD, 'hidden': D, 'experts': E, 'intermediate': F, 'top_k': K_TOP,
                            'tokens': T_TOTAL, 'weights': 'Q4_K', 'router': 'f32 + Zipf(1.1) bias',
                            'parallelism': f'ep{world}' if world > 1 else 'single',
+                           'ep_transport': args.transport if world > 1 else None,
                            'l2': 'inputs larger than L2 (641 MB expert weights, 256 MB hidden states)'},
                 'roofline': roof, 'cpu_baseline': cpu,
                 'e2e': {'value': e2e_value, 'unit': 'tokens/s', 'h2d_bytes_per_step': T_TOTAL * D * 4,
@@ -427,6 +431,8 @@ def main():
                 'flops_per_step': algorithmic_flops(T_TOTAL * K_TOP)}
         print(json.dumps(line), flush=True)
     if world > 1:
+        if hasattr(step, 'close'):
+            step.close()
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 

@@ -134,6 +134,18 @@ int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, flo
  * the sum of the k selected probabilities when renormalize != 0. */
 int b200q_moe_topk_dev(const float *logits, const float *sel_bias, int T, int E, int k, int renormalize, int *ids,
                        float *w, void *stream);
+/* Router + top-k in one call (b200q_moe_router_dev followed by
+ * b200q_moe_topk_dev).  For few tokens the router's K range is split across
+ * CTAs; the partial sums then go to ``workspace`` (f32, at least
+ * b200q_moe_route_workspace_bytes(T, E, D) bytes; may be NULL when that is 0,
+ * in which case the split is not used) and are added in a fixed order, so the
+ * logits may differ from b200q_moe_router_dev's in the last bits but are
+ * deterministic for a given (T, E, D) and GPU model.  ``logits`` receives the
+ * final logits (bias included) in both cases. */
+size_t b200q_moe_route_workspace_bytes(int T, int E, int D);
+int b200q_moe_route_dev(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E, int D,
+                        int k, int renormalize, float *logits, int *ids, float *w, void *workspace,
+                        size_t workspace_bytes, void *stream);
 /* Scratch rows needed by b200q_moe_dispatch_dev: block_counts and base are
  * int32 [b200q_moe_num_blocks(T) * E]. */
 int b200q_moe_num_blocks(int T);
@@ -178,6 +190,49 @@ void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas
 
 /* Number of kernel launches made by this library since load. */
 long long b200q_launch_count(void);
+
+/* ---- Expert-parallel exchange over NVLink peer memory (no reference
+ * counterpart: the reference runs the MoE block in one CPU process).  One
+ * context per rank (one process per GPU); every rank makes the same calls in
+ * the same order with the same epoch (1, 2, ... per layer call).
+ *   b200q_ep_create        allocate this rank's exchange region (counts inbox,
+ *                          flags, receive rows bf16 [max_recv_rows, d_model],
+ *                          return rows bf16 [max_send_rows, d_model]);
+ *   b200q_ep_handle        its CUDA IPC handle (b200q_ep_handle_bytes bytes),
+ *                          to be all-gathered by the caller;
+ *   b200q_ep_open          map every other rank's region (handles of all
+ *                          ranks, rank order); collective;
+ *   b200q_ep_exchange_counts_dev  offsets [world * local_experts + 1] of this
+ *                          rank's slots sorted by (owner rank, local expert)
+ *                          (b200q_moe_dispatch_dev on virtual expert ids);
+ *   b200q_ep_send_rows_dev gather h[token_of[slot]] as bf16 into the owner's
+ *                          receive buffer (expert-major, source-minor);
+ *   b200q_ep_experts_dev   wait for all ranks' rows, gate/up then down on the
+ *                          local experts; the down GEMM stores each output row
+ *                          (unweighted, bf16) into its source rank's return
+ *                          buffer; then signal every rank.  act: bf16
+ *                          [max_recv_rows, d_ff] scratch;
+ *   b200q_ep_combine_dev   wait for all ranks' outputs, y[t] = sum_j
+ *                          slot_w * ret[slot(t, j)] (f32 [T, d_model]).
+ * Waits give up after 5 s and set the device error word
+ * (b200q_check_device_error reports B200Q_ETIMEOUT).  b200q_ep_destroy must be
+ * called on all ranks after a barrier. */
+int b200q_ep_create(int world, int rank, int local_experts, int d_model, long long max_send_rows,
+                    long long max_recv_rows, void **ep);
+size_t b200q_ep_handle_bytes(void);
+int b200q_ep_handle(void *ep, void *handle);
+int b200q_ep_open(void *ep, const void *handles);
+int b200q_ep_destroy(void *ep);
+void *b200q_ep_recv_rows(void *ep);
+void *b200q_ep_return_rows(void *ep);
+const int *b200q_ep_group_offsets(void *ep);
+int b200q_ep_exchange_counts_dev(void *ep, const int *offsets, unsigned int epoch, void *stream);
+int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int *token_of, const int *offsets, int slots,
+                           unsigned int epoch, void *stream);
+int b200q_ep_experts_dev(void *ep, const void *gate_up, const void *down, int d_ff, void *act, unsigned int epoch,
+                         int max_ctas, void *stream);
+int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int T, int k, float *y,
+                         unsigned int epoch, void *stream);
 
 #ifdef __cplusplus
 }

@@ -18,6 +18,7 @@ B200Q_OK, B200Q_EINVAL, B200Q_ECUDA, B200Q_ETIMEOUT, B200Q_ENODEV, B200Q_EINDEX 
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _f32p = ctypes.POINTER(ctypes.c_float)
 _vp = ctypes.c_void_p
+_u32 = ctypes.c_uint
 _i, _ll, _sz = ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t
 
 # name -> (restype, argtypes); every function declared in include/b200quant.h
@@ -46,12 +47,26 @@ SIGNATURES = {
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     'b200q_moe_topk_dev': (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_moe_num_blocks': (_i, [_i]),
+    'b200q_moe_route_workspace_bytes': (_sz, [_i, _i, _i]),
+    'b200q_moe_route_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     'b200q_moe_dispatch_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_dispatch_noalloc_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_combine_dev': (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     'b200q_check_device_error': (_i, []),
     'b200q_gemv_tuning': (None, [_i, _i, _i, _i]),
     'b200q_launch_count': (_ll, []),
+    'b200q_ep_create': (_i, [_i, _i, _i, _i, _ll, _ll, ctypes.POINTER(_vp)]),
+    'b200q_ep_handle_bytes': (_sz, []),
+    'b200q_ep_handle': (_i, [_vp, _vp]),
+    'b200q_ep_open': (_i, [_vp, _vp]),
+    'b200q_ep_destroy': (_i, [_vp]),
+    'b200q_ep_recv_rows': (_vp, [_vp]),
+    'b200q_ep_return_rows': (_vp, [_vp]),
+    'b200q_ep_group_offsets': (_vp, [_vp]),
+    'b200q_ep_exchange_counts_dev': (_i, [_vp, _vp, _u32, _vp]),
+    'b200q_ep_send_rows_dev': (_i, [_vp, _vp, _i, _vp, _vp, _i, _u32, _vp]),
+    'b200q_ep_experts_dev': (_i, [_vp, _vp, _vp, _i, _vp, _u32, _i, _vp]),
+    'b200q_ep_combine_dev': (_i, [_vp, _vp, _vp, _i, _i, _vp, _u32, _vp]),
 }
 
 _LIB = None

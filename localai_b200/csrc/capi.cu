@@ -6,6 +6,7 @@
 // device-pointer API used by the PyTorch host code.
 #include "b200quant.h"
 #include "common.cuh"
+#include "ep.cuh"
 
 #include <cstdarg>
 #include <cstdio>
@@ -25,6 +26,10 @@ cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias
 cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, int E, int k, int renorm, int *ids,
                             float *wts, cudaStream_t st);
 int moe_num_blocks(int T);
+size_t moe_route_workspace_bytes(int T, int E, int D, int num_sms);
+cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E,
+                             int D, int k, int renorm, float *logits, int *ids, float *wts, float *ws,
+                             size_t ws_bytes, int num_sms, cudaStream_t st);
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
@@ -38,7 +43,26 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
-                               int *err, int num_sms, int max_ctas, cudaStream_t st);
+                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret);
+cudaError_t ep_create(int G, int me, int E_loc, int D, long long cap_send, long long cap_recv, void **out);
+cudaError_t ep_ipc_handle(void *ctx, void *handle64);
+size_t ep_ipc_handle_bytes();
+cudaError_t ep_open(void *ctx, const void *handles);
+cudaError_t ep_destroy(void *ctx);
+bool ep_is_open(void *ctx);
+void *ep_recv_rows(void *ctx);
+void *ep_ret_rows(void *ctx);
+EpDev *ep_dev(void *ctx);
+const int *ep_group_offsets(void *ctx);
+long long ep_cap_recv(void *ctx);
+long long ep_cap_send(void *ctx);
+int ep_local_experts(void *ctx);
+int ep_d_model(void *ctx);
+cudaError_t launch_ep_counts(void *ctx, const int *offsets, uint32_t epoch, int *err, cudaStream_t st);
+cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const int *offsets, int S, int T,
+                           uint32_t epoch, int *err, int num_sms, cudaStream_t st);
+cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaStream_t st);
+cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
 
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
@@ -379,7 +403,7 @@ B200Q_API int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, co
                                           out_is_bf16 ? nullptr : static_cast<float *>(out),
                                           out_is_bf16 ? static_cast<__nv_bfloat16 *>(out) : nullptr, ld_out,
                                           row_scale, static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err,
-                                          di->sms, max_ctas, (cudaStream_t)stream),
+                                          di->sms, max_ctas, (cudaStream_t)stream, nullptr),
                        "gemm");
 }
 
@@ -402,6 +426,29 @@ B200Q_API int b200q_moe_topk_dev(const float *logits, const float *sel_bias, int
 }
 
 B200Q_API int b200q_moe_num_blocks(int T) { return moe_num_blocks(T); }
+
+B200Q_API size_t b200q_moe_route_workspace_bytes(int T, int E, int D)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return 0;
+    return moe_route_workspace_bytes(T, E, D, di->sms);
+}
+
+B200Q_API int b200q_moe_route_dev(const float *h, const float *wr, const float *bias, const float *sel_bias, int T,
+                                  int E, int D, int k, int renormalize, float *logits, int *ids, float *w,
+                                  void *workspace, size_t workspace_bytes, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h || !wr || !logits || !ids || !w) return set_status(B200Q_EINVAL, "route: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += 2;
+    return cuda_status(launch_moe_route(h, wr, bias, sel_bias, T, E, D, k, renormalize, logits, ids, w,
+                                        static_cast<float *>(workspace), workspace_bytes, di->sms,
+                                        (cudaStream_t)stream),
+                       "route");
+}
 
 B200Q_API int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
                                      int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
@@ -473,3 +520,104 @@ B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group
 }
 
 B200Q_API long long b200q_launch_count(void) { return g_launches; }
+
+// ---------------------------------------------------------------- expert-parallel exchange over peer memory
+B200Q_API int b200q_ep_create(int world, int rank, int local_experts, int d_model, long long max_send_rows,
+                              long long max_recv_rows, void **ep)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep) return set_status(B200Q_EINVAL, "ep_create: null output");
+    return cuda_status(ep_create(world, rank, local_experts, d_model, max_send_rows, max_recv_rows, ep), "ep_create");
+}
+
+B200Q_API size_t b200q_ep_handle_bytes(void) { return ep_ipc_handle_bytes(); }
+
+B200Q_API int b200q_ep_handle(void *ep, void *handle)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !handle) return set_status(B200Q_EINVAL, "ep_handle: null pointer");
+    return cuda_status(ep_ipc_handle(ep, handle), "ep_handle");
+}
+
+B200Q_API int b200q_ep_open(void *ep, const void *handles)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !handles) return set_status(B200Q_EINVAL, "ep_open: null pointer");
+    return cuda_status(ep_open(ep, handles), "ep_open");
+}
+
+B200Q_API int b200q_ep_destroy(void *ep)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep) return set_status(B200Q_EINVAL, "ep_destroy: null pointer");
+    return cuda_status(ep_destroy(ep), "ep_destroy");
+}
+
+B200Q_API void *b200q_ep_recv_rows(void *ep) { return ep ? ep_recv_rows(ep) : nullptr; }
+B200Q_API void *b200q_ep_return_rows(void *ep) { return ep ? ep_ret_rows(ep) : nullptr; }
+B200Q_API const int *b200q_ep_group_offsets(void *ep) { return ep ? ep_group_offsets(ep) : nullptr; }
+
+B200Q_API int b200q_ep_exchange_counts_dev(void *ep, const int *offsets, unsigned int epoch, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !offsets) return set_status(B200Q_EINVAL, "ep_exchange_counts: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_ep_counts(ep, offsets, epoch, di->err, (cudaStream_t)stream), "ep_exchange_counts");
+}
+
+B200Q_API int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int *token_of, const int *offsets,
+                                     int slots, unsigned int epoch, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !h || !token_of || !offsets) return set_status(B200Q_EINVAL, "ep_send_rows: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_ep_send(ep, h, token_of, offsets, slots, T, epoch, di->err, di->sms,
+                                      (cudaStream_t)stream),
+                       "ep_send_rows");
+}
+
+B200Q_API int b200q_ep_experts_dev(void *ep, const void *gate_up, const void *down, int d_ff, void *act,
+                                   unsigned int epoch, int max_ctas, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !gate_up || !down || !act) return set_status(B200Q_EINVAL, "ep_experts: null pointer");
+    if (d_ff < 64 || d_ff % 64) return set_status(B200Q_EINVAL, "ep_experts: d_ff must be a multiple of 64");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int El = ep_local_experts(ep), D = ep_d_model(ep);
+    const long long cap = ep_cap_recv(ep);
+    const int *grp = ep_group_offsets(ep);
+    cudaError_t e = launch_ep_wait(ep, 1, epoch, di->err, st);
+    if (e == cudaSuccess)
+        e = launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(ep_recv_rows(ep)), cap, D, gate_up, El, 2 * d_ff,
+                               d_ff, d_ff, grp, nullptr, El, nullptr, nullptr, 0, nullptr,
+                               static_cast<__nv_bfloat16 *>(act), d_ff, di->err, di->sms, max_ctas, st, nullptr);
+    if (e == cudaSuccess)
+        e = launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(act), cap, d_ff, down, El, D, -1, D, grp,
+                               nullptr, El, nullptr, nullptr, D, nullptr, nullptr, 0, di->err, di->sms, max_ctas, st,
+                               ep_dev(ep));
+    if (e == cudaSuccess) e = launch_ep_signal(ep, epoch, st);
+    g_launches += 4;
+    return cuda_status(e, "ep_experts");
+}
+
+B200Q_API int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int T, int k, float *y,
+                                   unsigned int epoch, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !slot_of || !slot_w || !y) return set_status(B200Q_EINVAL, "ep_combine: null pointer");
+    if ((long long)T * k > ep_cap_send(ep)) return set_status(B200Q_EINVAL, "ep_combine: more slots than max_send_rows");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    const cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = launch_ep_wait(ep, 2, epoch, di->err, st);
+    if (e == cudaSuccess)
+        e = launch_moe_combine(ep_ret_rows(ep), true, slot_of, slot_w, T, k, ep_d_model(ep), y, st);
+    g_launches += 2;
+    return cuda_status(e, "ep_combine");
+}

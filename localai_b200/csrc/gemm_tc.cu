@@ -33,6 +33,7 @@
 // up rows of the same features in one tile, ordered so that every warp holds
 // 16 gate rows and the 16 matching up rows (lanes l and l+16).
 #include "common.cuh"
+#include "ep.cuh"
 
 #include <cuda.h>
 #include <algorithm>
@@ -66,6 +67,11 @@ struct TcArgs {
     const float *row_scale; // plain mode, optional: out *= row_scale[row]
     __nv_bfloat16 *act;     // gate/up mode: act[row * ld_act + f]
     long long ld_act;
+    // plain mode, optional: expert-parallel return.  Row r of group g (a run
+    // of rows received from source rank s) is stored as bf16 into rank s's
+    // return buffer at row ret_base[g*G + s] + (r - run_off[g*G + s]), through
+    // the peer mapping, instead of into out/out_bf16.
+    const EpDev *ep_ret;
     int *err;
 };
 
@@ -239,6 +245,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ int tile_pref[TC_MAX_GROUPS + 1];
     __shared__ int row_off_s[TC_MAX_GROUPS + 1];
     __shared__ int group_w_s[TC_MAX_GROUPS];
+    __shared__ int ret_run_s[EP_MAX_EXPERTS + 1];
+    __shared__ int ret_base_s[EP_MAX_EXPERTS];
+    __shared__ __nv_bfloat16 *ret_peer_s[EP_MAX_RANKS];
+    __shared__ int ret_G;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ksteps = a.k / TC_BK;
@@ -272,6 +282,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             tile_pref[a.groups] = acc;
         }
+    }
+    if (warp == 3 && a.ep_ret) {
+        const EpDev *ep = a.ep_ret;
+        const int G = ep->G, nrun = a.groups * G;
+        for (int i = lane; i <= nrun; i += 32) ret_run_s[i] = ep->run_off[i];
+        for (int i = lane; i < nrun; i += 32) ret_base_s[i] = ep->ret_base[i];
+        if (lane < G) ret_peer_s[lane] = ep->peer_ret[lane];
+        if (lane == 0) ret_G = G;
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -368,6 +386,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (col < c.rows)
                             a.act[(row_base + col) * a.ld_act + f] = __float2bfloat16_rn(silu_ref(gv) * uv);
                     }
+                } else if (a.ep_ret) {
+                    const int n = c.nt * TC_BM + 32 * ew + lane;
+                    const int G = ret_G;
+                    const int *run = ret_run_s + c.g * G;
+                    int s = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = 32 * ch + j;
+                        if (col < c.rows) {
+                            const int row = (int)(row_base + col);
+                            while (s + 1 < G && row >= run[s + 1]) ++s;      // warp-uniform
+                            const long long drow = ret_base_s[c.g * G + s] + (row - run[s]);
+                            ret_peer_s[s][drow * a.ld_out + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+                        }
+                    }
                 } else {
                     const int n = c.nt * TC_BM + 32 * ew + lane;
 #pragma unroll
@@ -387,6 +420,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
         }
+        if (a.ep_ret) __threadfence_system();        // peer stores complete before the signal
     } else if (warp >= 8) {
         // ------------------------------------------------ dequantisers
         const int dt = tid - 256;                   // 0..255
@@ -489,9 +523,10 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
-                               int *err, int num_sms, int max_ctas, cudaStream_t st)
+                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret)
 {
     if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
+    if (ep_ret && (up_offset >= 0 || groups > EP_MAX_EXPERTS)) return cudaErrorInvalidValue;
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
     if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
@@ -518,6 +553,7 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
     a.row_scale = row_scale;
     a.act = act;
     a.ld_act = ld_act;
+    a.ep_ret = ep_ret;
     a.err = err;
     const size_t smem = tc_gemm_smem_bytes(chunk);
     static bool attr = false;

@@ -19,82 +19,110 @@
 namespace b200q {
 
 // ---------------------------------------------------------------- router
-// f32, deterministic.  One CTA computes 16 tokens x 64 experts; its 256 threads
-// form two halves that each sweep half of every 128-wide K tile (thread:
-// 2 tokens x 4 experts, 128-bit shared loads along K), and the two halves'
-// sums are added in a fixed order at the end.  T/16 CTAs keep the GPU busy
-// even for a few thousand tokens.  Thread (tp, eq) owns tokens 2tp, 2tp+1 and
-// experts eq + 16j, so the 16 lanes of a half-warp read 16 consecutive rows of
-// the padded W tile (8 distinct 16-byte bank groups).
-constexpr int RT_TOK = 16, RT_EXP = 64, RT_BK = 128, RT_PAD = 4;
+// f32 and deterministic.  One CTA computes 64 tokens x 64 experts over a K
+// range; its 256 threads are four K-slices of 64 threads, each thread holding
+// 8 tokens x 8 experts (16 FMAs per 128-bit shared load), and the four slices'
+// sums are added in a fixed order at the end.  For few tokens the K range is
+// also split across CTAs (gridDim.z = S); those partials are written to a
+// scratch array [S, T, E] and summed, in z order, by the top-k kernel.
+constexpr int RT_TOK = 64, RT_EXP = 64, RT_BK = 128, RT_PAD = 4;
+constexpr int RT_TILE = RT_TOK * (RT_BK + RT_PAD);   // floats per operand tile
 
-__global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ h, const float *__restrict__ wr,
-                                                         const float *__restrict__ bias, float *__restrict__ logits,
-                                                         int T, int E, int D)
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes)
 {
-    __shared__ __align__(16) float hs[RT_TOK][RT_BK + RT_PAD];
-    __shared__ __align__(16) float ws[RT_EXP][RT_BK + RT_PAD];
-    __shared__ float part[RT_TOK][RT_EXP];
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem), "r"(src_bytes)
+                 : "memory");
+}
+
+// Double-buffered (cp.async) tiles: [buf][h | w][64 rows][RT_BK + RT_PAD].
+__global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ h, const float *__restrict__ wr,
+                                                         const float *__restrict__ bias, float *__restrict__ out,
+                                                         int T, int E, int D, int kchunk)
+{
+    extern __shared__ __align__(16) float rsm[];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * RT_TOK, e0 = blockIdx.y * RT_EXP;
-    const int half = tid >> 7, lt = tid & 127;
-    const int tp = lt >> 4, eq = lt & 15;             // token pair 0..7, expert quad 0..15
-    float acc[2][4] = {};
-    for (int k0 = 0; k0 < D; k0 += RT_BK) {
-        // h tile: 16 x 128 floats = 512 float4; W tile: 64 x 128 = 2048 float4
+    const int kbeg = blockIdx.z * kchunk, kend = min(D, kbeg + kchunk);
+    const int slice = tid >> 6, lt = tid & 63;
+    const int tt = lt >> 3, ee = lt & 7;              // tokens tt + 8i, experts ee + 8j
+    auto load_tile = [&](int buf, int k0) {
+        float *hs = rsm + buf * 2 * RT_TILE, *ws = hs + RT_TILE;
         for (int i = tid; i < RT_TOK * RT_BK / 4; i += 256) {
             const int r = i / (RT_BK / 4), c = (i % (RT_BK / 4)) * 4;
-            const int t = t0 + r, kk = k0 + c;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t < T && kk + 3 < D) v = __ldg(reinterpret_cast<const float4 *>(h + (long long)t * D + kk));
-            *reinterpret_cast<float4 *>(&hs[r][c]) = v;
+            const int t = t0 + r, e = e0 + r, kk = k0 + c;
+            const bool hv = t < T && kk < kend, wv = e < E && kk < kend;
+            cp_async16(hs + r * (RT_BK + RT_PAD) + c, hv ? h + (long long)t * D + kk : h, hv ? 16 : 0);
+            cp_async16(ws + r * (RT_BK + RT_PAD) + c, wv ? wr + (long long)e * D + kk : wr, wv ? 16 : 0);
         }
-        for (int i = tid; i < RT_EXP * RT_BK / 4; i += 256) {
-            const int r = i / (RT_BK / 4), c = (i % (RT_BK / 4)) * 4;
-            const int e = e0 + r, kk = k0 + c;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < E && kk + 3 < D) v = __ldg(reinterpret_cast<const float4 *>(wr + (long long)e * D + kk));
-            *reinterpret_cast<float4 *>(&ws[r][c]) = v;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    if (kbeg < kend) load_tile(0, kbeg);
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += RT_BK, buf ^= 1) {
+        if (k0 + RT_BK < kend) {
+            load_tile(buf ^ 1, k0 + RT_BK);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        const int kb = half * (RT_BK / 2);
-#pragma unroll 4
-        for (int c = kb; c < kb + RT_BK / 2; c += 4) {
-            const float4 a0 = *reinterpret_cast<const float4 *>(&hs[2 * tp][c]);
-            const float4 a1 = *reinterpret_cast<const float4 *>(&hs[2 * tp + 1][c]);
+        const float *hs = rsm + buf * 2 * RT_TILE, *ws = hs + RT_TILE;
+        const int cb = slice * (RT_BK / 4);
+#pragma unroll 2
+        for (int c = cb; c < cb + RT_BK / 4; c += 4) {
+            float4 a[8], b[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 b = *reinterpret_cast<const float4 *>(&ws[eq + 16 * j][c]);
-                acc[0][j] = fmaf(a0.x, b.x, fmaf(a0.y, b.y, fmaf(a0.z, b.z, fmaf(a0.w, b.w, acc[0][j]))));
-                acc[1][j] = fmaf(a1.x, b.x, fmaf(a1.y, b.y, fmaf(a1.z, b.z, fmaf(a1.w, b.w, acc[1][j]))));
-            }
+            for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4 *>(hs + (tt + 8 * i) * (RT_BK + RT_PAD) + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) b[j] = *reinterpret_cast<const float4 *>(ws + (ee + 8 * j) * (RT_BK + RT_PAD) + c);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    acc[i][j] = fmaf(a[i].w, b[j].w, fmaf(a[i].z, b[j].z, fmaf(a[i].y, b[j].y, fmaf(a[i].x, b[j].x, acc[i][j]))));
         }
         __syncthreads();
     }
-    if (half == 1) {
+    // fixed-order reduction of the four K-slices (reuses the tile buffers)
+    float *red = rsm;                                 // [3][64 tokens][64 experts]
+    if (slice > 0) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) part[2 * tp + i][eq + 16 * j] = acc[i][j];
+            for (int j = 0; j < 8; ++j) red[((slice - 1) * RT_TOK + tt + 8 * i) * RT_EXP + ee + 8 * j] = acc[i][j];
     }
     __syncthreads();
-    if (half == 0) {
+    if (slice == 0) {
+        float *dst = out + (long long)blockIdx.z * T * E;
+        const bool final = gridDim.z == 1;
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int t = t0 + 2 * tp + i, e = e0 + eq + 16 * j;
-                if (t < T && e < E)
-                    logits[(long long)t * E + e] = (acc[i][j] + part[2 * tp + i][eq + 16 * j]) + (bias ? bias[e] : 0.f);
+            for (int j = 0; j < 8; ++j) {
+                const int t = t0 + tt + 8 * i, e = e0 + ee + 8 * j;
+                float v = acc[i][j];
+#pragma unroll
+                for (int s2 = 0; s2 < 3; ++s2) v += red[(s2 * RT_TOK + tt + 8 * i) * RT_EXP + ee + 8 * j];
+                if (t < T && e < E) dst[(long long)t * E + e] = final ? v + (bias ? bias[e] : 0.f) : v;
             }
     }
 }
 
 // ---------------------------------------------------------------- top-k
 // One warp per token; E <= 32 * EPL.
+// With nsplit > 0, ``logits`` holds nsplit partial sums [nsplit, T, E] of the
+// router product: they are added in split order, plus ``bias``, and the final
+// logits are written to ``logits_out``.
 template <int EPL>
 __global__ void moe_topk_kernel(const float *__restrict__ logits, const float *__restrict__ sel_bias, int T, int E,
-                                int k, int renorm, int *__restrict__ ids, float *__restrict__ wts)
+                                int k, int renorm, int *__restrict__ ids, float *__restrict__ wts, int nsplit,
+                                const float *__restrict__ bias, float *__restrict__ logits_out)
 {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
@@ -104,7 +132,17 @@ __global__ void moe_topk_kernel(const float *__restrict__ logits, const float *_
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
         const int e = lane + 32 * i;
-        p[i] = e < E ? lr[e] : -INFINITY;
+        if (nsplit > 0) {
+            float v = 0.f;
+            if (e < E) {
+                for (int z = 0; z < nsplit; ++z) v += lr[(long long)z * T * E + e];
+                v += bias ? bias[e] : 0.f;
+                logits_out[(long long)warp * E + e] = v;
+            }
+            p[i] = e < E ? v : -INFINITY;
+        } else {
+            p[i] = e < E ? lr[e] : -INFINITY;
+        }
         m = fmaxf(m, p[i]);
     }
 #pragma unroll
@@ -302,15 +340,44 @@ __global__ void moe_combine_kernel(const RowT *__restrict__ out, const int *__re
 }
 
 // ---------------------------------------------------------------- launchers
+static size_t router_smem() { return (size_t)4 * RT_TILE * sizeof(float); }
+
+static cudaError_t router_launch(const float *h, const float *wr, const float *bias, float *out, int T, int E, int D,
+                                 int nsplit, cudaStream_t st)
+{
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)router_smem());
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const int kchunk = ((D + nsplit - 1) / nsplit + RT_BK - 1) / RT_BK * RT_BK;
+    dim3 grid((T + RT_TOK - 1) / RT_TOK, (E + RT_EXP - 1) / RT_EXP, nsplit);
+    moe_router_kernel<<<grid, 256, router_smem(), st>>>(h, wr, bias, out, T, E, D, kchunk);
+    return cudaGetLastError();
+}
+
+static bool router_args_ok(const float *h, const float *wr, int T, int E, int D)
+{
+    return T >= 1 && E >= 1 && D >= 4 && D % 4 == 0 && !(reinterpret_cast<uintptr_t>(h) & 15) &&
+           !(reinterpret_cast<uintptr_t>(wr) & 15);
+}
+
 cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
                               cudaStream_t st)
 {
-    if (T < 1 || E < 1 || D < 1 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) ||
-        (reinterpret_cast<uintptr_t>(wr) & 15))
-        return cudaErrorInvalidValue;
-    dim3 grid((T + RT_TOK - 1) / RT_TOK, (E + RT_EXP - 1) / RT_EXP);
-    moe_router_kernel<<<grid, 256, 0, st>>>(h, wr, bias, logits, T, E, D);
-    return cudaGetLastError();
+    if (!router_args_ok(h, wr, T, E, D)) return cudaErrorInvalidValue;
+    return router_launch(h, wr, bias, logits, T, E, D, 1, st);
+}
+
+template <typename... Args>
+static void topk_dispatch(int E, int grid, int threads, cudaStream_t st, Args... args)
+{
+    if (E <= 32) moe_topk_kernel<1><<<grid, threads, 0, st>>>(args...);
+    else if (E <= 64) moe_topk_kernel<2><<<grid, threads, 0, st>>>(args...);
+    else if (E <= 128) moe_topk_kernel<4><<<grid, threads, 0, st>>>(args...);
+    else moe_topk_kernel<8><<<grid, threads, 0, st>>>(args...);
 }
 
 cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, int E, int k, int renorm, int *ids,
@@ -318,10 +385,47 @@ cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, i
 {
     if (T < 1 || E < 1 || E > 256 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
     const int threads = 256, grid = (int)(((long long)T * 32 + threads - 1) / threads);
-    if (E <= 32) moe_topk_kernel<1><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
-    else if (E <= 64) moe_topk_kernel<2><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
-    else if (E <= 128) moe_topk_kernel<4><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
-    else moe_topk_kernel<8><<<grid, threads, 0, st>>>(logits, sel_bias, T, E, k, renorm, ids, wts);
+    topk_dispatch(E, grid, threads, st, logits, sel_bias, T, E, k, renorm, ids, wts, 0, (const float *)nullptr,
+                  (float *)nullptr);
+    return cudaGetLastError();
+}
+
+// Number of K splits across CTAs for T tokens: enough CTAs for two per SM.
+int moe_route_splits(int T, int E, int D, int num_sms)
+{
+    const long long ctas = (long long)((T + RT_TOK - 1) / RT_TOK) * ((E + RT_EXP - 1) / RT_EXP);
+    int s = 1;
+    while (s < 8 && ctas * s < 2LL * num_sms && (D / RT_BK) >= 2 * s) s *= 2;
+    return s;
+}
+
+size_t moe_route_workspace_bytes(int T, int E, int D, int num_sms)
+{
+    const int s = moe_route_splits(T, E, D, num_sms);
+    return s > 1 ? (size_t)s * T * E * sizeof(float) : 0;
+}
+
+// Router + top-k in two launches; partial sums in ``ws`` when the K range is
+// split across CTAs.
+cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E,
+                             int D, int k, int renorm, float *logits, int *ids, float *wts, float *ws,
+                             size_t ws_bytes, int num_sms, cudaStream_t st)
+{
+    if (!router_args_ok(h, wr, T, E, D) || E > 256 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
+    int s = moe_route_splits(T, E, D, num_sms);
+    if (s > 1 && (!ws || ws_bytes < (size_t)s * T * E * sizeof(float))) s = 1;
+    const int threads = 256, grid = (int)(((long long)T * 32 + threads - 1) / threads);
+    cudaError_t e;
+    if (s == 1) {
+        e = router_launch(h, wr, bias, logits, T, E, D, 1, st);
+        if (e != cudaSuccess) return e;
+        topk_dispatch(E, grid, threads, st, (const float *)logits, sel_bias, T, E, k, renorm, ids, wts, 0,
+                      (const float *)nullptr, (float *)nullptr);
+    } else {
+        e = router_launch(h, wr, nullptr, ws, T, E, D, s, st);
+        if (e != cudaSuccess) return e;
+        topk_dispatch(E, grid, threads, st, (const float *)ws, sel_bias, T, E, k, renorm, ids, wts, s, bias, logits);
+    }
     return cudaGetLastError();
 }
 

@@ -18,14 +18,30 @@ NVLink/NVSwitch) and the T tokens are sharded evenly; per layer call:
 Expert placement is greedy LPT on expected per-expert loads with E/G experts
 per rank, which keeps the busiest rank close to the mean under a skewed
 (Zipf) router.
+
+Two transports carry steps 3-5:
+
+* ``'nccl'``: NCCL ``all_to_all_single`` (counts, then rows with variable
+  splits, which needs one host synchronisation for the split sizes, then the
+  outputs); received rows form one GEMM group per (source rank, local expert).
+* ``'p2p'``: device-initiated exchange over NVLink peer memory (CUDA IPC
+  mappings of every rank's exchange region, plain stores, epoch flags; no
+  host synchronisation): a count-exchange kernel builds the layouts, a send
+  kernel gathers each routed row as bf16 straight into its owner's receive
+  buffer (expert-major, so each local expert is one GEMM group), and the down
+  GEMM's epilogue stores each output row straight into its source rank's
+  return buffer.  Needs peer access between all ranks' GPUs.
 """
 from __future__ import annotations
+
+import ctypes
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from .moe import QuantMoE
+from . import _lib
+from .moe import QuantMoE, _stream
 
 
 def lpt_placement(loads, n_ranks):
@@ -63,7 +79,8 @@ class EPMoE:
     ``local_experts=E/G``).
     """
 
-    def __init__(self, layer: QuantMoE, owner, local, group=None):
+    def __init__(self, layer: QuantMoE, owner, local, group=None, *, transport: str = 'nccl',
+                 max_tokens: int | None = None):
         self.layer = layer
         self.group = group
         self.G = dist.get_world_size(group)
@@ -77,8 +94,68 @@ class EPMoE:
         self.virt = torch.from_numpy((owner * self.E_loc + local).astype(np.int32)).to(dev)
         # GEMM group (source rank, local expert) -> local expert
         self.group_w = torch.arange(self.E_loc, dtype=torch.int32, device=dev).repeat(self.G)
+        if transport not in ('nccl', 'p2p'):
+            raise ValueError("transport must be 'nccl' or 'p2p'")
+        self.transport = transport
+        self.ctx = None
+        if transport == 'p2p':
+            if max_tokens is None or max_tokens < 1:
+                raise ValueError('the p2p transport needs max_tokens (tokens per rank per call)')
+            self._open_p2p(int(max_tokens), dev)
+
+    # -- p2p transport --------------------------------------------------------
+    def _open_p2p(self, max_tokens: int, dev):
+        L, lib = self.layer, self.layer.lib
+        self.max_tokens = max_tokens
+        cap_send = max_tokens * L.k
+        cap_recv = self.G * cap_send
+        ctx = ctypes.c_void_p()
+        _lib.check(lib.b200q_ep_create(self.G, self.rank, self.E_loc, L.D, cap_send, cap_recv, ctypes.byref(ctx)))
+        self.ctx = ctx
+        nb = int(lib.b200q_ep_handle_bytes())
+        mine = (ctypes.c_uint8 * nb)()
+        _lib.check(lib.b200q_ep_handle(ctx, mine))
+        t = torch.tensor(list(bytes(mine)), dtype=torch.uint8, device=dev)
+        every = torch.empty(self.G * nb, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(every, t, group=self.group)
+        handles = bytes(every.cpu().numpy().tobytes())
+        _lib.check(lib.b200q_ep_open(ctx, handles))
+        dist.barrier(group=self.group)
+        self.act = torch.empty((cap_recv, L.F), dtype=torch.bfloat16, device=dev)
+        self.epoch = 0
+
+    def close(self):
+        """Release the p2p exchange region (collective: every rank calls it)."""
+        if self.ctx is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            _lib.check(self.layer.lib.b200q_ep_destroy(self.ctx))
+            self.ctx = None
+
+    def _forward_p2p(self, h: torch.Tensor) -> torch.Tensor:
+        L, lib = self.layer, self.layer.lib
+        T, dev = h.shape[0], h.device
+        if T > self.max_tokens:
+            raise ValueError(f'{T} tokens exceed max_tokens={self.max_tokens}')
+        self.epoch = (self.epoch + 1) & 0xffffffff
+        ep = self.epoch
+        _, ids, w = L.route(h)
+        vids = self.virt[ids.long()]
+        offsets, slot_of, token_of, slot_w, _ = L.dispatch(h, vids, w, gather=False)
+        st = _stream()
+        _lib.check(lib.b200q_ep_exchange_counts_dev(self.ctx, offsets.data_ptr(), ep, st))
+        _lib.check(lib.b200q_ep_send_rows_dev(self.ctx, h.data_ptr(), T, token_of.data_ptr(), offsets.data_ptr(),
+                                              T * L.k, ep, st))
+        _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.gate_up.data_ptr(), L.down.data_ptr(), L.F,
+                                            self.act.data_ptr(), ep, 0, st))
+        y = torch.empty((T, L.D), dtype=torch.float32, device=dev)
+        _lib.check(lib.b200q_ep_combine_dev(self.ctx, slot_of.data_ptr(), slot_w.data_ptr(), T, L.k, y.data_ptr(),
+                                            ep, st))
+        return y
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
+        if self.transport == 'p2p':
+            return self._forward_p2p(h.contiguous())
         L = self.layer
         T, dev = h.shape[0], h.device
         h = h.contiguous()

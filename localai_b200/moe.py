@@ -57,14 +57,20 @@ class QuantMoE:
 
     # -- stages ---------------------------------------------------------------
     def route(self, h: torch.Tensor):
+        """Router logits, top-k expert ids and routing weights."""
         T = h.shape[0]
         dev = h.device
         logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
-        _lib.check(self.lib.b200q_moe_router_dev(
+        ids = torch.empty((T, self.k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, self.k), dtype=torch.float32, device=dev)
+        nws = self.lib.b200q_moe_route_workspace_bytes(T, self.E, self.D)
+        ws = torch.empty(nws // 4, dtype=torch.float32, device=dev) if nws else None
+        _lib.check(self.lib.b200q_moe_route_dev(
             h.data_ptr(), self.router_w.data_ptr(),
             None if self.router_bias is None else self.router_bias.data_ptr(),
-            logits.data_ptr(), T, self.E, self.D, _stream()))
-        ids, w = self.topk(logits)
+            None if self.sel_bias is None else self.sel_bias.data_ptr(),
+            T, self.E, self.D, self.k, self.renorm, logits.data_ptr(), ids.data_ptr(), w.data_ptr(),
+            None if ws is None else ws.data_ptr(), nws, _stream()))
         return logits, ids, w
 
     def topk(self, logits: torch.Tensor):

@@ -54,9 +54,28 @@ def main():
     torch.cuda.synchronize()
     err = float((y_ep - y_same).abs().max() / y_same.abs().max())
     err_fwd = float((y_ep - y_fwd).abs().max() / y_fwd.abs().max())
-    ok = torch.tensor([1 if (err == 0.0 and err_fwd < 1e-2) else 0], device=dev)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    good = err == 0.0 and err_fwd < 1e-2
     print(f'rank {rank}: ep vs single-GPU (same rounding) {err:.3e}, vs forward {err_fwd:.3e}', flush=True)
+    # peer-memory transport: same arithmetic, so bit-identical to the NCCL path;
+    # several calls in a row (epochs), one of them with a ragged shard
+    p2p = EPMoE(part, owner, local, transport='p2p', max_tokens=n)
+    for it in range(3):
+        y_p = p2p(shard)
+        d = float((y_p - y_ep).abs().max())
+        print(f'rank {rank}: p2p call {it} vs nccl max |diff| {d:.3e}', flush=True)
+        good = good and d == 0.0
+    m = n - 3 - rank                        # ragged: a different token count on every rank
+    y_p = p2p(shard[:m])
+    y_n = ep(shard[:m])
+    d = float((y_p - y_n).abs().max())
+    print(f'rank {rank}: p2p ragged ({m} tokens) vs nccl max |diff| {d:.3e}', flush=True)
+    good = good and d == 0.0
+    torch.cuda.synchronize()
+    st = full.lib.b200q_check_device_error()
+    good = good and st == 0
+    p2p.close()
+    ok = torch.tensor([1 if good else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()
     sys.exit(0 if int(ok.item()) == 1 else 1)
 

@@ -51,6 +51,43 @@ def test_topk_bit_exact_on_oracle_logits(E, k, renorm, bias):
     np.testing.assert_allclose(w.cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize('T,E,D', [(1, 64, 4096), (7, 64, 4096), (37, 100, 2048), (300, 64, 4096),
+                                   (4096, 64, 2048), (65, 17, 516)])
+def test_fused_route_split_and_unsplit(T, E, D):
+    """b200q_moe_route_dev: split-K (few tokens) and single-pass (many tokens)
+    logits against float64; its ids/weights equal the top-k kernel run on the
+    logits it returns; two calls agree bit for bit."""
+    from localai_b200 import _lib
+    rng = np.random.default_rng(T * 7 + E)
+    k = 4
+    wr = rng.normal(0, 1 / np.sqrt(D), size=(E, D)).astype(np.float32)
+    bias = rng.normal(scale=0.1, size=E).astype(np.float32)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    layer = QuantMoE.__new__(QuantMoE)
+    layer.lib = _lib.load()
+    layer.E, layer.D, layer.k, layer.renorm = E, D, k, 1
+    layer.router_w = torch.from_numpy(wr).cuda()
+    layer.router_bias = torch.from_numpy(bias).cuda()
+    layer.sel_bias = None
+    hd = torch.from_numpy(h).cuda()
+    logits, ids, w = layer.route(hd)
+    ref = h.astype(np.float64) @ wr.T.astype(np.float64) + bias
+    err = np.abs(logits.cpu().numpy() - ref).max() / np.abs(ref).max()
+    assert err < 1e-5, err
+    ids2, w2 = layer.topk(logits)
+    assert torch.equal(ids, ids2) and torch.equal(w, w2)
+    logits3, ids3, w3 = layer.route(hd)
+    assert torch.equal(logits, logits3) and torch.equal(ids, ids3) and torch.equal(w, w3)
+    # the separate router entry: same bar; identical when the fused call did not split
+    plain = torch.empty_like(logits)
+    _lib.check(layer.lib.b200q_moe_router_dev(hd.data_ptr(), layer.router_w.data_ptr(), layer.router_bias.data_ptr(),
+                                              plain.data_ptr(), T, E, D, torch.cuda.current_stream().cuda_stream))
+    err = np.abs(plain.cpu().numpy() - ref).max() / np.abs(ref).max()
+    assert err < 1e-5, err
+    if layer.lib.b200q_moe_route_workspace_bytes(T, E, D) == 0:
+        assert torch.equal(plain, logits)
+
+
 def test_router_logits_and_dispatch():
     rng = np.random.default_rng(3)
     E, D, F, k, T = 16, 512, 128, 4, 1000
