@@ -390,12 +390,13 @@ cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, i
     return cudaGetLastError();
 }
 
-// Number of K splits across CTAs for T tokens: enough CTAs for two per SM.
+// Number of K splits across CTAs for T tokens: enough CTAs for about two per
+// SM, each with at least one K tile.
 int moe_route_splits(int T, int E, int D, int num_sms)
 {
     const long long ctas = (long long)((T + RT_TOK - 1) / RT_TOK) * ((E + RT_EXP - 1) / RT_EXP);
     int s = 1;
-    while (s < 8 && ctas * s < 2LL * num_sms && (D / RT_BK) >= 2 * s) s *= 2;
+    while (s < 32 && ctas * s < 2LL * num_sms && (D / RT_BK) >= 2 * s) s *= 2;
     return s;
 }
 

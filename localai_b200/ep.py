@@ -41,7 +41,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .moe import QuantMoE, _stream
+from .moe import QuantMoE, _stream, pipelined_host_forward
 
 
 def lpt_placement(loads, n_ranks):
@@ -152,6 +152,12 @@ class EPMoE:
         _lib.check(lib.b200q_ep_combine_dev(self.ctx, slot_of.data_ptr(), slot_w.data_ptr(), T, L.k, y.data_ptr(),
                                             ep, st))
         return y
+
+    def forward_host(self, h_host: torch.Tensor, y_host: torch.Tensor | None = None, chunks: int = 4):
+        """forward() on this rank's host (pinned) tokens with the PCIe copies
+        overlapped with the computation; every rank must use the same number
+        of chunks."""
+        return pipelined_host_forward(self.forward, h_host, y_host, chunks, self.layer.router_w.device)
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         if self.transport == 'p2p':

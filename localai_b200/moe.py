@@ -29,6 +29,54 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+def pipelined_host_forward(fn, h_host: torch.Tensor, y_host: torch.Tensor | None, chunks: int, device):
+    """y_host = fn(h) for host (pinned) f32 h_host [T, D], in ``chunks`` token
+    chunks: the host->device copy of chunk c+1 and the device->host copy of
+    chunk c-1 run on their own streams while ``fn`` computes chunk c on the
+    current stream.  Returns y_host after the last copy has been queued; the
+    copies are ordered before any later work on the current stream."""
+    if h_host.is_cuda or h_host.dtype != torch.float32 or h_host.dim() != 2:
+        raise ValueError('h_host must be a host f32 [T, D] tensor')
+    T, D = h_host.shape
+    if y_host is None:
+        y_host = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
+    chunks = max(1, min(chunks, T))
+    bounds = [T * c // chunks for c in range(chunks + 1)]
+    rows = max(bounds[c + 1] - bounds[c] for c in range(chunks))
+    comp = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    s_in.wait_stream(comp)          # buffers below may reuse memory the current stream just released
+    s_out.wait_stream(comp)
+    hbuf = [torch.empty((rows, D), dtype=torch.float32, device=device) for _ in range(min(2, chunks))]
+    freed = [None, None]            # event: compute has finished reading hbuf[i]
+    done_out = []
+    for c in range(chunks):
+        a, b = bounds[c], bounds[c + 1]
+        buf = hbuf[c % 2][: b - a]
+        with torch.cuda.stream(s_in):
+            if freed[c % 2] is not None:
+                s_in.wait_event(freed[c % 2])
+            buf.copy_(h_host[a:b], non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(s_in)
+        comp.wait_event(ready)
+        y = fn(buf)
+        ev = torch.cuda.Event()
+        ev.record(comp)
+        freed[c % 2] = ev
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev)
+            y_host[a:b].copy_(y, non_blocking=True)
+            y.record_stream(s_out)
+            fin = torch.cuda.Event()
+            fin.record(s_out)
+            done_out.append(fin)
+    for b in hbuf:
+        b.record_stream(s_in)
+    comp.wait_event(done_out[-1])
+    return y_host
+
+
 class QuantMoE:
     def __init__(self, router_w: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *, d_model: int,
                  d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
@@ -137,5 +185,12 @@ class QuantMoE:
         offsets, slot_of, _, slot_w, xperm = self.dispatch(h, ids, w)
         out = self.experts(xperm, offsets, slot_w)
         return self.combine(out, slot_of, h.shape[0])
+
+    def forward_host(self, h_host: torch.Tensor, y_host: torch.Tensor | None = None, chunks: int = 4,
+                     device=None) -> torch.Tensor:
+        """forward() on host (pinned) hidden states, overlapping the PCIe copies
+        with the layer computation chunk by chunk (see pipelined_host_forward)."""
+        device = device or self.router_w.device
+        return pipelined_host_forward(self.forward, h_host, y_host, chunks, device)
 
     __call__ = forward

@@ -141,3 +141,18 @@ def test_layer_deterministic():
     b = layer(h)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize('chunks', [1, 3])
+def test_forward_host_equals_chunked_forward(chunks):
+    """forward_host (copies overlapped with compute) gives exactly forward()
+    of each token chunk."""
+    rng = np.random.default_rng(11)
+    E, D, F, k, T = 16, 512, 128, 4, 301
+    layer, *_ = make_layer(rng, E, D, F, k)
+    h = torch.from_numpy(rng.normal(size=(T, D)).astype(np.float32)).pin_memory()
+    y = layer.forward_host(h, chunks=chunks)
+    torch.cuda.synchronize()
+    bounds = [T * c // chunks for c in range(chunks + 1)]
+    ref = torch.cat([layer(h[a:b].cuda()).cpu() for a, b in zip(bounds[:-1], bounds[1:])])
+    assert torch.equal(y, ref)
