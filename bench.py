@@ -400,11 +400,26 @@ def main():
             for line in PROFILE_TRAFFIC.read_text().splitlines():
                 if line.startswith('traffic_bytes_per_launch:'):
                     traffic = float(line.split(':', 1)[1].split()[0])
+        # the down GEMM alone as well (same kernel, plain bf16 epilogue, K = 1408)
+        out_dn = torch.empty((slots, D), dtype=torch.bfloat16, device=dev)
+        down_call = lambda: ops.gemm_q4k(act, down, offsets, k=F, n_feat=D, w_rows_per_group=D, out=out_dn,
+                                         row_scale=slot_w)
+        down_call()
+        torch.cuda.synchronize()
+        g0.record()
+        for _ in range(gemm_reps):
+            down_call()
+        g1.record()
+        torch.cuda.synchronize()
+        down_ms = g0.elapsed_time(g1) / gemm_reps
+        down_flops = 2.0 * slots * D * F
         roof = {'kernel': 'tc_gemm_q4k_kernel (gate/up, fused SiLU*up)', 'bound': 'tensor',
                 'achieved': round(achieved, 1), 'peak': tc_burst, 'unit': 'TFLOP/s',
                 'frac': round(achieved / tc_burst, 3), 'traffic': traffic,
                 'peak_source': f'{peak_src} bf16 (burst; kernel timed alone)',
-                'flops_per_launch': flops, 'ms_per_launch': round(gemm_ms, 4)}
+                'flops_per_launch': flops, 'ms_per_launch': round(gemm_ms, 4),
+                'down_gemm': {'ms_per_launch': round(down_ms, 4), 'flops_per_launch': down_flops,
+                              'achieved': round(down_flops / (down_ms * 1e-3) / 1e12, 1)}}
 
     gemv = None
     if rank == 0 and not args.no_gemv and world == 1:

@@ -44,12 +44,27 @@ namespace b200q {
 constexpr int TC_BM = 128;              // weight rows per tile (MMA M)
 constexpr int TC_BN = 256;              // activation rows per tile (MMA N)
 constexpr int TC_BK = 64;               // K per stage (bf16, 128 bytes)
-constexpr int TC_STAGES = 3;            // A/B pipeline depth
-constexpr int TC_RAW_STAGES = 2;        // raw weight chunk pipeline depth
+#ifndef TC_A_STAGES_CFG
+#define TC_A_STAGES_CFG 2
+#endif
+#ifndef TC_B_STAGES_CFG
+#define TC_B_STAGES_CFG 3
+#endif
+#ifndef TC_RAW_STAGES_CFG
+#define TC_RAW_STAGES_CFG 4
+#endif
+constexpr int TC_A_STAGES = TC_A_STAGES_CFG;     // dequantised weight tiles (dequant warps -> MMA)
+constexpr int TC_B_STAGES = TC_B_STAGES_CFG;     // activation tiles (TMA -> MMA)
+constexpr int TC_RAW_STAGES = TC_RAW_STAGES_CFG; // raw Q4_K chunks, 4 K-steps each (TMA -> dequant warps)
 constexpr int TC_THREADS = 512;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;     // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;     // 32 KB
-constexpr int TC_MAX_GROUPS = 1024;
+constexpr int TC_MAX_GROUPS = 256;
+// Epilogue staging: each of the 4 epilogue warps transposes its 32-row chunk
+// through shared memory so that global stores are 16-byte vectors along the
+// output row.  Rows are padded to 36 words (conflict-free 128-bit reads).
+constexpr int TC_STG_STRIDE = 36;
+constexpr int TC_STG_BYTES = 32 * TC_STG_STRIDE * 4;   // 4608 per warp
 
 struct TcArgs {
     int n_tiles;            // weight-row tiles per group (N/128, or F/64 in gate/up mode)
@@ -231,13 +246,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // 1024-aligned base for the swizzled tiles
     const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = base;
-    const uint32_t sB = sA + TC_STAGES * TC_A_BYTES;
-    const uint32_t sRaw = sB + TC_STAGES * TC_B_BYTES;
+    const uint32_t sB = sA + TC_A_STAGES * TC_A_BYTES;
+    const uint32_t sRaw = sB + TC_B_STAGES * TC_B_BYTES;
     const uint32_t raw_stage_bytes = (uint32_t)(TC_BM * a.raw_chunk_bytes);
-    const uint32_t sBar = (sRaw + TC_RAW_STAGES * raw_stage_bytes + 7u) & ~7u;
-    const uint32_t full = sBar;                               // [STAGES]   8 dequant warps + TMA tx
-    const uint32_t empty = full + 8 * TC_STAGES;              // [STAGES]   MMA commit
-    const uint32_t raw_full = empty + 8 * TC_STAGES;          // [RAW]      TMA tx
+    const uint32_t sStg = (sRaw + TC_RAW_STAGES * raw_stage_bytes + 15u) & ~15u;
+    const uint32_t sBar = sStg + 4 * TC_STG_BYTES;
+    const uint32_t full_a = sBar;                             // [A]        8 dequant warps
+    const uint32_t empty_a = full_a + 8 * TC_A_STAGES;        // [A]        MMA commit
+    const uint32_t full_b = empty_a + 8 * TC_A_STAGES;        // [B]        TMA tx
+    const uint32_t empty_b = full_b + 8 * TC_B_STAGES;        // [B]        MMA commit
+    const uint32_t raw_full = empty_b + 8 * TC_B_STAGES;      // [RAW]      TMA tx
     const uint32_t raw_empty = raw_full + 8 * TC_RAW_STAGES;  // [RAW]      8 dequant warps
     const uint32_t acc_full = raw_empty + 8 * TC_RAW_STAGES;  // [2]        MMA commit
     const uint32_t acc_empty = acc_full + 16;                 // [2]        4 epilogue warps
@@ -254,9 +272,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int ksteps = a.k / TC_BK;
 
     if (tid == 0) {
-        for (int s = 0; s < TC_STAGES; ++s) {
-            mbar_init(full + 8 * s, 8 + 1);
-            mbar_init(empty + 8 * s, 1);
+        for (int s = 0; s < TC_A_STAGES; ++s) {
+            mbar_init(full_a + 8 * s, 8);
+            mbar_init(empty_a + 8 * s, 1);
+        }
+        for (int s = 0; s < TC_B_STAGES; ++s) {
+            mbar_init(full_b + 8 * s, 1);
+            mbar_init(empty_b + 8 * s, 1);
         }
         for (int s = 0; s < TC_RAW_STAGES; ++s) {
             mbar_init(raw_full + 8 * s, 1);
@@ -304,30 +326,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bool ok = true;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ raw weight producer (TMA)
         if (lane == 0) {
-            int q = 0, rq = 0;
+            const int nchunks = (ksteps + 3) / 4;
+            int rq = 0;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
                 const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
                 const int wrow0 = group_w_s[c.g] * a.w_rows_per_group + (gate_up ? c.nt * 64 : c.nt * TC_BM);
                 const int wrow1 = gate_up ? wrow0 + a.up_offset : wrow0 + 64;
+                for (int rc = 0; rc < nchunks; ++rc, ++rq) {
+                    const int rs = rq % TC_RAW_STAGES;
+                    if (rq >= TC_RAW_STAGES && !mbar_wait(raw_empty + 8 * rs, ((rq / TC_RAW_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                    const uint32_t dst = sRaw + rs * raw_stage_bytes;
+                    mbar_arrive_expect_tx(raw_full + 8 * rs, raw_stage_bytes);
+                    const int xb = rc * a.raw_chunk_bytes;
+                    tma_load_2d(dst, &map_w, xb, wrow0, raw_full + 8 * rs);
+                    tma_load_2d(dst + 64 * a.raw_chunk_bytes, &map_w, xb, wrow1, raw_full + 8 * rs);
+                }
+            }
+        }
+    } else if (warp == 3) {
+        // ------------------------------------------------ activation producer (TMA)
+        if (lane == 0) {
+            int q = 0;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
                 const int xrow = row_off_s[c.g] + c.m0;
-                for (int ks = 0; ks < ksteps && ok; ++ks) {
-                    if ((ks & 3) == 0) {
-                        const int rs = rq % TC_RAW_STAGES;
-                        if (rq >= TC_RAW_STAGES && !mbar_wait(raw_empty + 8 * rs, ((rq / TC_RAW_STAGES) + 1) & 1, a.err)) { ok = false; break; }
-                        const uint32_t dst = sRaw + rs * raw_stage_bytes;
-                        mbar_arrive_expect_tx(raw_full + 8 * rs, raw_stage_bytes);
-                        const int xb = (ks >> 2) * a.raw_chunk_bytes;
-                        tma_load_2d(dst, &map_w, xb, wrow0, raw_full + 8 * rs);
-                        tma_load_2d(dst + 64 * a.raw_chunk_bytes, &map_w, xb, wrow1, raw_full + 8 * rs);
-                        ++rq;
-                    }
-                    const int s = q % TC_STAGES;
-                    if (q >= TC_STAGES && !mbar_wait(empty + 8 * s, ((q / TC_STAGES) + 1) & 1, a.err)) { ok = false; break; }
-                    mbar_arrive_expect_tx(full + 8 * s, TC_B_BYTES);
-                    tma_load_2d(sB + s * TC_B_BYTES, &map_x, ks * TC_BK, xrow, full + 8 * s);
-                    ++q;
+                for (int ks = 0; ks < ksteps; ++ks, ++q) {
+                    const int s = q % TC_B_STAGES;
+                    if (q >= TC_B_STAGES && !mbar_wait(empty_b + 8 * s, ((q / TC_B_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(full_b + 8 * s, TC_B_BYTES);
+                    tma_load_2d(sB + s * TC_B_BYTES, &map_x, ks * TC_BK, xrow, full_b + 8 * s);
                 }
             }
         }
@@ -344,15 +373,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * TC_BN);
                 for (int ks = 0; ks < ksteps; ++ks) {
-                    const int s = q % TC_STAGES;
-                    if (!mbar_wait(full + 8 * s, (q / TC_STAGES) & 1, a.err)) { ok = false; break; }
+                    const int sa = q % TC_A_STAGES, sb = q % TC_B_STAGES;
+                    if (!mbar_wait(full_b + 8 * sb, (q / TC_B_STAGES) & 1, a.err)) { ok = false; break; }
+                    if (!mbar_wait(full_a + 8 * sa, (q / TC_A_STAGES) & 1, a.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t as = sA + s * TC_A_BYTES, bs = sB + s * TC_B_BYTES;
+                    const uint32_t as = sA + sa * TC_A_BYTES, bs = sB + sb * TC_B_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk)
                         umma_bf16(d_tmem, sw128_desc(as + 32 * kk), sw128_desc(bs + 32 * kk), idesc,
                                   (ks > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(empty + 8 * s);
+                    umma_commit(empty_a + 8 * sa);
+                    umma_commit(empty_b + 8 * sb);
                     ++q;
                 }
                 if (!ok) break;
@@ -362,6 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------ epilogue
         const int ew = warp - 4;
+        float *stg = reinterpret_cast<float *>(smem_raw + (sStg - smem_addr(smem_raw)) + ew * TC_STG_BYTES);
         int acc = 0;
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
             const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
@@ -374,47 +406,80 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 uint32_t v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * ew) << 16) + (uint32_t)(ab * TC_BN + 32 * ch), v);
                 tmem_ld_wait();
+                const int nrow = min(32, c.rows - 32 * ch);            // valid rows of this chunk
+                const long long row0 = row_base + 32 * ch;
                 if (gate_up) {
-                    const int f = c.nt * 64 + 16 * ew + (lane & 15);
+                    // lanes 0-15: gate of feature 16ew+l (rows j), lanes 16-31: up (rows 16+j)
                     const bool lo = lane < 16;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float mine_g = __uint_as_float(v[j]), mine_h = __uint_as_float(v[16 + j]);
                         const float recv = __shfl_xor_sync(0xffffffffu, lo ? mine_h : mine_g, 16);
                         const float gv = lo ? mine_g : recv, uv = lo ? recv : mine_h;
-                        const int col = 32 * ch + (lo ? j : 16 + j);
-                        if (col < c.rows)
-                            a.act[(row_base + col) * a.ld_act + f] = __float2bfloat16_rn(silu_ref(gv) * uv);
+                        const int r = lo ? j : 16 + j;
+                        stg[r * TC_STG_STRIDE + (lo ? 0 : 16) + (lane & 15)] = silu_ref(gv) * uv;
                     }
-                } else if (a.ep_ret) {
-                    const int n = c.nt * TC_BM + 32 * ew + lane;
-                    const int G = ret_G;
-                    const int *run = ret_run_s + c.g * G;
-                    int s = 0;
+                    __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int col = 32 * ch + j;
-                        if (col < c.rows) {
-                            const int row = (int)(row_base + col);
-                            while (s + 1 < G && row >= run[s + 1]) ++s;      // warp-uniform
-                            const long long drow = ret_base_s[c.g * G + s] + (row - run[s]);
-                            ret_peer_s[s][drow * a.ld_out + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+                    for (int it = 0; it < 2; ++it) {
+                        const int r = it * 16 + (lane >> 1), part = lane & 1;
+                        if (r < nrow) {
+                            const float *src = stg + r * TC_STG_STRIDE + (r >= 16 ? 16 : 0) + part * 8;
+                            const float4 x0 = *reinterpret_cast<const float4 *>(src);
+                            const float4 x1 = *reinterpret_cast<const float4 *>(src + 4);
+                            const uint4 o = make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w),
+                                                       pack_bf16(x1.x, x1.y), pack_bf16(x1.z, x1.w));
+                            *reinterpret_cast<uint4 *>(a.act + (row0 + r) * a.ld_act + c.nt * 64 + 16 * ew +
+                                                       part * 8) = o;
                         }
                     }
                 } else {
-                    const int n = c.nt * TC_BM + 32 * ew + lane;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int col = 32 * ch + j;
-                        if (col < c.rows) {
-                            const long long row = row_base + col;
-                            const float sc = a.row_scale ? __ldg(a.row_scale + row) : 1.0f;
-                            const float val = __uint_as_float(v[j]) * sc;
-                            if (a.out_bf16) a.out_bf16[row * a.ld_out + n] = __float2bfloat16_rn(val);
-                            else a.out[row * a.ld_out + n] = val;
+                    for (int j = 0; j < 32; ++j) stg[j * TC_STG_STRIDE + lane] = __uint_as_float(v[j]);
+                    __syncwarp();
+                    const int n0 = c.nt * TC_BM + 32 * ew;
+                    if (a.out_bf16 || a.ep_ret) {
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            const int r = it * 8 + (lane >> 2), part = lane & 3;
+                            if (r < nrow) {
+                                const long long row = row0 + r;
+                                const float sc = a.row_scale ? __ldg(a.row_scale + row) : 1.0f;
+                                const float *src = stg + r * TC_STG_STRIDE + part * 8;
+                                const float4 x0 = *reinterpret_cast<const float4 *>(src);
+                                const float4 x1 = *reinterpret_cast<const float4 *>(src + 4);
+                                const uint4 o = make_uint4(pack_bf16(x0.x * sc, x0.y * sc),
+                                                           pack_bf16(x0.z * sc, x0.w * sc),
+                                                           pack_bf16(x1.x * sc, x1.y * sc),
+                                                           pack_bf16(x1.z * sc, x1.w * sc));
+                                __nv_bfloat16 *dst;
+                                if (a.ep_ret) {
+                                    const int G = ret_G;
+                                    const int *run = ret_run_s + c.g * G;
+                                    int s = 0;
+                                    while (s + 1 < G && row >= run[s + 1]) ++s;
+                                    dst = ret_peer_s[s] + (long long)(ret_base_s[c.g * G + s] + (row - run[s])) * a.ld_out;
+                                } else {
+                                    dst = a.out_bf16 + row * a.ld_out;
+                                }
+                                *reinterpret_cast<uint4 *>(dst + n0 + part * 8) = o;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int it = 0; it < 8; ++it) {
+                            const int r = it * 4 + (lane >> 3), part = lane & 7;
+                            if (r < nrow) {
+                                const long long row = row0 + r;
+                                const float sc = a.row_scale ? __ldg(a.row_scale + row) : 1.0f;
+                                float4 x = *reinterpret_cast<const float4 *>(stg + r * TC_STG_STRIDE + part * 4);
+                                x.x *= sc; x.y *= sc; x.z *= sc; x.w *= sc;
+                                *reinterpret_cast<float4 *>(a.out + row * a.ld_out + n0 + part * 4) = x;
+                            }
                         }
                     }
                 }
+                __syncwarp();                                          // staging reused by the next chunk
             }
             tc_fence_before();
             __syncwarp();
@@ -433,13 +498,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int ks = 0; ks < ksteps && ok; ++ks) {
                 const int rs = rq % TC_RAW_STAGES;
                 if ((ks & 3) == 0 && !mbar_wait(raw_full + 8 * rs, (rq / TC_RAW_STAGES) & 1, a.err)) { ok = false; break; }
-                const int s = q % TC_STAGES;
-                if (q >= TC_STAGES && !mbar_wait(empty + 8 * s, ((q / TC_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                const int s = q % TC_A_STAGES;
+                if (q >= TC_A_STAGES && !mbar_wait(empty_a + 8 * s, ((q / TC_A_STAGES) + 1) & 1, a.err)) { ok = false; break; }
                 const uint32_t raw_row = sRaw + rs * raw_stage_bytes + (uint32_t)(raw_r * a.raw_chunk_bytes);
                 dequant_q4k_half(raw_row, ks & 3, h, sA + s * TC_A_BYTES + (uint32_t)(r * 128), r);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(full + 8 * s);
+                if (lane == 0) mbar_arrive(full_a + 8 * s);
                 ++q;
                 if ((ks & 3) == 3 || ks == ksteps - 1) {
                     __syncwarp();
@@ -511,7 +576,9 @@ static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows,
 
 size_t tc_gemm_smem_bytes(int chunk_bytes)
 {
-    return 1024 + (size_t)TC_STAGES * (TC_A_BYTES + TC_B_BYTES) + (size_t)TC_RAW_STAGES * TC_BM * chunk_bytes + 256;
+    return 1024 + (size_t)TC_A_STAGES * TC_A_BYTES + (size_t)TC_B_STAGES * TC_B_BYTES +
+           (size_t)TC_RAW_STAGES * TC_BM * chunk_bytes + 16 +
+           4 * TC_STG_BYTES + 256;
 }
 
 // Grouped GEMM, Q4_K weights.
@@ -527,6 +594,13 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
 {
     if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
     if (ep_ret && (up_offset >= 0 || groups > EP_MAX_EXPERTS)) return cudaErrorInvalidValue;
+    // the epilogue stores 16-byte vectors along output rows
+    if (up_offset >= 0 && ((reinterpret_cast<uintptr_t>(act) & 15) || ld_act % 8)) return cudaErrorInvalidValue;
+    if (up_offset < 0 && !ep_ret &&
+        (out_bf16 ? ((reinterpret_cast<uintptr_t>(out_bf16) & 15) || ld_out % 8)
+                  : ((reinterpret_cast<uintptr_t>(out) & 15) || ld_out % 4)))
+        return cudaErrorInvalidValue;
+    if (ep_ret && ld_out % 8) return cudaErrorInvalidValue;
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
     if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
