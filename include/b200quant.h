@@ -125,6 +125,15 @@ int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *
 
 /* ---- MoE layer stages (engine/zaya.py:274-307, generalised to top-k) ----
  * All buffers are device memory owned by the caller; nothing is allocated. */
+/* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
+ * weights.  w_row_bytes is the byte distance between weight rows (0: packed
+ * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed
+ * size is not (k not a multiple of 2048) need a padded copy.  Q6_K needs k a
+ * multiple of 256 when rows are packed; every type needs k a multiple of 64. */
+int b200q_gemm_dev(int ggml_type, const void *x_bf16, long long x_rows, int k, const void *w, long long w_row_bytes,
+                   int groups, int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
+                   const int *group_w, int n_weight_groups, void *out, int out_is_bf16, long long ld_out,
+                   const float *row_scale, void *act_bf16, long long ld_act, int max_ctas, void *stream);
 /* logits[t*E + e] = h[t] . wr[e] + bias[e] (f32; bias may be NULL). */
 int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
                          void *stream);
@@ -208,7 +217,8 @@ long long b200q_launch_count(void);
  *   b200q_ep_send_rows_dev gather h[token_of[slot]] as bf16 into the owner's
  *                          receive buffer (expert-major, source-minor);
  *   b200q_ep_experts_dev   wait for all ranks' rows, gate/up then down on the
- *                          local experts; the down GEMM stores each output row
+ *                          local experts (weights as for b200q_gemm_dev: type,
+ *                          row strides, 0 = packed); the down GEMM stores each output row
  *                          (unweighted, bf16) into its source rank's return
  *                          buffer; then signal every rank.  act: bf16
  *                          [max_recv_rows, d_ff] scratch;
@@ -229,7 +239,8 @@ const int *b200q_ep_group_offsets(void *ep);
 int b200q_ep_exchange_counts_dev(void *ep, const int *offsets, unsigned int epoch, void *stream);
 int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int *token_of, const int *offsets, int slots,
                            unsigned int epoch, void *stream);
-int b200q_ep_experts_dev(void *ep, const void *gate_up, const void *down, int d_ff, void *act, unsigned int epoch,
+int b200q_ep_experts_dev(void *ep, int ggml_type, const void *gate_up, long long gate_up_row_bytes,
+                         const void *down, long long down_row_bytes, int d_ff, void *act, unsigned int epoch,
                          int max_ctas, void *stream);
 int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int T, int k, float *y,
                          unsigned int epoch, void *stream);

@@ -44,6 +44,8 @@ SIGNATURES = {
     'b200q_dequant_bf16_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
     'b200q_gemv_dev': (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _ll, _ll, _vp]),
     'b200q_gemm_q4k_dev': (_i, [_vp, _ll, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll, _i, _vp]),
+    'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
+                            _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     'b200q_moe_topk_dev': (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_moe_num_blocks': (_i, [_i]),
@@ -65,7 +67,7 @@ SIGNATURES = {
     'b200q_ep_group_offsets': (_vp, [_vp]),
     'b200q_ep_exchange_counts_dev': (_i, [_vp, _vp, _u32, _vp]),
     'b200q_ep_send_rows_dev': (_i, [_vp, _vp, _i, _vp, _vp, _i, _u32, _vp]),
-    'b200q_ep_experts_dev': (_i, [_vp, _vp, _vp, _i, _vp, _u32, _i, _vp]),
+    'b200q_ep_experts_dev': (_i, [_vp, _i, _vp, _ll, _vp, _ll, _i, _vp, _u32, _i, _vp]),
     'b200q_ep_combine_dev': (_i, [_vp, _vp, _vp, _i, _i, _vp, _u32, _vp]),
 }
 

@@ -39,7 +39,8 @@ cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T,
                                         int *offsets, int *slot_of, int *token_of, float *slot_w,
                                         __nv_bfloat16 *xperm, cudaStream_t st);
 int noalloc_dispatch_max();
-cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
+cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, int k, const void *w,
+                           long long w_row_bytes, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
@@ -398,12 +399,34 @@ B200Q_API int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, co
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(x_bf16), x_rows, k, w, groups,
+    return cuda_status(launch_tc_gemm(T_Q4_K, static_cast<const __nv_bfloat16 *>(x_bf16), x_rows, k, w, 0, groups,
                                           w_rows_per_group, up_offset, n_feat, row_off, group_w, n_weight_groups,
                                           out_is_bf16 ? nullptr : static_cast<float *>(out),
                                           out_is_bf16 ? static_cast<__nv_bfloat16 *>(out) : nullptr, ld_out,
                                           row_scale, static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err,
                                           di->sms, max_ctas, (cudaStream_t)stream, nullptr),
+                       "gemm");
+}
+
+B200Q_API int b200q_gemm_dev(int ggml_type, const void *x_bf16, long long x_rows, int k, const void *w,
+                             long long w_row_bytes, int groups, int w_rows_per_group, int up_offset, int n_feat,
+                             const int *row_off, const int *group_w, int n_weight_groups, void *out, int out_is_bf16,
+                             long long ld_out, const float *row_scale, void *act_bf16, long long ld_act, int max_ctas,
+                             void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!x_bf16 || !w || !row_off) return set_status(B200Q_EINVAL, "gemm: null pointer");
+    if (up_offset >= 0 ? !act_bf16 : !out) return set_status(B200Q_EINVAL, "gemm: missing output");
+    if (group_w && n_weight_groups < 1) return set_status(B200Q_EINVAL, "gemm: n_weight_groups must be >= 1");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_tc_gemm(ggml_type, static_cast<const __nv_bfloat16 *>(x_bf16), x_rows, k, w,
+                                      w_row_bytes, groups, w_rows_per_group, up_offset, n_feat, row_off, group_w,
+                                      n_weight_groups, out_is_bf16 ? nullptr : static_cast<float *>(out),
+                                      out_is_bf16 ? static_cast<__nv_bfloat16 *>(out) : nullptr, ld_out, row_scale,
+                                      static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
+                                      (cudaStream_t)stream, nullptr),
                        "gemm");
 }
 
@@ -580,7 +603,8 @@ B200Q_API int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int 
                        "ep_send_rows");
 }
 
-B200Q_API int b200q_ep_experts_dev(void *ep, const void *gate_up, const void *down, int d_ff, void *act,
+B200Q_API int b200q_ep_experts_dev(void *ep, int ggml_type, const void *gate_up, long long gate_up_row_bytes,
+                                   const void *down, long long down_row_bytes, int d_ff, void *act,
                                    unsigned int epoch, int max_ctas, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
@@ -594,11 +618,13 @@ B200Q_API int b200q_ep_experts_dev(void *ep, const void *gate_up, const void *do
     const int *grp = ep_group_offsets(ep);
     cudaError_t e = launch_ep_wait(ep, 1, epoch, di->err, st);
     if (e == cudaSuccess)
-        e = launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(ep_recv_rows(ep)), cap, D, gate_up, El, 2 * d_ff,
+        e = launch_tc_gemm(ggml_type, static_cast<const __nv_bfloat16 *>(ep_recv_rows(ep)), cap, D, gate_up,
+                           gate_up_row_bytes, El, 2 * d_ff,
                                d_ff, d_ff, grp, nullptr, El, nullptr, nullptr, 0, nullptr,
                                static_cast<__nv_bfloat16 *>(act), d_ff, di->err, di->sms, max_ctas, st, nullptr);
     if (e == cudaSuccess)
-        e = launch_tc_gemm_q4k(static_cast<const __nv_bfloat16 *>(act), cap, d_ff, down, El, D, -1, D, grp,
+        e = launch_tc_gemm(ggml_type, static_cast<const __nv_bfloat16 *>(act), cap, d_ff, down, down_row_bytes, El, D,
+                           -1, D, grp,
                                nullptr, El, nullptr, nullptr, D, nullptr, nullptr, 0, di->err, di->sms, max_ctas, st,
                                ep_dev(ep));
     if (e == cudaSuccess) e = launch_ep_signal(ep, epoch, st);

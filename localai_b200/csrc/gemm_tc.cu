@@ -50,12 +50,17 @@ constexpr int TC_BK = 64;               // K per stage (bf16, 128 bytes)
 #ifndef TC_B_STAGES_CFG
 #define TC_B_STAGES_CFG 3
 #endif
-#ifndef TC_RAW_STAGES_CFG
-#define TC_RAW_STAGES_CFG 4
-#endif
 constexpr int TC_A_STAGES = TC_A_STAGES_CFG;     // dequantised weight tiles (dequant warps -> MMA)
 constexpr int TC_B_STAGES = TC_B_STAGES_CFG;     // activation tiles (TMA -> MMA)
-constexpr int TC_RAW_STAGES = TC_RAW_STAGES_CFG; // raw Q4_K chunks, 4 K-steps each (TMA -> dequant warps)
+// Raw weight chunks (one 256-value run of blocks per row, 4 K-steps), TMA ->
+// dequant warps.  The box of each type is 16-byte sized: Q4_K 144 B (a
+// super-block), Q8_0 272 B (8 blocks, as 136 uint16), Q6_K 240 B (as 120
+// uint16) -- an aligned window around the 210-byte super-block, whose start
+// within the window is (chunk * 210) mod 16.
+template <int WT> struct TcW;
+template <> struct TcW<T_Q4_K> { static constexpr int CHUNK = 144, RAW = 4, ELEM = 1; };
+template <> struct TcW<T_Q6_K> { static constexpr int CHUNK = 240, RAW = 2, ELEM = 2; };
+template <> struct TcW<T_Q8_0> { static constexpr int CHUNK = 272, RAW = 2, ELEM = 2; };
 constexpr int TC_THREADS = 512;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;     // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;     // 32 KB
@@ -74,7 +79,7 @@ struct TcArgs {
     const int *group_w;     // optional [groups]: weight index of each group (default: g)
     int w_rows_per_group;   // weight rows of one group in the raw tensor map
     int up_offset;          // gate/up mode: row offset of the up half (F); < 0: plain mode
-    int raw_chunk_bytes;    // bytes of one 256-value block
+    int raw_chunk_bytes;    // bytes of one raw chunk box row (TcW<WT>::CHUNK)
     // epilogue
     float *out;             // plain mode: out[row * ld_out + n] (f32), or
     __nv_bfloat16 *out_bf16;//             out_bf16[row * ld_out + n]
@@ -214,6 +219,92 @@ __device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, int p, int h,
     }
 }
 
+// N consecutive 32-bit words of shared memory starting at an even address.
+template <int N>
+__device__ __forceinline__ void lds_run_a2(uint32_t addr, uint32_t (&w)[N])
+{
+    if (addr & 2u) {
+        uint32_t prev = lds32(addr - 2);
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t nxt = lds32(addr + 2 + 4 * i);
+            w[i] = __funnelshift_r(prev, nxt, 16);
+            prev = nxt;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) w[i] = lds32(addr + 4 * i);
+    }
+}
+
+__device__ __forceinline__ void sts_a_chunk(uint32_t a_row, int r, int chunk, const uint32_t (&o)[4])
+{
+    const uint32_t dst = a_row + (((uint32_t)chunk ^ (uint32_t)(r & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                 : "memory");
+}
+
+// Q6_K (engine/dequant.py:146-167): K-step p of the super-block at ``blk``
+// (even address), half h: values 64p+32h+j = 128*hq + 32*u + j with
+// hq = p/2, u = 2(p&1)+h; q = low nibble of ql[64hq+32h+j] (high nibble for
+// u >= 2) | ((qh[32hq+j] >> 2u) & 3) << 4; value d * scale[8hq+2u+j/16] *
+// (q - 32), exact in f32 and rounded once to bf16.
+__device__ __forceinline__ void dequant_q6k_half(uint32_t blk, int p, int h, uint32_t a_row, int r)
+{
+    const int hq = p >> 1, u = 2 * (p & 1) + h;
+    uint32_t ql[8], qh[8];
+    lds_run_a2<8>(blk + 64 * hq + 32 * h, ql);
+    lds_run_a2<8>(blk + 128 + 32 * hq, qh);
+    const uint32_t scw = lds_u16(blk + 192 + 8 * hq + 2 * u);
+    const float d = h2f(lds_u16(blk + 208));
+    const float s0 = d * (float)(int)(int8_t)(scw & 0xffu), s1 = d * (float)(int)(int8_t)(scw >> 8);
+    const bool hi_nib = (p & 1) != 0;
+    const int sh = 2 * u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const int wi = 2 * c + ww;
+            const uint32_t nib = hi_nib ? ((ql[wi] >> 4) & 0x0F0F0F0Fu) : (ql[wi] & 0x0F0F0F0Fu);
+            const uint32_t q = nib | (((qh[wi] >> sh) & 0x03030303u) << 4);
+            const float sc = wi < 4 ? s0 : s1;
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b)       // 2^23 + q - (2^23 + 32) = q - 32, exact
+                v[b] = sc * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388640.0f);
+            o[2 * ww] = pack_bf16(v[0], v[1]);
+            o[2 * ww + 1] = pack_bf16(v[2], v[3]);
+        }
+        sts_a_chunk(a_row, r, 4 * h + c, o);
+    }
+}
+
+// Q8_0 (engine/dequant.py:75-78): K-step p, half h = block 2p+h of the
+// 8-block chunk: value d * q (int8), exact in f32, rounded once to bf16.
+__device__ __forceinline__ void dequant_q8_0_half(uint32_t chunk, int p, int h, uint32_t a_row, int r)
+{
+    const uint32_t blk = chunk + 34u * (uint32_t)(2 * p + h);
+    const float d = h2f(lds_u16(blk));
+    uint32_t qs[8];
+    lds_run_a2<8>(blk + 2, qs);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const uint32_t q = qs[2 * c + ww] ^ 0x80808080u;   // int8 + 128
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b)       // 2^23 + (q + 128) - (2^23 + 128) = q, exact
+                v[b] = d * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388736.0f);
+            o[2 * ww] = pack_bf16(v[0], v[1]);
+            o[2 * ww + 1] = pack_bf16(v[2], v[3]);
+        }
+        sts_a_chunk(a_row, r, 4 * h + c, o);
+    }
+}
+
 // ---------------------------------------------------------------- kernel
 struct TileCoord {
     int g, nt, m0, rows;    // group, weight-row tile, first activation row (local), valid rows
@@ -238,10 +329,12 @@ __device__ __forceinline__ TileCoord tile_coord(int t, const int *tile_pref, con
     return c;
 }
 
+template <int WT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-                       const TcArgs a)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+                   const TcArgs a)
 {
+    constexpr int TC_RAW_STAGES = TcW<WT>::RAW;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-aligned base for the swizzled tiles
     const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
@@ -339,7 +432,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (rq >= TC_RAW_STAGES && !mbar_wait(raw_empty + 8 * rs, ((rq / TC_RAW_STAGES) + 1) & 1, a.err)) { ok = false; break; }
                     const uint32_t dst = sRaw + rs * raw_stage_bytes;
                     mbar_arrive_expect_tx(raw_full + 8 * rs, raw_stage_bytes);
-                    const int xb = rc * a.raw_chunk_bytes;
+                    // box start (in map elements): 16-byte aligned, see TcW
+                    const int xb = WT == T_Q4_K ? rc * 144 : WT == T_Q8_0 ? rc * 136 : ((rc * 210) & ~15) >> 1;
                     tma_load_2d(dst, &map_w, xb, wrow0, raw_full + 8 * rs);
                     tma_load_2d(dst + 64 * a.raw_chunk_bytes, &map_w, xb, wrow1, raw_full + 8 * rs);
                 }
@@ -501,7 +595,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int s = q % TC_A_STAGES;
                 if (q >= TC_A_STAGES && !mbar_wait(empty_a + 8 * s, ((q / TC_A_STAGES) + 1) & 1, a.err)) { ok = false; break; }
                 const uint32_t raw_row = sRaw + rs * raw_stage_bytes + (uint32_t)(raw_r * a.raw_chunk_bytes);
-                dequant_q4k_half(raw_row, ks & 3, h, sA + s * TC_A_BYTES + (uint32_t)(r * 128), r);
+                const uint32_t a_row = sA + s * TC_A_BYTES + (uint32_t)(r * 128);
+                if (WT == T_Q4_K) dequant_q4k_half(raw_row, ks & 3, h, a_row, r);
+                else if (WT == T_Q6_K) dequant_q6k_half(raw_row + (uint32_t)(((ks >> 2) * 210) & 15), ks & 3, h, a_row, r);
+                else dequant_q8_0_half(raw_row, ks & 3, h, a_row, r);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_a + 8 * s);
@@ -557,36 +654,57 @@ static cudaError_t make_map_bf16(CUtensorMap *m, const void *ptr, long long rows
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// raw bytes [rows, row_bytes], box [chunk_bytes x 64 rows], no swizzle.
-static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows, long long row_bytes, int chunk_bytes)
+// raw bytes [rows, row_bytes] seen as elements of elem_bytes (1 or 2), box
+// [chunk_bytes x 64 rows], no swizzle.  Reads past the end of a row come
+// back as zeros (only the Q6_K window of the last super-block reaches there).
+static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows, long long row_bytes, int chunk_bytes,
+                                int elem_bytes)
 {
     PFN_encodeTiled enc = get_encode();
     if (!enc) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || row_bytes % 16 || chunk_bytes % 16 || chunk_bytes > 256)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || row_bytes % 16 || chunk_bytes % 16 ||
+        chunk_bytes / elem_bytes > 256)
         return cudaErrorInvalidValue;
-    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / elem_bytes), (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)chunk_bytes, 64};
+    cuuint32_t box[2] = {(cuuint32_t)(chunk_bytes / elem_bytes), 64};
     cuuint32_t es[2] = {1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+    CUresult r = enc(m, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                     const_cast<void *>(ptr), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-size_t tc_gemm_smem_bytes(int chunk_bytes)
+template <int WT>
+static size_t tc_gemm_smem_bytes()
 {
     return 1024 + (size_t)TC_A_STAGES * TC_A_BYTES + (size_t)TC_B_STAGES * TC_B_BYTES +
-           (size_t)TC_RAW_STAGES * TC_BM * chunk_bytes + 16 +
-           4 * TC_STG_BYTES + 256;
+           (size_t)TcW<WT>::RAW * TC_BM * TcW<WT>::CHUNK + 16 + 4 * TC_STG_BYTES + 256;
 }
 
-// Grouped GEMM, Q4_K weights.
+template <int WT>
+static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const TcArgs &a, int grid, cudaStream_t st)
+{
+    static bool attr = false;
+    const size_t smem = tc_gemm_smem_bytes<WT>();
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    tc_gemm_kernel<WT><<<grid, TC_THREADS, smem, st>>>(mx, mw, a);
+    return cudaGetLastError();
+}
+
+// Grouped GEMM, Q4_K / Q6_K / Q8_0 weights.
 //   x        bf16 [x_rows, k] activations (rows of group g: row_off[g]..row_off[g+1])
-//   w        raw Q4_K bytes of groups*w_rows_per_group rows of k values each
+//   w        raw GGUF blocks of groups*w_rows_per_group rows of k values each,
+//            w_row_bytes apart (0: packed rows; must be a multiple of 16)
 //   up_offset >= 0: gate/up mode over n_feat features (act bf16 [x_rows, ld_act]);
 //            < 0: plain mode over n_feat output columns (out f32 [x_rows, ld_out]).
-cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, const void *w, int groups,
+cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, int k, const void *w,
+                           long long w_row_bytes, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
@@ -604,13 +722,24 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
     if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
-    const int chunk = 144;
-    const long long kpad = ((long long)k + 255) / 256 * 256;     // raw rows hold whole super-blocks
-    const long long row_bytes = kpad / 256 * chunk;
+    if (wtype != T_Q4_K && wtype != T_Q6_K && wtype != T_Q8_0) return cudaErrorInvalidValue;
+    if (wtype != T_Q8_0 && w_row_bytes == 0 && k % 256 && wtype != T_Q4_K) return cudaErrorInvalidValue;
+    const int chunk = wtype == T_Q4_K ? TcW<T_Q4_K>::CHUNK : wtype == T_Q6_K ? TcW<T_Q6_K>::CHUNK : TcW<T_Q8_0>::CHUNK;
+    const int elem = wtype == T_Q4_K ? 1 : 2;
+    long long row_bytes = w_row_bytes;
+    if (row_bytes == 0) {
+        // packed rows (Q4_K rows hold whole super-blocks: k rounded up to 256)
+        row_bytes = wtype == T_Q4_K ? ((long long)k + 255) / 256 * 144
+                  : wtype == T_Q6_K ? (long long)k / 256 * 210 : (long long)k / 32 * 34;
+    }
+    const long long min_bytes = wtype == T_Q4_K ? ((long long)k + 255) / 256 * 144
+                              : wtype == T_Q6_K ? ((long long)k + 255) / 256 * 210 : ((long long)k + 31) / 32 * 34;
+    if (row_bytes < min_bytes) return cudaErrorInvalidValue;
     CUtensorMap mx, mw;
     cudaError_t e = make_map_bf16(&mx, x, x_rows, k, TC_BN);
     if (e != cudaSuccess) return e;
-    e = make_map_raw(&mw, w, (long long)(group_w ? n_weight_groups : groups) * w_rows_per_group, row_bytes, chunk);
+    e = make_map_raw(&mw, w, (long long)(group_w ? n_weight_groups : groups) * w_rows_per_group, row_bytes, chunk,
+                     elem);
     if (e != cudaSuccess) return e;
     TcArgs a;
     a.n_tiles = gu ? n_feat / 64 : n_feat / TC_BM;
@@ -629,17 +758,11 @@ cudaError_t launch_tc_gemm_q4k(const __nv_bfloat16 *x, long long x_rows, int k, 
     a.ld_act = ld_act;
     a.ep_ret = ep_ret;
     a.err = err;
-    const size_t smem = tc_gemm_smem_bytes(chunk);
-    static bool attr = false;
-    if (!attr) {
-        e = cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
     int grid = num_sms;
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-    tc_gemm_q4k_kernel<<<grid, TC_THREADS, smem, st>>>(mx, mw, a);
-    return cudaGetLastError();
+    if (wtype == T_Q4_K) return tc_launch<T_Q4_K>(mx, mw, a, grid, st);
+    if (wtype == T_Q6_K) return tc_launch<T_Q6_K>(mx, mw, a, grid, st);
+    return tc_launch<T_Q8_0>(mx, mw, a, grid, st);
 }
 
 } // namespace b200q

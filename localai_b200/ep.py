@@ -146,8 +146,8 @@ class EPMoE:
         _lib.check(lib.b200q_ep_exchange_counts_dev(self.ctx, offsets.data_ptr(), ep, st))
         _lib.check(lib.b200q_ep_send_rows_dev(self.ctx, h.data_ptr(), T, token_of.data_ptr(), offsets.data_ptr(),
                                               T * L.k, ep, st))
-        _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.gate_up.data_ptr(), L.down.data_ptr(), L.F,
-                                            self.act.data_ptr(), ep, 0, st))
+        _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride, L.down.data_ptr(),
+                                            L.dn_stride, L.F, self.act.data_ptr(), ep, 0, st))
         y = torch.empty((T, L.D), dtype=torch.float32, device=dev)
         _lib.check(lib.b200q_ep_combine_dev(self.ctx, slot_of.data_ptr(), slot_w.data_ptr(), T, L.k, y.data_ptr(),
                                             ep, st))

@@ -11,18 +11,22 @@ same block batched over T tokens and generalised to top-k:
     out = w_slot * (down act)    per expert       b200q_gemm_q4k_dev (plain mode, tcgen05; bf16 rows)
     y[t] = sum_j out[slot(t, j)]                  b200q_moe_combine_dev
 
-Expert weights are the raw GGUF Q4_K tensors in ZAYA's layout: ``gate_up``
-[E, 2F, D] (gate rows first, then up rows, as ``np.split(packed, 2)`` reads
-them, engine/zaya.py:304) and ``down`` [E, D, F_pad] with F_pad the next
-multiple of 256 (padded sub-blocks decode to zero).
+Expert weights are raw GGUF Q4_K, Q6_K or Q8_0 tensors in ZAYA's layout:
+``gate_up`` [E, 2F, D] (gate rows first, then up rows, as
+``np.split(packed, 2)`` reads them, engine/zaya.py:304) and ``down``
+[E, D, F_pad] with F_pad the next multiple of the type's block (256 for the
+K-quants, 32 for Q8_0; padded values decode to zero).  Rows whose byte size
+is not a multiple of 16 (e.g. Q6_K with 1024 columns, 840 B) are copied once
+into 16-byte-padded rows, which the tensor-core GEMM loads with TMA.
 """
 from __future__ import annotations
 
 import torch
 
 from . import _lib
+from .ops import packed_row_bytes, pad_rows
 
-Q4_K = 12
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
 
 
 def _stream():
@@ -82,13 +86,15 @@ class QuantMoE:
                  d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
                  sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K,
                  local_experts: int | None = None):
-        if ggml_type != Q4_K:
-            raise NotImplementedError('the tensor-core expert path supports Q4_K expert weights')
-        if d_ff % 64 or d_model % 128:
-            raise ValueError('d_ff must be a multiple of 64 and d_model of 128')
+        if ggml_type not in (Q4_K, Q6_K, Q8_0):
+            raise NotImplementedError('the tensor-core expert path supports Q4_K, Q6_K and Q8_0 expert weights')
+        if d_ff % 64 or d_model % 128 or (ggml_type != Q8_0 and d_model % 256):
+            raise ValueError('d_ff must be a multiple of 64 and d_model of 128 (256 for K-quants)')
         self.E = router_w.shape[0]
         self.D, self.F, self.k = d_model, d_ff, top_k
-        self.F_pad = (d_ff + 255) // 256 * 256
+        self.type = ggml_type
+        blk = 32 if ggml_type == Q8_0 else 256
+        self.F_pad = (d_ff + blk - 1) // blk * blk
         self.router_w = router_w.contiguous().float()
         self.router_bias = None if router_bias is None else router_bias.contiguous().float()
         self.sel_bias = None if sel_bias is None else sel_bias.contiguous().float()
@@ -97,10 +103,14 @@ class QuantMoE:
         self.down = down.contiguous()
         # expert tensors may hold a subset of the experts (expert parallelism)
         self.E_held = self.E if local_experts is None else local_experts
-        gu_bytes = self.E_held * 2 * d_ff * (d_model // 256) * 144
-        dn_bytes = self.E_held * d_model * (self.F_pad // 256) * 144
+        rb_gu, rb_dn = packed_row_bytes(ggml_type, d_model), packed_row_bytes(ggml_type, self.F_pad)
+        gu_bytes = self.E_held * 2 * d_ff * rb_gu
+        dn_bytes = self.E_held * d_model * rb_dn
         if self.gate_up.numel() != gu_bytes or self.down.numel() != dn_bytes:
-            raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of Q4_K')
+            raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of GGML type {ggml_type}')
+        # device copies with 16-byte rows where the packed rows are not
+        self.gate_up, self.gu_stride = pad_rows(self.gate_up, self.E_held * 2 * d_ff, rb_gu)
+        self.down, self.dn_stride = pad_rows(self.down, self.E_held * d_model, rb_dn)
         self.lib = _lib.load()
 
     # -- stages ---------------------------------------------------------------
@@ -158,12 +168,13 @@ class QuantMoE:
         groups = offsets.numel() - 1
         gw = None if group_w is None else group_w.data_ptr()
         act = torch.empty((S, self.F), dtype=torch.bfloat16, device=dev)
-        _lib.check(self.lib.b200q_gemm_q4k_dev(
-            xperm.data_ptr(), S, self.D, self.gate_up.data_ptr(), groups, 2 * self.F, self.F, self.F,
-            offsets.data_ptr(), gw, self.E_held, None, 0, 0, None, act.data_ptr(), self.F, max_ctas, _stream()))
+        _lib.check(self.lib.b200q_gemm_dev(
+            self.type, xperm.data_ptr(), S, self.D, self.gate_up.data_ptr(), self.gu_stride, groups, 2 * self.F,
+            self.F, self.F, offsets.data_ptr(), gw, self.E_held, None, 0, 0, None, act.data_ptr(), self.F,
+            max_ctas, _stream()))
         out = torch.empty((S, self.D), dtype=out_dtype, device=dev)
-        _lib.check(self.lib.b200q_gemm_q4k_dev(
-            act.data_ptr(), S, self.F, self.down.data_ptr(), groups, self.D, -1, self.D,
+        _lib.check(self.lib.b200q_gemm_dev(
+            self.type, act.data_ptr(), S, self.F, self.down.data_ptr(), self.dn_stride, groups, self.D, -1, self.D,
             offsets.data_ptr(), gw, self.E_held, out.data_ptr(), 1 if out_dtype == torch.bfloat16 else 0, self.D,
             None if slot_w is None else slot_w.data_ptr(), None, 0, max_ctas, _stream()))
         return out

@@ -86,21 +86,45 @@ def check_device_error() -> None:
         raise _lib.B200QError(f'kernel error word {code}')
 
 
-def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k: int, n_feat: int,
-             w_rows_per_group: int, up_offset: int = -1, out: torch.Tensor | None = None,
-             row_scale: torch.Tensor | None = None, act: torch.Tensor | None = None,
-             group_w: torch.Tensor | None = None, n_weight_groups: int = 0, out_dtype=torch.float32,
-             max_ctas: int = 0) -> torch.Tensor:
-    """Grouped tensor-core GEMM with in-kernel Q4_K dequantisation.
+def packed_row_bytes(ggml_type: int, k: int) -> int:
+    """Bytes of one GGUF row of k values (Q4_K rows rounded up to whole super-blocks)."""
+    if ggml_type == 12:
+        return (k + 255) // 256 * 144
+    if ggml_type == 14:
+        return (k + 255) // 256 * 210
+    if ggml_type == 8:
+        return (k + 31) // 32 * 34
+    raise ValueError(f'unsupported ggml type {ggml_type} for the tensor-core path')
+
+
+def pad_rows(w: torch.Tensor, rows: int, row_bytes: int) -> tuple[torch.Tensor, int]:
+    """Copy of ``rows`` packed rows of ``row_bytes`` with each row padded to a
+    multiple of 16 bytes (the tensor-core GEMM loads rows with TMA); returns
+    (tensor, stride).  Rows already 16-byte sized are returned unchanged."""
+    if row_bytes % 16 == 0:
+        return w, row_bytes
+    stride = (row_bytes + 15) // 16 * 16
+    out = torch.zeros((rows, stride), dtype=torch.uint8, device=w.device)
+    out[:, :row_bytes] = w.reshape(rows, row_bytes)
+    return out.reshape(-1), stride
+
+
+def gemm_quant(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k: int, n_feat: int,
+               w_rows_per_group: int, ggml_type: int = 12, w_row_bytes: int = 0, up_offset: int = -1,
+               out: torch.Tensor | None = None, row_scale: torch.Tensor | None = None,
+               act: torch.Tensor | None = None, group_w: torch.Tensor | None = None, n_weight_groups: int = 0,
+               out_dtype=torch.float32, max_ctas: int = 0) -> torch.Tensor:
+    """Grouped tensor-core GEMM with in-kernel dequantisation of Q4_K (12),
+    Q6_K (14) or Q8_0 (8) weights.
 
     ``x_bf16`` [rows, k] bf16 activations; group g owns rows
     ``row_off[g]:row_off[g+1]`` (int32 CUDA tensor, groups+1 entries) and the
-    weight rows ``wg*w_rows_per_group ...`` of ``w`` (raw Q4_K bytes), with
-    ``wg = group_w[g]`` when ``group_w`` is given (then ``w`` holds
-    ``n_weight_groups`` weight groups), else ``wg = g``.  Plain mode
-    (``up_offset < 0``) returns [rows, n_feat] in ``out_dtype`` (f32 or bf16);
-    gate/up mode returns bf16 [rows, n_feat] = SiLU(gate) * up with up rows at
-    ``f + up_offset``.
+    weight rows ``wg*w_rows_per_group ...`` of ``w`` (raw GGUF bytes,
+    ``w_row_bytes`` apart, 0 = packed), with ``wg = group_w[g]`` when
+    ``group_w`` is given (then ``w`` holds ``n_weight_groups`` weight groups),
+    else ``wg = g``.  Plain mode (``up_offset < 0``) returns [rows, n_feat] in
+    ``out_dtype`` (f32 or bf16); gate/up mode returns bf16 [rows, n_feat] =
+    SiLU(gate) * up with up rows at ``f + up_offset``.
     """
     if x_bf16.dtype != torch.bfloat16 or not x_bf16.is_cuda or x_bf16.dim() != 2 or x_bf16.shape[1] != k:
         raise ValueError('x must be a CUDA bf16 [rows, k] tensor')
@@ -112,26 +136,31 @@ def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, k:
     wgroups = n_weight_groups if group_w is not None else groups
     if group_w is not None and (group_w.dtype != torch.int32 or group_w.numel() != groups):
         raise ValueError('group_w must be an int32 tensor with one entry per group')
-    kpad = (k + 255) // 256 * 256
-    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < wgroups * w_rows_per_group * (kpad // 256) * 144:
-        raise ValueError('w must hold the weight groups as Q4_K rows')
+    stride = w_row_bytes or packed_row_bytes(ggml_type, k)
+    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < wgroups * w_rows_per_group * stride:
+        raise ValueError('w must hold the weight groups as GGUF rows')
     lib = _lib.load()
     gw = None if group_w is None else group_w.data_ptr()
     if up_offset >= 0:
         if act is None:
             act = torch.empty((rows, n_feat), dtype=torch.bfloat16, device=x_bf16.device)
-        st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, up_offset,
-                                    n_feat, row_off.data_ptr(), gw, wgroups, None, 0, 0, None, act.data_ptr(),
-                                    act.stride(0), max_ctas, _stream())
+        st = lib.b200q_gemm_dev(ggml_type, x_bf16.data_ptr(), rows, k, w.data_ptr(), w_row_bytes, groups,
+                                w_rows_per_group, up_offset, n_feat, row_off.data_ptr(), gw, wgroups, None, 0, 0,
+                                None, act.data_ptr(), act.stride(0), max_ctas, _stream())
         _lib.check(st)
         return act
     if out is None:
         out = torch.empty((rows, n_feat), dtype=out_dtype, device=x_bf16.device)
     if out.dtype not in (torch.float32, torch.bfloat16):
         raise ValueError('out must be f32 or bf16')
-    st = lib.b200q_gemm_q4k_dev(x_bf16.data_ptr(), rows, k, w.data_ptr(), groups, w_rows_per_group, -1, n_feat,
-                                row_off.data_ptr(), gw, wgroups, out.data_ptr(),
-                                1 if out.dtype == torch.bfloat16 else 0, out.stride(0),
-                                None if row_scale is None else row_scale.data_ptr(), None, 0, max_ctas, _stream())
+    st = lib.b200q_gemm_dev(ggml_type, x_bf16.data_ptr(), rows, k, w.data_ptr(), w_row_bytes, groups,
+                            w_rows_per_group, -1, n_feat, row_off.data_ptr(), gw, wgroups, out.data_ptr(),
+                            1 if out.dtype == torch.bfloat16 else 0, out.stride(0),
+                            None if row_scale is None else row_scale.data_ptr(), None, 0, max_ctas, _stream())
     _lib.check(st)
     return out
+
+
+def gemm_q4k(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, **kw) -> torch.Tensor:
+    """gemm_quant for Q4_K weights (packed rows)."""
+    return gemm_quant(x_bf16, w, row_off, ggml_type=12, **kw)
