@@ -246,6 +246,83 @@ def gemv_probe(torch, ops, synth, hbm_peak):
     return res
 
 
+def _graph_time_us(torch, fn_list, reps_per_graph, replays=5):
+    """Mean device time (us) of one call, captured in a CUDA graph that cycles
+    through ``fn_list`` (one entry per weight copy)."""
+    for f in fn_list:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps_per_graph):
+                fn_list[i % len(fn_list)]()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (replays * reps_per_graph)
+
+
+def dense_ffn_probe(torch, synth, hbm_peak, tc_peak):
+    """Configuration 2: dense Q4_K FFN (gate/up [14336 x 4096], down [4096 x
+    14336]) at T = 1 (GEMV path) and T = 512 (tensor-core path), three weight
+    copies (297 MB, > 2 x L2) cycled in a CUDA graph."""
+    from localai_b200.ffn import QuantFFN
+    Dm, Ff = 4096, 14336
+    rng = np.random.default_rng(2)
+    dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
+    raws = [synth.q4_k(rng, Ff, Dm), synth.q4_k(rng, Ff, Dm), synth.q4_k(rng, Dm, Ff)]
+    ffns = []
+    for _ in range(3):
+        ffns.append(QuantFFN(dev(raws[0]), dev(raws[1]), dev(raws[2]), d_model=Dm, d_ff=Ff))
+    wbytes = sum(len(r) for r in raws)
+    res = {}
+    for T in (1, 512):
+        x = torch.randn(T, Dm, device='cuda')
+        us = _graph_time_us(torch, [lambda f=f: f(x) for f in ffns], 30 if T == 1 else 6)
+        flops = 2.0 * T * 3 * Ff * Dm
+        ent = {'us_per_call': round(us, 2), 'flops': flops}
+        if T == 1:
+            nbytes = wbytes + 4 * (Dm + 2 * Ff + Ff + Dm)
+            ent.update({'GB_s': round(nbytes / (us * 1e-6) / 1e9, 1),
+                        'frac_of_measured_hbm': round(nbytes / (us * 1e-6) / 1e9 / hbm_peak, 3),
+                        'bytes_per_call': nbytes, 'path': 'GEMV [gate;up] + silu*up + GEMV down'})
+        else:
+            ent.update({'TFLOP_s': round(flops / (us * 1e-6) / 1e12, 1),
+                        'frac_of_measured_bf16': round(flops / (us * 1e-6) / 1e12 / tc_peak, 3),
+                        'path': 'tcgen05 GEMM gate/up (fused SiLU*up) + GEMM down'})
+        res[f'T{T}'] = ent
+    del ffns
+    return res
+
+
+def moe_q6k_probe(torch, synth):
+    """Configuration 3: Q6_K MoE, D=2048, E=16, F=1024, top-2, T = 1, 64, 4096
+    (two layer copies, 165 MB, cycled in a CUDA graph)."""
+    from localai_b200.moe import QuantMoE
+    E3, D3, F3, k3 = 16, 2048, 1024, 2
+    rng = np.random.default_rng(3)
+    dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
+    gu = b''.join(synth.q6_k(rng, 2 * F3, D3) for _ in range(E3))
+    dn = b''.join(synth.q6_k(rng, D3, F3) for _ in range(E3))
+    wr3 = torch.from_numpy(rng.normal(0, 0.02, size=(E3, D3)).astype(np.float32)).cuda()
+    layers = [QuantMoE(wr3, dev(gu), dev(dn), d_model=D3, d_ff=F3, top_k=k3, ggml_type=14) for _ in range(2)]
+    res = {}
+    for T in (1, 64, 4096):
+        h3 = torch.randn(T, D3, device='cuda')
+        us = _graph_time_us(torch, [lambda L=L: L(h3) for L in layers], 20 if T < 4096 else 6)
+        res[f'T{T}'] = {'us_per_call': round(us, 2), 'tokens_per_s': round(T / (us * 1e-6), 1)}
+    del layers
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -325,8 +402,22 @@ def main():
         sampler.start()
         time.sleep(1.0)
     barrier()
+    # warm-up: at least W steps and at least WARM_S seconds of back-to-back
+    # work, so that the timed steps run at the clocks the GPU holds under load
+    # (after the CPU-side set-up an idle GPU needs some time to ramp up); every
+    # rank runs the same number of steps (rank 0 decides)
+    WARM_S = 0.3
+    t_w = time.time()
     for _ in range(args.warmup):
         step(h)
+    torch.cuda.synchronize()
+    per = max(1e-4, (time.time() - t_w) / args.warmup)
+    extra = torch.tensor([max(0, int(WARM_S / per) + 1 - args.warmup)], device=dev)
+    if world > 1:
+        dist.broadcast(extra, 0)
+    for _ in range(int(extra.item())):
+        step(h)
+    warm_steps = args.warmup + int(extra.item())
     torch.cuda.synchronize()
     ops.check_device_error()
 
@@ -421,9 +512,11 @@ def main():
                 'down_gemm': {'ms_per_launch': round(down_ms, 4), 'flops_per_launch': down_flops,
                               'achieved': round(down_flops / (down_ms * 1e-3) / 1e12, 1)}}
 
-    gemv = None
+    gemv = ffn2 = moe3 = None
     if rank == 0 and not args.no_gemv and world == 1:
         gemv = gemv_probe(torch, ops, synth, hbm_peak)
+        ffn2 = dense_ffn_probe(torch, synth, hbm_peak, tc_burst)
+        moe3 = moe_q6k_probe(torch, synth)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -433,7 +526,7 @@ def main():
 
     if rank == 0:
         line = {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
-                'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'strong',
+                'warmup': warm_steps, 'ms_per_step': ms, 'higher_is_better': True, 'scaling': 'strong',
                 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
                 'config': {'workload': WORKLOAD, 'hidden': D, 'experts': E, 'intermediate': F, 'top_k': K_TOP,
                            'tokens': T_TOTAL, 'weights': 'Q4_K', 'router': 'f32 + Zipf(1.1) bias',
@@ -445,6 +538,7 @@ def main():
                         'd2h_bytes_per_step': T_TOTAL * D * 4, 'chunks': args.e2e_chunks,
                         'api': 'EPMoE.forward_host' if world > 1 else 'QuantMoE.forward_host'},
                 'gpu_launches': int(launches), 'clocks': clocks, 'gemv': gemv,
+                'config2_dense_ffn_q4k': ffn2, 'config3_moe_q6k': moe3,
                 'flops_per_step': algorithmic_flops(T_TOTAL * K_TOP)}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -125,6 +125,10 @@ int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *
 
 /* ---- MoE layer stages (engine/zaya.py:274-307, generalised to top-k) ----
  * All buffers are device memory owned by the caller; nothing is allocated. */
+/* Dense FFN activation (engine/model.py:161-166): out[t, f] =
+ * silu(gu[t, f]) * gu[t, F + f] for f32 gu [T, 2F] (gate columns, then up
+ * columns) and out [T, F]; silu(g) = g / (1 + exp(-clip(g, -80, 80))). */
+int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, void *stream);
 /* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
  * weights.  w_row_bytes is the byte distance between weight rows (0: packed
  * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed

@@ -65,6 +65,8 @@ cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const
 cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaStream_t st);
 cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
 
+cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, int num_sms, cudaStream_t st);
+
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
 long long g_launches = 0;
@@ -428,6 +430,16 @@ B200Q_API int b200q_gemm_dev(int ggml_type, const void *x_bf16, long long x_rows
                                       static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
                                       (cudaStream_t)stream, nullptr),
                        "gemm");
+}
+
+B200Q_API int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!gate_up || !out) return set_status(B200Q_EINVAL, "silu_mul: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_silu_mul(gate_up, T, F, out, di->sms, (cudaStream_t)stream), "silu_mul");
 }
 
 B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,
