@@ -334,6 +334,8 @@ def main():
     ap.add_argument('--no-gemv', action='store_true')
     ap.add_argument('--transport', default='p2p', choices=['p2p', 'nccl'],
                     help='expert-parallel exchange (N > 1): NVLink peer memory or NCCL all-to-all')
+    ap.add_argument('--phases', action='store_true',
+                    help='N > 1, p2p: add per-rank stage times of one layer call ("ep_phases")')
     ap.add_argument('--e2e-chunks', type=int, default=4,
                     help='token chunks of the end-to-end leg (PCIe copies overlapped with compute)')
     ap.add_argument('--tokens', type=int, default=T_TOTAL,
@@ -512,6 +514,12 @@ def main():
                 'down_gemm': {'ms_per_launch': round(down_ms, 4), 'flops_per_launch': down_flops,
                               'achieved': round(down_flops / (down_ms * 1e-3) / 1e12, 1)}}
 
+    phases = None
+    if world > 1 and args.phases and args.transport == 'p2p':
+        mine_ph = step.phase_times(h)
+        allp = [None] * world
+        dist.all_gather_object(allp, mine_ph)
+        phases = {f'rank{r}': p for r, p in enumerate(allp)}
     gemv = ffn2 = moe3 = None
     if rank == 0 and not args.no_gemv and world == 1:
         gemv = gemv_probe(torch, ops, synth, hbm_peak)
@@ -538,7 +546,7 @@ def main():
                         'd2h_bytes_per_step': T_TOTAL * D * 4, 'chunks': args.e2e_chunks,
                         'api': 'EPMoE.forward_host' if world > 1 else 'QuantMoE.forward_host'},
                 'gpu_launches': int(launches), 'clocks': clocks, 'gemv': gemv,
-                'config2_dense_ffn_q4k': ffn2, 'config3_moe_q6k': moe3,
+                'config2_dense_ffn_q4k': ffn2, 'config3_moe_q6k': moe3, 'ep_phases': phases,
                 'flops_per_step': algorithmic_flops(T_TOTAL * K_TOP)}
         print(json.dumps(line), flush=True)
     if world > 1:

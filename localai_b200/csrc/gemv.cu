@@ -320,53 +320,84 @@ template <int NW> struct XPackWords { static constexpr int N = ((3 * NW + 7) + 3
 // (token, unit), one 4-value word each; max/sums use shuffles inside the
 // NW-lane segment.  Every lane of the calling warps must execute this.
 template <int T>
+__device__ __forceinline__ void quantize_x_task(const float4 f, bool valid, int task, uint32_t xs)
+{
+    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
+    const int k = task % NW, tu = task / NW;
+    float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
+#pragma unroll
+    for (int o = 1; o < NW; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? 8388607.0f / m : 0.f;
+    const float v[4] = {f.x, f.y, f.z, f.w};
+    uint32_t p2 = 0, p1 = 0, p0 = 0;
+    int qs = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        int q = __float2int_rn(v[e] * inv);
+        q = max(-8388607, min(8388607, q));
+        p2 |= (uint32_t)((q >> 16) & 0xff) << (8 * e);
+        p1 |= (uint32_t)((q >> 8) & 0xff) << (8 * e);
+        p0 |= (uint32_t)(q & 0xff) << (8 * e);
+        qs += q;
+    }
+    float sm = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);      // 16-value runs
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);      // 32-value runs
+    if (valid) {
+        const uint32_t o = xs + (uint32_t)tu * N * 4;
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(p2) : "memory");
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(p1) : "memory");
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(p0) : "memory");
+        if (k == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(m > 0.f ? m / 8388607.0f : 0.f)) : "memory");
+        if ((k & 7) == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(sm)) : "memory");
+        if ((k & 3) == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)qs)) : "memory");
+    }
+}
+
+template <int T>
+__device__ __forceinline__ float4 quantize_x_load(const float *__restrict__ x, int cols, int units, int tasks, int task)
+{
+    constexpr int NW = Unit<T>::NW;
+    if (task >= tasks) return make_float4(0.f, 0.f, 0.f, 0.f);
+    const int k = task % NW, tu = task / NW;
+    const int u = tu % units, t = tu / units;
+    int c0 = 0, c1 = 0;
+    unit_cols<T>(u, c0, c1);
+    return __ldg(reinterpret_cast<const float4 *>(x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7)));
+}
+
+// Cooperative quantisation of x [ntok, cols] into packed per-unit words in
+// shared memory (xs[(t * units + u) * N ...]).  NW consecutive lanes handle one
+// (token, unit), one 4-value word each; max/sums use shuffles inside the
+// NW-lane segment.  Every lane of the calling warps must execute this.  When a
+// thread has at most 8 tasks (decode), all of its loads are issued before any
+// is used, so the activation costs one L2 round trip instead of one per task.
+template <int T>
 __device__ __forceinline__ void quantize_x_smem(const float *__restrict__ x, int cols, int units, int ntok,
                                                 uint32_t xs, int tid, int nthreads)
 {
-    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
+    constexpr int NW = Unit<T>::NW;
+    constexpr int MAXIT = 8;
     const int tasks = ntok * units * NW;
+    const int iters = (tasks + nthreads - 1) / nthreads;
+    if (iters <= MAXIT) {
+        float4 f[MAXIT];
+#pragma unroll
+        for (int i = 0; i < MAXIT; ++i)
+            if (i < iters) f[i] = quantize_x_load<T>(x, cols, units, tasks, i * nthreads + tid);
+#pragma unroll
+        for (int i = 0; i < MAXIT; ++i)
+            if (i < iters) quantize_x_task<T>(f[i], i * nthreads + tid < tasks, i * nthreads + tid, xs);
+        return;
+    }
     for (int base = 0; base < tasks; base += nthreads) {
         const int task = base + tid;
-        const bool valid = task < tasks;
-        const int k = task % NW, tu = task / NW;
-        const int u = tu % units, t = tu / units;
-        int c0 = 0, c1 = 0;
-        if (valid) unit_cols<T>(u, c0, c1);
-        const float4 f = valid ? __ldg(reinterpret_cast<const float4 *>(x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7)))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
-#pragma unroll
-        for (int o = 1; o < NW; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float inv = m > 0.f ? 8388607.0f / m : 0.f;
-        const float v[4] = {f.x, f.y, f.z, f.w};
-        uint32_t p2 = 0, p1 = 0, p0 = 0;
-        int qs = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int q = __float2int_rn(v[e] * inv);
-            q = max(-8388607, min(8388607, q));
-            p2 |= (uint32_t)((q >> 16) & 0xff) << (8 * e);
-            p1 |= (uint32_t)((q >> 8) & 0xff) << (8 * e);
-            p0 |= (uint32_t)(q & 0xff) << (8 * e);
-            qs += q;
-        }
-        float sm = (v[0] + v[1]) + (v[2] + v[3]);
-#pragma unroll
-        for (int o = 1; o < 4; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);      // 16-value runs
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);      // 32-value runs
-        if (valid) {
-            const uint32_t o = xs + (uint32_t)tu * N * 4;
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(p2) : "memory");
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(p1) : "memory");
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(p0) : "memory");
-            if (k == 0)
-                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(m > 0.f ? m / 8388607.0f : 0.f)) : "memory");
-            if ((k & 7) == 0)
-                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(sm)) : "memory");
-            if ((k & 3) == 0)
-                asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)qs)) : "memory");
-        }
+        quantize_x_task<T>(quantize_x_load<T>(x, cols, units, tasks, task), task < tasks, task, xs);
     }
 }
 

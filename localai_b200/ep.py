@@ -132,26 +132,54 @@ class EPMoE:
             _lib.check(self.layer.lib.b200q_ep_destroy(self.ctx))
             self.ctx = None
 
-    def _forward_p2p(self, h: torch.Tensor) -> torch.Tensor:
+    def _forward_p2p(self, h: torch.Tensor, marks: list | None = None) -> torch.Tensor:
         L, lib = self.layer, self.layer.lib
         T, dev = h.shape[0], h.device
         if T > self.max_tokens:
             raise ValueError(f'{T} tokens exceed max_tokens={self.max_tokens}')
+
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
+
         self.epoch = (self.epoch + 1) & 0xffffffff
         ep = self.epoch
+        mark('start')
         _, ids, w = L.route(h)
+        mark('route')
         vids = self.virt[ids.long()]
         offsets, slot_of, token_of, slot_w, _ = L.dispatch(h, vids, w, gather=False)
+        mark('dispatch')
         st = _stream()
         _lib.check(lib.b200q_ep_exchange_counts_dev(self.ctx, offsets.data_ptr(), ep, st))
+        mark('counts')
         _lib.check(lib.b200q_ep_send_rows_dev(self.ctx, h.data_ptr(), T, token_of.data_ptr(), offsets.data_ptr(),
                                               T * L.k, ep, st))
+        mark('send')
         _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride, L.down.data_ptr(),
                                             L.dn_stride, L.F, self.act.data_ptr(), ep, 0, st))
+        mark('experts')
         y = torch.empty((T, L.D), dtype=torch.float32, device=dev)
         _lib.check(lib.b200q_ep_combine_dev(self.ctx, slot_of.data_ptr(), slot_w.data_ptr(), T, L.k, y.data_ptr(),
                                             ep, st))
+        mark('combine')
         return y
+
+    def phase_times(self, h: torch.Tensor) -> dict:
+        """One p2p layer call with CUDA events between its stages; returns the
+        milliseconds of each stage on this rank ('experts' includes the wait
+        for every rank's rows, 'combine' the wait for the returned outputs).
+        Collective: every rank calls it."""
+        if self.transport != 'p2p':
+            raise ValueError('phase_times needs the p2p transport')
+        marks = []
+        self._forward_p2p(h.contiguous(), marks)
+        torch.cuda.synchronize()
+        out = {marks[i][0]: round(marks[i - 1][1].elapsed_time(marks[i][1]), 4) for i in range(1, len(marks))}
+        out['total'] = round(marks[0][1].elapsed_time(marks[-1][1]), 4)
+        return out
 
     def forward_host(self, h_host: torch.Tensor, y_host: torch.Tensor | None = None, chunks: int = 4):
         """forward() on this rank's host (pinned) tokens with the PCIe copies
