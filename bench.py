@@ -185,6 +185,88 @@ def cpu_reference_moe(tokens, threads=8):
     return tokens / dt, ('reference' if lib is not None else 'port'), cores, dt
 
 
+def cpu_reference_extras(threads=8):
+    """The reference's CPU path for configurations 1-3 (its own kernels built
+    from its sources into oracle/_ref/, ``threads`` pool threads; NumPy SiLU,
+    router and top-k as engine/model.py:161-166 and engine/zaya.py:274-307).
+    Bounded samples; returns {} when the compiled reference is unavailable."""
+    so = ROOT / 'oracle' / '_ref' / 'libnative_quant_ref.so'
+    if not so.exists():
+        return {}
+    from localai_b200 import synth
+    from oracle import quant_oracle as o
+    lib = ctypes.CDLL(str(so))
+    cores = min(threads, os.cpu_count() or 1)
+    vp = ctypes.c_void_p
+
+    def mv(fn, raw, x, rows, cols):
+        out = np.empty(rows, np.float32)
+        xb = np.ascontiguousarray(x, np.float32)
+        getattr(lib, fn)(np.frombuffer(raw, np.uint8).ctypes.data_as(vp), xb.ctypes.data_as(vp),
+                         out.ctypes.data_as(vp), rows, cols, cores)
+        return out
+
+    def mm(fn, raw, x, rows, cols):
+        out = np.empty((rows, x.shape[0]), np.float32)
+        xb = np.ascontiguousarray(x, np.float32)
+        getattr(lib, fn)(np.frombuffer(raw, np.uint8).ctypes.data_as(vp), xb.ctypes.data_as(vp),
+                         out.ctypes.data_as(vp), rows, cols, x.shape[0], cores)
+        return out
+
+    def timed(f, min_s=0.3, max_reps=200):
+        f()
+        n, t0 = 0, time.perf_counter()
+        while n < max_reps and (n == 0 or time.perf_counter() - t0 < min_s):
+            f()
+            n += 1
+        return (time.perf_counter() - t0) / n
+
+    silu = lambda g: g / (1.0 + np.exp(-np.clip(g, -80, 80)))
+    res = {'cores': cores, 'kind': 'reference'}
+    rng = np.random.default_rng(5)
+    # configuration 1: Q4_K GEMV 4096 x 4096
+    w1 = synth.q4_k(rng, 4096, 4096)
+    x1 = rng.normal(size=4096).astype(np.float32)
+    t1 = timed(lambda: mv('localai_q4k_matvec', w1, x1, 4096, 4096))
+    res['config1_gemv'] = {'us_per_call': round(t1 * 1e6, 1), 'GB_s': round(9469952 / t1 / 1e9, 2)}
+    # configuration 2: dense Q4_K FFN (gate/up 14336 x 4096, down 4096 x 14336)
+    g2, u2, d2 = synth.q4_k(rng, 14336, 4096), synth.q4_k(rng, 14336, 4096), synth.q4_k(rng, 4096, 14336)
+
+    def ffn1():
+        x = x1
+        return mv('localai_q4k_matvec', d2, silu(mv('localai_q4k_matvec', g2, x, 14336, 4096)) *
+                  mv('localai_q4k_matvec', u2, x, 14336, 4096), 4096, 14336)
+    t2 = timed(ffn1)
+    X = rng.normal(size=(512, 4096)).astype(np.float32)
+
+    def ffn512():
+        gt = mm('localai_q4k_matmul', g2, X, 14336, 4096)
+        ut = mm('localai_q4k_matmul', u2, X, 14336, 4096)
+        return mm('localai_q4k_matmul', d2, (silu(gt) * ut).T, 4096, 14336)
+    t512 = timed(ffn512, min_s=0.0, max_reps=1)
+    res['config2_dense_ffn'] = {'T1_us': round(t2 * 1e6, 1), 'T512_ms': round(t512 * 1e3, 1),
+                                'T512_TFLOP_s': round(180388626432.0 / t512 / 1e12, 4)}
+    # configuration 3: Q6_K MoE (D 2048, 16 experts, F 1024, top-2), ZAYA-style per-token matvecs
+    E3, D3, F3 = 16, 2048, 1024
+    gu3 = [synth.q6_k(rng, 2 * F3, D3) for _ in range(E3)]
+    dn3 = [synth.q6_k(rng, D3, F3) for _ in range(E3)]
+    wr3 = rng.normal(0, 0.02, size=(E3, D3)).astype(np.float32)
+    H = rng.normal(size=(64, D3)).astype(np.float32)
+
+    def moe_tokens(n):
+        ids, w = o.route_topk(H[:n] @ wr3.T, 2)
+        for t in range(n):
+            for j in range(2):
+                e = int(ids[t, j])
+                gu = mv('localai_q6k_matvec', gu3[e], H[t], 2 * F3, D3)
+                mv('localai_q6k_matvec', dn3[e], silu(gu[:F3]) * gu[F3:], D3, F3) * w[t, j]
+    t_1 = timed(lambda: moe_tokens(1))
+    t_64 = timed(lambda: moe_tokens(64), min_s=0.0, max_reps=1)
+    res['config3_moe_q6k'] = {'T1_us': round(t_1 * 1e6, 1), 'T64_tokens_per_s': round(64 / t_64, 1),
+                              'path': 'per-token router + native Q6_K matvecs (engine/zaya.py:274-307)'}
+    return res
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
@@ -531,6 +613,8 @@ def main():
         v, kind, cores, dt = cpu_reference_moe(args.cpu_tokens)
         cpu = {'value': v, 'unit': 'tokens/s', 'cores': cores, 'kind': kind,
                'sample': f'{args.cpu_tokens} of {T_TOTAL} tokens (same layer shapes and routing), {dt:.1f} s'}
+        if not args.no_gemv:
+            cpu['other_configs'] = cpu_reference_extras()
 
     if rank == 0:
         line = {'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
