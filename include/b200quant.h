@@ -125,6 +125,18 @@ int b200q_gemm_q4k_dev(const void *x_bf16, long long x_rows, int k, const void *
 
 /* ---- MoE layer stages (engine/zaya.py:274-307, generalised to top-k) ----
  * All buffers are device memory owned by the caller; nothing is allocated. */
+/* ZAYA router chain steps (engine/zaya.py:274-307), f32, one row per token:
+ * state = x (+ prev * w_eda when both are given), out = rmsnorm(state) * norm_w
+ * (x / sqrt(mean(x^2) + eps) * w, engine/model.py:82).  prev/w_eda may be NULL. */
+int b200q_zaya_router_prep_dev(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
+                               int R, float eps, float *state, float *out, void *stream);
+/* In place exact GELU: x * (1 + erf(x / sqrt 2)) / 2 (engine/zaya.py:181-186). */
+int b200q_gelu_dev(float *x, long long n, void *stream);
+/* Copy bf16 rows [offsets[group], offsets[group+1]) of src [*, D] into dst
+ * (D a multiple of 8, 16-byte aligned rows; at most max_rows rows): the
+ * output rows of ZAYA's skip route are the routed input rows. */
+int b200q_copy_rows_range_dev(const void *src_bf16, void *dst_bf16, const int *offsets, int group, int D,
+                              int max_rows, void *stream);
 /* Dense FFN activation (engine/model.py:161-166): out[t, f] =
  * silu(gu[t, f]) * gu[t, F + f] for f32 gu [T, 2F] (gate columns, then up
  * columns) and out [T, F]; silu(g) = g / (1 + exp(-clip(g, -80, 80))). */

@@ -44,6 +44,9 @@ SIGNATURES = {
     'b200q_dequant_bf16_dev': (_i, [_i, _vp, _vp, _ll, _vp]),
     'b200q_gemv_dev': (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _ll, _ll, _vp]),
     'b200q_gemm_q4k_dev': (_i, [_vp, _ll, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll, _i, _vp]),
+    'b200q_zaya_router_prep_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp, _vp]),
+    'b200q_gelu_dev': (_i, [_vp, _ll, _vp]),
+    'b200q_copy_rows_range_dev': (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     'b200q_silu_mul_dev': (_i, [_vp, _i, _i, _vp, _vp]),
     'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
                             _i, _vp]),

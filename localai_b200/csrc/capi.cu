@@ -66,6 +66,11 @@ cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaS
 cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
 
 cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, int num_sms, cudaStream_t st);
+cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
+                                    int R, float eps, float *state, float *out, cudaStream_t st);
+cudaError_t launch_gelu(float *x, long long n, int num_sms, cudaStream_t st);
+cudaError_t launch_copy_rows_range(const void *src, void *dst, const int *offsets, int g, int D, int max_rows,
+                                   int num_sms, cudaStream_t st);
 
 // Library-wide state shared with the other translation units.
 std::recursive_mutex g_lock;
@@ -430,6 +435,39 @@ B200Q_API int b200q_gemm_dev(int ggml_type, const void *x_bf16, long long x_rows
                                       static_cast<__nv_bfloat16 *>(act_bf16), ld_act, di->err, di->sms, max_ctas,
                                       (cudaStream_t)stream, nullptr),
                        "gemm");
+}
+
+B200Q_API int b200q_zaya_router_prep_dev(const float *x, const float *prev, const float *w_eda, const float *norm_w,
+                                         int T, int R, float eps, float *state, float *out, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!x || !norm_w || !state || !out) return set_status(B200Q_EINVAL, "zaya_router_prep: null pointer");
+    ++g_launches;
+    return cuda_status(launch_zaya_router_prep(x, prev, w_eda, norm_w, T, R, eps, state, out, (cudaStream_t)stream),
+                       "zaya_router_prep");
+}
+
+B200Q_API int b200q_gelu_dev(float *x, long long n, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!x) return set_status(B200Q_EINVAL, "gelu: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_gelu(x, n, di->sms, (cudaStream_t)stream), "gelu");
+}
+
+B200Q_API int b200q_copy_rows_range_dev(const void *src_bf16, void *dst_bf16, const int *offsets, int group, int D,
+                                        int max_rows, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!src_bf16 || !dst_bf16 || !offsets) return set_status(B200Q_EINVAL, "copy_rows_range: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_copy_rows_range(src_bf16, dst_bf16, offsets, group, D, max_rows, di->sms,
+                                              (cudaStream_t)stream),
+                       "copy_rows_range");
 }
 
 B200Q_API int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, void *stream)

@@ -140,18 +140,24 @@ class QuantMoE:
             T, self.E, self.k, self.renorm, ids.data_ptr(), w.data_ptr(), _stream()))
         return ids, w
 
-    def dispatch(self, h: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, gather: bool = True):
+    def dispatch(self, h: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, gather: bool = True,
+                 n_experts: int | None = None, k: int | None = None):
+        """Stable counting sort of the (token, j) pairs by expert id; rows
+        gathered as bf16 when ``gather``.  ``n_experts``/``k`` override the
+        layer's (ZAYA routes over experts + 1 with k = 1)."""
+        E = self.E if n_experts is None else n_experts
+        k = self.k if k is None else k
         T, dev = ids.shape[0], ids.device
-        S = T * self.k
+        S = T * k
         nblk = self.lib.b200q_moe_num_blocks(T)
-        scratch = torch.empty((2, nblk * self.E), dtype=torch.int32, device=dev)
-        offsets = torch.empty(self.E + 1, dtype=torch.int32, device=dev)
+        scratch = torch.empty((2, nblk * E), dtype=torch.int32, device=dev)
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
         slot_of = torch.empty(S, dtype=torch.int32, device=dev)
         token_of = torch.empty(S, dtype=torch.int32, device=dev)
         slot_w = torch.empty(S, dtype=torch.float32, device=dev)
         xperm = torch.empty((S, self.D), dtype=torch.bfloat16, device=dev) if gather else None
         _lib.check(self.lib.b200q_moe_dispatch_dev(
-            ids.data_ptr(), w.data_ptr(), T, self.k, self.E, h.data_ptr() if gather else None, self.D,
+            ids.data_ptr(), w.data_ptr(), T, k, E, h.data_ptr() if gather else None, self.D,
             scratch[0].data_ptr(), scratch[1].data_ptr(), offsets.data_ptr(), slot_of.data_ptr(),
             token_of.data_ptr(), slot_w.data_ptr(), None if xperm is None else xperm.data_ptr(), _stream()))
         return offsets, slot_of, token_of, slot_w, xperm
@@ -179,12 +185,13 @@ class QuantMoE:
             None if slot_w is None else slot_w.data_ptr(), None, 0, max_ctas, _stream()))
         return out
 
-    def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int, slot_w: torch.Tensor | None = None):
+    def combine(self, out: torch.Tensor, slot_of: torch.Tensor, T: int, slot_w: torch.Tensor | None = None,
+                k: int | None = None):
         """y[t] = sum_j (slot_w) * out[slot(t, j)]; pass slot_w when out is unweighted."""
         y = torch.empty((T, self.D), dtype=torch.float32, device=out.device)
         _lib.check(self.lib.b200q_moe_combine_dev(out.data_ptr(), 1 if out.dtype == torch.bfloat16 else 0,
                                                   slot_of.data_ptr(), None if slot_w is None else slot_w.data_ptr(),
-                                                  T, self.k, self.D, y.data_ptr(), _stream()))
+                                                  T, self.k if k is None else k, self.D, y.data_ptr(), _stream()))
         return y
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:

@@ -18,6 +18,15 @@ What each function restates (paths are relative to the reference project):
   top-k (stable: larger value first, lower index wins ties, as np.argmax).
 * ``moe_forward_f64``                  engine/zaya.py:303-306 per token, summed
   over the k selected experts with the routing weights.
+* ``rmsnorm_f32``                      engine/model.py:82
+* ``gelu_exact``                       engine/zaya.py:181-186 (erf evaluated in
+  float64 per element, result rounded to f32)
+* ``zaya_router_f32``                  engine/zaya.py:278-296 router chain:
+  projection, EDA term, RMSNorm, two GELU layers, logits over E+1 routes,
+  softmax, top-1 over probs + route biases (first index on ties), weight =
+  the unbiased probability
+* ``zaya_moe_f64``                     engine/zaya.py:297-307: the selected
+  expert's FFN (or, for the skip route E, the block input) times its weight
 
 Rounding contract (bit-exact dequant): every product in the reference
 formulas is exact in f32 (fp16 ``d`` has 11 significant bits; 6-bit scales and
@@ -260,4 +269,64 @@ def moe_forward_f64(h, ids, weights, experts, t_gu, t_dn, d_model, d_ff, d_ff_pa
         out = expert_ffn_f64(experts[e][0], experts[e][1], t_gu, t_dn,
                              d_model, d_ff, d_ff_padded, h[rows])
         y[rows] += out * weights[rows, slots].astype(np.float64)[:, None]
+    return y
+
+
+def rmsnorm_f32(x, w, eps):
+    """x * (1 / sqrt(mean(x * x) + eps)) * w, f32 (engine/model.py:82)."""
+    x = np.asarray(x, np.float32)
+    return x * (np.float32(1.0) / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + np.float32(eps))) * w
+
+
+def gelu_exact(x):
+    """Exact GELU, erf in float64 per element (engine/zaya.py:181-186)."""
+    import math
+    flat = np.asarray(x, np.float32).reshape(-1)
+    out = np.fromiter((v * (1.0 + math.erf(float(v) / math.sqrt(2.0))) * 0.5 for v in flat),
+                      dtype=np.float32, count=flat.size)
+    return out.reshape(np.shape(x))
+
+
+def _linear_f32(x, w, b=None):
+    y = (np.asarray(x, np.float32) @ np.asarray(w, np.float32).T).astype(np.float32)
+    return y if b is None else (y + b).astype(np.float32)
+
+
+def zaya_router_f32(h, w_in, w_gate, w_mlp2, w_mlp4, norm_w, biases, eps, prev=None, w_eda=None,
+                    b_in=None, b_gate=None, b_mlp2=None, b_mlp4=None):
+    """Batched restatement of the router chain of engine/zaya.py:278-296.
+
+    Returns (expert [T], weight [T], probs [T, E+1], router_state [T, R]);
+    expert == E is the learned skip route.
+    """
+    r = _linear_f32(h, w_in, b_in)
+    if prev is not None and w_eda is not None:
+        r = (r + prev * w_eda).astype(np.float32)
+    state = r.copy()
+    r = rmsnorm_f32(r, norm_w, eps)
+    r = gelu_exact(_linear_f32(r, w_gate, b_gate))
+    r = gelu_exact(_linear_f32(r, w_mlp2, b_mlp2))
+    logits = _linear_f32(r, w_mlp4, b_mlp4)
+    logits = logits - logits.max(axis=-1, keepdims=True)
+    probs = np.exp(logits)
+    probs = (probs / probs.sum(axis=-1, keepdims=True)).astype(np.float32)
+    route = probs + biases
+    expert = np.argmax(route, axis=-1)
+    weight = probs[np.arange(len(expert)), expert]
+    return expert, weight, probs, state
+
+
+def zaya_moe_f64(h, expert, weight, experts, t_gu, t_dn, d_model, d_ff, d_ff_padded):
+    """engine/zaya.py:297-307 for a batch: y[t] = w[t] * FFN_e(h[t]), or
+    w[t] * h[t] for the skip route e == len(experts)."""
+    h = np.atleast_2d(np.asarray(h, np.float32))
+    E = len(experts)
+    y = np.zeros(h.shape, np.float64)
+    for e in np.unique(expert):
+        rows = np.nonzero(expert == e)[0]
+        if e == E:
+            out = h[rows].astype(np.float64)
+        else:
+            out = expert_ffn_f64(experts[e][0], experts[e][1], t_gu, t_dn, d_model, d_ff, d_ff_padded, h[rows])
+        y[rows] = out * weight[rows].astype(np.float64)[:, None]
     return y

@@ -208,3 +208,34 @@ def test_reference_q4k_is_approximate():
                            out.ctypes.data_as(ctypes.c_void_p), rows, cols, 4)
     err = o.normwise_rel_err(out, o.matvec_f64(raw, 12, rows, cols, x))
     assert 1e-3 < err < 5e-2
+
+
+def test_zaya_router_oracle_matches_reference_golden():
+    """The batched router-chain restatement reproduces the reference's own
+    ZayaModel._moe (engine/zaya.py:274-307) on the committed fixture: same
+    routes (skip route included), router state and block output to f32
+    accuracy (the fixture's experts are f32 matrices)."""
+    d = np.load(Path(__file__).resolve().parent / 'golden' / 'zaya_moe_golden.npz')
+    H, P = d['H'], d['P']
+    T = H.shape[0]
+    use_prev = (np.arange(T) % 3) != 0
+    Pm = np.where(use_prev[:, None], P, 0.0).astype(np.float32)
+    # rows without a previous router state: EDA term absent (zero prev is the same)
+    e, w, probs, state = o.zaya_router_f32(H, d['ffn_gate_inp_weight'], d['ffn_gate_weight'],
+                                           d['zaya_router_mlp2_weight'], d['zaya_router_mlp4_weight'],
+                                           d['ffn_norm_weight'], d['zaya_router_biases_weight'], float(d['eps']),
+                                           prev=Pm, w_eda=d['zaya_router_eda_weight'], b_in=d['b_in'])
+    np.testing.assert_allclose(state, d['S'], rtol=1e-5, atol=1e-6)
+    E = d['gu'].shape[0]
+    y = np.zeros_like(H, dtype=np.float64)
+    for t in range(T):
+        if e[t] == E:
+            y[t] = H[t] * w[t]
+        else:
+            g = d['gu'][e[t]] @ H[t]
+            F = g.shape[0] // 2
+            act = o.silu(g[:F]) * g[F:]
+            y[t] = (d['dn'][e[t]] @ act) * w[t]
+    ref_routes_skip = np.sum(e == E)
+    assert ref_routes_skip > 0 and ref_routes_skip < T          # the fixture exercises both kinds
+    assert o.normwise_rel_err(y, d['Y']) < 1e-5
