@@ -486,22 +486,11 @@ def main():
         sampler.start()
         time.sleep(1.0)
     barrier()
-    # warm-up: at least W steps and at least WARM_S seconds of back-to-back
-    # work, so that the timed steps run at the clocks the GPU holds under load
-    # (after the CPU-side set-up an idle GPU needs some time to ramp up); every
-    # rank runs the same number of steps (rank 0 decides)
-    WARM_S = 0.3
-    t_w = time.time()
+    # warm-up: W steps (more would push the part into its power-capped
+    # regime before the timed region; it idles at full clock)
     for _ in range(args.warmup):
         step(h)
-    torch.cuda.synchronize()
-    per = max(1e-4, (time.time() - t_w) / args.warmup)
-    extra = torch.tensor([max(0, int(WARM_S / per) + 1 - args.warmup)], device=dev)
-    if world > 1:
-        dist.broadcast(extra, 0)
-    for _ in range(int(extra.item())):
-        step(h)
-    warm_steps = args.warmup + int(extra.item())
+    warm_steps = args.warmup
     torch.cuda.synchronize()
     ops.check_device_error()
 
