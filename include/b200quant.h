@@ -137,10 +137,29 @@ int b200q_gelu_dev(float *x, long long n, void *stream);
  * output rows of ZAYA's skip route are the routed input rows. */
 int b200q_copy_rows_range_dev(const void *src_bf16, void *dst_bf16, const int *offsets, int group, int D,
                               int max_rows, void *stream);
-/* Dense FFN activation (engine/model.py:161-166): out[t, f] =
+/* Dense FFN activation (engine/model.py:161-166): out[t * ld_out + f] =
  * silu(gu[t, f]) * gu[t, F + f] for f32 gu [T, 2F] (gate columns, then up
- * columns) and out [T, F]; silu(g) = g / (1 + exp(-clip(g, -80, 80))). */
-int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, void *stream);
+ * columns), ld_out >= F; silu(g) = g / (1 + exp(-clip(g, -80, 80))). */
+int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, long long ld_out, void *stream);
+/* Grouped decode GEMV (MoE experts at small batch): for every group g with
+ * tokens n_g = grp_off[g+1] - grp_off[g] (device array, e.g. the dispatch
+ * offsets; every n_g <= max_tokens <= 64), y[grp_off[g] + t, r] =
+ * sum_c W_g[r, c] * x[grp_off[g] + t, c] for r < rows, with W_g = the raw
+ * GGUF rows at w + g * w_group_stride bytes, x f32 rows of cols values, y
+ * rows ys_t floats apart; weight rows w_row_bytes apart (0: packed; a padded
+ * stride's tail bytes are not read).  Groups without tokens read no weights.
+ * active_groups: how many groups are expected to hold tokens (sizes the
+ * grid).  max_tokens may not exceed b200q_gemv_grouped_max_tokens(type, cols)
+ * (the quantised activations of one group live in shared memory).  x and y
+ * hold x_rows rows; a group whose offsets fall outside them (or exceed
+ * max_tokens) is skipped and the device error word set (B200Q_EINDEX).  f32
+ * accumulation as b200q_gemv_dev. */
+int b200q_gemv_grouped_max_tokens(int ggml_type, int cols);
+int b200q_gemv_grouped_dev(int ggml_type, const void *w, long long w_group_stride, long long w_row_bytes,
+                           int n_groups, const int *grp_off, const float *x, float *y, long long ys_t, int rows,
+                           int cols, int max_tokens, int x_rows, int active_groups, void *stream);
+/* out[s, :] = h[token_of[s], :] for s < S (f32 rows of D values, D % 4 == 0). */
+int b200q_moe_gather_f32_dev(const float *h, const int *token_of, int S, int D, float *out, void *stream);
 /* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
  * weights.  w_row_bytes is the byte distance between weight rows (0: packed
  * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed

@@ -47,7 +47,10 @@ SIGNATURES = {
     'b200q_zaya_router_prep_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp, _vp]),
     'b200q_gelu_dev': (_i, [_vp, _ll, _vp]),
     'b200q_copy_rows_range_dev': (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
-    'b200q_silu_mul_dev': (_i, [_vp, _i, _i, _vp, _vp]),
+    'b200q_silu_mul_dev': (_i, [_vp, _i, _i, _vp, _ll, _vp]),
+    'b200q_gemv_grouped_max_tokens': (_i, [_i, _i]),
+    'b200q_gemv_grouped_dev': (_i, [_i, _vp, _ll, _ll, _i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
+    'b200q_moe_gather_f32_dev': (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
                             _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),

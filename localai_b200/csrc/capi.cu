@@ -65,7 +65,13 @@ cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const
 cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaStream_t st);
 cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
 
-cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, int num_sms, cudaStream_t st);
+cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, long long ld_out, int num_sms, cudaStream_t st);
+cudaError_t launch_gemv_grouped(int type, const void *w, long long w_group_stride, int n_groups, const int *grp_off,
+                                const float *x, float *y, long long ys_t, int rows, int cols, int max_tokens,
+                                int x_rows, int active_groups, long long row_stride, int *err, int num_sms,
+                                cudaStream_t st);
+int gemv_grouped_max_tokens(int type, int cols);
+cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st);
 cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
                                     int R, float eps, float *state, float *out, cudaStream_t st);
 cudaError_t launch_gelu(float *x, long long n, int num_sms, cudaStream_t st);
@@ -470,14 +476,43 @@ B200Q_API int b200q_copy_rows_range_dev(const void *src_bf16, void *dst_bf16, co
                        "copy_rows_range");
 }
 
-B200Q_API int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, void *stream)
+B200Q_API int b200q_silu_mul_dev(const float *gate_up, int T, int F, float *out, long long ld_out, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!gate_up || !out) return set_status(B200Q_EINVAL, "silu_mul: null pointer");
+    if (ld_out < F) return set_status(B200Q_EINVAL, "silu_mul: ld_out < F");
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_silu_mul(gate_up, T, F, out, di->sms, (cudaStream_t)stream), "silu_mul");
+    return cuda_status(launch_silu_mul(gate_up, T, F, out, ld_out, di->sms, (cudaStream_t)stream), "silu_mul");
+}
+
+B200Q_API int b200q_gemv_grouped_max_tokens(int ggml_type, int cols) { return gemv_grouped_max_tokens(ggml_type, cols); }
+
+B200Q_API int b200q_gemv_grouped_dev(int ggml_type, const void *w, long long w_group_stride, long long w_row_bytes,
+                                     int n_groups, const int *grp_off, const float *x, float *y, long long ys_t,
+                                     int rows, int cols, int max_tokens, int x_rows, int active_groups, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!w || !x || !y || !grp_off) return set_status(B200Q_EINVAL, "gemv_grouped: null pointer");
+    if ((reinterpret_cast<uintptr_t>(w) & 1) || (reinterpret_cast<uintptr_t>(x) & 15) || (w_group_stride & 1))
+        return set_status(B200Q_EINVAL, "gemv_grouped: weights must be 2-byte and x 16-byte aligned");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    if (w_row_bytes & 1) return set_status(B200Q_EINVAL, "gemv_grouped: odd row stride");
+    return cuda_status(launch_gemv_grouped(ggml_type, w, w_group_stride, n_groups, grp_off, x, y, ys_t, rows, cols,
+                                           max_tokens, x_rows, active_groups, w_row_bytes, di->err, di->sms,
+                                           (cudaStream_t)stream),
+                       "gemv_grouped");
+}
+
+B200Q_API int b200q_moe_gather_f32_dev(const float *h, const int *token_of, int S, int D, float *out, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h || !token_of || !out) return set_status(B200Q_EINVAL, "gather_f32: null pointer");
+    ++g_launches;
+    return cuda_status(launch_moe_gather_f32(h, token_of, S, D, out, (cudaStream_t)stream), "gather_f32");
 }
 
 B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,

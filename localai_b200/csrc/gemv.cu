@@ -47,6 +47,14 @@ struct GemvArgs {
     int stage_bytes;      // bytes per shared stage buffer
     int stages;
     int *err;
+    // grouped mode (grp_off != nullptr): blockIdx.y = group g, whose weights
+    // start at w + g * w_group_stride and whose tokens are rows
+    // [grp_off[g], grp_off[g+1]) of x and y (at most ``tokens`` of them)
+    const int *grp_off;
+    long long w_group_stride;
+    int grp_rows;         // rows of x and y: every group's range must lie inside
+    int n_groups;         // host side: grid.y
+    int active_groups;    // host side: groups expected to hold tokens (sizes grid.x)
 };
 
 // Unit geometry per type: values per unit, units per block, x words per unit.
@@ -478,8 +486,31 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
     const int ncons = a.groups * a.nct;
     const int nwarps_c = ncons >> 5;
     const int nwg = a.nct >> 5;                                   // warps per group
-    const int npass = (a.tokens + NTOK - 1) / NTOK;
-    const int slot_floats = npass * nwarps_c * V;                  // partials of one stage
+    const uint8_t *wsrc = a.w;
+    const float *xsrc = a.x;
+    float *ydst = a.y;
+    int tokens = a.tokens;
+    if (a.grp_off) {
+        // which experts run, and on how many tokens, comes from the previous kernel
+        pdl_wait();
+        const int t0 = a.grp_off[blockIdx.y], t1 = a.grp_off[blockIdx.y + 1];
+        if (t0 < 0 || t1 < t0 || t1 > a.grp_rows || t1 - t0 > a.tokens) {      // offsets not usable: touch nothing
+            if (threadIdx.x == 0) atomicExch(a.err, ERR_BAD_INDEX);
+            pdl_launch_dependents();
+            return;
+        }
+        tokens = t1 - t0;
+        if (tokens == 0) {
+            pdl_launch_dependents();
+            return;
+        }
+        wsrc += (long long)blockIdx.y * a.w_group_stride;
+        xsrc += (long long)t0 * a.cols;
+        ydst += (long long)t0 * a.ys_t;
+    }
+    const int npass = (tokens + NTOK - 1) / NTOK;
+    const int npass_max = (a.tokens + NTOK - 1) / NTOK;           // shared layout is sized for a.tokens
+    const int slot_floats = npass_max * nwarps_c * V;             // partials of one stage
     const uint32_t sbase = smem_addr(smem);
     const uint32_t full0 = sbase, empty0 = sbase + 8 * a.stages;
     float *red = reinterpret_cast<float *>(smem + 128);
@@ -525,11 +556,11 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
                     const int g = pg % a.groups, pass = pg / a.groups;
                     const int rr = vi / NTOK, t = vi % NTOK;
                     const int lr = g + rr * a.groups, tok = pass * NTOK + t;
-                    if (lr < nr && tok < a.tokens) {
+                    if (lr < nr && tok < tokens) {
                         const float *pp = slot + (pass * nwarps_c + g * nwg) * V + vi;
                         float v = 0.f;
                         for (int w = 0; w < nwg; ++w) v += pp[w * V];
-                        a.y[tok * a.ys_t + (row0 + lr) * a.ys_r] = v;
+                        ydst[tok * a.ys_t + (row0 + lr) * a.ys_r] = v;
                     }
                 }
                 __syncwarp();
@@ -537,7 +568,7 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
             if (it < n_it && lane == 0) {
                 const long long row0 = r_begin + (long long)it * a.stage_rows;
                 const int nr = (int)min((long long)a.stage_rows, r_end - row0);
-                const uint8_t *gs = a.w + row0 * a.rb;
+                const uint8_t *gs = wsrc + row0 * a.rb;
                 const uint8_t *ge = gs + (long long)nr * a.rb;
                 const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(gs) & ~(uintptr_t)15);
                 const uint8_t *a1 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(ge) & ~(uintptr_t)15);
@@ -579,7 +610,7 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
     }
     XU<NW> X[CPT][NTOK];
     pdl_wait();                                          // x may come from the previous kernel
-    quantize_x_smem<T>(a.x, a.cols, a.units, a.tokens, xbuf, tid, ncons);
+    quantize_x_smem<T>(xsrc, a.cols, a.units, tokens, xbuf, tid, ncons);
     named_bar_sync(1, ncons);
     auto load_x = [&](int pass) {
 #pragma unroll
@@ -587,7 +618,7 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
 #pragma unroll
             for (int t = 0; t < NTOK; ++t) {
                 const int tok = pass * NTOK + t;
-                const bool v = uval[i] && tok < a.tokens;
+                const bool v = uval[i] && tok < tokens;
                 load_unit_x<T>(xbuf + (uint32_t)(((v ? tok : 0) * a.units + uidx[i]) * NX * 4), v, X[i][t]);
             }
     };
@@ -598,7 +629,7 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
         if (!mbar_wait(full0 + 8 * s, (it / a.stages) & 1, a.err)) return;
         const long long row0 = r_begin + (long long)it * a.stage_rows;
         const int nr = (int)min((long long)a.stage_rows, r_end - row0);
-        const uintptr_t gs = reinterpret_cast<uintptr_t>(a.w + row0 * a.rb);
+        const uintptr_t gs = reinterpret_cast<uintptr_t>(wsrc + row0 * a.rb);
         const uint32_t base = stage0 + (uint32_t)s * a.stage_bytes + (uint32_t)(gs & 15);
         float *slot = red + s * slot_floats;
         for (int pass = 0; pass < npass; ++pass) {
@@ -700,8 +731,9 @@ static cudaError_t run_cfg(GemvArgs a, int threads, size_t smem, int num_sms, cu
     if (g_ctas_per_sm > 0 && per_sm > g_ctas_per_sm) per_sm = g_ctas_per_sm;
     const long long tiles = (a.rows + a.stage_rows - 1) / a.stage_rows;
     long long grid = (long long)num_sms * per_sm;
+    if (a.grp_off) grid = (grid + a.active_groups - 1) / a.active_groups;
     if (grid > tiles) grid = tiles;
-    return launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, st, a);
+    return launch_pdl(kern, dim3((unsigned)grid, a.grp_off ? (unsigned)a.n_groups : 1u), dim3(threads), smem, st, a);
 }
 
 template <int T, int CPT, int NTOK, int RPG>
@@ -740,7 +772,9 @@ static cudaError_t run_type(GemvArgs a, int cpt, int ntok, int rpg, int threads,
 
 // One launch over tokens [0, tokens) of the given x/y.
 static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r,
-                                     int rows, int cols, int tokens, int *err, int num_sms, cudaStream_t st)
+                                     int rows, int cols, int tokens, int *err, int num_sms, cudaStream_t st,
+                                     const int *grp_off = nullptr, long long w_group_stride = 0, int n_groups = 0,
+                                     int active_groups = 1, long long row_stride = 0, int grp_rows = 0)
 {
     const int vals = type_vals(type), bytes = type_bytes(type);
     const int upb = (vals == 256) ? 4 : 1;     // 64-value units in a K-quant block
@@ -758,7 +792,9 @@ static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, fl
         if (n + 32 <= cp) { cpt = c; ntok = nt; nct = n; cap = cp; }
     }
     if (!cpt) return cudaErrorInvalidValue;
-    const int rb = (cols / vals) * bytes;
+    // bytes between rows: packed, or a caller's padded stride (the padding is never read)
+    const int rb = row_stride ? (int)row_stride : (cols / vals) * bytes;
+    if (rb < (cols / vals) * bytes) return cudaErrorInvalidValue;
     int rpg = 1;
     if (cpt * ntok == 1) {
         if (g_rpg_max >= 4 && 4 * rb <= g_stage_target / 2) rpg = 4;
@@ -793,8 +829,13 @@ static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, fl
     a.stage_bytes = stage_bytes;
     a.stages = stages;
     a.err = err;
+    a.grp_off = grp_off;
+    a.w_group_stride = w_group_stride;
+    a.grp_rows = grp_rows;
+    a.n_groups = n_groups;
+    a.active_groups = std::max(1, std::min(active_groups, std::max(1, n_groups)));
     const int threads = groups * nct + 32;
-    const bool al = (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (rb & 15) == 0;
+    const bool al = (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (rb & 15) == 0 && (w_group_stride & 15) == 0;
     switch (type) {
     case T_Q4_K: return run_type<T_Q4_K>(a, cpt, ntok, rpg, threads, smem, num_sms, st, al);
     case T_Q5_K: return run_type<T_Q5_K>(a, cpt, ntok, rpg, threads, smem, num_sms, st, al);
@@ -825,6 +866,30 @@ cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long 
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+// Grouped launch: for every group g with tokens (grp_off[g+1] - grp_off[g],
+// at most max_tokens <= 64), y[grp_off[g] + t, r] = sum_c W_g[r, c] * x[grp_off[g] + t, c]
+// with W_g at w + g * w_group_stride.  Groups without tokens read nothing.
+int gemv_grouped_max_tokens(int type, int cols)
+{
+    const int vals = type_vals(type), bytes = type_bytes(type);
+    if (!bytes || cols < vals || cols % vals) return 0;
+    const int units = (cols / vals) * ((vals == 256) ? 4 : 1);
+    const size_t per_tok = (size_t)units * ((vals == 256) ? XPackWords<16>::N : XPackWords<8>::N) * 4;
+    return (int)std::min<size_t>(64, (128 * 1024) / per_tok);
+}
+
+cudaError_t launch_gemv_grouped(int type, const void *w, long long w_group_stride, int n_groups, const int *grp_off,
+                                const float *x, float *y, long long ys_t, int rows, int cols, int max_tokens,
+                                int x_rows, int active_groups, long long row_stride, int *err, int num_sms,
+                                cudaStream_t st)
+{
+    if (rows < 1 || max_tokens < 1 || n_groups < 1 || !grp_off || x_rows < 1 ||
+        max_tokens > gemv_grouped_max_tokens(type, cols))
+        return cudaErrorInvalidValue;
+    return launch_gemv_chunk(type, w, x, y, ys_t, 1, rows, cols, max_tokens, err, num_sms, st, grp_off,
+                             w_group_stride, n_groups, active_groups, row_stride, x_rows);
 }
 
 } // namespace b200q

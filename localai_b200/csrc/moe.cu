@@ -291,6 +291,26 @@ __global__ void __launch_bounds__(256) moe_assign_kernel(const int *__restrict__
     }
 }
 
+// out[slot, :] = h[token_of[slot], :] (f32, for the GEMV decode path); one warp per row.
+__global__ void moe_gather_f32_kernel(const float *__restrict__ h, const int *__restrict__ token_of, long long S, int D,
+                                      float *__restrict__ out)
+{
+    const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= S) return;
+    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)token_of[row] * D);
+    float4 *dst = reinterpret_cast<float4 *>(out + row * D);
+    for (int c = lane; c < D / 4; c += 32) dst[c] = __ldg(src + c);
+}
+
+cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st)
+{
+    if (S < 1 || D < 4 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    moe_gather_f32_kernel<<<(unsigned)(((long long)S * 32 + 255) / 256), 256, 0, st>>>(h, token_of, S, D, out);
+    return cudaGetLastError();
+}
+
 // xperm[slot, :] = bf16(h[token_of[slot], :]); one warp per slot row.
 __global__ void moe_gather_kernel(const float *__restrict__ h, const int *__restrict__ token_of, long long S, int D,
                                   __nv_bfloat16 *__restrict__ xperm)

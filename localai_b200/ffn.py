@@ -69,7 +69,7 @@ class QuantFFN:
         if not use_gemm:
             gu = ops.gemv(self.gate_up, x2, self.t_gu, 2 * self.F, self.D)
             act = torch.empty((T, self.F), dtype=torch.float32, device=dev)
-            _lib.check(self.lib.b200q_silu_mul_dev(gu.data_ptr(), T, self.F, act.data_ptr(), _stream()))
+            _lib.check(self.lib.b200q_silu_mul_dev(gu.data_ptr(), T, self.F, act.data_ptr(), self.F, _stream()))
             y = ops.gemv(self.down, act, self.t_dn, self.D, self.F)
         else:
             gu_w, s_gu, dn_w, s_dn = self._gemm_weights()

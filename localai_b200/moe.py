@@ -112,6 +112,9 @@ class QuantMoE:
         self.gate_up, self.gu_stride = pad_rows(self.gate_up, self.E_held * 2 * d_ff, rb_gu)
         self.down, self.dn_stride = pad_rows(self.down, self.E_held * d_model, rb_dn)
         self.lib = _lib.load()
+        # decode-sized batches (T * k slots up to this) take the grouped GEMV path
+        self.small_slots = min(self.lib.b200q_gemv_grouped_max_tokens(ggml_type, d_model),
+                               self.lib.b200q_gemv_grouped_max_tokens(ggml_type, self.F_pad))
 
     # -- stages ---------------------------------------------------------------
     def route(self, h: torch.Tensor):
@@ -194,12 +197,44 @@ class QuantMoE:
                                                   T, self.k if k is None else k, self.D, y.data_ptr(), _stream()))
         return y
 
+    def experts_small(self, h: torch.Tensor, offsets: torch.Tensor, token_of: torch.Tensor, *,
+                      n_groups: int | None = None):
+        """Decode path: f32 rows of the routed tokens through grouped GEMVs
+        (gate/up, silu*up, down) with f32 accumulation; returns unweighted
+        f32 [slots, D].  Experts without tokens read no weights."""
+        S, dev = token_of.numel(), h.device
+        G = self.E_held if n_groups is None else n_groups
+        xs = torch.empty((S, self.D), dtype=torch.float32, device=dev)
+        _lib.check(self.lib.b200q_moe_gather_f32_dev(h.data_ptr(), token_of.data_ptr(), S, self.D, xs.data_ptr(),
+                                                     _stream()))
+        gu = torch.empty((S, 2 * self.F), dtype=torch.float32, device=dev)
+        active = max(1, min(G, S))
+        _lib.check(self.lib.b200q_gemv_grouped_dev(
+            self.type, self.gate_up.data_ptr(), 2 * self.F * self.gu_stride, self.gu_stride, G, offsets.data_ptr(),
+            xs.data_ptr(), gu.data_ptr(), 2 * self.F, 2 * self.F, self.D, S, S, active, _stream()))
+        if self.F_pad != self.F:
+            act = torch.zeros((S, self.F_pad), dtype=torch.float32, device=dev)
+        else:
+            act = torch.empty((S, self.F_pad), dtype=torch.float32, device=dev)
+        _lib.check(self.lib.b200q_silu_mul_dev(gu.data_ptr(), S, self.F, act.data_ptr(), self.F_pad, _stream()))
+        out = torch.empty((S, self.D), dtype=torch.float32, device=dev)
+        _lib.check(self.lib.b200q_gemv_grouped_dev(
+            self.type, self.down.data_ptr(), self.D * self.dn_stride, self.dn_stride, G, offsets.data_ptr(),
+            act.data_ptr(), out.data_ptr(), self.D, self.D, self.F_pad, S, S, active, _stream()))
+        return out
+
     def forward(self, h: torch.Tensor) -> torch.Tensor:
-        """y[T, D] for hidden states h[T, D] (f32)."""
+        """y[T, D] for hidden states h[T, D] (f32).  Up to ``small_slots``
+        routed rows take the grouped-GEMV decode path (f32 accumulation),
+        larger batches the tensor-core path (bf16 operands)."""
         if h.dtype != torch.float32 or not h.is_cuda or h.dim() != 2 or h.shape[1] != self.D:
             raise ValueError('h must be a CUDA f32 [T, d_model] tensor')
         h = h.contiguous()
         _, ids, w = self.route(h)
+        if h.shape[0] * self.k <= self.small_slots:
+            offsets, slot_of, token_of, slot_w, _ = self.dispatch(h, ids, w, gather=False)
+            out = self.experts_small(h, offsets, token_of)
+            return self.combine(out, slot_of, h.shape[0], slot_w)
         offsets, slot_of, _, slot_w, xperm = self.dispatch(h, ids, w)
         out = self.experts(xperm, offsets, slot_w)
         return self.combine(out, slot_of, h.shape[0])
