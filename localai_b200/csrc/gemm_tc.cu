@@ -185,10 +185,12 @@ __device__ __forceinline__ float silu_ref(float g)
 // ---------------------------------------------------------------- dequant
 // Q4_K: one K-step (pair p of a super-block) of one tile row and one half
 // (h = 0: sub-block 2p, low nibbles -> K columns 0..31; h = 1: sub-block
-// 2p+1, high nibbles -> K columns 32..63) into the SWIZZLE_128B A tile.
-__device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, int p, int h, uint32_t a_row, int r)
+// 2p+1, high nibbles -> K columns 32..63) into the SWIZZLE_128B A tile.  The
+// block header (d, dmin, scales) is passed in: it serves all four K-steps of
+// the block and is read from shared memory once per block.
+__device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, const uint4 hdr, int p, int h, uint32_t a_row,
+                                                 int r)
 {
-    const uint4 hdr = lds128(raw_row);
     const uint4 q0 = lds128(raw_row + 16 + 32 * p), q1 = lds128(raw_row + 32 + 32 * p);
     // bytes [sc(2p), sc(2p+1), mn(2p), mn(2p+1)] (engine/dequant.py:108-113)
     const uint32_t sp = k_scales_packed(hdr, p);
@@ -588,6 +590,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // raw row of tile row r
         const int raw_r = gate_up ? ((l < 16) ? 16 * ew + (l & 15) : 64 + 16 * ew + (l & 15)) : r;
         int q = 0, rq = 0;
+        uint4 hdr = make_uint4(0, 0, 0, 0);
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < ksteps && ok; ++ks) {
                 const int rs = rq % TC_RAW_STAGES;
@@ -596,7 +599,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (q >= TC_A_STAGES && !mbar_wait(empty_a + 8 * s, ((q / TC_A_STAGES) + 1) & 1, a.err)) { ok = false; break; }
                 const uint32_t raw_row = sRaw + rs * raw_stage_bytes + (uint32_t)(raw_r * a.raw_chunk_bytes);
                 const uint32_t a_row = sA + s * TC_A_BYTES + (uint32_t)(r * 128);
-                if (WT == T_Q4_K) dequant_q4k_half(raw_row, ks & 3, h, a_row, r);
+                if (WT == T_Q4_K) {
+                    if ((ks & 3) == 0) hdr = lds128(raw_row);
+                    dequant_q4k_half(raw_row, hdr, ks & 3, h, a_row, r);
+                }
                 else if (WT == T_Q6_K) dequant_q6k_half(raw_row + (uint32_t)(((ks >> 2) * 210) & 15), ks & 3, h, a_row, r);
                 else dequant_q8_0_half(raw_row, ks & 3, h, a_row, r);
                 fence_proxy_async_smem();
