@@ -71,6 +71,17 @@ cudaError_t launch_gemv_grouped(int type, const void *w, long long w_group_strid
                                 int x_rows, int active_groups, long long row_stride, int *err, int num_sms,
                                 cudaStream_t st);
 int gemv_grouped_max_tokens(int type, int cols);
+cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
+                               float *out, int *err, cudaStream_t st);
+cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
+                               cudaStream_t st);
+cudaError_t launch_rope_kv(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos, float *kc,
+                           float *vc, int max_seq, int *err, cudaStream_t st);
+size_t attn_scratch_floats(int H, int hd, int max_seq);
+cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
+                               int max_seq, float *part, float *out, cudaStream_t st);
+cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
+                          cudaStream_t st);
 cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st);
 cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
                                     int R, float eps, float *state, float *out, cudaStream_t st);
@@ -731,4 +742,65 @@ B200Q_API int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *sl
         e = launch_moe_combine(ep_ret_rows(ep), true, slot_of, slot_w, T, k, ep_d_model(ep), y, st);
     g_launches += 2;
     return cuda_status(e, "ep_combine");
+}
+
+// ---------------------------------------------------------------- decode step (Llama)
+B200Q_API int b200q_dequant_row_dev(int ggml_type, const void *raw, long long row_bytes, int cols, const int *row_idx,
+                                    int rows, float *out, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!raw || !row_idx || !out) return set_status(B200Q_EINVAL, "dequant_row: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_dequant_row(ggml_type, raw, row_bytes, cols, row_idx, rows, out, di->err,
+                                          (cudaStream_t)stream),
+                       "dequant_row");
+}
+
+B200Q_API int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
+                                    void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!x || !w || !h) return set_status(B200Q_EINVAL, "add_rmsnorm: null pointer");
+    ++g_launches;
+    return cuda_status(launch_add_rmsnorm(x, delta, w, T, D, eps, h, (cudaStream_t)stream), "add_rmsnorm");
+}
+
+B200Q_API int b200q_rope_kv_dev(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos,
+                                float *k_cache, float *v_cache, int max_seq, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!qkv || !pos || !k_cache || !v_cache) return set_status(B200Q_EINVAL, "rope_kv: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += 2;
+    return cuda_status(launch_rope_kv(qkv, H, KV, hd, rotary, base, pos, k_cache, v_cache, max_seq, di->err,
+                                      (cudaStream_t)stream),
+                       "rope_kv");
+}
+
+B200Q_API size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq)
+{
+    return attn_scratch_floats(H, hd, max_seq);
+}
+
+B200Q_API int b200q_attn_decode_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H,
+                                    int KV, int hd, int max_seq, float *scratch, float *out, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!q || !k_cache || !v_cache || !pos || !scratch || !out) return set_status(B200Q_EINVAL, "attn: null pointer");
+    g_launches += 2;
+    return cuda_status(launch_attn_decode(q, k_cache, v_cache, pos, H, KV, hd, max_seq, scratch, out,
+                                          (cudaStream_t)stream),
+                       "attn_decode");
+}
+
+B200Q_API int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
+                               void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!logits || !token) return set_status(B200Q_EINVAL, "argmax: null pointer");
+    ++g_launches;
+    return cuda_status(launch_argmax(logits, V, token, pos, out_tokens, max_tokens, (cudaStream_t)stream), "argmax");
 }

@@ -142,4 +142,46 @@ cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, l
     return launch_dequant_t<__nv_bfloat16>(type, raw, out, nblocks, num_sms, st);
 }
 
+// One row of a quantised [rows, cols] matrix, the row index read from device
+// memory (the token embedding lookup of a decode step whose token is chosen on
+// the device): out[c] = dequant(raw row *row_idx)[c], bit-exact as above.
+template <int T>
+__global__ void dequant_row_kernel(const uint8_t *__restrict__ raw, long long row_bytes, int cols,
+                                   const int *__restrict__ row_idx, int rows, float *__restrict__ out, int *err)
+{
+    const int r = *row_idx;
+    if (r < 0 || r >= rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
+        return;
+    }
+    const long long runs = cols / 32;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < runs; i += (long long)gridDim.x * blockDim.x) {
+        const long long vals = Fmt<T>::VALS;
+        const long long blk = (i * 32) / vals;
+        const int sub = (int)((i * 32 - blk * vals) / 32);
+        float v[32];
+        decode_run<T>(raw + r * row_bytes + blk * Fmt<T>::BYTES, sub, v);
+        float4 *o = reinterpret_cast<float4 *>(out + i * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+}
+
+cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
+                               float *out, int *err, cudaStream_t st)
+{
+    if (cols < 32 || cols % type_vals(type) || (reinterpret_cast<uintptr_t>(out) & 15)) return cudaErrorInvalidValue;
+    const int runs = cols / 32, threads = 128, grid = (runs + threads - 1) / threads;
+    const uint8_t *r = static_cast<const uint8_t *>(raw);
+    switch (type) {
+    case T_Q4_0: dequant_row_kernel<T_Q4_0><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    case T_Q8_0: dequant_row_kernel<T_Q8_0><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    case T_Q4_K: dequant_row_kernel<T_Q4_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    case T_Q5_K: dequant_row_kernel<T_Q5_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    case T_Q6_K: dequant_row_kernel<T_Q6_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
 } // namespace b200q

@@ -1,0 +1,187 @@
+"""Greedy decode of the reference's Llama decoder on the GPU.
+
+``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama', no RoPE
+scaling) runs one token through every layer with NumPy and the native
+quantised matvecs.  ``QuantLlama`` keeps every weight on the device in its raw
+GGUF form and runs one token per *step*:
+
+    x = emb[token]                                  b200q_dequant_row_dev
+    per layer:
+        h = rmsnorm(x) * attn_norm                  b200q_add_rmsnorm_dev
+        qkv = [Wq; Wk; Wv] h                        b200q_gemv_dev (one GEMV)
+        rope(q, k); cache[pos] = k, v               b200q_rope_kv_dev
+        att = softmax(q k^T / sqrt(hd)) v           b200q_attn_decode_dev
+        x += Wo att; h = rmsnorm(x) * ffn_norm      b200q_gemv_dev, b200q_add_rmsnorm_dev
+        x += Wdown silu([Wgate; Wup] h)             b200q_gemv_dev, b200q_silu_mul_dev, b200q_gemv_dev
+    logits = Wout (rmsnorm(x) * output_norm)        b200q_gemv_dev
+    token = argmax(logits); pos += 1                b200q_argmax_dev
+
+The position and the token live in device memory, so a step is captured once
+in a CUDA graph and replayed per token without host synchronisation
+(``capture()``); prompt tokens are fed by overwriting the device token before
+each step.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops
+from .moe import _stream
+
+
+@dataclass
+class LlamaConfig:
+    n_layers: int
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    d_ff: int
+    vocab: int
+    rope_base: float = 10000.0
+    rope_dim: int | None = None       # default: head_dim
+    eps: float = 1e-5
+    max_seq: int = 2048
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.n_heads
+
+
+class QuantLlama:
+    """``weights``: ``{'token_embd': (raw, type), 'output': (raw, type),
+    'output_norm': f32, 'layers': [ {'attn_q': (raw, type), 'attn_k', 'attn_v',
+    'attn_output', 'ffn_gate', 'ffn_up', 'ffn_down': (raw, type),
+    'attn_norm': f32, 'ffn_norm': f32}, ... ]}`` with raw uint8 CUDA tensors of
+    GGUF blocks (rows = output features) and f32 CUDA norm vectors."""
+
+    def __init__(self, weights: dict, cfg: LlamaConfig):
+        self.cfg = c = cfg
+        if c.d_model % c.n_heads or c.n_heads % c.n_kv_heads:
+            raise ValueError('heads must divide d_model and kv heads must divide heads')
+        self.lib = _lib.load()
+        hd = c.head_dim
+        self.rotary = min(c.rope_dim or hd, hd)
+        self.rotary -= self.rotary % 2
+        dev = weights['output_norm'].device
+        self.dev = dev
+        self.emb, self.t_emb = weights['token_embd']
+        self.out_w, self.t_out = weights['output']
+        self.out_norm = weights['output_norm'].float().contiguous()
+        self.layers = []
+        for lw in weights['layers']:
+            tq = lw['attn_q'][1]
+            if lw['attn_k'][1] != tq or lw['attn_v'][1] != tq or lw['ffn_up'][1] != lw['ffn_gate'][1]:
+                raise ValueError('q/k/v and gate/up must share their GGML type')
+            self.layers.append({
+                'qkv': (torch.cat([lw['attn_q'][0].reshape(-1), lw['attn_k'][0].reshape(-1),
+                                   lw['attn_v'][0].reshape(-1)]), tq),
+                'o': lw['attn_output'],
+                'gu': (torch.cat([lw['ffn_gate'][0].reshape(-1), lw['ffn_up'][0].reshape(-1)]), lw['ffn_gate'][1]),
+                'down': lw['ffn_down'],
+                'attn_norm': lw['attn_norm'].float().contiguous(),
+                'ffn_norm': lw['ffn_norm'].float().contiguous(),
+            })
+        f32 = dict(dtype=torch.float32, device=dev)
+        kvd = c.n_kv_heads * hd
+        self.k_cache = torch.zeros((c.n_layers, c.max_seq, kvd), **f32)
+        self.v_cache = torch.zeros((c.n_layers, c.max_seq, kvd), **f32)
+        self.x = torch.zeros(c.d_model, **f32)
+        self.h = torch.zeros(c.d_model, **f32)
+        self.qkv = torch.zeros(c.n_heads * hd + 2 * kvd, **f32)
+        self.att = torch.zeros(c.d_model, **f32)
+        self.o = torch.zeros(c.d_model, **f32)
+        self.gu = torch.zeros(2 * c.d_ff, **f32)
+        self.act = torch.zeros(c.d_ff, **f32)
+        self.dn = torch.zeros(c.d_model, **f32)
+        self.logits = torch.zeros(c.vocab, **f32)
+        self.scratch = torch.zeros(self.lib.b200q_attn_decode_scratch_floats(c.n_heads, hd, c.max_seq), **f32)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(c.max_seq, dtype=torch.int32, device=dev)   # argmax after position p
+        self.emb_row_bytes = ops.row_bytes(self.t_emb, c.d_model)
+        self.graph = None
+
+    # -- one step -------------------------------------------------------------
+    def _gemv(self, w, x, y, rows, cols):
+        raw, t = w
+        _lib.check(self.lib.b200q_gemv_dev(t, raw.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 1, rows, 1,
+                                           _stream()))
+
+    def _step(self):
+        c, lib, st = self.cfg, self.lib, _stream()
+        hd, kvd = c.head_dim, c.n_kv_heads * c.head_dim
+        _lib.check(lib.b200q_dequant_row_dev(self.t_emb, self.emb.data_ptr(), self.emb_row_bytes, c.d_model,
+                                             self.token.data_ptr(), c.vocab, self.x.data_ptr(), st))
+        delta = None
+        for li, L in enumerate(self.layers):
+            _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), None if delta is None else delta.data_ptr(),
+                                                 L['attn_norm'].data_ptr(), 1, c.d_model, c.eps, self.h.data_ptr(),
+                                                 st))
+            self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            _lib.check(lib.b200q_rope_kv_dev(self.qkv.data_ptr(), c.n_heads, c.n_kv_heads, hd, self.rotary,
+                                             c.rope_base, self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                             c.max_seq, st))
+            _lib.check(lib.b200q_attn_decode_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                 self.pos.data_ptr(), c.n_heads, c.n_kv_heads, hd, c.max_seq,
+                                                 self.scratch.data_ptr(), self.att.data_ptr(), st))
+            self._gemv(L['o'], self.att, self.o, c.d_model, c.d_model)
+            _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), self.o.data_ptr(), L['ffn_norm'].data_ptr(), 1,
+                                                 c.d_model, c.eps, self.h.data_ptr(), st))
+            self._gemv(L['gu'], self.h, self.gu, 2 * c.d_ff, c.d_model)
+            _lib.check(lib.b200q_silu_mul_dev(self.gu.data_ptr(), 1, c.d_ff, self.act.data_ptr(), c.d_ff, st))
+            self._gemv(L['down'], self.act, self.dn, c.d_model, c.d_ff)
+            delta = self.dn
+        _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), delta.data_ptr(), self.out_norm.data_ptr(), 1,
+                                             c.d_model, c.eps, self.h.data_ptr(), st))
+        self._gemv((self.out_w, self.t_out), self.h, self.logits, c.vocab, c.d_model)
+        _lib.check(lib.b200q_argmax_dev(self.logits.data_ptr(), c.vocab, self.token.data_ptr(), self.pos.data_ptr(),
+                                        self.tokens.data_ptr(), c.max_seq, st))
+
+    def step(self):
+        """One token through the model (graph replay once captured)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+    def capture(self):
+        """Capture one step in a CUDA graph (after one eager step has set up
+        every kernel's attributes).  Replays reuse the same buffers."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self._step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = g
+
+    # -- driving ------------------------------------------------------------
+    def reset(self):
+        self.pos.zero_()
+        self.token.zero_()
+
+    def set_token(self, token: int):
+        self.token.fill_(int(token))
+
+    def generate(self, prompt: list[int], n_new: int) -> list[int]:
+        """Greedy continuation of ``prompt`` (reference: repetition penalty 1,
+        argmax sampling).  Returns the n_new generated token ids."""
+        c = self.cfg
+        if not prompt or len(prompt) + n_new > c.max_seq:
+            raise ValueError('prompt + new tokens must fit max_seq')
+        self.reset()
+        for t in prompt:
+            self.set_token(t)
+            self.step()
+        for _ in range(n_new - 1):
+            self.step()
+        p = len(prompt)
+        return self.tokens[p - 1:p - 1 + n_new].tolist()
+
+    def logits_at(self) -> torch.Tensor:
+        """Logits of the last step."""
+        return self.logits

@@ -25,6 +25,9 @@ What each function restates (paths are relative to the reference project):
   projection, EDA term, RMSNorm, two GELU layers, logits over E+1 routes,
   softmax, top-1 over probs + route biases (first index on ties), weight =
   the unbiased probability
+* ``llama_decode_f64``                 engine/model.py:174-240 (LlamaModel.forward,
+  arch 'llama', no RoPE scaling): token by token with a KV cache, adjacent-
+  pair RoPE, grouped-query attention, SiLU FFN, in float64
 * ``zaya_moe_f64``                     engine/zaya.py:297-307: the selected
   expert's FFN (or, for the skip route E, the block input) times its weight
 
@@ -330,3 +333,61 @@ def zaya_moe_f64(h, expert, weight, experts, t_gu, t_dn, d_model, d_ff, d_ff_pad
             out = expert_ffn_f64(experts[e][0], experts[e][1], t_gu, t_dn, d_model, d_ff, d_ff_padded, h[rows])
         y[rows] = out * weight[rows].astype(np.float64)[:, None]
     return y
+
+
+def llama_decode_f64(w, cfg, tokens):
+    """Logits after each token of ``tokens`` (positions 0, 1, ...), float64.
+
+    ``w``: {'token_embd': [V, D], 'output': [V, D], 'output_norm': [D],
+    'layers': [{'attn_q': [H*hd, D], 'attn_k': [KV*hd, D], 'attn_v',
+    'attn_output': [D, D], 'ffn_gate': [F, D], 'ffn_up', 'ffn_down': [D, F],
+    'attn_norm': [D], 'ffn_norm': [D]}]} as float arrays; ``cfg`` with
+    n_heads, n_kv_heads, rope_base, eps (and optional rope_dim).
+    """
+    H, KV = cfg['n_heads'], cfg['n_kv_heads']
+    D = w['token_embd'].shape[1]
+    hd = D // H
+    rotary = min(cfg.get('rope_dim') or hd, hd)
+    rotary -= rotary % 2
+    half = rotary // 2
+    eps = cfg['eps']
+    norm = lambda x, g: x * (1.0 / np.sqrt(np.mean(x * x) + eps)) * g
+    nl = len(w['layers'])
+    kc = [[] for _ in range(nl)]
+    vc = [[] for _ in range(nl)]
+    out = []
+    for pos, tok in enumerate(tokens):
+        x = w['token_embd'][tok].astype(np.float64)
+        inv = 1.0 / (cfg['rope_base'] ** (np.arange(half, dtype=np.float64) / max(half, 1)))
+        ang = pos * inv
+        c, s_ = np.cos(ang), np.sin(ang)
+
+        def rope(a):
+            z = a.copy()
+            e, o = a[:, 0:rotary:2].copy(), a[:, 1:rotary:2].copy()
+            z[:, 0:rotary:2] = e * c - o * s_
+            z[:, 1:rotary:2] = e * s_ + o * c
+            return z
+        for li, L in enumerate(w['layers']):
+            pre = x
+            h = norm(x, L['attn_norm'])
+            q = rope((L['attn_q'] @ h).reshape(H, hd))
+            k = rope((L['attn_k'] @ h).reshape(KV, hd))
+            v = (L['attn_v'] @ h).reshape(KV, hd)
+            kc[li].append(k)
+            vc[li].append(v)
+            ks, vs = np.stack(kc[li]), np.stack(vc[li])          # [L, KV, hd]
+            g = H // KV
+            att = np.empty((H, hd))
+            for hh in range(H):
+                sc = ks[:, hh // g, :] @ q[hh] / np.sqrt(hd)
+                p = np.exp(sc - sc.max())
+                p /= p.sum()
+                att[hh] = p @ vs[:, hh // g, :]
+            x = pre + L['attn_output'] @ att.reshape(-1)
+            pre = x
+            h = norm(x, L['ffn_norm'])
+            gt, up = L['ffn_gate'] @ h, L['ffn_up'] @ h
+            x = pre + L['ffn_down'] @ (gt / (1.0 + np.exp(-np.clip(gt, -80, 80))) * up)
+        out.append(w['output'] @ norm(x, w['output_norm']))
+    return np.stack(out)

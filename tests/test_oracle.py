@@ -239,3 +239,18 @@ def test_zaya_router_oracle_matches_reference_golden():
     ref_routes_skip = np.sum(e == E)
     assert ref_routes_skip > 0 and ref_routes_skip < T          # the fixture exercises both kinds
     assert o.normwise_rel_err(y, d['Y']) < 1e-5
+
+
+def test_llama_decode_oracle_matches_reference_golden():
+    """The float64 decoder restatement reproduces the reference's own
+    LlamaModel.forward (engine/model.py:174-240) on the committed fixture:
+    RoPE layout, grouped-query attention, norms and FFN (f32 weights)."""
+    d = np.load(Path(__file__).resolve().parent / 'golden' / 'llama_decode_golden.npz')
+    NL = 2
+    w = {'token_embd': d['token_embd_weight'], 'output': d['output_weight'], 'output_norm': d['output_norm_weight'],
+         'layers': [{n: d[f'blk_{l}_{n}_weight'] for n in ('attn_q', 'attn_k', 'attn_v', 'attn_output', 'ffn_gate',
+                                                             'ffn_up', 'ffn_down', 'attn_norm', 'ffn_norm')}
+                    for l in range(NL)]}
+    cfg = {'n_heads': 4, 'n_kv_heads': 2, 'rope_base': 10000.0, 'eps': 1e-5}
+    got = o.llama_decode_f64(w, cfg, list(d['tokens']))
+    assert o.normwise_rel_err(got, d['logits'].astype(np.float64)) < 1e-5
