@@ -264,6 +264,19 @@ def cpu_reference_extras(threads=8):
     t_64 = timed(lambda: moe_tokens(64), min_s=0.0, max_reps=1)
     res['config3_moe_q6k'] = {'T1_us': round(t_1 * 1e6, 1), 'T64_tokens_per_s': round(64 / t_64, 1),
                               'path': 'per-token router + native Q6_K matvecs (engine/zaya.py:274-307)'}
+    # configuration 4: one Q8_0 decode token = 32 layers x (q, k, v, o, gate, up, down) + output matvec;
+    # one layer's matvecs and a 1/8 slice of the output matrix are timed and extrapolated
+    Dm, Ff, KVd = 4096, 14336, 1024
+    mats = [(synth.q8_0(rng, r, c_), r, c_) for r, c_ in ((Dm, Dm), (KVd, Dm), (KVd, Dm), (Dm, Dm), (Ff, Dm), (Ff, Dm),
+                                                          (Dm, Ff))]
+    outs = synth.q8_0(rng, 128256 // 8, Dm)
+    xs = {Dm: rng.normal(size=Dm).astype(np.float32), Ff: rng.normal(size=Ff).astype(np.float32)}
+    t_layer = timed(lambda: [mv('localai_q8_0_matvec', m, xs[c_], r, c_) for m, r, c_ in mats], min_s=0.5, max_reps=5)
+    t_outs = timed(lambda: mv('localai_q8_0_matvec', outs, xs[Dm], 128256 // 8, Dm), min_s=0.2, max_reps=10)
+    t_tok = 32 * t_layer + 8 * t_outs
+    res['config4_decode_q8_0'] = {'decode_tokens_per_s': round(1.0 / t_tok, 3), 'ms_per_token': round(t_tok * 1e3, 1),
+                                  'sample': 'one layer of matvecs x 32 + 1/8 of the output matrix x 8 '
+                                            '(matvecs only; attention and norms not included)'}
     return res
 
 
@@ -382,6 +395,78 @@ def dense_ffn_probe(torch, synth, hbm_peak, tc_peak):
                         'path': 'tcgen05 GEMM gate/up (fused SiLU*up) + GEMM down'})
         res[f'T{T}'] = ent
     del ffns
+    return res
+
+
+def _q8_0_device(torch, rows, cols, gen, d_sigma=0.005):
+    """Synthetic Q8_0 matrix generated on the device (same distribution as
+    synth.q8_0: d = fp16(|N(0, d_sigma)|), q uniform in [-127, 127])."""
+    nb = rows * (cols // 32)
+    d = (torch.randn(nb, device='cuda', generator=gen) * d_sigma).abs().half()
+    q = torch.randint(-127, 128, (nb, 32), device='cuda', dtype=torch.int8, generator=gen)
+    blocks = torch.empty((nb, 34), dtype=torch.uint8, device='cuda')
+    blocks[:, 0:2] = d.view(torch.uint8).reshape(nb, 2)
+    blocks[:, 2:] = q.view(torch.uint8)
+    return blocks.reshape(-1)
+
+
+def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
+    """Configuration 4: Llama-3-8B-shaped decoder (32 layers, hidden 4096, 32
+    heads / 8 KV heads, FFN 14336, vocabulary 128256), every matrix Q8_0 (8.53
+    GB), greedy: a prompt of ``prompt_len`` random token ids fed through the
+    captured decode step (untimed), then ``new_tokens`` timed steps."""
+    from localai_b200.decoder import LlamaConfig, QuantLlama
+    NL, Dm, H, KV, Ff, V = 32, 4096, 32, 8, 14336, 128256
+    hd = Dm // H
+    gen = torch.Generator(device='cuda')
+    gen.manual_seed(4)
+    ones = torch.ones(Dm, device='cuda')
+    layers = []
+    for _ in range(NL):
+        layers.append({'attn_q': (_q8_0_device(torch, H * hd, Dm, gen), 8),
+                       'attn_k': (_q8_0_device(torch, KV * hd, Dm, gen), 8),
+                       'attn_v': (_q8_0_device(torch, KV * hd, Dm, gen), 8),
+                       'attn_output': (_q8_0_device(torch, Dm, Dm, gen), 8),
+                       'ffn_gate': (_q8_0_device(torch, Ff, Dm, gen), 8),
+                       'ffn_up': (_q8_0_device(torch, Ff, Dm, gen), 8),
+                       'ffn_down': (_q8_0_device(torch, Dm, Ff, gen), 8),
+                       'attn_norm': ones, 'ffn_norm': ones})
+    w = {'token_embd': (_q8_0_device(torch, V, Dm, gen), 8), 'output': (_q8_0_device(torch, V, Dm, gen), 8),
+         'output_norm': ones, 'layers': layers}
+    cfg = LlamaConfig(n_layers=NL, d_model=Dm, n_heads=H, n_kv_heads=KV, d_ff=Ff, vocab=V, rope_base=500000.0,
+                      eps=1e-5, max_seq=prompt_len + new_tokens)
+    model = QuantLlama(w, cfg)
+    del w, layers
+    wbytes = 34 * (NL * ((H * hd + 2 * KV * hd) * Dm + Dm * Dm + 2 * Ff * Dm + Dm * Ff) + 2 * V * Dm) // 32
+    prompt = torch.randint(0, V, (prompt_len,), generator=torch.Generator().manual_seed(5)).tolist()
+    model.reset()
+    model.set_token(prompt[0])
+    model.step()
+    model.capture()
+    model.reset()
+    t0 = time.time()
+    for t in prompt:
+        model.set_token(t)
+        model.step()
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(new_tokens):
+        model.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / new_tokens
+    ctx = prompt_len + new_tokens / 2
+    kv_bytes = 2 * NL * ctx * KV * hd * 4
+    nbytes = wbytes + kv_bytes
+    res = {'decode_tokens_per_s': round(1e3 / ms, 1), 'ms_per_token': round(ms, 3),
+           'GB_s': round(nbytes / (ms * 1e-3) / 1e9, 1), 'frac_of_measured_hbm': round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3),
+           'bytes_per_token': int(nbytes), 'weights_bytes': int(wbytes), 'prompt_tokens': prompt_len,
+           'timed_tokens': new_tokens, 'prefill_tokenwise_s': round(prefill_s, 2),
+           'launches_per_token': 4 + NL * 11, 'path': 'CUDA graph of one step: 7 GEMVs/layer + norms, RoPE, attention'}
+    del model
+    torch.cuda.empty_cache()
     return res
 
 
@@ -591,11 +676,12 @@ def main():
         allp = [None] * world
         dist.all_gather_object(allp, mine_ph)
         phases = {f'rank{r}': p for r, p in enumerate(allp)}
-    gemv = ffn2 = moe3 = None
+    gemv = ffn2 = moe3 = dec4 = None
     if rank == 0 and not args.no_gemv and world == 1:
         gemv = gemv_probe(torch, ops, synth, hbm_peak)
         ffn2 = dense_ffn_probe(torch, synth, hbm_peak, tc_burst)
         moe3 = moe_q6k_probe(torch, synth)
+        dec4 = decode_probe(torch, hbm_peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -619,7 +705,8 @@ def main():
                         'd2h_bytes_per_step': T_TOTAL * D * 4, 'chunks': args.e2e_chunks,
                         'api': 'EPMoE.forward_host' if world > 1 else 'QuantMoE.forward_host'},
                 'gpu_launches': int(launches), 'clocks': clocks, 'gemv': gemv,
-                'config2_dense_ffn_q4k': ffn2, 'config3_moe_q6k': moe3, 'ep_phases': phases,
+                'config2_dense_ffn_q4k': ffn2, 'config3_moe_q6k': moe3, 'config4_decode_q8_0': dec4,
+                'ep_phases': phases,
                 'flops_per_step': algorithmic_flops(T_TOTAL * K_TOP)}
         print(json.dumps(line), flush=True)
     if world > 1:
