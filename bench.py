@@ -464,7 +464,7 @@ def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
            'GB_s': round(nbytes / (ms * 1e-3) / 1e9, 1), 'frac_of_measured_hbm': round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3),
            'bytes_per_token': int(nbytes), 'weights_bytes': int(wbytes), 'prompt_tokens': prompt_len,
            'timed_tokens': new_tokens, 'prefill_tokenwise_s': round(prefill_s, 2),
-           'launches_per_token': 4 + NL * 11, 'path': 'CUDA graph of one step: 7 GEMVs/layer + norms, RoPE, attention'}
+           'launches_per_token': 5 + NL * 11, 'path': 'CUDA graph of one step: 7 GEMVs/layer + norms, RoPE, attention'}
     del model
     torch.cuda.empty_cache()
     return res

@@ -295,7 +295,9 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *                           h / (H / KV)); scratch of
  *                           b200q_attn_decode_scratch_floats floats
  *   b200q_argmax_dev        *token = argmax(logits) (first index on ties);
- *                           with pos: out_tokens[*pos] = token, ++*pos */
+ *                           with pos: out_tokens[*pos] = token, ++*pos;
+ *                           key: optional zero-initialised 64-bit device word
+ *                           for the grid-wide version (cleared again after use) */
 int b200q_dequant_row_dev(int ggml_type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
                           float *out, void *stream);
 int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
@@ -305,7 +307,8 @@ int b200q_rope_kv_dev(float *qkv, int H, int KV, int hd, int rotary, float base,
 size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq);
 int b200q_attn_decode_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H, int KV,
                           int hd, int max_seq, float *scratch, float *out, void *stream);
-int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens, void *stream);
+int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
+                     unsigned long long *key, void *stream);
 
 #ifdef __cplusplus
 }

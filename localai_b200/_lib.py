@@ -69,7 +69,7 @@ SIGNATURES = {
     'b200q_rope_kv_dev': (_i, [_vp, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _vp, _i, _vp]),
     'b200q_attn_decode_scratch_floats': (_sz, [_i, _i, _i]),
     'b200q_attn_decode_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
-    'b200q_argmax_dev': (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp]),
+    'b200q_argmax_dev': (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp, _vp]),
     'b200q_ep_create': (_i, [_i, _i, _i, _i, _ll, _ll, ctypes.POINTER(_vp)]),
     'b200q_ep_handle_bytes': (_sz, []),
     'b200q_ep_handle': (_i, [_vp, _vp]),

@@ -81,7 +81,7 @@ size_t attn_scratch_floats(int H, int hd, int max_seq);
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
                                int max_seq, float *part, float *out, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
-                          cudaStream_t st);
+                          unsigned long long *key, int num_sms, cudaStream_t st);
 cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st);
 cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
                                     int R, float eps, float *state, float *out, cudaStream_t st);
@@ -797,10 +797,14 @@ B200Q_API int b200q_attn_decode_dev(const float *q, const float *k_cache, const 
 }
 
 B200Q_API int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
-                               void *stream)
+                               unsigned long long *key, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!logits || !token) return set_status(B200Q_EINVAL, "argmax: null pointer");
-    ++g_launches;
-    return cuda_status(launch_argmax(logits, V, token, pos, out_tokens, max_tokens, (cudaStream_t)stream), "argmax");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += key ? 2 : 1;
+    return cuda_status(launch_argmax(logits, V, token, pos, out_tokens, max_tokens, key, di->sms,
+                                     (cudaStream_t)stream),
+                       "argmax");
 }

@@ -20,33 +20,61 @@
 
 namespace b200q {
 
-constexpr int ATT_CHUNK = 128;
+constexpr int ATT_CHUNK = 64;
 
-// x += delta (when given); h = x / sqrt(mean(x^2) + eps) * w  (engine/model.py:82)
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ delta,
-                                                          const float *__restrict__ w, int D, float eps,
-                                                          float *__restrict__ h)
+// x += delta (when given); h = x / sqrt(mean(x^2) + eps) * w  (engine/model.py:82).
+// One CTA of 512 threads per row; every thread loads its (up to 8) float4
+// groups of x and delta before anything is stored, so the row costs one
+// memory round trip; the sum of squares is reduced in a fixed order.
+constexpr int NORM_THREADS = 512, NORM_VEC = 8;
+__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ delta,
+                                                                   const float *__restrict__ w, int D, float eps,
+                                                                   float *__restrict__ h)
 {
-    __shared__ float red[256];
+    __shared__ float red[NORM_THREADS / 32];
     const long long t = blockIdx.x;
-    float *xr = x + t * D;
+    float4 *xr = reinterpret_cast<float4 *>(x + t * D);
+    const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + t * D) : nullptr;
+    const int n4 = D / 4;
+    float4 v[NORM_VEC];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        float v = xr[i];
-        if (delta) {
-            v = v + delta[t * D + i];
-            xr[i] = v;
+#pragma unroll
+    for (int k = 0; k < NORM_VEC; ++k) {
+        const int i = threadIdx.x + k * NORM_THREADS;
+        v[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (dr) {
+#pragma unroll
+        for (int k = 0; k < NORM_VEC; ++k) {
+            const int i = threadIdx.x + k * NORM_THREADS;
+            if (i < n4) {
+                const float4 d = dr[i];
+                v[k].x += d.x; v[k].y += d.y; v[k].z += d.z; v[k].w += d.w;
+            }
         }
-        ss = fmaf(v, v, ss);
     }
-    red[threadIdx.x] = ss;
+#pragma unroll
+    for (int k = 0; k < NORM_VEC; ++k)
+        ss = fmaf(v[k].w, v[k].w, fmaf(v[k].z, v[k].z, fmaf(v[k].y, v[k].y, fmaf(v[k].x, v[k].x, ss))));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-        if ((int)threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-        __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NORM_THREADS / 32; ++i) tot += red[i];
+    const float inv = 1.0f / sqrtf(tot / (float)D + eps);
+    const float4 *wr = reinterpret_cast<const float4 *>(w);
+    float4 *hr = reinterpret_cast<float4 *>(h + t * D);
+#pragma unroll
+    for (int k = 0; k < NORM_VEC; ++k) {
+        const int i = threadIdx.x + k * NORM_THREADS;
+        if (i < n4) {
+            if (dr) xr[i] = v[k];
+            const float4 g = wr[i];
+            hr[i] = make_float4(v[k].x * inv * g.x, v[k].y * inv * g.y, v[k].z * inv * g.z, v[k].w * inv * g.w);
+        }
     }
-    const float inv = 1.0f / sqrtf(red[0] / (float)D + eps);
-    for (int i = threadIdx.x; i < D; i += blockDim.x) h[t * D + i] = xr[i] * inv * w[i];
 }
 
 // qkv = [q (H*hd) | k (KV*hd) | v (KV*hd)]: rotate q and k in place over the
@@ -88,77 +116,88 @@ __global__ void kv_store_kernel(const float *__restrict__ qkv, int H, int KV, in
     }
 }
 
-// One CTA per (KV head g, chunk c of positions).  Scores of the G = H/KV query
-// heads of group g over positions [c*ATT_CHUNK, min(pos+1, ...)); writes the
-// chunk's max, sum of exp and exp-weighted V per query head.
-__global__ void __launch_bounds__(128) attn_chunk_kernel(const float *__restrict__ q, const float *__restrict__ kc,
-                                                         const float *__restrict__ vc, const int *__restrict__ pos_p,
-                                                         int H, int KV, int hd, int max_seq,
-                                                         float *__restrict__ part)
+// One CTA per (KV head g, chunk c of ATT_CHUNK positions), 256 threads.  The
+// chunk's K and V rows are staged in shared memory (rows padded by one float
+// so that threads reading different rows hit different banks); thread
+// (query head j, position l) computes one score; warp j does the softmax
+// statistics of head j with shuffles; then every thread accumulates two
+// (head, dim) outputs of P V.  Writes per query head the chunk's max, sum of
+// exp and exp-weighted V.
+constexpr int ATT_THREADS = 256;
+__global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__restrict__ q, const float *__restrict__ kc,
+                                                                 const float *__restrict__ vc,
+                                                                 const int *__restrict__ pos_p, int H, int KV, int hd,
+                                                                 int max_seq, float *__restrict__ part)
 {
     extern __shared__ float asm_[];
     const int G = H / KV, g = blockIdx.x, c = blockIdx.y;
     const int L = min(*pos_p + 1, max_seq);
     const int l0 = c * ATT_CHUNK, l1 = min(L, l0 + ATT_CHUNK);
     const int nch = gridDim.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int stride = hd + 1;
+    float *qs = asm_;                          // [G][hd]
+    float *ks = qs + G * hd;                   // [ATT_CHUNK][hd + 1]
+    float *vs = ks + ATT_CHUNK * stride;       // [ATT_CHUNK][hd + 1]
+    float *sc = vs + ATT_CHUNK * stride;       // [G][ATT_CHUNK]
+    float *stat = sc + G * ATT_CHUNK;          // [G][2]: max, 1/sum not used; max, sum
     // part layout: [H][nch][hd + 2]: acc[hd], max, sum
-    float *qs = asm_;                         // [G][hd]
-    float *sc = qs + G * hd;                  // [G][ATT_CHUNK]
-    __shared__ float red[128];
-    const int tid = threadIdx.x;
+    if (l1 <= l0) {                            // chunk past the current position
+        for (int i = tid; i < G * (hd + 2); i += blockDim.x) {
+            const int j = i / (hd + 2), d = i % (hd + 2);
+            part[((long long)(g * G + j) * nch + c) * (hd + 2) + d] = d == hd ? -INFINITY : 0.f;
+        }
+        return;
+    }
+    const int n = l1 - l0;
     for (int i = tid; i < G * hd; i += blockDim.x) qs[i] = q[(long long)g * G * hd + i];
+    for (int i = tid; i < n * hd; i += blockDim.x) {
+        const int l = i / hd, d = i % hd;
+        ks[l * stride + d] = kc[((long long)(l0 + l) * KV + g) * hd + d];
+        vs[l * stride + d] = vc[((long long)(l0 + l) * KV + g) * hd + d];
+    }
     __syncthreads();
     const float rs = sqrtf((float)hd);
-    // scores: one position per thread
-    for (int l = l0 + tid; l < l0 + ATT_CHUNK; l += blockDim.x) {
-        if (l < l1) {
-            const float *kr = kc + ((long long)l * KV + g) * hd;
-            for (int j = 0; j < G; ++j) {
-                float d = 0.f;
-                for (int e = 0; e < hd; ++e) d = fmaf(qs[j * hd + e], kr[e], d);
-                sc[j * ATT_CHUNK + (l - l0)] = d / rs;
-            }
-        } else {
-            for (int j = 0; j < G; ++j) sc[j * ATT_CHUNK + (l - l0)] = -INFINITY;
+    for (int i = tid; i < G * ATT_CHUNK; i += blockDim.x) {
+        const int j = i / ATT_CHUNK, l = i % ATT_CHUNK;
+        float s = -INFINITY;
+        if (l < n) {
+            float d = 0.f;
+            for (int e = 0; e < hd; ++e) d = fmaf(qs[j * hd + e], ks[l * stride + e], d);
+            s = d / rs;
+        }
+        sc[j * ATT_CHUNK + l] = s;
+    }
+    __syncthreads();
+    for (int j = warp; j < G; j += ATT_THREADS / 32) {
+        float m = -INFINITY;
+        for (int l = lane; l < ATT_CHUNK; l += 32) m = fmaxf(m, sc[j * ATT_CHUNK + l]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sum = 0.f;
+        for (int l = lane; l < ATT_CHUNK; l += 32) {
+            const float e = l < n ? expf(sc[j * ATT_CHUNK + l] - m) : 0.f;
+            sc[j * ATT_CHUNK + l] = e;
+            sum += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            stat[2 * j] = m;
+            stat[2 * j + 1] = sum;
         }
     }
     __syncthreads();
-    for (int j = 0; j < G; ++j) {
-        // chunk max and sum of exp (fixed-order tree)
-        float m = -INFINITY;
-        for (int l = tid; l < ATT_CHUNK; l += blockDim.x) m = fmaxf(m, sc[j * ATT_CHUNK + l]);
-        red[tid] = m;
-        __syncthreads();
-        for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-            if (tid < o) red[tid] = fmaxf(red[tid], red[tid + o]);
-            __syncthreads();
-        }
-        m = red[0];
-        __syncthreads();
-        float s = 0.f;
-        for (int l = tid; l < ATT_CHUNK; l += blockDim.x) {
-            const float e = (l0 + l < l1) ? expf(sc[j * ATT_CHUNK + l] - m) : 0.f;
-            sc[j * ATT_CHUNK + l] = e;
-            s += e;
-        }
-        red[tid] = s;
-        __syncthreads();
-        for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-            if (tid < o) red[tid] += red[tid + o];
-            __syncthreads();
-        }
+    for (int i = tid; i < G * hd; i += blockDim.x) {
+        const int j = i / hd, d = i % hd;
+        float a = 0.f;
+        for (int l = 0; l < n; ++l) a = fmaf(sc[j * ATT_CHUNK + l], vs[l * stride + d], a);
         float *pp = part + ((long long)(g * G + j) * nch + c) * (hd + 2);
-        if (tid == 0) {
-            pp[hd] = l1 > l0 ? m : -INFINITY;
-            pp[hd + 1] = l1 > l0 ? red[0] : 0.f;
+        pp[d] = a;
+        if (d == 0) {
+            pp[hd] = stat[2 * j];
+            pp[hd + 1] = stat[2 * j + 1];
         }
-        __syncthreads();
-        for (int d = tid; d < hd; d += blockDim.x) {
-            float a = 0.f;
-            for (int l = l0; l < l1; ++l) a = fmaf(sc[j * ATT_CHUNK + (l - l0)], vc[((long long)l * KV + g) * hd + d], a);
-            pp[d] = a;
-        }
-        __syncthreads();
     }
 }
 
@@ -226,8 +265,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
                                cudaStream_t st)
 {
-    if (T < 1 || D < 1) return cudaErrorInvalidValue;
-    add_rmsnorm_kernel<<<T, 256, 0, st>>>(x, delta, w, D, eps, h);
+    if (T < 1 || D < 4 || D % 4 || D > 4 * NORM_THREADS * NORM_VEC || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (delta && (reinterpret_cast<uintptr_t>(delta) & 15)))
+        return cudaErrorInvalidValue;
+    add_rmsnorm_kernel<<<T, NORM_THREADS, 0, st>>>(x, delta, w, D, eps, h);
     return cudaGetLastError();
 }
 
@@ -253,18 +295,78 @@ cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc,
 {
     if (H < 1 || KV < 1 || H % KV || hd < 1 || max_seq < 1) return cudaErrorInvalidValue;
     const int G = H / KV, nch = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
-    const size_t smem = (size_t)(G * hd + G * ATT_CHUNK) * sizeof(float);
-    if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    attn_chunk_kernel<<<dim3(KV, nch), 128, smem, st>>>(q, kc, vc, pos, H, KV, hd, max_seq, part);
+    const size_t smem = (size_t)(G * hd + 2 * ATT_CHUNK * (hd + 1) + G * ATT_CHUNK + 2 * G) * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = smem;
+    }
+    attn_chunk_kernel<<<dim3(KV, nch), ATT_THREADS, smem, st>>>(q, kc, vc, pos, H, KV, hd, max_seq, part);
     attn_combine_kernel<<<H, 128, 0, st>>>(part, nch, hd, out);
     return cudaGetLastError();
 }
 
+// Grid-wide argmax: every CTA reduces a slice, then one 64-bit atomicMax of
+// the key (order-preserving bits of the value << 32 | ~index), so the largest
+// value wins and, among equal values, the lowest index (np.argmax).  The
+// finishing thread decodes the token, records it, advances pos and clears the
+// key for the next step.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i)
+{
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)o << 32) | (0xFFFFFFFFu - (uint32_t)i);
+}
+
+__global__ void __launch_bounds__(256) argmax_part_kernel(const float *__restrict__ logits, int V,
+                                                          unsigned long long *key)
+{
+    __shared__ unsigned long long red[8];
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(logits[i], i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < 8; ++i) best = red[i] > best ? red[i] : best;
+        atomicMax(key, best);
+    }
+}
+
+__global__ void argmax_finish_kernel(unsigned long long *key, int *token, int *pos_p, int *out_tokens, int max_tokens)
+{
+    const unsigned long long k = *key;
+    const int t = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+    *token = t;
+    if (pos_p) {
+        const int p = *pos_p;
+        if (out_tokens && p >= 0 && p < max_tokens) out_tokens[p] = t;
+        *pos_p = p + 1;
+    }
+    *key = 0ull;
+}
+
 cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
-                          cudaStream_t st)
+                          unsigned long long *key, int num_sms, cudaStream_t st)
 {
     if (V < 1) return cudaErrorInvalidValue;
-    argmax_kernel<<<1, 1024, 0, st>>>(logits, V, token, pos, out_tokens, max_tokens);
+    if (!key) {
+        argmax_kernel<<<1, 1024, 0, st>>>(logits, V, token, pos, out_tokens, max_tokens);
+        return cudaGetLastError();
+    }
+    int grid = (V + 255) / 256;
+    if (grid > num_sms) grid = num_sms;
+    argmax_part_kernel<<<grid, 256, 0, st>>>(logits, V, key);
+    argmax_finish_kernel<<<1, 1, 0, st>>>(key, token, pos, out_tokens, max_tokens);
     return cudaGetLastError();
 }
 

@@ -100,6 +100,7 @@ class QuantLlama:
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self.tokens = torch.zeros(c.max_seq, dtype=torch.int32, device=dev)   # argmax after position p
+        self.amax_key = torch.zeros(1, dtype=torch.int64, device=dev)         # grid-wide argmax word
         self.emb_row_bytes = ops.row_bytes(self.t_emb, c.d_model)
         self.graph = None
 
@@ -138,7 +139,7 @@ class QuantLlama:
                                              c.d_model, c.eps, self.h.data_ptr(), st))
         self._gemv((self.out_w, self.t_out), self.h, self.logits, c.vocab, c.d_model)
         _lib.check(lib.b200q_argmax_dev(self.logits.data_ptr(), c.vocab, self.token.data_ptr(), self.pos.data_ptr(),
-                                        self.tokens.data_ptr(), c.max_seq, st))
+                                        self.tokens.data_ptr(), c.max_seq, self.amax_key.data_ptr(), st))
 
     def step(self):
         """One token through the model (graph replay once captured)."""
