@@ -444,12 +444,17 @@ def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
     model.step()
     model.capture()
     model.reset()
-    t0 = time.time()
-    for t in prompt:
-        model.set_token(t)
-        model.step()
+    model.prefill(prompt[:64])                       # set-up of the prefill path (untimed)
+    model.reset()
     torch.cuda.synchronize()
-    prefill_s = time.time() - t0
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    model.prefill(prompt)
+    p1.record()
+    torch.cuda.synchronize()
+    prefill_ms = p0.elapsed_time(p1)
+    params = NL * ((H * hd + 2 * KV * hd) * Dm + Dm * Dm + 3 * Ff * Dm)
+    prefill_flops = 2.0 * params * prompt_len + 4.0 * NL * H * hd * prompt_len * (prompt_len + 1) / 2
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(new_tokens):
@@ -463,7 +468,10 @@ def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
     res = {'decode_tokens_per_s': round(1e3 / ms, 1), 'ms_per_token': round(ms, 3),
            'GB_s': round(nbytes / (ms * 1e-3) / 1e9, 1), 'frac_of_measured_hbm': round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 3),
            'bytes_per_token': int(nbytes), 'weights_bytes': int(wbytes), 'prompt_tokens': prompt_len,
-           'timed_tokens': new_tokens, 'prefill_tokenwise_s': round(prefill_s, 2),
+           'timed_tokens': new_tokens,
+           'prefill': {'ms': round(prefill_ms, 2), 'tokens_per_s': round(prompt_len / (prefill_ms * 1e-3), 1),
+                       'TFLOP_s': round(prefill_flops / (prefill_ms * 1e-3) / 1e12, 1), 'flops': prefill_flops,
+                       'path': 'tcgen05 GEMMs over the prompt rows + causal attention kernel'},
            'launches_per_token': 5 + NL * 11, 'path': 'CUDA graph of one step: 7 GEMVs/layer + norms, RoPE, attention'}
     del model
     torch.cuda.empty_cache()

@@ -283,13 +283,17 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
 /* ---- Decode step of the reference's Llama decoder (engine/model.py:174-240)
  * around the quantised GEMVs; every call reads the position / token from
  * device memory, so a whole step can be captured in a CUDA graph.
- *   b200q_dequant_row_dev   out[cols] = row *row_idx of a quantised matrix
- *                           (bit-exact; the token embedding lookup)
- *   b200q_add_rmsnorm_dev   x += delta (when not NULL); h = rmsnorm(x) * w
- *   b200q_rope_kv_dev       qkv = [q H*hd | k KV*hd | v KV*hd]: adjacent-pair
- *                           RoPE of q and k at *pos over the first ``rotary``
- *                           dims, then k, v stored at cache[*pos]
- *                           (cache layout [max_seq][KV][hd])
+ *   b200q_dequant_row_dev   out[i][cols] = row row_idx[i] of a quantised matrix,
+ *                           i < n (bit-exact; the token embedding lookup)
+ *   b200q_add_rmsnorm_dev   per row t < T: x += delta (when not NULL);
+ *                           rmsnorm(x) * w written to h (f32) and/or h_bf16
+ *   b200q_rope_kv_dev       rows t < T of qkv = [q H*hd | k KV*hd | v KV*hd]
+ *                           at positions *pos + t: adjacent-pair RoPE of q and
+ *                           k over the first ``rotary`` dims, then k, v stored
+ *                           at cache[*pos + t] (cache layout [max_seq][KV][hd])
+ *   b200q_attn_prefill_dev  causal attention of T query rows (positions
+ *                           *pos + t, q from the rotated qkv rows) over cache
+ *                           positions 0 .. *pos + t; out bf16 [T][H*hd]
  *   b200q_attn_decode_dev   out[H*hd] = softmax(q k^T / sqrt(hd)) v over
  *                           positions 0..*pos (GQA: head h uses KV head
  *                           h / (H / KV)); scratch of
@@ -299,11 +303,13 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *                           key: optional zero-initialised 64-bit device word
  *                           for the grid-wide version (cleared again after use) */
 int b200q_dequant_row_dev(int ggml_type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
-                          float *out, void *stream);
+                          int n, float *out, void *stream);
 int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
-                          void *stream);
-int b200q_rope_kv_dev(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos, float *k_cache,
-                      float *v_cache, int max_seq, void *stream);
+                          void *h_bf16, void *stream);
+int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
+                      float *k_cache, float *v_cache, int max_seq, void *stream);
+int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T, int H,
+                           int KV, int hd, int max_seq, void *out_bf16, void *stream);
 size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq);
 int b200q_attn_decode_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H, int KV,
                           int hd, int max_seq, float *scratch, float *out, void *stream);

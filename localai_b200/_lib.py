@@ -64,9 +64,10 @@ SIGNATURES = {
     'b200q_check_device_error': (_i, []),
     'b200q_gemv_tuning': (None, [_i, _i, _i, _i]),
     'b200q_launch_count': (_ll, []),
-    'b200q_dequant_row_dev': (_i, [_i, _vp, _ll, _i, _vp, _i, _vp, _vp]),
-    'b200q_add_rmsnorm_dev': (_i, [_vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp]),
-    'b200q_rope_kv_dev': (_i, [_vp, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _vp, _i, _vp]),
+    'b200q_dequant_row_dev': (_i, [_i, _vp, _ll, _i, _vp, _i, _i, _vp, _vp]),
+    'b200q_add_rmsnorm_dev': (_i, [_vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp, _vp]),
+    'b200q_rope_kv_dev': (_i, [_vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _vp, _i, _vp]),
+    'b200q_attn_prefill_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     'b200q_attn_decode_scratch_floats': (_sz, [_i, _i, _i]),
     'b200q_attn_decode_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_argmax_dev': (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp, _vp]),

@@ -72,11 +72,13 @@ cudaError_t launch_gemv_grouped(int type, const void *w, long long w_group_strid
                                 cudaStream_t st);
 int gemv_grouped_max_tokens(int type, int cols);
 cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
-                               float *out, int *err, cudaStream_t st);
+                               int n, float *out, int *err, cudaStream_t st);
 cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
-                               cudaStream_t st);
-cudaError_t launch_rope_kv(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos, float *kc,
-                           float *vc, int max_seq, int *err, cudaStream_t st);
+                               __nv_bfloat16 *hb, cudaStream_t st);
+cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
+                           float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st);
+cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
+                                int KV, int hd, int max_seq, __nv_bfloat16 *out, cudaStream_t st);
 size_t attn_scratch_floats(int H, int hd, int max_seq);
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
                                int max_seq, float *part, float *out, cudaStream_t st);
@@ -746,28 +748,30 @@ B200Q_API int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *sl
 
 // ---------------------------------------------------------------- decode step (Llama)
 B200Q_API int b200q_dequant_row_dev(int ggml_type, const void *raw, long long row_bytes, int cols, const int *row_idx,
-                                    int rows, float *out, void *stream)
+                                    int rows, int n, float *out, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!raw || !row_idx || !out) return set_status(B200Q_EINVAL, "dequant_row: null pointer");
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_dequant_row(ggml_type, raw, row_bytes, cols, row_idx, rows, out, di->err,
+    return cuda_status(launch_dequant_row(ggml_type, raw, row_bytes, cols, row_idx, rows, n, out, di->err,
                                           (cudaStream_t)stream),
                        "dequant_row");
 }
 
 B200Q_API int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
-                                    void *stream)
+                                    void *h_bf16, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
-    if (!x || !w || !h) return set_status(B200Q_EINVAL, "add_rmsnorm: null pointer");
+    if (!x || !w || (!h && !h_bf16)) return set_status(B200Q_EINVAL, "add_rmsnorm: null pointer");
     ++g_launches;
-    return cuda_status(launch_add_rmsnorm(x, delta, w, T, D, eps, h, (cudaStream_t)stream), "add_rmsnorm");
+    return cuda_status(launch_add_rmsnorm(x, delta, w, T, D, eps, h, static_cast<__nv_bfloat16 *>(h_bf16),
+                                          (cudaStream_t)stream),
+                       "add_rmsnorm");
 }
 
-B200Q_API int b200q_rope_kv_dev(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos,
+B200Q_API int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
                                 float *k_cache, float *v_cache, int max_seq, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
@@ -775,8 +779,8 @@ B200Q_API int b200q_rope_kv_dev(float *qkv, int H, int KV, int hd, int rotary, f
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     g_launches += 2;
-    return cuda_status(launch_rope_kv(qkv, H, KV, hd, rotary, base, pos, k_cache, v_cache, max_seq, di->err,
-                                      (cudaStream_t)stream),
+    return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, base, pos, k_cache, v_cache, max_seq, di->err,
+                                      di->sms, (cudaStream_t)stream),
                        "rope_kv");
 }
 
@@ -807,4 +811,15 @@ B200Q_API int b200q_argmax_dev(const float *logits, int V, int *token, int *pos,
     return cuda_status(launch_argmax(logits, V, token, pos, out_tokens, max_tokens, key, di->sms,
                                      (cudaStream_t)stream),
                        "argmax");
+}
+
+B200Q_API int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T,
+                                     int H, int KV, int hd, int max_seq, void *out_bf16, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!qkv || !k_cache || !v_cache || !pos || !out_bf16) return set_status(B200Q_EINVAL, "attn_prefill: null pointer");
+    ++g_launches;
+    return cuda_status(launch_attn_prefill(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq,
+                                           static_cast<__nv_bfloat16 *>(out_bf16), (cudaStream_t)stream),
+                       "attn_prefill");
 }

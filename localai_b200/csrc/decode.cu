@@ -17,6 +17,7 @@
 // ATT_CHUNK (one CTA per KV head and chunk, partial max / sum / weighted V),
 // then combines the chunks in a fixed order.
 #include "common.cuh"
+#include <algorithm>
 
 namespace b200q {
 
@@ -29,7 +30,7 @@ constexpr int ATT_CHUNK = 64;
 constexpr int NORM_THREADS = 512, NORM_VEC = 8;
 __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ delta,
                                                                    const float *__restrict__ w, int D, float eps,
-                                                                   float *__restrict__ h)
+                                                                   float *__restrict__ h, __nv_bfloat16 *__restrict__ hb)
 {
     __shared__ float red[NORM_THREADS / 32];
     const long long t = blockIdx.x;
@@ -65,14 +66,21 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
     for (int i = 0; i < NORM_THREADS / 32; ++i) tot += red[i];
     const float inv = 1.0f / sqrtf(tot / (float)D + eps);
     const float4 *wr = reinterpret_cast<const float4 *>(w);
-    float4 *hr = reinterpret_cast<float4 *>(h + t * D);
 #pragma unroll
     for (int k = 0; k < NORM_VEC; ++k) {
         const int i = threadIdx.x + k * NORM_THREADS;
         if (i < n4) {
             if (dr) xr[i] = v[k];
             const float4 g = wr[i];
-            hr[i] = make_float4(v[k].x * inv * g.x, v[k].y * inv * g.y, v[k].z * inv * g.z, v[k].w * inv * g.w);
+            const float4 o = make_float4(v[k].x * inv * g.x, v[k].y * inv * g.y, v[k].z * inv * g.z, v[k].w * inv * g.w);
+            if (h) reinterpret_cast<float4 *>(h + t * D)[i] = o;
+            if (hb) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t *>(&a);
+                u.y = *reinterpret_cast<uint32_t *>(&b);
+                reinterpret_cast<uint2 *>(hb + t * D)[i] = u;
+            }
         }
     }
 }
@@ -80,22 +88,26 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
 // qkv = [q (H*hd) | k (KV*hd) | v (KV*hd)]: rotate q and k in place over the
 // first ``rotary`` dims (adjacent pairs, engine/model.py:205-217):
 // inv_j = 1 / base^(j / half), angle = pos * inv_j.
-__global__ void rope_kernel(float *__restrict__ qkv, int H, int KV, int hd, int rotary, float base,
+// Rows t of qkv (row stride (H + 2 KV) * hd) are positions *pos_p + t.
+__global__ void rope_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd, int rotary, float base,
                             const int *__restrict__ pos_p, int max_seq, int *err)
 {
-    const int pos = *pos_p;
-    if (pos < 0 || pos >= max_seq) {
+    const int pos0 = *pos_p;
+    if (pos0 < 0 || pos0 + T > max_seq) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
         return;
     }
     const int half = rotary / 2;
     const int pairs = (H + KV) * half;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += gridDim.x * blockDim.x) {
-        const int hh = i / half, j = i % half;
+    const long long row = (long long)(H + 2 * KV) * hd;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * pairs;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / pairs), r = (int)(i % pairs);
+        const int hh = r / half, j = r % half;
         const float inv = 1.0f / powf(base, (float)j / (float)half);
-        const float ang = (float)pos * inv;
+        const float ang = (float)(pos0 + t) * inv;
         const float c = cosf(ang), s = sinf(ang);
-        float *a = qkv + (long long)hh * hd + 2 * j;
+        float *a = qkv + t * row + (long long)hh * hd + 2 * j;
         const float e = a[0], o = a[1];
         a[0] = e * c - o * s;
         a[1] = e * s + o * c;
@@ -103,16 +115,20 @@ __global__ void rope_kernel(float *__restrict__ qkv, int H, int KV, int hd, int 
 }
 
 // cache[pos] = k, v (cache layout [max_seq][KV][hd], as the reference's KVCache)
-__global__ void kv_store_kernel(const float *__restrict__ qkv, int H, int KV, int hd, const int *__restrict__ pos_p,
-                                float *__restrict__ kc, float *__restrict__ vc, int max_seq)
+__global__ void kv_store_kernel(const float *__restrict__ qkv, int T, int H, int KV, int hd,
+                                const int *__restrict__ pos_p, float *__restrict__ kc, float *__restrict__ vc,
+                                int max_seq)
 {
-    const int pos = *pos_p;
-    if (pos < 0 || pos >= max_seq) return;
+    const int pos0 = *pos_p;
+    if (pos0 < 0 || pos0 + T > max_seq) return;
     const int n = KV * hd;
-    const float *k = qkv + (long long)H * hd, *v = k + n;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        kc[(long long)pos * n + i] = k[i];
-        vc[(long long)pos * n + i] = v[i];
+    const long long row = (long long)(H + 2 * KV) * hd;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / n), e = (int)(i % n);
+        const float *k = qkv + t * row + (long long)H * hd;
+        kc[(long long)(pos0 + t) * n + e] = k[e];
+        vc[(long long)(pos0 + t) * n + e] = k[n + e];
     }
 }
 
@@ -201,6 +217,119 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__
     }
 }
 
+// Causal prefill attention (engine/model.py:130-160, forward_sequence): query
+// row t (position *pos_p + t, rotated q in qkv row t) attends to cache
+// positions 0 .. *pos_p + t.  CTA = (query head h, tile of PF_Q query rows),
+// 256 threads: thread (row r = tid / 8, s = tid % 8) owns dims s, s+8, ...
+// of row r.  Key tiles of PF_K positions are staged in shared memory (rows
+// padded by one float); online softmax per row (running max and sum, the
+// 8 threads of a row combine with shuffles); output bf16 for the O GEMM.
+constexpr int PF_Q = 32, PF_K = 64, PF_THREADS = 256;
+__global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *__restrict__ qkv,
+                                                                  const float *__restrict__ kc,
+                                                                  const float *__restrict__ vc,
+                                                                  const int *__restrict__ pos_p, int T, int H, int KV,
+                                                                  int hd, int max_seq, __nv_bfloat16 *__restrict__ out)
+{
+    extern __shared__ float pf[];
+    const int h = blockIdx.x, t0 = blockIdx.y * PF_Q;
+    if (t0 >= T) return;
+    const int g = h / (H / KV);
+    const int p0 = *pos_p;
+    if (p0 < 0 || p0 + T > max_seq) return;
+    const int nq = min(PF_Q, T - t0);
+    const int st = hd + 1;
+    float *qs = pf;                    // [PF_Q][hd + 1]
+    float *ks = qs + PF_Q * st;        // [PF_K][hd + 1]
+    float *vs = ks + PF_K * st;        // [PF_K][hd + 1]
+    float *ps = vs + PF_K * st;        // [PF_Q][PF_K + 1]
+    const int tid = threadIdx.x, r = tid >> 3, s = tid & 7;
+    const long long R = (long long)(H + 2 * KV) * hd;
+    for (int i = tid; i < PF_Q * hd; i += PF_THREADS) {
+        const int rr = i / hd, d = i % hd;
+        qs[rr * st + d] = rr < nq ? qkv[(t0 + rr) * R + (long long)h * hd + d] : 0.f;
+    }
+    const int nd = hd / 8;             // dims per thread (<= 16)
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const int my_last = p0 + t0 + r;                     // last key position row r may see
+    const int kmax = p0 + t0 + nq - 1;
+    const float rs = sqrtf((float)hd);
+    for (int k0 = 0; k0 <= kmax; k0 += PF_K) {
+        const int nk = min(PF_K, kmax + 1 - k0);
+        __syncthreads();                                  // previous tile fully used
+        for (int i = tid; i < nk * hd; i += PF_THREADS) {
+            const int j = i / hd, d = i % hd;
+            ks[j * st + d] = kc[((long long)(k0 + j) * KV + g) * hd + d];
+            vs[j * st + d] = vc[((long long)(k0 + j) * KV + g) * hd + d];
+        }
+        __syncthreads();
+        float sc[8];
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int j = s + 8 * i;
+            float v = -INFINITY;
+            if (r < nq && j < nk && k0 + j <= my_last) {
+                float dsum = 0.f;
+                for (int e = 0; e < hd; ++e) dsum = fmaf(qs[r * st + e], ks[j * st + e], dsum);
+                v = dsum / rs;
+            }
+            sc[i] = v;
+            tmax = fmaxf(tmax, v);
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        const float mn = fmaxf(m, tmax);
+        const float scale = (m == -INFINITY) ? 0.f : expf(m - mn);
+        float psum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float p = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mn);
+            ps[r * (PF_K + 1) + s + 8 * i] = p;
+            psum += p;
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+        l = l * scale + psum;
+        m = mn;
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc[k] *= scale;
+        for (int j = 0; j < nk; ++j) {
+            const float p = ps[r * (PF_K + 1) + j];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                if (k < nd) acc[k] = fmaf(p, vs[j * st + s + 8 * k], acc[k]);
+        }
+    }
+    if (r < nq) {
+        const float inv = 1.0f / l;
+        __nv_bfloat16 *o = out + (long long)(t0 + r) * H * hd + (long long)h * hd;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (k < nd) o[s + 8 * k] = __float2bfloat16_rn(acc[k] * inv);
+    }
+}
+
+cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
+                                int KV, int hd, int max_seq, __nv_bfloat16 *out, cudaStream_t st)
+{
+    if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 8 || hd > 128 || hd % 8 || max_seq < 1) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((PF_Q + 2 * PF_K) * (hd + 1) + PF_Q * (PF_K + 1)) * sizeof(float);
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr = smem;
+    }
+    attn_prefill_kernel<<<dim3(H, (T + PF_Q - 1) / PF_Q), PF_THREADS, smem, st>>>(qkv, kc, vc, pos, T, H, KV, hd,
+                                                                                   max_seq, out);
+    return cudaGetLastError();
+}
+
 // out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in order.
 __global__ void attn_combine_kernel(const float *__restrict__ part, int nch, int hd, float *__restrict__ out)
 {
@@ -263,24 +392,29 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 }
 
 cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
-                               cudaStream_t st)
+                               __nv_bfloat16 *hb, cudaStream_t st)
 {
     if (T < 1 || D < 4 || D % 4 || D > 4 * NORM_THREADS * NORM_VEC || (reinterpret_cast<uintptr_t>(x) & 15) ||
         (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
-        (delta && (reinterpret_cast<uintptr_t>(delta) & 15)))
+        (reinterpret_cast<uintptr_t>(hb) & 7) || (!h && !hb) || (delta && (reinterpret_cast<uintptr_t>(delta) & 15)))
         return cudaErrorInvalidValue;
-    add_rmsnorm_kernel<<<T, NORM_THREADS, 0, st>>>(x, delta, w, D, eps, h);
+    add_rmsnorm_kernel<<<T, NORM_THREADS, 0, st>>>(x, delta, w, D, eps, h, hb);
     return cudaGetLastError();
 }
 
-cudaError_t launch_rope_kv(float *qkv, int H, int KV, int hd, int rotary, float base, const int *pos, float *kc,
-                           float *vc, int max_seq, int *err, cudaStream_t st)
+cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
+                           float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st)
 {
-    if (H < 1 || KV < 1 || H % KV || hd < 2 || rotary < 0 || rotary > hd || rotary % 2 || max_seq < 1)
+    if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 2 || rotary < 0 || rotary > hd || rotary % 2 || max_seq < 1)
         return cudaErrorInvalidValue;
-    const int pairs = (H + KV) * (rotary / 2);
-    if (pairs > 0) rope_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(qkv, H, KV, hd, rotary, base, pos, max_seq, err);
-    kv_store_kernel<<<(KV * hd + 255) / 256, 256, 0, st>>>(qkv, H, KV, hd, pos, kc, vc, max_seq);
+    const long long pairs = (long long)T * (H + KV) * (rotary / 2);
+    const long long cap = 8LL * num_sms;
+    if (pairs > 0) {
+        const long long g = std::min(cap, (pairs + 255) / 256);
+        rope_kernel<<<(int)g, 256, 0, st>>>(qkv, T, H, KV, hd, rotary, base, pos, max_seq, err);
+    }
+    const long long n = (long long)T * KV * hd;
+    kv_store_kernel<<<(int)std::min(cap, (n + 255) / 256), 256, 0, st>>>(qkv, T, H, KV, hd, pos, kc, vc, max_seq);
     return cudaGetLastError();
 }
 

@@ -149,7 +149,9 @@ template <int T>
 __global__ void dequant_row_kernel(const uint8_t *__restrict__ raw, long long row_bytes, int cols,
                                    const int *__restrict__ row_idx, int rows, float *__restrict__ out, int *err)
 {
-    const int r = *row_idx;
+    // blockIdx.y: which of the requested rows (row_idx[y] -> out row y)
+    const int r = row_idx[blockIdx.y];
+    out += (long long)blockIdx.y * cols;
     if (r < 0 || r >= rows) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
         return;
@@ -168,10 +170,12 @@ __global__ void dequant_row_kernel(const uint8_t *__restrict__ raw, long long ro
 }
 
 cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
-                               float *out, int *err, cudaStream_t st)
+                               int n, float *out, int *err, cudaStream_t st)
 {
-    if (cols < 32 || cols % type_vals(type) || (reinterpret_cast<uintptr_t>(out) & 15)) return cudaErrorInvalidValue;
-    const int runs = cols / 32, threads = 128, grid = (runs + threads - 1) / threads;
+    if (cols < 32 || cols % type_vals(type) || n < 1 || n > 65535 || (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    const int runs = cols / 32, threads = 128;
+    const dim3 grid((runs + threads - 1) / threads, n);
     const uint8_t *r = static_cast<const uint8_t *>(raw);
     switch (type) {
     case T_Q4_0: dequant_row_kernel<T_Q4_0><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;

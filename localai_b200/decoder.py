@@ -20,6 +20,14 @@ The position and the token live in device memory, so a step is captured once
 in a CUDA graph and replayed per token without host synchronisation
 (``capture()``); prompt tokens are fed by overwriting the device token before
 each step.
+
+``prefill(tokens)`` runs a whole prompt at once (``LlamaModel.forward_sequence``,
+engine/model.py:118-170): embedding rows, then per layer RMSNorm (bf16 out),
+the tensor-core GEMMs (QKV, O, gate/up with fused SiLU*up, down) over all
+prompt rows, RoPE and the KV-cache store for every row, and causal
+grouped-query attention (``b200q_attn_prefill_dev``); the last row goes
+through the output head and argmax like a decode step, so decoding continues
+from there.  bf16 tensor-core operands: logits within 1e-2 of the f32 path.
 """
 from __future__ import annotations
 
@@ -114,15 +122,15 @@ class QuantLlama:
         c, lib, st = self.cfg, self.lib, _stream()
         hd, kvd = c.head_dim, c.n_kv_heads * c.head_dim
         _lib.check(lib.b200q_dequant_row_dev(self.t_emb, self.emb.data_ptr(), self.emb_row_bytes, c.d_model,
-                                             self.token.data_ptr(), c.vocab, self.x.data_ptr(), st))
+                                             self.token.data_ptr(), c.vocab, 1, self.x.data_ptr(), st))
         delta = None
         for li, L in enumerate(self.layers):
             _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), None if delta is None else delta.data_ptr(),
                                                  L['attn_norm'].data_ptr(), 1, c.d_model, c.eps, self.h.data_ptr(),
-                                                 st))
+                                                 None, st))
             self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            _lib.check(lib.b200q_rope_kv_dev(self.qkv.data_ptr(), c.n_heads, c.n_kv_heads, hd, self.rotary,
+            _lib.check(lib.b200q_rope_kv_dev(self.qkv.data_ptr(), 1, c.n_heads, c.n_kv_heads, hd, self.rotary,
                                              c.rope_base, self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                              c.max_seq, st))
             _lib.check(lib.b200q_attn_decode_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
@@ -130,14 +138,79 @@ class QuantLlama:
                                                  self.scratch.data_ptr(), self.att.data_ptr(), st))
             self._gemv(L['o'], self.att, self.o, c.d_model, c.d_model)
             _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), self.o.data_ptr(), L['ffn_norm'].data_ptr(), 1,
-                                                 c.d_model, c.eps, self.h.data_ptr(), st))
+                                                 c.d_model, c.eps, self.h.data_ptr(), None, st))
             self._gemv(L['gu'], self.h, self.gu, 2 * c.d_ff, c.d_model)
             _lib.check(lib.b200q_silu_mul_dev(self.gu.data_ptr(), 1, c.d_ff, self.act.data_ptr(), c.d_ff, st))
             self._gemv(L['down'], self.act, self.dn, c.d_model, c.d_ff)
             delta = self.dn
         _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), delta.data_ptr(), self.out_norm.data_ptr(), 1,
-                                             c.d_model, c.eps, self.h.data_ptr(), st))
+                                             c.d_model, c.eps, self.h.data_ptr(), None, st))
         self._gemv((self.out_w, self.t_out), self.h, self.logits, c.vocab, c.d_model)
+        _lib.check(lib.b200q_argmax_dev(self.logits.data_ptr(), c.vocab, self.token.data_ptr(), self.pos.data_ptr(),
+                                        self.tokens.data_ptr(), c.max_seq, self.amax_key.data_ptr(), st))
+
+    # -- batched prompt --------------------------------------------------------
+    def _gemm_w(self, key, w, rows, cols):
+        """16-byte-row copy of a weight for the tensor-core path (made once)."""
+        cache = self.__dict__.setdefault('_gemm_cache', {})
+        if key not in cache:
+            raw, t = w
+            cache[key] = ops.pad_rows(raw, rows, ops.packed_row_bytes(t, cols)) + (t,)
+        return cache[key]
+
+    def prefill(self, tokens: list[int]) -> None:
+        """All prompt tokens at positions pos, pos+1, ... in one pass; leaves
+        the argmax of the last token in ``tokens[pos + len - 1]`` and advances
+        pos by len(tokens)."""
+        c, lib, st = self.cfg, self.lib, _stream()
+        T = len(tokens)
+        if T < 1:
+            raise ValueError('empty prompt')
+        dev, hd = self.dev, c.head_dim
+        kvd = c.n_kv_heads * hd
+        nq = c.n_heads * hd + 2 * kvd
+        ids = torch.tensor(tokens, dtype=torch.int32, device=dev)
+        X = torch.empty((T, c.d_model), dtype=torch.float32, device=dev)
+        _lib.check(lib.b200q_dequant_row_dev(self.t_emb, self.emb.data_ptr(), self.emb_row_bytes, c.d_model,
+                                             ids.data_ptr(), c.vocab, T, X.data_ptr(), st))
+        Hb = torch.empty((T, c.d_model), dtype=torch.bfloat16, device=dev)
+        qkv = torch.empty((T, nq), dtype=torch.float32, device=dev)
+        attb = torch.empty((T, c.d_model), dtype=torch.bfloat16, device=dev)
+        O = torch.empty((T, c.d_model), dtype=torch.float32, device=dev)
+        act = torch.empty((T, c.d_ff), dtype=torch.bfloat16, device=dev)
+        Dn = torch.empty((T, c.d_model), dtype=torch.float32, device=dev)
+        off = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        delta = None
+        for li, L in enumerate(self.layers):
+            _lib.check(lib.b200q_add_rmsnorm_dev(X.data_ptr(), None if delta is None else delta.data_ptr(),
+                                                 L['attn_norm'].data_ptr(), T, c.d_model, c.eps, None, Hb.data_ptr(),
+                                                 st))
+            wq, sq, tq = self._gemm_w(('qkv', li), L['qkv'], nq, c.d_model)
+            ops.gemm_quant(Hb, wq, off, k=c.d_model, n_feat=nq, w_rows_per_group=nq, ggml_type=tq, w_row_bytes=sq,
+                           out=qkv)
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
+                                             self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), c.max_seq, st))
+            _lib.check(lib.b200q_attn_prefill_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.pos.data_ptr(),
+                                                  T, c.n_heads, c.n_kv_heads, hd, c.max_seq, attb.data_ptr(), st))
+            wo, so, to = self._gemm_w(('o', li), L['o'], c.d_model, c.d_model)
+            ops.gemm_quant(attb, wo, off, k=c.d_model, n_feat=c.d_model, w_rows_per_group=c.d_model, ggml_type=to,
+                           w_row_bytes=so, out=O)
+            _lib.check(lib.b200q_add_rmsnorm_dev(X.data_ptr(), O.data_ptr(), L['ffn_norm'].data_ptr(), T, c.d_model,
+                                                 c.eps, None, Hb.data_ptr(), st))
+            wg, sg, tg = self._gemm_w(('gu', li), L['gu'], 2 * c.d_ff, c.d_model)
+            ops.gemm_quant(Hb, wg, off, k=c.d_model, n_feat=c.d_ff, w_rows_per_group=2 * c.d_ff, up_offset=c.d_ff,
+                           ggml_type=tg, w_row_bytes=sg, act=act)
+            wd, sd, td = self._gemm_w(('down', li), L['down'], c.d_model, c.d_ff)
+            ops.gemm_quant(act, wd, off, k=c.d_ff, n_feat=c.d_model, w_rows_per_group=c.d_model, ggml_type=td,
+                           w_row_bytes=sd, out=Dn)
+            delta = Dn
+        # last row -> output head, as a decode step
+        self.x.copy_(X[T - 1])
+        _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), Dn[T - 1].data_ptr(), self.out_norm.data_ptr(), 1,
+                                             c.d_model, c.eps, self.h.data_ptr(), None, st))
+        self._gemv((self.out_w, self.t_out), self.h, self.logits, c.vocab, c.d_model)
+        self.pos.add_(T - 1)
         _lib.check(lib.b200q_argmax_dev(self.logits.data_ptr(), c.vocab, self.token.data_ptr(), self.pos.data_ptr(),
                                         self.tokens.data_ptr(), c.max_seq, self.amax_key.data_ptr(), st))
 

@@ -95,3 +95,27 @@ def test_long_context_crosses_attention_chunks():
         if p in (127, 128, 200, 269):
             torch.cuda.synchronize()
             assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+
+
+@pytest.mark.parametrize('t', [8, 12])
+def test_prefill_matches_oracle_then_decode_continues(t):
+    """Batched prefill (tensor cores, bf16 weights and activations): last-token
+    logits against the float64 oracle, then decoding continues from the cache
+    it filled.  Bar 3e-2 normwise: each bf16 tensor-core op stays within 1e-2,
+    and two layers of random (untrained) weights compound those roundings."""
+    rng = np.random.default_rng(40 + t)
+    model, ref_w, cfg = build(rng, t, max_seq=160)
+    prompt = [int(v) for v in rng.integers(0, 300, size=70)]       # crosses one 64-position key tile
+    ref = o.llama_decode_f64(ref_w, cfg, prompt + [9, 123])
+    model.reset()
+    model.prefill(prompt)
+    torch.cuda.synchronize()
+    assert int(model.pos.item()) == len(prompt)
+    err = o.normwise_rel_err(model.logits.cpu().numpy(), ref[len(prompt) - 1])
+    assert err < 3e-2, ('prefill logits', err)
+    for i, tok in enumerate([9, 123]):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        err = o.normwise_rel_err(model.logits.cpu().numpy(), ref[len(prompt) + i])
+        assert err < 3e-2, ('decode step after prefill', i, err)
