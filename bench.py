@@ -472,7 +472,9 @@ def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
            'prefill': {'ms': round(prefill_ms, 2), 'tokens_per_s': round(prompt_len / (prefill_ms * 1e-3), 1),
                        'TFLOP_s': round(prefill_flops / (prefill_ms * 1e-3) / 1e12, 1), 'flops': prefill_flops,
                        'path': 'tcgen05 GEMMs over the prompt rows + causal attention kernel'},
-           'launches_per_token': 5 + NL * 11, 'path': 'CUDA graph of one step: 7 GEMVs/layer + norms, RoPE, attention'}
+           'launches_per_token': 5 + NL * 10,
+           'path': 'CUDA graph of one step: per layer 4 GEMVs + 2 norms, RoPE/KV store, 2 attention kernels, SiLU*up; '
+                   'every launch programmatic-dependent'}
     del model
     torch.cuda.empty_cache()
     return res

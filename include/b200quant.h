@@ -282,7 +282,10 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
 
 /* ---- Decode step of the reference's Llama decoder (engine/model.py:174-240)
  * around the quantised GEMVs; every call reads the position / token from
- * device memory, so a whole step can be captured in a CUDA graph.
+ * device memory, so a whole step can be captured in a CUDA graph.  Their
+ * kernels are launched programmatic-dependent: each lets the next kernel of
+ * the stream launch at once (a following GEMV starts streaming its weights)
+ * and reads nothing before the previous kernel has completed.
  *   b200q_dequant_row_dev   out[i][cols] = row row_idx[i] of a quantised matrix,
  *                           i < n (bit-exact; the token embedding lookup)
  *   b200q_add_rmsnorm_dev   per row t < T: x += delta (when not NULL);

@@ -778,7 +778,7 @@ B200Q_API int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int ro
     if (!qkv || !pos || !k_cache || !v_cache) return set_status(B200Q_EINVAL, "rope_kv: null pointer");
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
-    g_launches += 2;
+    ++g_launches;
     return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, base, pos, k_cache, v_cache, max_seq, di->err,
                                       di->sms, (cudaStream_t)stream),
                        "rope_kv");

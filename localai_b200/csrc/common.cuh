@@ -134,6 +134,44 @@ __device__ __forceinline__ uint64_t policy_evict_last()
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Entry of every small kernel on the decode chain: the next kernel (usually a
+// GEMV that starts streaming its constant weights at once) may launch now,
+// and nothing of the previous kernel is read before it has completed.  Every
+// kernel waits before it can complete, so completion stays transitive along
+// the stream.
+__device__ __forceinline__ void pdl_enter()
+{
+    pdl_launch_dependents();
+    pdl_wait();
+}
+
+// Launch with programmatic stream serialization (the kernel may start while
+// the previous kernel of the stream is still running; see pdl_enter).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                     Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// silu(g) * u with silu(g) = g / (1 + exp(-clip(g, -80, 80)))
+// (engine/model.py:161-166; the clip only keeps exp finite).
+__device__ __forceinline__ float silu_mul(float g, float u)
+{
+    const float c = fminf(fmaxf(g, -80.f), 80.f);
+    return g / (1.0f + expf(-c)) * u;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

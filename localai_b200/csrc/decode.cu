@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
                                                                    float *__restrict__ h, __nv_bfloat16 *__restrict__ hb)
 {
     __shared__ float red[NORM_THREADS / 32];
+    pdl_enter();
     const long long t = blockIdx.x;
     float4 *xr = reinterpret_cast<float4 *>(x + t * D);
     const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + t * D) : nullptr;
@@ -87,48 +88,57 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
 
 // qkv = [q (H*hd) | k (KV*hd) | v (KV*hd)]: rotate q and k in place over the
 // first ``rotary`` dims (adjacent pairs, engine/model.py:205-217):
-// inv_j = 1 / base^(j / half), angle = pos * inv_j.
-// Rows t of qkv (row stride (H + 2 KV) * hd) are positions *pos_p + t.
-__global__ void rope_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd, int rotary, float base,
-                            const int *__restrict__ pos_p, int max_seq, int *err)
+// inv_j = 1 / base^(j / half), angle = pos * inv_j; and store the rotated k
+// and v of every row into the caches (layout [max_seq][KV][hd], as the
+// reference's KVCache).  Rows t of qkv (row stride (H + 2 KV) * hd) are
+// positions *pos_p + t.  Work items of one row: H*half q pairs, KV*half k
+// pairs (rotated, then stored), KV*(hd - rotary) unrotated k values and KV*hd
+// v values (both only stored).
+__global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd, int rotary, float base,
+                               const int *__restrict__ pos_p, float *__restrict__ kc, float *__restrict__ vc,
+                               int max_seq, int *err)
 {
+    pdl_enter();
     const int pos0 = *pos_p;
     if (pos0 < 0 || pos0 + T > max_seq) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
         return;
     }
     const int half = rotary / 2;
-    const int pairs = (H + KV) * half;
+    const int nq = H * half, nk = KV * half, nkr = KV * (hd - rotary), nv = KV * hd;
+    const long long per_row = (long long)nq + nk + nkr + nv;
     const long long row = (long long)(H + 2 * KV) * hd;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * pairs;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / pairs), r = (int)(i % pairs);
-        const int hh = r / half, j = r % half;
-        const float inv = 1.0f / powf(base, (float)j / (float)half);
-        const float ang = (float)(pos0 + t) * inv;
-        const float c = cosf(ang), s = sinf(ang);
-        float *a = qkv + t * row + (long long)hh * hd + 2 * j;
-        const float e = a[0], o = a[1];
-        a[0] = e * c - o * s;
-        a[1] = e * s + o * c;
-    }
-}
-
-// cache[pos] = k, v (cache layout [max_seq][KV][hd], as the reference's KVCache)
-__global__ void kv_store_kernel(const float *__restrict__ qkv, int T, int H, int KV, int hd,
-                                const int *__restrict__ pos_p, float *__restrict__ kc, float *__restrict__ vc,
-                                int max_seq)
-{
-    const int pos0 = *pos_p;
-    if (pos0 < 0 || pos0 + T > max_seq) return;
     const int n = KV * hd;
-    const long long row = (long long)(H + 2 * KV) * hd;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * n;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * per_row;
          i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / n), e = (int)(i % n);
-        const float *k = qkv + t * row + (long long)H * hd;
-        kc[(long long)(pos0 + t) * n + e] = k[e];
-        vc[(long long)(pos0 + t) * n + e] = k[n + e];
+        const int t = (int)(i / per_row);
+        int r = (int)(i % per_row);
+        float *qr = qkv + t * row;
+        float *kcr = kc + (long long)(pos0 + t) * n, *vcr = vc + (long long)(pos0 + t) * n;
+        if (r < nq + nk) {                               // a rotated pair of q or k
+            const bool is_k = r >= nq;
+            if (is_k) r -= nq;
+            const int hh = r / half, j = r % half;
+            const float inv = 1.0f / powf(base, (float)j / (float)half);
+            const float ang = (float)(pos0 + t) * inv;
+            const float c = cosf(ang), s = sinf(ang);
+            const long long off = (long long)((is_k ? H : 0) + hh) * hd + 2 * j;
+            const float e = qr[off], o = qr[off + 1];
+            const float e2 = e * c - o * s, o2 = e * s + o * c;
+            qr[off] = e2;
+            qr[off + 1] = o2;
+            if (is_k) {
+                kcr[hh * hd + 2 * j] = e2;
+                kcr[hh * hd + 2 * j + 1] = o2;
+            }
+        } else if (r < nq + nk + nkr) {                  // k beyond the rotary dims
+            r -= nq + nk;
+            const int hh = r / (hd - rotary), d = rotary + r % (hd - rotary);
+            kcr[hh * hd + d] = qr[(long long)(H + hh) * hd + d];
+        } else {                                         // v
+            r -= nq + nk + nkr;
+            vcr[r] = qr[(long long)(H + KV) * hd + r];
+        }
     }
 }
 
@@ -146,6 +156,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__
                                                                  int max_seq, float *__restrict__ part)
 {
     extern __shared__ float asm_[];
+    pdl_enter();
     const int G = H / KV, g = blockIdx.x, c = blockIdx.y;
     const int L = min(*pos_p + 1, max_seq);
     const int l0 = c * ATT_CHUNK, l1 = min(L, l0 + ATT_CHUNK);
@@ -232,6 +243,7 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
                                                                   int hd, int max_seq, __nv_bfloat16 *__restrict__ out)
 {
     extern __shared__ float pf[];
+    pdl_enter();
     const int h = blockIdx.x, t0 = blockIdx.y * PF_Q;
     if (t0 >= T) return;
     const int g = h / (H / KV);
@@ -325,14 +337,14 @@ cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *
         if (e != cudaSuccess) return e;
         attr = smem;
     }
-    attn_prefill_kernel<<<dim3(H, (T + PF_Q - 1) / PF_Q), PF_THREADS, smem, st>>>(qkv, kc, vc, pos, T, H, KV, hd,
-                                                                                   max_seq, out);
-    return cudaGetLastError();
+    return launch_pdl(attn_prefill_kernel, dim3(H, (T + PF_Q - 1) / PF_Q), dim3(PF_THREADS), smem, st, qkv, kc, vc, pos,
+                      T, H, KV, hd, max_seq, out);
 }
 
 // out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in order.
 __global__ void attn_combine_kernel(const float *__restrict__ part, int nch, int hd, float *__restrict__ out)
 {
+    pdl_enter();
     const int h = blockIdx.x;
     const float *ph = part + (long long)h * nch * (hd + 2);
     float M = -INFINITY;
@@ -360,6 +372,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 {
     __shared__ float bv[1024];
     __shared__ int bi[1024];
+    pdl_enter();
     float best = -INFINITY;
     int idx = 0x7fffffff;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -398,8 +411,7 @@ cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int
         (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
         (reinterpret_cast<uintptr_t>(hb) & 7) || (!h && !hb) || (delta && (reinterpret_cast<uintptr_t>(delta) & 15)))
         return cudaErrorInvalidValue;
-    add_rmsnorm_kernel<<<T, NORM_THREADS, 0, st>>>(x, delta, w, D, eps, h, hb);
-    return cudaGetLastError();
+    return launch_pdl(add_rmsnorm_kernel, dim3(T), dim3(NORM_THREADS), 0, st, x, delta, w, D, eps, h, hb);
 }
 
 cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
@@ -407,15 +419,11 @@ cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary,
 {
     if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 2 || rotary < 0 || rotary > hd || rotary % 2 || max_seq < 1)
         return cudaErrorInvalidValue;
-    const long long pairs = (long long)T * (H + KV) * (rotary / 2);
-    const long long cap = 8LL * num_sms;
-    if (pairs > 0) {
-        const long long g = std::min(cap, (pairs + 255) / 256);
-        rope_kernel<<<(int)g, 256, 0, st>>>(qkv, T, H, KV, hd, rotary, base, pos, max_seq, err);
-    }
-    const long long n = (long long)T * KV * hd;
-    kv_store_kernel<<<(int)std::min(cap, (n + 255) / 256), 256, 0, st>>>(qkv, T, H, KV, hd, pos, kc, vc, max_seq);
-    return cudaGetLastError();
+    const long long items = (long long)T * ((long long)(H + KV) * (rotary / 2) + (long long)KV * (hd - rotary) +
+                                            (long long)KV * hd);
+    const long long g = std::min(8LL * num_sms, (items + 255) / 256);
+    return launch_pdl(rope_kv_kernel, dim3((unsigned)g), dim3(256), 0, st, qkv, T, H, KV, hd, rotary, base, pos, kc,
+                      vc, max_seq, err);
 }
 
 size_t attn_scratch_floats(int H, int hd, int max_seq)
@@ -437,9 +445,10 @@ cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc,
         if (e != cudaSuccess) return e;
         attr = smem;
     }
-    attn_chunk_kernel<<<dim3(KV, nch), ATT_THREADS, smem, st>>>(q, kc, vc, pos, H, KV, hd, max_seq, part);
-    attn_combine_kernel<<<H, 128, 0, st>>>(part, nch, hd, out);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(attn_chunk_kernel, dim3(KV, nch), dim3(ATT_THREADS), smem, st, q, kc, vc, pos, H, KV, hd,
+                               max_seq, part);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, part, nch, hd, out);
 }
 
 // Grid-wide argmax: every CTA reduces a slice, then one 64-bit atomicMax of
@@ -458,6 +467,7 @@ __global__ void __launch_bounds__(256) argmax_part_kernel(const float *__restric
                                                           unsigned long long *key)
 {
     __shared__ unsigned long long red[8];
+    pdl_enter();
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
         const unsigned long long k = argmax_key(logits[i], i);
@@ -478,6 +488,7 @@ __global__ void __launch_bounds__(256) argmax_part_kernel(const float *__restric
 
 __global__ void argmax_finish_kernel(unsigned long long *key, int *token, int *pos_p, int *out_tokens, int max_tokens)
 {
+    pdl_enter();
     const unsigned long long k = *key;
     const int t = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
     *token = t;
@@ -494,14 +505,13 @@ cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int 
 {
     if (V < 1) return cudaErrorInvalidValue;
     if (!key) {
-        argmax_kernel<<<1, 1024, 0, st>>>(logits, V, token, pos, out_tokens, max_tokens);
-        return cudaGetLastError();
+        return launch_pdl(argmax_kernel, dim3(1), dim3(1024), 0, st, logits, V, token, pos, out_tokens, max_tokens);
     }
     int grid = (V + 255) / 256;
     if (grid > num_sms) grid = num_sms;
-    argmax_part_kernel<<<grid, 256, 0, st>>>(logits, V, key);
-    argmax_finish_kernel<<<1, 1, 0, st>>>(key, token, pos, out_tokens, max_tokens);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(argmax_part_kernel, dim3(grid), dim3(256), 0, st, logits, V, key);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(argmax_finish_kernel, dim3(1), dim3(1), 0, st, key, token, pos, out_tokens, max_tokens);
 }
 
 } // namespace b200q

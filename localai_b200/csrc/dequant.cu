@@ -150,6 +150,7 @@ __global__ void dequant_row_kernel(const uint8_t *__restrict__ raw, long long ro
                                    const int *__restrict__ row_idx, int rows, float *__restrict__ out, int *err)
 {
     // blockIdx.y: which of the requested rows (row_idx[y] -> out row y)
+    pdl_enter();
     const int r = row_idx[blockIdx.y];
     out += (long long)blockIdx.y * cols;
     if (r < 0 || r >= rows) {
@@ -178,14 +179,13 @@ cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, i
     const dim3 grid((runs + threads - 1) / threads, n);
     const uint8_t *r = static_cast<const uint8_t *>(raw);
     switch (type) {
-    case T_Q4_0: dequant_row_kernel<T_Q4_0><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
-    case T_Q8_0: dequant_row_kernel<T_Q8_0><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
-    case T_Q4_K: dequant_row_kernel<T_Q4_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
-    case T_Q5_K: dequant_row_kernel<T_Q5_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
-    case T_Q6_K: dequant_row_kernel<T_Q6_K><<<grid, threads, 0, st>>>(r, row_bytes, cols, row_idx, rows, out, err); break;
+    case T_Q4_0: return launch_pdl(dequant_row_kernel<T_Q4_0>, grid, dim3(threads), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
+    case T_Q8_0: return launch_pdl(dequant_row_kernel<T_Q8_0>, grid, dim3(threads), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
+    case T_Q4_K: return launch_pdl(dequant_row_kernel<T_Q4_K>, grid, dim3(threads), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
+    case T_Q5_K: return launch_pdl(dequant_row_kernel<T_Q5_K>, grid, dim3(threads), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
+    case T_Q6_K: return launch_pdl(dequant_row_kernel<T_Q6_K>, grid, dim3(threads), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 } // namespace b200q

@@ -9,13 +9,12 @@ namespace b200q {
 
 __global__ void silu_mul_kernel(const float *__restrict__ gu, int T, int F, float *__restrict__ out, long long ld_out)
 {
+    pdl_enter();
     const long long n = (long long)T * F;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const long long t = i / F;
         const int f = (int)(i - t * F);
-        const float g = gu[t * 2 * F + f], u = gu[t * 2 * F + F + f];
-        const float c = fminf(fmaxf(g, -80.f), 80.f);
-        out[t * ld_out + f] = g / (1.0f + expf(-c)) * u;
+        out[t * ld_out + f] = silu_mul(gu[t * 2 * F + f], gu[t * 2 * F + F + f]);
     }
 }
 
@@ -25,8 +24,7 @@ cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, long long
     const long long n = (long long)T * F;
     long long blocks = (n + 255) / 256;
     if (blocks > 8LL * num_sms) blocks = 8LL * num_sms;
-    silu_mul_kernel<<<(int)blocks, 256, 0, st>>>(gu, T, F, out, ld_out);
-    return cudaGetLastError();
+    return launch_pdl(silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0, st, gu, T, F, out, ld_out);
 }
 
 } // namespace b200q

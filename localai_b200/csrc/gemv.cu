@@ -323,89 +323,126 @@ __device__ __forceinline__ void unit_dot(uint32_t blk, int c, const XU<Unit<T>::
 // 3*NW plane words, then s, sum[2], qsum[4], padded to a multiple of 4 words.
 template <int NW> struct XPackWords { static constexpr int N = ((3 * NW + 7) + 3) / 4 * 4; };
 
-// Cooperative quantisation of x [ntok, cols] into packed per-unit words in
-// shared memory (xs[(t * units + u) * N ...]).  NW consecutive lanes handle one
-// (token, unit), one 4-value word each; max/sums use shuffles inside the
-// NW-lane segment.  Every lane of the calling warps must execute this.
+// One quantisation task: word k = task % NW of (token, unit) task / NW, i.e.
+// 4 values, packed into the three planes; the unit's max and sums are
+// reduced with shuffles across its NW consecutive lanes, so every lane of the
+// warp must execute quantize_x_word (``valid`` only masks the stores).  The
+// arithmetic and the stores are separate steps so that a thread's tasks of
+// one batch overlap.
+struct XWord {
+    uint32_t p2, p1, p0;   // byte planes of the four values
+    float m, sm;           // unit max |x|, sum of x over the 32-value run
+    int qs;                // sum of xq over the 16-value run
+};
+
 template <int T>
-__device__ __forceinline__ void quantize_x_task(const float4 f, bool valid, int task, uint32_t xs)
+__device__ __forceinline__ XWord quantize_x_word(const float4 f)
 {
-    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
-    const int k = task % NW, tu = task / NW;
+    constexpr int NW = Unit<T>::NW;
+    XWord r;
     float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
 #pragma unroll
     for (int o = 1; o < NW; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float inv = m > 0.f ? 8388607.0f / m : 0.f;
-    const float v[4] = {f.x, f.y, f.z, f.w};
-    uint32_t p2 = 0, p1 = 0, p0 = 0;
-    int qs = 0;
+    // Grid step s = m / (2^23 - 1) and its inverse: values are quantised with
+    // inv and reconstructed with s, which agree to f32 rounding (a |q| that
+    // rounds past 2^23 - 1 is clamped).
+    const float inv = m > 0.f ? __frcp_rn(m) * 8388607.0f : 0.f;
+    int q[4];
+    q[0] = __float2int_rn(f.x * inv);
+    q[1] = __float2int_rn(f.y * inv);
+    q[2] = __float2int_rn(f.z * inv);
+    q[3] = __float2int_rn(f.w * inv);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        int q = __float2int_rn(v[e] * inv);
-        q = max(-8388607, min(8388607, q));
-        p2 |= (uint32_t)((q >> 16) & 0xff) << (8 * e);
-        p1 |= (uint32_t)((q >> 8) & 0xff) << (8 * e);
-        p0 |= (uint32_t)(q & 0xff) << (8 * e);
-        qs += q;
-    }
-    float sm = (v[0] + v[1]) + (v[2] + v[3]);
+    for (int e = 0; e < 4; ++e) q[e] = max(-8388607, min(8388607, q[e]));
+    // byte b of the four values -> one word per plane (two's complement, so
+    // q = 65536 * (int8)b2 + 256 * b1 + b0)
+    auto plane = [&](uint32_t b) {
+        const uint32_t sel = b | ((4u + b) << 4);
+        return __byte_perm(__byte_perm((uint32_t)q[0], (uint32_t)q[1], sel),
+                           __byte_perm((uint32_t)q[2], (uint32_t)q[3], sel), 0x5410);
+    };
+    r.p2 = plane(2);
+    r.p1 = plane(1);
+    r.p0 = plane(0);
+    int qs = (q[0] + q[1]) + (q[2] + q[3]);
+    float sm = (f.x + f.y) + (f.z + f.w);
 #pragma unroll
     for (int o = 1; o < 4; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);      // 16-value runs
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);      // 32-value runs
-    if (valid) {
-        const uint32_t o = xs + (uint32_t)tu * N * 4;
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(p2) : "memory");
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(p1) : "memory");
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(p0) : "memory");
-        if (k == 0)
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(m > 0.f ? m / 8388607.0f : 0.f)) : "memory");
-        if ((k & 7) == 0)
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(sm)) : "memory");
-        if ((k & 3) == 0)
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)qs)) : "memory");
-    }
+    r.m = m;
+    r.sm = sm;
+    r.qs = qs;
+    return r;
 }
 
 template <int T>
-__device__ __forceinline__ float4 quantize_x_load(const float *__restrict__ x, int cols, int units, int tasks, int task)
+__device__ __forceinline__ void store_x_word(const XWord &r, int task, uint32_t xs)
+{
+    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
+    const int k = task % NW, tu = task / NW;
+    const uint32_t o = xs + (uint32_t)tu * N * 4;
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(r.p2) : "memory");
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(r.p1) : "memory");
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(r.p0) : "memory");
+    if (k == 0)
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(r.m * (1.0f / 8388607.0f))) : "memory");
+    if ((k & 7) == 0)
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(r.sm)) : "memory");
+    if ((k & 3) == 0)
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)r.qs)) : "memory");
+}
+
+// Address of the float4 of x that quantisation task ``task`` reads (task <
+// tasks): row t of x, the 4 columns of word k of unit u.
+template <int T>
+__device__ __forceinline__ const float *quantize_x_addr(const float *__restrict__ x, int cols, int units, int task)
 {
     constexpr int NW = Unit<T>::NW;
-    if (task >= tasks) return make_float4(0.f, 0.f, 0.f, 0.f);
     const int k = task % NW, tu = task / NW;
     const int u = tu % units, t = tu / units;
     int c0 = 0, c1 = 0;
     unit_cols<T>(u, c0, c1);
-    return __ldg(reinterpret_cast<const float4 *>(x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7)));
+    return x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7);
 }
 
 // Cooperative quantisation of x [ntok, cols] into packed per-unit words in
 // shared memory (xs[(t * units + u) * N ...]).  NW consecutive lanes handle one
 // (token, unit), one 4-value word each; max/sums use shuffles inside the
-// NW-lane segment.  Every lane of the calling warps must execute this.  When a
-// thread has at most 8 tasks (decode), all of its loads are issued before any
-// is used, so the activation costs one L2 round trip instead of one per task.
+// NW-lane segment.  Every lane of the calling warps must execute this.  A
+// thread's tasks are taken in batches of MAXIT whose loads are all issued
+// before any is used, so the activation costs one L2 round trip per batch.
 template <int T>
-__device__ __forceinline__ void quantize_x_smem(const float *__restrict__ x, int cols, int units, int ntok,
-                                                uint32_t xs, int tid, int nthreads)
+__device__ __forceinline__ void quantize_x_smem(const float *__restrict__ x, int cols, int units, int ntok, uint32_t xs,
+                                                int tid, int nthreads)
 {
     constexpr int NW = Unit<T>::NW;
     constexpr int MAXIT = 8;
     const int tasks = ntok * units * NW;
     const int iters = (tasks + nthreads - 1) / nthreads;
-    if (iters <= MAXIT) {
+    for (int i0 = 0; i0 < iters; i0 += MAXIT) {
         float4 f[MAXIT];
 #pragma unroll
-        for (int i = 0; i < MAXIT; ++i)
-            if (i < iters) f[i] = quantize_x_load<T>(x, cols, units, tasks, i * nthreads + tid);
+        for (int i = 0; i < MAXIT; ++i) {
+            const int task = (i0 + i) * nthreads + tid;
+            f[i] = (i0 + i < iters && task < tasks)
+                       ? __ldg(reinterpret_cast<const float4 *>(quantize_x_addr<T>(x, cols, units, task)))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        // arithmetic of QB tasks at a time, then their stores (register budget)
+        constexpr int QB = 4;
 #pragma unroll
-        for (int i = 0; i < MAXIT; ++i)
-            if (i < iters) quantize_x_task<T>(f[i], i * nthreads + tid < tasks, i * nthreads + tid, xs);
-        return;
-    }
-    for (int base = 0; base < tasks; base += nthreads) {
-        const int task = base + tid;
-        quantize_x_task<T>(quantize_x_load<T>(x, cols, units, tasks, task), task < tasks, task, xs);
+        for (int i1 = 0; i1 < MAXIT; i1 += QB) {
+            XWord r[QB];
+#pragma unroll
+            for (int i = 0; i < QB; ++i)
+                if (i0 + i1 + i < iters) r[i] = quantize_x_word<T>(f[i1 + i]);   // warp-uniform condition
+#pragma unroll
+            for (int i = 0; i < QB; ++i) {
+                const int task = (i0 + i1 + i) * nthreads + tid;
+                if (i0 + i1 + i < iters && task < tasks) store_x_word<T>(r[i], task, xs);
+            }
+        }
     }
 }
 
@@ -673,23 +710,6 @@ __global__ void __launch_bounds__(GemvCap<CPT, NTOK>::THREADS) gemv_kernel(const
 }
 
 // ---------------------------------------------------------------- host side
-// Launch with programmatic stream serialization (PDL).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args)
-{
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, args...);
-}
-
 // Tuning knobs (defaults chosen on B200): target bytes of weights per stage
 // and number of stages.
 static int g_stage_target = 48 * 1024;
@@ -812,7 +832,7 @@ static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, fl
     const size_t smem = smem_of(stages);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
 
-    GemvArgs a;
+    GemvArgs a = {};
     a.w = static_cast<const uint8_t *>(w);
     a.x = x;
     a.y = y;

@@ -119,3 +119,55 @@ def test_prefill_matches_oracle_then_decode_continues(t):
         torch.cuda.synchronize()
         err = o.normwise_rel_err(model.logits.cpu().numpy(), ref[len(prompt) + i])
         assert err < 3e-2, ('decode step after prefill', i, err)
+
+
+@pytest.mark.parametrize('T,rotary', [(1, 64), (5, 32), (3, 0)])
+def test_rope_kv_store_partial_rotary(T, rotary):
+    """b200q_rope_kv_dev: q and k rotated over the first ``rotary`` dims in
+    adjacent pairs (engine/model.py:205-217), rotated k and v stored in the
+    caches at positions pos..pos+T-1; dims past ``rotary`` pass unchanged."""
+    from localai_b200 import _lib, ops
+    rng = np.random.default_rng(T + rotary)
+    H, KV, hd, max_seq, base, p0 = 4, 2, 64, 16, 10000.0, 7
+    qkv = rng.normal(size=(T, (H + 2 * KV) * hd)).astype(np.float32)
+    half = rotary // 2
+    ref = qkv.astype(np.float64).copy()
+    if half:
+        inv = 1.0 / base ** (np.arange(half) / half)
+        for t in range(T):
+            ang = (p0 + t) * inv
+            c, s = np.cos(ang), np.sin(ang)
+            for hh in range(H + KV):
+                a = ref[t, hh * hd:hh * hd + rotary]
+                e, od = a[0::2].copy(), a[1::2].copy()
+                a[0::2], a[1::2] = e * c - od * s, e * s + od * c
+    kc = torch.full((max_seq, KV * hd), float('nan'), device='cuda')
+    vc = torch.full((max_seq, KV * hd), float('nan'), device='cuda')
+    qd = torch.from_numpy(qkv).cuda()
+    pos = torch.tensor([p0], dtype=torch.int32, device='cuda')
+    lib = _lib.load()
+    _lib.check(lib.b200q_rope_kv_dev(qd.data_ptr(), T, H, KV, hd, rotary, base, pos.data_ptr(), kc.data_ptr(),
+                                     vc.data_ptr(), max_seq, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    np.testing.assert_allclose(qd.cpu().numpy(), ref, rtol=0, atol=2e-5)
+    k_ref = ref[:, H * hd:(H + KV) * hd]
+    v_ref = ref[:, (H + KV) * hd:]
+    np.testing.assert_allclose(kc[p0:p0 + T].cpu().numpy(), k_ref, rtol=0, atol=2e-5)
+    np.testing.assert_allclose(vc[p0:p0 + T].cpu().numpy(), v_ref, rtol=0, atol=0)
+    assert torch.isnan(kc[:p0]).all() and torch.isnan(kc[p0 + T:]).all()
+
+
+def test_rope_kv_position_out_of_range_is_reported():
+    from localai_b200 import _lib, ops
+    lib = _lib.load()
+    qkv = torch.zeros((2, 8 * 64), device='cuda')
+    kc = torch.zeros((4, 2 * 64), device='cuda')
+    vc = torch.zeros((4, 2 * 64), device='cuda')
+    pos = torch.tensor([3], dtype=torch.int32, device='cuda')        # 3 + 2 > max_seq 4
+    _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), 2, 4, 2, 64, 64, 10000.0, pos.data_ptr(), kc.data_ptr(),
+                                     vc.data_ptr(), 4, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    with pytest.raises(_lib.B200QError):
+        ops.check_device_error()
+    assert not kc.any() and not vc.any()

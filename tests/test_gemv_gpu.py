@@ -162,3 +162,4 @@ def test_deterministic_repeat():
     a = native_quant.matvec(raw, x, 1024, 4096, 12)
     b = native_quant.matvec(raw, x, 1024, 4096, 12)
     assert np.array_equal(bits(a), bits(b))
+
