@@ -16,15 +16,15 @@
 //   its units stay in registers for the whole kernel.  Groups take different
 //   rows of a stage.  x is read once per CTA; the only shared-memory traffic
 //   is the weight stream itself.
-// * Integer dot products.  Each thread converts its x values once to 24-bit
-//   fixed point, xq = rint(x / s) with s = max|x_unit| / (2^23 - 1), held as
+// * Integer dot products.  x is converted once per CTA to fixed point,
+//   xq = rint(x / s) with s = max|x_unit| / (2^22 - 4) (|xq| < 2^22), held as
 //   three byte planes (xq = 65536*b2 + 256*b1 + b0; b2 signed, b1/b0
 //   unsigned).  The unpacked 4/5/6/8-bit quants are multiplied against the
 //   planes with dp4a (4 products per instruction, exact int32 sums) and every
 //   sub-block sum is scaled and accumulated in f32.  The activation grid step
-//   is 2^-24 of the unit's max |x| -- the same order as f32 rounding -- so
-//   results agree with the f32 dot product to f32 accuracy (the reference
-//   itself quantises x to int8 for Q4_K/Q5_K and int16 for Q6_K,
+//   is ~2^-22 of the unit's max |x| -- the order of f32 rounding -- so
+//   results agree with the f32 dot product to f32-level accuracy (the
+//   reference itself quantises x to int8 for Q4_K/Q5_K and int16 for Q6_K,
 //   engine/native_quant.cpp:53-109).
 // * Per-stage partial sums are reduced with warp shuffles, then across the
 //   group's warps through shared memory in a fixed order (deterministic).
@@ -65,7 +65,7 @@ template <> struct Unit<T_Q6_K> { static constexpr int UV = 64, UPB = 4, NW = 16
 template <> struct Unit<T_Q8_0> { static constexpr int UV = 32, UPB = 1, NW = 8; };
 template <> struct Unit<T_Q4_0> { static constexpr int UV = 32, UPB = 1, NW = 8; };
 
-// Activation slice of one unit in 24-bit fixed point (three byte planes).
+// Activation slice of one unit in fixed point (three byte planes).
 template <int NW>
 struct XU {
     uint32_t b2[NW];    // signed top bytes of xq, 4 per word
@@ -323,125 +323,115 @@ __device__ __forceinline__ void unit_dot(uint32_t blk, int c, const XU<Unit<T>::
 // 3*NW plane words, then s, sum[2], qsum[4], padded to a multiple of 4 words.
 template <int NW> struct XPackWords { static constexpr int N = ((3 * NW + 7) + 3) / 4 * 4; };
 
-// One quantisation task: word k = task % NW of (token, unit) task / NW, i.e.
-// 4 values, packed into the three planes; the unit's max and sums are
-// reduced with shuffles across its NW consecutive lanes, so every lane of the
-// warp must execute quantize_x_word (``valid`` only masks the stores).  The
-// arithmetic and the stores are separate steps so that a thread's tasks of
-// one batch overlap.
-struct XWord {
-    uint32_t p2, p1, p0;   // byte planes of the four values
-    float m, sm;           // unit max |x|, sum of x over the 32-value run
-    int qs;                // sum of xq over the 16-value run
-};
+// One quantisation task covers 16 consecutive values of one (token, unit):
+// words 4j .. 4j+3 (j = task % L, L = NW / 4 lanes per unit) of unit task / L.
+// The L lanes of a unit are consecutive, so the unit's max |x| takes log2(L)
+// shuffles and the 32-value sums one; the 16-value sums of xq stay inside the
+// thread.  Quantisation: xq = rint(x * inv), inv = (2^22 - 4) / max|x| (so
+// |xq| < 2^22 and the rounding is one FMA with the 1.5 * 2^23 magic constant),
+// reconstructed with s = max|x| / (2^22 - 4); the two agree to f32 rounding.
+constexpr float XQ_RANGE = 4194300.0f;          // 2^22 - 4
+constexpr float XQ_MAGIC = 12582912.0f;         // 1.5 * 2^23
+constexpr int XQ_MAGIC_BITS = 0x4B400000;
 
+// Columns of x that quantisation task ``task`` reads (16 of them, from the
+// returned pointer on): row t of x, words 4j .. 4j+3 of unit u.  With one
+// token the unit index needs no division.
 template <int T>
-__device__ __forceinline__ XWord quantize_x_word(const float4 f)
+__device__ __forceinline__ const float *quantize_x_addr(const float *__restrict__ x, int cols, int units, int ntok,
+                                                        int task)
 {
-    constexpr int NW = Unit<T>::NW;
-    XWord r;
-    float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
-#pragma unroll
-    for (int o = 1; o < NW; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // Grid step s = m / (2^23 - 1) and its inverse: values are quantised with
-    // inv and reconstructed with s, which agree to f32 rounding (a |q| that
-    // rounds past 2^23 - 1 is clamped).
-    const float inv = m > 0.f ? __frcp_rn(m) * 8388607.0f : 0.f;
-    int q[4];
-    q[0] = __float2int_rn(f.x * inv);
-    q[1] = __float2int_rn(f.y * inv);
-    q[2] = __float2int_rn(f.z * inv);
-    q[3] = __float2int_rn(f.w * inv);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) q[e] = max(-8388607, min(8388607, q[e]));
-    // byte b of the four values -> one word per plane (two's complement, so
-    // q = 65536 * (int8)b2 + 256 * b1 + b0)
-    auto plane = [&](uint32_t b) {
-        const uint32_t sel = b | ((4u + b) << 4);
-        return __byte_perm(__byte_perm((uint32_t)q[0], (uint32_t)q[1], sel),
-                           __byte_perm((uint32_t)q[2], (uint32_t)q[3], sel), 0x5410);
-    };
-    r.p2 = plane(2);
-    r.p1 = plane(1);
-    r.p0 = plane(0);
-    int qs = (q[0] + q[1]) + (q[2] + q[3]);
-    float sm = (f.x + f.y) + (f.z + f.w);
-#pragma unroll
-    for (int o = 1; o < 4; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);      // 16-value runs
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);      // 32-value runs
-    r.m = m;
-    r.sm = sm;
-    r.qs = qs;
-    return r;
-}
-
-template <int T>
-__device__ __forceinline__ void store_x_word(const XWord &r, int task, uint32_t xs)
-{
-    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N;
-    const int k = task % NW, tu = task / NW;
-    const uint32_t o = xs + (uint32_t)tu * N * 4;
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * k), "r"(r.p2) : "memory");
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (NW + k)), "r"(r.p1) : "memory");
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (2 * NW + k)), "r"(r.p0) : "memory");
-    if (k == 0)
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(r.m * (1.0f / 8388607.0f))) : "memory");
-    if ((k & 7) == 0)
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (k >> 3))), "r"(__float_as_uint(r.sm)) : "memory");
-    if ((k & 3) == 0)
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + (k >> 2))), "r"(__float_as_uint((float)r.qs)) : "memory");
-}
-
-// Address of the float4 of x that quantisation task ``task`` reads (task <
-// tasks): row t of x, the 4 columns of word k of unit u.
-template <int T>
-__device__ __forceinline__ const float *quantize_x_addr(const float *__restrict__ x, int cols, int units, int task)
-{
-    constexpr int NW = Unit<T>::NW;
-    const int k = task % NW, tu = task / NW;
-    const int u = tu % units, t = tu / units;
+    constexpr int L = Unit<T>::NW / 4;
+    const int j = task % L, tu = task / L;
+    const int u = ntok == 1 ? tu : tu % units, t = ntok == 1 ? 0 : tu / units;
     int c0 = 0, c1 = 0;
     unit_cols<T>(u, c0, c1);
+    const int k = 4 * j;                                          // first word of the task
     return x + (long long)t * cols + (k < 8 ? c0 : c1) + 4 * (k & 7);
 }
 
+// Quantise one task's 16 values v[] and store its words (every lane of the
+// warp must call this: the unit max and the 32-value sums use shuffles;
+// ``valid`` masks the stores).
+template <int T>
+__device__ __forceinline__ void quantize_x_task16(const float4 (&v)[4], bool valid, int task, uint32_t xs)
+{
+    constexpr int NW = Unit<T>::NW, N = XPackWords<NW>::N, L = NW / 4;
+    const int j = task % L, tu = task / L;
+    float m = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[w].x), fabsf(v[w].y)), fmaxf(fabsf(v[w].z), fabsf(v[w].w))));
+#pragma unroll
+    for (int o = 1; o < L; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? __frcp_rn(m) * XQ_RANGE : 0.f;
+    uint32_t p2[4], p1[4], p0[4];
+    int qs = 0;
+    float sm = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float e[4] = {v[w].x, v[w].y, v[w].z, v[w].w};
+        uint32_t q[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            q[c] = (uint32_t)(__float_as_int(fmaf(e[c], inv, XQ_MAGIC)) - XQ_MAGIC_BITS);   // rint(e * inv)
+            qs += (int)q[c];
+        }
+        sm += (e[0] + e[1]) + (e[2] + e[3]);
+        // byte b of the four values -> one word per plane (two's complement:
+        // q = 65536 * (int8)b2 + 256 * b1 + b0)
+#pragma unroll
+        for (int b = 0; b < 3; ++b) {
+            const uint32_t sel = (uint32_t)b | ((4u + b) << 4);
+            const uint32_t word = __byte_perm(__byte_perm(q[0], q[1], sel), __byte_perm(q[2], q[3], sel), 0x5410);
+            (b == 2 ? p2 : b == 1 ? p1 : p0)[w] = word;
+        }
+    }
+    sm += __shfl_xor_sync(0xffffffffu, sm, 1);       // the two tasks of a 32-value run
+    if (valid) {
+        const uint32_t o = xs + (uint32_t)tu * N * 4;
+        const uint32_t k = 4u * j;
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(o + 4 * k), "r"(p2[0]), "r"(p2[1]), "r"(p2[2]), "r"(p2[3]) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(o + 4 * (NW + k)), "r"(p1[0]), "r"(p1[1]), "r"(p1[2]), "r"(p1[3]) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(o + 4 * (2 * NW + k)), "r"(p0[0]), "r"(p0[1]), "r"(p0[2]), "r"(p0[3]) : "memory");
+        if (j == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW)), "r"(__float_as_uint(m * (1.0f / XQ_RANGE))) : "memory");
+        if ((j & 1) == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 1 + (j >> 1))), "r"(__float_as_uint(sm)) : "memory");
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(o + 4 * (3 * NW + 3 + j)), "r"(__float_as_uint((float)qs)) : "memory");
+    }
+}
+
 // Cooperative quantisation of x [ntok, cols] into packed per-unit words in
-// shared memory (xs[(t * units + u) * N ...]).  NW consecutive lanes handle one
-// (token, unit), one 4-value word each; max/sums use shuffles inside the
-// NW-lane segment.  Every lane of the calling warps must execute this.  A
-// thread's tasks are taken in batches of MAXIT whose loads are all issued
-// before any is used, so the activation costs one L2 round trip per batch.
+// shared memory (xs[(t * units + u) * N ...]); every lane of the calling warps
+// must execute this.  A thread's tasks are taken in batches of MAXIT whose
+// loads are all issued before any is used (one L2 round trip per batch).
 template <int T>
 __device__ __forceinline__ void quantize_x_smem(const float *__restrict__ x, int cols, int units, int ntok, uint32_t xs,
                                                 int tid, int nthreads)
 {
-    constexpr int NW = Unit<T>::NW;
-    constexpr int MAXIT = 8;
-    const int tasks = ntok * units * NW;
+    constexpr int L = Unit<T>::NW / 4;
+    constexpr int MAXIT = 4;
+    const int tasks = ntok * units * L;
     const int iters = (tasks + nthreads - 1) / nthreads;
     for (int i0 = 0; i0 < iters; i0 += MAXIT) {
-        float4 f[MAXIT];
+        float4 f[MAXIT][4];
 #pragma unroll
         for (int i = 0; i < MAXIT; ++i) {
             const int task = (i0 + i) * nthreads + tid;
-            f[i] = (i0 + i < iters && task < tasks)
-                       ? __ldg(reinterpret_cast<const float4 *>(quantize_x_addr<T>(x, cols, units, task)))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        // arithmetic of QB tasks at a time, then their stores (register budget)
-        constexpr int QB = 4;
+            if (i0 + i < iters && task < tasks) {
+                const float4 *p = reinterpret_cast<const float4 *>(quantize_x_addr<T>(x, cols, units, ntok, task));
 #pragma unroll
-        for (int i1 = 0; i1 < MAXIT; i1 += QB) {
-            XWord r[QB];
+                for (int w = 0; w < 4; ++w) f[i][w] = __ldg(p + w);
+            } else {
 #pragma unroll
-            for (int i = 0; i < QB; ++i)
-                if (i0 + i1 + i < iters) r[i] = quantize_x_word<T>(f[i1 + i]);   // warp-uniform condition
-#pragma unroll
-            for (int i = 0; i < QB; ++i) {
-                const int task = (i0 + i1 + i) * nthreads + tid;
-                if (i0 + i1 + i < iters && task < tasks) store_x_word<T>(r[i], task, xs);
+                for (int w = 0; w < 4; ++w) f[i][w] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+        }
+#pragma unroll
+        for (int i = 0; i < MAXIT; ++i) {
+            const int task = (i0 + i) * nthreads + tid;
+            if (i0 + i < iters) quantize_x_task16<T>(f[i], task < tasks, task, xs);   // warp-uniform condition
         }
     }
 }
