@@ -300,7 +300,9 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *   b200q_attn_decode_dev   out[H*hd] = softmax(q k^T / sqrt(hd)) v over
  *                           positions 0..*pos (GQA: head h uses KV head
  *                           h / (H / KV)); scratch of
- *                           b200q_attn_decode_scratch_floats floats
+ *                           b200q_attn_decode_scratch_floats floats; hd a
+ *                           multiple of 4 up to 128, H / KV <= 8, q and the
+ *                           caches 16-byte aligned
  *   b200q_argmax_dev        *token = argmax(logits) (first index on ties);
  *                           with pos: out_tokens[*pos] = token, ++*pos;
  *                           key: optional zero-initialised 64-bit device word

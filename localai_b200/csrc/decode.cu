@@ -142,32 +142,44 @@ __global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, in
     }
 }
 
-// One CTA per (KV head g, chunk c of ATT_CHUNK positions), 256 threads.  The
-// chunk's K and V rows are staged in shared memory (rows padded by one float
-// so that threads reading different rows hit different banks); thread
-// (query head j, position l) computes one score; warp j does the softmax
-// statistics of head j with shuffles; then every thread accumulates two
-// (head, dim) outputs of P V.  Writes per query head the chunk's max, sum of
-// exp and exp-weighted V.
-constexpr int ATT_THREADS = 256;
+// One CTA per (KV head g, chunk c of ATT_CHUNK positions), 256 threads (8
+// warps).  The G = H / KV query rows of the group, the chunk's K rows and V
+// rows are staged densely in shared memory with 16-byte cp.async (all in
+// flight at once).  Scores: warp w takes positions w, w + 8, ...; lane i holds
+// dims 4i .. 4i+3 of the G query rows in registers, reads the same dims of the
+// K row (one 128-bit shared load, no bank conflicts) and the G partial dots
+// are summed across the warp with shuffles.  Warp j < G then does the softmax
+// statistics of head j.  P V: warp w accumulates positions w, w + 8, ... for
+// dims 4i .. 4i+3 of every head; the eight per-warp partials (stored where
+// the K rows were) are added in warp order.  Writes per query head the
+// chunk's max, sum of exp and exp-weighted V.  Needs hd % 4 == 0, hd <= 128,
+// G <= 8.
+constexpr int ATT_THREADS = 256, ATT_WARPS = ATT_THREADS / 32, ATT_MAXG = 8;
+
+__device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+
 __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__restrict__ q, const float *__restrict__ kc,
                                                                  const float *__restrict__ vc,
                                                                  const int *__restrict__ pos_p, int H, int KV, int hd,
                                                                  int max_seq, float *__restrict__ part)
 {
-    extern __shared__ float asm_[];
+    extern __shared__ __align__(16) float asm_[];
     pdl_enter();
     const int G = H / KV, g = blockIdx.x, c = blockIdx.y;
     const int L = min(*pos_p + 1, max_seq);
     const int l0 = c * ATT_CHUNK, l1 = min(L, l0 + ATT_CHUNK);
     const int nch = gridDim.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int stride = hd + 1;
+    const int hd4 = hd >> 2;
     float *qs = asm_;                          // [G][hd]
-    float *ks = qs + G * hd;                   // [ATT_CHUNK][hd + 1]
-    float *vs = ks + ATT_CHUNK * stride;       // [ATT_CHUNK][hd + 1]
-    float *sc = vs + ATT_CHUNK * stride;       // [G][ATT_CHUNK]
-    float *stat = sc + G * ATT_CHUNK;          // [G][2]: max, 1/sum not used; max, sum
+    float *ks = qs + G * hd;                   // [ATT_CHUNK][hd]; later [ATT_WARPS][G][hd] partials of P V
+    float *vs = ks + ATT_CHUNK * hd;           // [ATT_CHUNK][hd]
+    float *sc = vs + ATT_CHUNK * hd;           // [G][ATT_CHUNK]
+    float *stat = sc + G * ATT_CHUNK;          // [G][2]: max, sum
     // part layout: [H][nch][hd + 2]: acc[hd], max, sum
     if (l1 <= l0) {                            // chunk past the current position
         for (int i = tid; i < G * (hd + 2); i += blockDim.x) {
@@ -177,26 +189,39 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__
         return;
     }
     const int n = l1 - l0;
-    for (int i = tid; i < G * hd; i += blockDim.x) qs[i] = q[(long long)g * G * hd + i];
-    for (int i = tid; i < n * hd; i += blockDim.x) {
-        const int l = i / hd, d = i % hd;
-        ks[l * stride + d] = kc[((long long)(l0 + l) * KV + g) * hd + d];
-        vs[l * stride + d] = vc[((long long)(l0 + l) * KV + g) * hd + d];
+    for (int i = tid; i < G * hd4; i += ATT_THREADS) cp_async16_cg(qs + 4 * i, q + (long long)g * G * hd + 4 * i);
+    for (int i = tid; i < n * hd4; i += ATT_THREADS) {
+        const int l = i / hd4, d4 = i - l * hd4;
+        const long long src = ((long long)(l0 + l) * KV + g) * hd + 4 * d4;
+        cp_async16_cg(ks + l * hd + 4 * d4, kc + src);
+        cp_async16_cg(vs + l * hd + 4 * d4, vc + src);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+
+    const bool lv = lane < hd4;                // this lane's dims exist
+    float4 qr[ATT_MAXG];
+#pragma unroll
+    for (int j = 0; j < ATT_MAXG; ++j)
+        qr[j] = (j < G && lv) ? reinterpret_cast<const float4 *>(qs)[j * hd4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
     const float rs = sqrtf((float)hd);
-    for (int i = tid; i < G * ATT_CHUNK; i += blockDim.x) {
-        const int j = i / ATT_CHUNK, l = i % ATT_CHUNK;
-        float s = -INFINITY;
-        if (l < n) {
-            float d = 0.f;
-            for (int e = 0; e < hd; ++e) d = fmaf(qs[j * hd + e], ks[l * stride + e], d);
-            s = d / rs;
+    for (int l = warp; l < ATT_CHUNK; l += ATT_WARPS) {
+        const float4 kv = (l < n && lv) ? reinterpret_cast<const float4 *>(ks)[l * hd4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float s[ATT_MAXG];
+#pragma unroll
+        for (int j = 0; j < ATT_MAXG; ++j)
+            s[j] = fmaf(qr[j].w, kv.w, fmaf(qr[j].z, kv.z, fmaf(qr[j].y, kv.y, qr[j].x * kv.x)));
+#pragma unroll
+        for (int j = 0; j < ATT_MAXG; ++j) {
+            if (j < G) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+                if (lane == 0) sc[j * ATT_CHUNK + l] = l < n ? s[j] / rs : -INFINITY;
+            }
         }
-        sc[j * ATT_CHUNK + l] = s;
     }
     __syncthreads();
-    for (int j = warp; j < G; j += ATT_THREADS / 32) {
+    for (int j = warp; j < G; j += ATT_WARPS) {
         float m = -INFINITY;
         for (int l = lane; l < ATT_CHUNK; l += 32) m = fmaxf(m, sc[j * ATT_CHUNK + l]);
 #pragma unroll
@@ -215,10 +240,35 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__
         }
     }
     __syncthreads();
-    for (int i = tid; i < G * hd; i += blockDim.x) {
-        const int j = i / hd, d = i % hd;
+    float4 acc[ATT_MAXG];
+#pragma unroll
+    for (int j = 0; j < ATT_MAXG; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int l = warp; l < n; l += ATT_WARPS) {
+        const float4 vv = lv ? reinterpret_cast<const float4 *>(vs)[l * hd4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < ATT_MAXG; ++j) {
+            if (j < G) {
+                const float p = sc[j * ATT_CHUNK + l];
+                acc[j].x = fmaf(p, vv.x, acc[j].x);
+                acc[j].y = fmaf(p, vv.y, acc[j].y);
+                acc[j].z = fmaf(p, vv.z, acc[j].z);
+                acc[j].w = fmaf(p, vv.w, acc[j].w);
+            }
+        }
+    }
+    // the K rows are no longer read (scores are done): per-warp partials go there
+    float *red = ks;
+    if (lv) {
+#pragma unroll
+        for (int j = 0; j < ATT_MAXG; ++j)
+            if (j < G) reinterpret_cast<float4 *>(red)[(warp * G + j) * hd4 + lane] = acc[j];
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hd; i += ATT_THREADS) {
+        const int j = i / hd, d = i - j * hd;
         float a = 0.f;
-        for (int l = 0; l < n; ++l) a = fmaf(sc[j * ATT_CHUNK + l], vs[l * stride + d], a);
+#pragma unroll
+        for (int w = 0; w < ATT_WARPS; ++w) a += red[(w * G + j) * hd + d];
         float *pp = part + ((long long)(g * G + j) * nch + c) * (hd + 2);
         pp[d] = a;
         if (d == 0) {
@@ -435,9 +485,12 @@ size_t attn_scratch_floats(int H, int hd, int max_seq)
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
                                int max_seq, float *part, float *out, cudaStream_t st)
 {
-    if (H < 1 || KV < 1 || H % KV || hd < 1 || max_seq < 1) return cudaErrorInvalidValue;
+    if (H < 1 || KV < 1 || H % KV || hd < 4 || hd > 128 || hd % 4 || H / KV > ATT_MAXG || max_seq < 1 ||
+        (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kc) & 15) ||
+        (reinterpret_cast<uintptr_t>(vc) & 15))
+        return cudaErrorInvalidValue;
     const int G = H / KV, nch = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
-    const size_t smem = (size_t)(G * hd + 2 * ATT_CHUNK * (hd + 1) + G * ATT_CHUNK + 2 * G) * sizeof(float);
+    const size_t smem = (size_t)(G * hd + 2 * ATT_CHUNK * hd + G * ATT_CHUNK + 2 * G) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static size_t attr = 0;
     if (smem > attr) {
