@@ -280,19 +280,27 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__
 
 // Causal prefill attention (engine/model.py:130-160, forward_sequence): query
 // row t (position *pos_p + t, rotated q in qkv row t) attends to cache
-// positions 0 .. *pos_p + t.  CTA = (query head h, tile of PF_Q query rows),
-// 256 threads: thread (row r = tid / 8, s = tid % 8) owns dims s, s+8, ...
-// of row r.  Key tiles of PF_K positions are staged in shared memory (rows
-// padded by one float); online softmax per row (running max and sum, the
-// 8 threads of a row combine with shuffles); output bf16 for the O GEMM.
-constexpr int PF_Q = 32, PF_K = 64, PF_THREADS = 256;
+// positions 0 .. *pos_p + t.  CTA = (query head h, tile of PF_Q = 64 query
+// rows), 256 threads as a 16 x 16 grid (ty, tx).  Per tile of PF_K = 64 key
+// positions (K and V rows staged with 16-byte cp.async, the next tile's K
+// loading during P V and its V during the next scores):
+//   scores  thread (ty, tx) computes rows 4ty .. 4ty+3 x keys tx + 16j (j < 4)
+//           from 128-bit shared loads (8 FMAs per load; keys interleaved by
+//           16 so that the K reads of a quarter warp hit distinct banks);
+//   softmax online per row (running max and sum), the 16 threads of a row
+//           combine with shuffles; probabilities go to shared memory;
+//   P V     thread (ty, tx) accumulates rows 4ty .. 4ty+3 x dims 64c + 4tx ..
+//           64c + 4tx + 3 (c < hd / 64).
+// f32 throughout; output bf16 for the O GEMM.  Needs hd = 64 or 128.
+constexpr int PF_Q = 64, PF_K = 64, PF_THREADS = 256;
+
 __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *__restrict__ qkv,
                                                                   const float *__restrict__ kc,
                                                                   const float *__restrict__ vc,
                                                                   const int *__restrict__ pos_p, int T, int H, int KV,
                                                                   int hd, int max_seq, __nv_bfloat16 *__restrict__ out)
 {
-    extern __shared__ float pf[];
+    extern __shared__ __align__(16) float pf[];
     pdl_enter();
     const int h = blockIdx.x, t0 = blockIdx.y * PF_Q;
     if (t0 >= T) return;
@@ -300,87 +308,157 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
     const int p0 = *pos_p;
     if (p0 < 0 || p0 + T > max_seq) return;
     const int nq = min(PF_Q, T - t0);
-    const int st = hd + 1;
-    float *qs = pf;                    // [PF_Q][hd + 1]
-    float *ks = qs + PF_Q * st;        // [PF_K][hd + 1]
-    float *vs = ks + PF_K * st;        // [PF_K][hd + 1]
-    float *ps = vs + PF_K * st;        // [PF_Q][PF_K + 1]
-    const int tid = threadIdx.x, r = tid >> 3, s = tid & 7;
+    const int st = hd + 4, pst = PF_K + 4, hd4 = hd >> 2, nc = hd >> 6;
+    float *qs = pf;                    // [PF_Q][hd + 4]
+    float *ks = qs + PF_Q * st;        // [PF_K][hd + 4]
+    float *vs = ks + PF_K * st;        // [PF_K][hd + 4]
+    float *ps = vs + PF_K * st;        // [PF_Q][PF_K + 4]
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     const long long R = (long long)(H + 2 * KV) * hd;
-    for (int i = tid; i < PF_Q * hd; i += PF_THREADS) {
-        const int rr = i / hd, d = i % hd;
-        qs[rr * st + d] = rr < nq ? qkv[(t0 + rr) * R + (long long)h * hd + d] : 0.f;
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = tid; i < PF_Q * hd4; i += PF_THREADS) {
+        const int rr = i / hd4, d4 = i - rr * hd4;
+        float *dst = qs + rr * st + 4 * d4;
+        if (rr < nq) cp_async16_cg(dst, qkv + (t0 + rr) * R + (long long)h * hd + 4 * d4);
+        else *reinterpret_cast<float4 *>(dst) = zero4;
     }
-    const int nd = hd / 8;             // dims per thread (<= 16)
-    float acc[16];
+    const int kmax = p0 + t0 + nq - 1;              // last key position any row of the tile sees
+    // rows [k0, k0 + nk) of the cache into dst; rows nk .. PF_K-1 zero
+    auto load_rows = [&](float *dst, const float *cache, int k0) {
+        const int nk = min(PF_K, kmax + 1 - k0);
+        for (int i = tid; i < PF_K * hd4; i += PF_THREADS) {
+            const int jj = i / hd4, d4 = i - jj * hd4;
+            float *d = dst + jj * st + 4 * d4;
+            if (jj < nk) cp_async16_cg(d, cache + ((long long)(k0 + jj) * KV + g) * hd + 4 * d4);
+            else *reinterpret_cast<float4 *>(d) = zero4;
+        }
+    };
+    load_rows(ks, kc, 0);
+    load_rows(vs, vc, 0);
+
+    float m[4], l[4], acc[4][8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    const int my_last = p0 + t0 + r;                     // last key position row r may see
-    const int kmax = p0 + t0 + nq - 1;
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) acc[i][d] = 0.f;
+    }
     const float rs = sqrtf((float)hd);
     for (int k0 = 0; k0 <= kmax; k0 += PF_K) {
         const int nk = min(PF_K, kmax + 1 - k0);
-        __syncthreads();                                  // previous tile fully used
-        for (int i = tid; i < nk * hd; i += PF_THREADS) {
-            const int j = i / hd, d = i % hd;
-            ks[j * st + d] = kc[((long long)(k0 + j) * KV + g) * hd + d];
-            vs[j * st + d] = vc[((long long)(k0 + j) * KV + g) * hd + d];
-        }
-        __syncthreads();
-        float sc[8];
-        float tmax = -INFINITY;
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();                                  // this tile's K and V (and q) are in place
+        float sc[4][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int j = s + 8 * i;
-            float v = -INFINITY;
-            if (r < nq && j < nk && k0 + j <= my_last) {
-                float dsum = 0.f;
-                for (int e = 0; e < hd; ++e) dsum = fmaf(qs[r * st + e], ks[j * st + e], dsum);
-                v = dsum / rs;
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) sc[i][jj] = 0.f;
+        for (int e = 0; e < hd; e += 4) {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4 *>(qs + (4 * ty + i) * st + e);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) kv[jj] = *reinterpret_cast<const float4 *>(ks + (tx + 16 * jj) * st + e);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj)
+                    sc[i][jj] = fmaf(qv[i].w, kv[jj].w,
+                                     fmaf(qv[i].z, kv[jj].z, fmaf(qv[i].y, kv[jj].y, fmaf(qv[i].x, kv[jj].x, sc[i][jj]))));
+        }
+        float scale[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = 4 * ty + i;
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int key = tx + 16 * jj;
+                const bool ok = row < nq && key < nk && k0 + key <= p0 + t0 + row;
+                sc[i][jj] = ok ? sc[i][jj] / rs : -INFINITY;
+                tmax = fmaxf(tmax, sc[i][jj]);
             }
-            sc[i] = v;
-            tmax = fmaxf(tmax, v);
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+            const float mn = fmaxf(m[i], tmax);
+            scale[i] = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mn);
+            float psum = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const float p = (sc[i][jj] == -INFINITY) ? 0.f : expf(sc[i][jj] - mn);
+                ps[row * pst + tx + 16 * jj] = p;
+                psum += p;
+            }
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+            l[i] = l[i] * scale[i] + psum;
+            m[i] = mn;
+#pragma unroll
+            for (int d = 0; d < 8; ++d) acc[i][d] *= scale[i];
         }
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        const float mn = fmaxf(m, tmax);
-        const float scale = (m == -INFINITY) ? 0.f : expf(m - mn);
-        float psum = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float p = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mn);
-            ps[r * (PF_K + 1) + s + 8 * i] = p;
-            psum += p;
+        __syncthreads();                                  // probabilities complete; K no longer read
+        if (k0 + PF_K <= kmax) {
+            load_rows(ks, kc, k0 + PF_K);                 // next K lands during P V
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
+        for (int kk = 0; kk < PF_K; kk += 4) {
+            float4 pv[4];
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-        l = l * scale + psum;
-        m = mn;
-        __syncwarp();
+            for (int i = 0; i < 4; ++i) pv[i] = *reinterpret_cast<const float4 *>(ps + (4 * ty + i) * pst + kk);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc[k] *= scale;
-        for (int j = 0; j < nk; ++j) {
-            const float p = ps[r * (PF_K + 1) + j];
+            for (int q4 = 0; q4 < 4; ++q4) {
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
-                if (k < nd) acc[k] = fmaf(p, vs[j * st + s + 8 * k], acc[k]);
+                for (int c = 0; c < 2; ++c) {
+                    if (c < nc) {
+                        const float4 vv = *reinterpret_cast<const float4 *>(vs + (kk + q4) * st + 64 * c + 4 * tx);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float p = q4 == 0 ? pv[i].x : q4 == 1 ? pv[i].y : q4 == 2 ? pv[i].z : pv[i].w;
+                            acc[i][4 * c] = fmaf(p, vv.x, acc[i][4 * c]);
+                            acc[i][4 * c + 1] = fmaf(p, vv.y, acc[i][4 * c + 1]);
+                            acc[i][4 * c + 2] = fmaf(p, vv.z, acc[i][4 * c + 2]);
+                            acc[i][4 * c + 3] = fmaf(p, vv.w, acc[i][4 * c + 3]);
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();                                  // V and the probabilities no longer read
+        if (k0 + PF_K <= kmax) {
+            load_rows(vs, vc, k0 + PF_K);                 // next V lands during the next scores
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
     }
-    if (r < nq) {
-        const float inv = 1.0f / l;
-        __nv_bfloat16 *o = out + (long long)(t0 + r) * H * hd + (long long)h * hd;
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-            if (k < nd) o[s + 8 * k] = __float2bfloat16_rn(acc[k] * inv);
+    for (int i = 0; i < 4; ++i) {
+        const int row = 4 * ty + i;
+        if (row < nq) {
+            const float inv = 1.0f / l[i];
+            __nv_bfloat16 *o = out + (long long)(t0 + row) * H * hd + (long long)h * hd;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                if (c < nc) {
+                    __nv_bfloat162 a = __floats2bfloat162_rn(acc[i][4 * c] * inv, acc[i][4 * c + 1] * inv);
+                    __nv_bfloat162 b = __floats2bfloat162_rn(acc[i][4 * c + 2] * inv, acc[i][4 * c + 3] * inv);
+                    uint2 u;
+                    u.x = *reinterpret_cast<uint32_t *>(&a);
+                    u.y = *reinterpret_cast<uint32_t *>(&b);
+                    *reinterpret_cast<uint2 *>(o + 64 * c + 4 * tx) = u;
+                }
+            }
+        }
     }
 }
 
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
                                 int KV, int hd, int max_seq, __nv_bfloat16 *out, cudaStream_t st)
 {
-    if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 8 || hd > 128 || hd % 8 || max_seq < 1) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)((PF_Q + 2 * PF_K) * (hd + 1) + PF_Q * (PF_K + 1)) * sizeof(float);
+    if (T < 1 || H < 1 || KV < 1 || H % KV || (hd != 64 && hd != 128) || max_seq < 1 ||
+        (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(kc) & 15) ||
+        (reinterpret_cast<uintptr_t>(vc) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
+        return cudaErrorInvalidValue;
+    const size_t smem = (size_t)((PF_Q + 2 * PF_K) * (hd + 4) + PF_Q * (PF_K + 4)) * sizeof(float);
     static size_t attr = 0;
     if (smem > attr) {
         cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
