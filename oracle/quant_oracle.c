@@ -8,8 +8,8 @@
  * Q8_0 :75-78, Q4_0 :62-66, Q4_K :97-120, Q5_K :122-144, Q6_K :146-167) with
  * the same f32 rounding: every product is exact in f32, and Q4_K/Q5_K round
  * once at the subtraction of the minimum term.  matvec/matmul accumulate the
- * decoded f32 weights in double precision -- the survey's numeric oracle
- * ``dequantize(raw) @ x`` in float64.
+ * decoded f32 weights in double precision -- the numeric oracle of the GEMV
+ * and MoE paths, ``dequantize(raw) @ x`` in float64.
  */
 #include <stdint.h>
 #include <string.h>

@@ -11,8 +11,8 @@ What each function restates (paths are relative to the reference project):
 * ``LAYOUT`` / ``block_layout``        engine/dequant.py:6-17
 * ``dequantize``                       engine/dequant.py:27-167 (NumPy branch);
   the numba branch (engine/numba_kernels.py:49-106) gives the same f32 bits.
-* ``matvec_f64`` / ``matmul_f64``      the survey's numeric oracle:
-  ``dequantize(raw) @ x`` evaluated in float64.
+* ``matvec_f64`` / ``matmul_f64``      the numeric oracle of the GEMV and MoE
+  paths: ``dequantize(raw) @ x`` evaluated in float64.
 * ``silu``                             engine/zaya.py:305 / engine/model.py:232
 * ``route_topk``                       engine/zaya.py:290-296 generalised to
   top-k (stable: larger value first, lower index wins ties, as np.argmax).

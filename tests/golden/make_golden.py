@@ -1,9 +1,8 @@
 """Generate the golden dequantization fixtures from the reference engine itself.
 
-Run once in a container that has the reference checkout (path given by
-``--reference``, default ``/root/reference``):
+Run once in a container that has the reference checkout:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 The reference engine package is copied to a temporary directory first (its
 numba kernels are ``cache=True`` and write ``__pycache__`` next to the
@@ -87,7 +86,7 @@ def _load_engine(ref_root: Path, tmp: Path, with_numba: bool):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default='/root/reference')
+    ap.add_argument('--reference', required=True, help='path of the reference checkout')
     ap.add_argument('--out', default=str(HERE / 'dequant_golden.npz'))
     args = ap.parse_args()
     rng = np.random.default_rng(20260101)
