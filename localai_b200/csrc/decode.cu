@@ -55,6 +55,13 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
             }
         }
     }
+    const float4 *wr = reinterpret_cast<const float4 *>(w);
+    float4 wv[NORM_VEC];                       // norm weights: loaded before the reduction
+#pragma unroll
+    for (int k = 0; k < NORM_VEC; ++k) {
+        const int i = threadIdx.x + k * NORM_THREADS;
+        wv[k] = i < n4 ? wr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
     for (int k = 0; k < NORM_VEC; ++k)
         ss = fmaf(v[k].w, v[k].w, fmaf(v[k].z, v[k].z, fmaf(v[k].y, v[k].y, fmaf(v[k].x, v[k].x, ss))));
@@ -66,13 +73,12 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
 #pragma unroll
     for (int i = 0; i < NORM_THREADS / 32; ++i) tot += red[i];
     const float inv = 1.0f / sqrtf(tot / (float)D + eps);
-    const float4 *wr = reinterpret_cast<const float4 *>(w);
 #pragma unroll
     for (int k = 0; k < NORM_VEC; ++k) {
         const int i = threadIdx.x + k * NORM_THREADS;
         if (i < n4) {
             if (dr) xr[i] = v[k];
-            const float4 g = wr[i];
+            const float4 g = wv[k];
             const float4 o = make_float4(v[k].x * inv * g.x, v[k].y * inv * g.y, v[k].z * inv * g.z, v[k].w * inv * g.w);
             if (h) reinterpret_cast<float4 *>(h + t * D)[i] = o;
             if (hb) {
@@ -469,25 +475,47 @@ cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *
                       T, H, KV, hd, max_seq, out);
 }
 
-// out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in order.
+// out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in
+// order.  One CTA per query head: the chunk weights exp(m_c - M) / S are
+// computed once into shared memory (chunks past the position have
+// m_c = -inf, weight 0), then thread d sums its column over the chunks.
+constexpr int COMB_MAX_CHUNKS = 2048;
 __global__ void attn_combine_kernel(const float *__restrict__ part, int nch, int hd, float *__restrict__ out)
 {
+    __shared__ float wsh[COMB_MAX_CHUNKS];
+    __shared__ float red[32];
     pdl_enter();
-    const int h = blockIdx.x;
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const float *ph = part + (long long)h * nch * (hd + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, ph[c * (hd + 2) + hd]);
-    float S = 0.f;
-    for (int c = 0; c < nch; ++c) {
+    float mloc = -INFINITY;
+    for (int c = tid; c < nch; c += blockDim.x) {
         const float mc = ph[c * (hd + 2) + hd];
-        if (mc != -INFINITY) S += expf(mc - M) * ph[c * (hd + 2) + hd + 1];
+        wsh[c] = mc;
+        mloc = fmaxf(mloc, mc);
     }
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+    if (lane == 0) red[warp] = mloc;
+    __syncthreads();
+    float M = -INFINITY;
+    for (int i = 0; i < nw; ++i) M = fmaxf(M, red[i]);
+    __syncthreads();                           // red is reused below
+    float sloc = 0.f;
+    for (int c = tid; c < nch; c += blockDim.x) {
+        const float mc = wsh[c];
+        const float e = mc == -INFINITY ? 0.f : expf(mc - M);
+        wsh[c] = e;
+        sloc += e * ph[c * (hd + 2) + hd + 1];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sloc += __shfl_xor_sync(0xffffffffu, sloc, o);
+    if (lane == 0) red[warp] = sloc;
+    __syncthreads();
+    float S = 0.f;
+    for (int i = 0; i < nw; ++i) S += red[i];
+    for (int d = tid; d < hd; d += blockDim.x) {
         float a = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            const float mc = ph[c * (hd + 2) + hd];
-            if (mc != -INFINITY) a += expf(mc - M) * ph[c * (hd + 2) + d];
-        }
+        for (int c = 0; c < nch; ++c) a = fmaf(wsh[c], ph[c * (hd + 2) + d], a);
         out[(long long)h * hd + d] = a / S;
     }
 }
@@ -569,7 +597,7 @@ cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc,
         return cudaErrorInvalidValue;
     const int G = H / KV, nch = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
     const size_t smem = (size_t)(G * hd + 2 * ATT_CHUNK * hd + G * ATT_CHUNK + 2 * G) * sizeof(float);
-    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 200 * 1024 || nch > COMB_MAX_CHUNKS) return cudaErrorInvalidValue;
     static size_t attr = 0;
     if (smem > attr) {
         cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
