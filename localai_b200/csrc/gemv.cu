@@ -14,8 +14,12 @@
 //   full row, each thread owning CPT fixed units (64 values of a K-quant
 //   super-block, or one 32-value Q8_0/Q4_0 block); the activation values of
 //   its units stay in registers for the whole kernel.  Groups take different
-//   rows of a stage.  x is read once per CTA; the only shared-memory traffic
-//   is the weight stream itself.
+//   rows of a stage.  x is read once per CTA: quantised in the prologue into
+//   shared memory (one 16-value task per thread at a time), then loaded into
+//   the consumers' registers; after that the shared-memory traffic is the
+//   weight stream and the per-stage partial sums.
+// * Grouped mode (MoE experts at small batch): blockIdx.y selects a weight
+//   matrix and a token range read from device offsets (validated in-kernel).
 // * Integer dot products.  x is converted once per CTA to fixed point,
 //   xq = rint(x / s) with s = max|x_unit| / (2^22 - 4) (|xq| < 2^22), held as
 //   three byte planes (xq = 65536*b2 + 256*b1 + b0; b2 signed, b1/b0
