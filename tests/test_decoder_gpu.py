@@ -171,3 +171,25 @@ def test_rope_kv_position_out_of_range_is_reported():
     with pytest.raises(_lib.B200QError):
         ops.check_device_error()
     assert not kc.any() and not vc.any()
+
+
+def test_head_dim_128_grouped_query_decode_and_prefill():
+    """The Llama-3-8B head shape (head dim 128, four query heads per KV head):
+    decode steps at 1e-3 and a 70-token prefill (two key tiles) at the bf16
+    bar, against the float64 oracle."""
+    rng = np.random.default_rng(128)
+    model, ref_w, cfg = build(rng, 8, NL=1, D=512, H=4, KV=1, F=256, max_seq=96)
+    tokens = [int(v) for v in rng.integers(0, 300, size=6)]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    prompt = [int(v) for v in rng.integers(0, 300, size=70)]
+    ref = o.llama_decode_f64(ref_w, cfg, prompt)
+    model.reset()
+    model.prefill(prompt)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
