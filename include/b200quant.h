@@ -65,6 +65,16 @@ void localai_q5k_matmul(const uint8_t *raw, const float *vectors, float *out, in
 void localai_q6k_matmul(const uint8_t *raw, const float *vectors, float *out, int rows, int cols, int tokens,
                         int threads);
 
+/* Batched calls of the five localai_*_matmul functions (the reference's
+ * prefill path, decoded_matmul_row, engine/native_quant.cpp:620-703) with at
+ * least ``tokens`` tokens (default 32) run on the tcgen05 tensor cores -- bf16
+ * operands, f32 accumulation, normwise error ~3e-3 -- when the weights are
+ * Q4_K, Q6_K or Q8_0 with a multiple of 128 rows and packed rows of whole
+ * 16-byte units (Q4_K: any cols; Q8_0: cols % 256 == 0; Q6_K: cols % 2048 ==
+ * 0); every other call runs the f32 GEMV (~1e-6).  0 keeps every call on the
+ * GEMV; a negative value only queries.  Returns the previous setting. */
+int b200q_matmul_tensor_core_min_tokens(int tokens);
+
 /* Status of the last call made by this process (B200Q_* code) and its
  * message.  Replaces the reference's silent failure / None return
  * (engine/native_quant.py:66-99). */
@@ -158,8 +168,10 @@ int b200q_gemv_grouped_max_tokens(int ggml_type, int cols);
 int b200q_gemv_grouped_dev(int ggml_type, const void *w, long long w_group_stride, long long w_row_bytes,
                            int n_groups, const int *grp_off, const float *x, float *y, long long ys_t, int rows,
                            int cols, int max_tokens, int x_rows, int active_groups, void *stream);
-/* out[s, :] = h[token_of[s], :] for s < S (f32 rows of D values, D % 4 == 0). */
-int b200q_moe_gather_f32_dev(const float *h, const int *token_of, int S, int D, float *out, void *stream);
+/* out[s, :] = h[token_of[s], :] for s < S (f32 rows of D values, D % 4 == 0);
+ * h has h_rows rows: a row whose token is outside [0, h_rows) is left
+ * unwritten and the device error word set (B200Q_EINDEX). */
+int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *token_of, int S, int D, float *out, void *stream);
 /* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
  * weights.  w_row_bytes is the byte distance between weight rows (0: packed
  * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed
@@ -196,7 +208,10 @@ int b200q_moe_num_blocks(int T);
 /* Stable counting sort of the T*k routed pairs by expert (slot order inside an
  * expert follows (token, j) order): offsets int32 [E+1], slot_of int32 [T*k],
  * token_of int32 [T*k], slot_w f32 [T*k] (routing weight per slot), and, if
- * xperm_bf16 != NULL, xperm[slot] = bf16(h[token_of[slot]]) (bf16 [T*k, D]). */
+ * xperm_bf16 != NULL, xperm[slot] = bf16(h[token_of[slot]]) (bf16 [T*k, D];
+ * h 16-byte and xperm 8-byte aligned, D % 4 == 0).  A pair whose expert id is
+ * outside [0, E) gets slot_of = -1 and no slot (offsets[E] < T*k), and the
+ * device error word is set (B200Q_EINDEX from b200q_check_device_error). */
 int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
                            int *block_counts, int *base, int *offsets, int *slot_of, int *token_of, float *slot_w,
                            void *xperm_bf16, void *stream);
@@ -208,22 +223,28 @@ int b200q_moe_dispatch_dev(const int *ids, const float *w, int T, int k, int E, 
  * array of 256 KB that every GPU loading the library keeps until exit, so the
  * call needs no block_counts/base buffers and calls no cudaMalloc, cudaFree or
  * allocating library routine.  Limit: b200q_moe_num_blocks(T) * E <= 32768
- * (larger calls return B200Q_EINVAL with a message).  The first call on a
- * device looks up the array's device address; make that first call before
- * any stream capture.  All calls share the array (it keeps the last call's
- * contents; nothing in it must start at zero because each call writes every
- * entry it reads), so calls that overlap on the GPU race. */
+ * (larger calls return B200Q_EINVAL with a message).  Every call looks up the
+ * array's device address on the current device (no allocation); the first
+ * call on a device also loads the library's device code there, so make it
+ * before any stream capture.  All calls share the array (it keeps the last
+ * call's contents; nothing in it must start at zero because each call writes
+ * every entry it reads), so calls that overlap on the GPU race.  A bad expert
+ * id is handled as in b200q_moe_dispatch_dev; it is recorded in an error word
+ * inside the array, which b200q_check_device_error reads and clears. */
 int b200q_moe_dispatch_noalloc_dev(const int *ids, const float *w, int T, int k, int E, const float *h, int D,
                                    int *offsets, int *slot_of, int *token_of, float *slot_w, void *xperm_bf16,
                                    void *stream);
 /* y[t] = sum_{j<k} w_j * out[slot_of[t*k + j]] in j order (f32 [T, D]), with
  * w_j = slot_w[slot] if slot_w != NULL, else 1 (rows already weighted); the
- * rows of out are f32, or bf16 when out_is_bf16 != 0. */
+ * rows of out (T*k of them) are f32, or bf16 when out_is_bf16 != 0.  A slot
+ * outside [0, T*k) -- the dispatch writes -1 for a pair whose expert id was
+ * out of range -- adds nothing. */
 int b200q_moe_combine_dev(const void *out, int out_is_bf16, const int *slot_of, const float *slot_w, int T, int k,
                           int D, float *y, void *stream);
 
 /* Device error word: returns and clears the sticky kernel error of the
- * current device (0 if none).  Synchronises the device. */
+ * current device (0 if none), including the error word of
+ * b200q_moe_dispatch_noalloc_dev.  Synchronises the device. */
 int b200q_check_device_error(void);
 
 /* Tuning knobs of the GEMV: bytes of weights per pipeline stage, stage
@@ -259,12 +280,14 @@ long long b200q_launch_count(void);
  *                          [max_recv_rows, d_ff] scratch;
  *   b200q_ep_combine_dev   wait for all ranks' outputs, y[t] = sum_j
  *                          slot_w * ret[slot(t, j)] (f32 [T, d_model]).
- * Waits give up after 5 s and set the device error word
+ * Waits give up after 5 s (b200q_ep_set_wait_limit_ns changes the limit for
+ * later launches; 0 restores 5 s) and set the device error word
  * (b200q_check_device_error reports B200Q_ETIMEOUT).  b200q_ep_destroy must be
  * called on all ranks after a barrier. */
 int b200q_ep_create(int world, int rank, int local_experts, int d_model, long long max_send_rows,
                     long long max_recv_rows, void **ep);
 size_t b200q_ep_handle_bytes(void);
+void b200q_ep_set_wait_limit_ns(unsigned long long ns);
 int b200q_ep_handle(void *ep, void *handle);
 int b200q_ep_open(void *ep, const void *handles);
 int b200q_ep_destroy(void *ep);
@@ -296,7 +319,9 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *                           at cache[*pos + t] (cache layout [max_seq][KV][hd])
  *   b200q_attn_prefill_dev  causal attention of T query rows (positions
  *                           *pos + t, q from the rotated qkv rows) over cache
- *                           positions 0 .. *pos + t; out bf16 [T][H*hd]
+ *                           positions 0 .. *pos + t; out bf16 [T][H*hd]; if
+ *                           *pos < 0 or *pos + T > max_seq nothing is written
+ *                           and the device error word is set (B200Q_EINDEX)
  *   b200q_attn_decode_dev   out[H*hd] = softmax(q k^T / sqrt(hd)) v over
  *                           positions 0..*pos (GQA: head h uses KV head
  *                           h / (H / KV)); scratch of

@@ -33,6 +33,7 @@ SIGNATURES = {
     'localai_q4k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
     'localai_q5k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
     'localai_q6k_matmul': (None, [_u8p, _f32p, _f32p, _i, _i, _i, _i]),
+    'b200q_matmul_tensor_core_min_tokens': (_i, [_i]),
     'b200q_last_status': (_i, []),
     'b200q_last_error': (ctypes.c_char_p, []),
     'b200q_init': (_i, [_i]),
@@ -50,7 +51,7 @@ SIGNATURES = {
     'b200q_silu_mul_dev': (_i, [_vp, _i, _i, _vp, _ll, _vp]),
     'b200q_gemv_grouped_max_tokens': (_i, [_i, _i]),
     'b200q_gemv_grouped_dev': (_i, [_i, _vp, _ll, _ll, _i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
-    'b200q_moe_gather_f32_dev': (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    'b200q_moe_gather_f32_dev': (_i, [_vp, _i, _vp, _i, _i, _vp, _vp]),
     'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
                             _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -73,6 +74,7 @@ SIGNATURES = {
     'b200q_argmax_dev': (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp, _vp]),
     'b200q_ep_create': (_i, [_i, _i, _i, _i, _ll, _ll, ctypes.POINTER(_vp)]),
     'b200q_ep_handle_bytes': (_sz, []),
+    'b200q_ep_set_wait_limit_ns': (None, [ctypes.c_ulonglong]),
     'b200q_ep_handle': (_i, [_vp, _vp]),
     'b200q_ep_open': (_i, [_vp, _vp]),
     'b200q_ep_destroy': (_i, [_vp]),

@@ -33,18 +33,21 @@ cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias,
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
-cudaError_t launch_moe_combine(const void *out, bool out_bf16, const int *slot_of, const float *slot_w, int T, int k,
+cudaError_t launch_moe_combine(const void *out, bool out_bf16, long long n_rows, const int *slot_of,
+                               const float *slot_w, int T, int k,
                                int D, float *y, cudaStream_t st);
 cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                         int *offsets, int *slot_of, int *token_of, float *slot_w,
                                         __nv_bfloat16 *xperm, cudaStream_t st);
 int noalloc_dispatch_max();
+cudaError_t noalloc_dispatch_take_error(int *code);
 cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, int k, const void *w,
                            long long w_row_bytes, int groups,
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
-                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret);
+                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret,
+                               bool out_t = false);
 cudaError_t ep_create(int G, int me, int E_loc, int D, long long cap_send, long long cap_recv, void **out);
 cudaError_t ep_ipc_handle(void *ctx, void *handle64);
 size_t ep_ipc_handle_bytes();
@@ -64,8 +67,10 @@ cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const
                            uint32_t epoch, int *err, int num_sms, cudaStream_t st);
 cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaStream_t st);
 cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
+void ep_set_wait_ns(unsigned long long ns);
 
 cudaError_t launch_silu_mul(const float *gu, int T, int F, float *out, long long ld_out, int num_sms, cudaStream_t st);
+cudaError_t launch_f32_to_bf16(const float *x, long long n, __nv_bfloat16 *out, int num_sms, cudaStream_t st);
 cudaError_t launch_gemv_grouped(int type, const void *w, long long w_group_stride, int n_groups, const int *grp_off,
                                 const float *x, float *y, long long ys_t, int rows, int cols, int max_tokens,
                                 int x_rows, int active_groups, long long row_stride, int *err, int num_sms,
@@ -78,13 +83,14 @@ cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int
 cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
                            float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
-                                int KV, int hd, int max_seq, __nv_bfloat16 *out, cudaStream_t st);
+                                int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st);
 size_t attn_scratch_floats(int H, int hd, int max_seq);
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
                                int max_seq, float *part, float *out, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
                           unsigned long long *key, int num_sms, cudaStream_t st);
-cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st);
+cudaError_t launch_moe_gather_f32(const float *h, int T, const int *token_of, int S, int D, float *out, int *err,
+                                  cudaStream_t st);
 cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
                                     int R, float eps, float *state, float *out, cudaStream_t st);
 cudaError_t launch_gelu(float *x, long long n, int num_sms, cudaStream_t st);
@@ -156,6 +162,10 @@ struct HostCtx {
     size_t xcap = 0;
     float *y = nullptr;
     size_t ycap = 0;
+    __nv_bfloat16 *xb = nullptr;   // bf16 activations of the tensor-core matmul
+    size_t xbcap = 0;
+    int *row_off = nullptr;        // device {0, tokens}: the one group of that matmul
+    size_t row_off_cap = 0;
     int *herr = nullptr;   // pinned host copy of the error word
 };
 static HostCtx g_host;
@@ -206,6 +216,23 @@ static const uint8_t *lookup_registered(const uint8_t *raw, size_t n)
     return nullptr;
 }
 
+// Batched Part-1 calls (the reference's prefill path: decoded_matmul_row,
+// engine/native_quant.cpp:620-703) with at least this many tokens run on the
+// tensor cores (bf16 operands, f32 accumulation) when the type and shape allow
+// it; smaller batches, other types and other shapes take the f32 GEMV.
+// 0 keeps every call on the GEMV.
+static int g_tc_min_tokens = 32;
+
+// Q4_K/Q6_K/Q8_0 weights whose packed rows are whole 16-byte units (the GEMM
+// streams them with TMA), a multiple of 128 rows and of 64 columns.
+static bool tc_matmul_shape_ok(int type, const void *wdev, int rows, int cols)
+{
+    if (type != T_Q4_K && type != T_Q6_K && type != T_Q8_0) return false;
+    if (rows % 128 || cols % 64 || (reinterpret_cast<uintptr_t>(wdev) & 15)) return false;
+    const long long rb = (long long)(cols / type_vals(type)) * type_bytes(type);
+    return rb % 16 == 0;
+}
+
 // One Part-1 call: upload, launch, download, wait, report.
 static void host_call(int type, const uint8_t *raw, const float *x, float *out, int rows, int cols, int tokens,
                       bool matmul)
@@ -238,10 +265,25 @@ static void host_call(int type, const uint8_t *raw, const float *x, float *out, 
     if (e != cudaSuccess) { cuda_status(e, "input upload"); return; }
     // Reference output layout: matvec [rows]; matmul [rows][tokens]
     // (engine/native_quant.py:148-156).
-    const long long ys_t = matmul ? 1 : rows, ys_r = matmul ? tokens : 1;
-    e = launch_gemv(type, wdev, g_host.x, g_host.y, ys_t, ys_r, rows, cols, tokens, di->err, di->sms, st);
-    ++g_launches;
-    if (e != cudaSuccess) { cuda_status(e, "gemv launch"); return; }
+    if (matmul && g_tc_min_tokens > 0 && tokens >= g_tc_min_tokens && tc_matmul_shape_ok(type, wdev, rows, cols)) {
+        const size_t xbbytes = (size_t)tokens * cols * sizeof(__nv_bfloat16);
+        if (grow((void **)&g_host.xb, &g_host.xbcap, xbbytes) != B200Q_OK) return;
+        if (grow((void **)&g_host.row_off, &g_host.row_off_cap, 2 * sizeof(int)) != B200Q_OK) return;
+        const int off[2] = {0, tokens};
+        e = cudaMemcpyAsync(g_host.row_off, off, sizeof(off), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = launch_f32_to_bf16(g_host.x, (long long)tokens * cols, g_host.xb, di->sms, st);
+        if (e == cudaSuccess)
+            e = launch_tc_gemm(type, g_host.xb, tokens, cols, wdev, 0, 1, rows, -1, rows, g_host.row_off, nullptr, 1,
+                               g_host.y, nullptr, tokens, nullptr, nullptr, 0, di->err, di->sms, 0, st, nullptr,
+                               true);
+        g_launches += 2;
+        if (e != cudaSuccess) { cuda_status(e, "tensor-core matmul launch"); return; }
+    } else {
+        const long long ys_t = matmul ? 1 : rows, ys_r = matmul ? tokens : 1;
+        e = launch_gemv(type, wdev, g_host.x, g_host.y, ys_t, ys_r, rows, cols, tokens, di->err, di->sms, st);
+        ++g_launches;
+        if (e != cudaSuccess) { cuda_status(e, "gemv launch"); return; }
+    }
     e = cudaMemcpyAsync(out, g_host.y, ybytes, cudaMemcpyDeviceToHost, st);
     if (e != cudaSuccess) { cuda_status(e, "output download"); return; }
     e = cudaMemcpyAsync(g_host.herr, di->err, sizeof(int), cudaMemcpyDeviceToHost, st);
@@ -317,6 +359,14 @@ B200Q_API void localai_q6k_matmul(const uint8_t *raw, const float *v, float *out
 {
     (void)threads;
     host_call(T_Q6_K, raw, v, out, rows, cols, tokens, true);
+}
+
+B200Q_API int b200q_matmul_tensor_core_min_tokens(int tokens)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    const int prev = g_tc_min_tokens;
+    if (tokens >= 0) g_tc_min_tokens = tokens;
+    return prev;
 }
 
 B200Q_API int b200q_last_status(void) { return g_status; }
@@ -520,12 +570,16 @@ B200Q_API int b200q_gemv_grouped_dev(int ggml_type, const void *w, long long w_g
                        "gemv_grouped");
 }
 
-B200Q_API int b200q_moe_gather_f32_dev(const float *h, const int *token_of, int S, int D, float *out, void *stream)
+B200Q_API int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *token_of, int S, int D, float *out,
+                                       void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!h || !token_of || !out) return set_status(B200Q_EINVAL, "gather_f32: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_moe_gather_f32(h, token_of, S, D, out, (cudaStream_t)stream), "gather_f32");
+    return cuda_status(launch_moe_gather_f32(h, h_rows, token_of, S, D, out, di->err, (cudaStream_t)stream),
+                       "gather_f32");
 }
 
 B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,
@@ -615,7 +669,8 @@ B200Q_API int b200q_moe_combine_dev(const void *out, int out_is_bf16, const int 
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!out || !slot_of || !y) return set_status(B200Q_EINVAL, "combine: null pointer");
     ++g_launches;
-    return cuda_status(launch_moe_combine(out, out_is_bf16 != 0, slot_of, slot_w, T, k, D, y, (cudaStream_t)stream),
+    return cuda_status(launch_moe_combine(out, out_is_bf16 != 0, (long long)T * k, slot_of, slot_w, T, k, D, y,
+                                          (cudaStream_t)stream),
                        "combine");
 }
 
@@ -630,8 +685,12 @@ B200Q_API int b200q_check_device_error(void)
     e = cudaMemcpy(&v, di->err, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_status(e, "error word read");
     if (v) cudaMemset(di->err, 0, sizeof(int));
+    // the allocation-free dispatch keeps its own error word in static device memory
+    int v2 = 0;
+    e = noalloc_dispatch_take_error(&v2);
+    if (e != cudaSuccess) return cuda_status(e, "error word read");
     set_status(B200Q_OK, nullptr);
-    return v;
+    return v ? v : v2;
 }
 
 B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas_per_sm)
@@ -652,6 +711,12 @@ B200Q_API int b200q_ep_create(int world, int rank, int local_experts, int d_mode
 }
 
 B200Q_API size_t b200q_ep_handle_bytes(void) { return ep_ipc_handle_bytes(); }
+
+B200Q_API void b200q_ep_set_wait_limit_ns(unsigned long long ns)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    ep_set_wait_ns(ns);
+}
 
 B200Q_API int b200q_ep_handle(void *ep, void *handle)
 {
@@ -741,7 +806,7 @@ B200Q_API int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *sl
     const cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = launch_ep_wait(ep, 2, epoch, di->err, st);
     if (e == cudaSuccess)
-        e = launch_moe_combine(ep_ret_rows(ep), true, slot_of, slot_w, T, k, ep_d_model(ep), y, st);
+        e = launch_moe_combine(ep_ret_rows(ep), true, ep_cap_send(ep), slot_of, slot_w, T, k, ep_d_model(ep), y, st);
     g_launches += 2;
     return cuda_status(e, "ep_combine");
 }
@@ -818,8 +883,10 @@ B200Q_API int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, con
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!qkv || !k_cache || !v_cache || !pos || !out_bf16) return set_status(B200Q_EINVAL, "attn_prefill: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
     return cuda_status(launch_attn_prefill(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq,
-                                           static_cast<__nv_bfloat16 *>(out_bf16), (cudaStream_t)stream),
+                                           static_cast<__nv_bfloat16 *>(out_bf16), di->err, (cudaStream_t)stream),
                        "attn_prefill");
 }

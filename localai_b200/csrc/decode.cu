@@ -304,7 +304,8 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
                                                                   const float *__restrict__ kc,
                                                                   const float *__restrict__ vc,
                                                                   const int *__restrict__ pos_p, int T, int H, int KV,
-                                                                  int hd, int max_seq, __nv_bfloat16 *__restrict__ out)
+                                                                  int hd, int max_seq, __nv_bfloat16 *__restrict__ out,
+                                                                  int *err)
 {
     extern __shared__ __align__(16) float pf[];
     pdl_enter();
@@ -312,7 +313,10 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
     if (t0 >= T) return;
     const int g = h / (H / KV);
     const int p0 = *pos_p;
-    if (p0 < 0 || p0 + T > max_seq) return;
+    if (p0 < 0 || p0 + T > max_seq) {          // positions outside the cache: write nothing, report
+        if (threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
+        return;
+    }
     const int nq = min(PF_Q, T - t0);
     const int st = hd + 4, pst = PF_K + 4, hd4 = hd >> 2, nc = hd >> 6;
     float *qs = pf;                    // [PF_Q][hd + 4]
@@ -458,7 +462,7 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
 }
 
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
-                                int KV, int hd, int max_seq, __nv_bfloat16 *out, cudaStream_t st)
+                                int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st)
 {
     if (T < 1 || H < 1 || KV < 1 || H % KV || (hd != 64 && hd != 128) || max_seq < 1 ||
         (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(kc) & 15) ||
@@ -472,7 +476,7 @@ cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *
         attr = smem;
     }
     return launch_pdl(attn_prefill_kernel, dim3(H, (T + PF_Q - 1) / PF_Q), dim3(PF_THREADS), smem, st, qkv, kc, vc, pos,
-                      T, H, KV, hd, max_seq, out);
+                      T, H, KV, hd, max_seq, out, err);
 }
 
 // out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in

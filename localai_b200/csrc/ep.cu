@@ -12,7 +12,7 @@
 //   (gate/up GEMM on the received rows; down GEMM whose epilogue stores each
 //    output row straight into the source rank's return buffer)
 //   ep_signal_kernel   raise ret_flag at every rank.
-// All waits are bounded (EP_WAIT_NS); a wait that runs out sets the device
+// All waits are bounded (g_ep_wait_ns); a wait that runs out sets the device
 // error word and the kernel returns, so the host sees an error instead of a
 // hang.
 #include "common.cuh"
@@ -22,7 +22,10 @@
 
 namespace b200q {
 
-constexpr uint64_t EP_WAIT_NS = 5000000000ull;   // 5 s
+// Time limit of every wait on another rank's flag (default 5 s), settable
+// with b200q_ep_set_wait_limit_ns; passed to each waiting kernel at launch.
+static unsigned long long g_ep_wait_ns = 5000000000ull;
+void ep_set_wait_ns(unsigned long long ns) { g_ep_wait_ns = ns ? ns : 5000000000ull; }
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v)
 {
@@ -35,13 +38,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
     return v;
 }
 
-// Wait until *flag has reached ``epoch`` (wrap-safe comparison).
-__device__ bool ep_wait_flag(const uint32_t *flag, uint32_t epoch, int *err)
+// Wait until *flag has reached ``epoch`` (wrap-safe comparison), for at most
+// limit_ns nanoseconds (and 2^30 polls).
+__device__ bool ep_wait_flag(const uint32_t *flag, uint32_t epoch, int *err, uint64_t limit_ns)
 {
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 0;; ++it) {
         if ((int)(ld_acquire_sys(flag) - epoch) >= 0) return true;
-        if ((it & 63) == 63 && (global_timer_ns() - t0 > EP_WAIT_NS || it > (1u << 30))) {
+        if ((it & 63) == 63 && (global_timer_ns() - t0 > limit_ns || it > (1u << 30))) {
             atomicExch(err, ERR_WAIT_TIMEOUT);
             return false;
         }
@@ -50,7 +54,7 @@ __device__ bool ep_wait_flag(const uint32_t *flag, uint32_t epoch, int *err)
 }
 
 __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__restrict__ offsets, uint32_t epoch,
-                                                        int *err)
+                                                        int *err, uint64_t limit_ns)
 {
     __shared__ int cnt[EP_MAX_RANKS][EP_MAX_EXPERTS];
     __shared__ int ok_s, blocked_s;
@@ -69,7 +73,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
     __threadfence_system();
     __syncthreads();
     if (tid < G) st_release_sys(&ep->peer_shared[tid]->cnt_flag[me], epoch);
-    if (tid < G && !ep_wait_flag(&mine->cnt_flag[tid], epoch, err)) ok_s = 0;
+    if (tid < G && !ep_wait_flag(&mine->cnt_flag[tid], epoch, err, limit_ns)) ok_s = 0;
     __syncthreads();
     if (!ok_s) {
         // no layout: send nothing, receive nothing
@@ -141,7 +145,9 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__
     if (tid < G) peer_s[tid] = ep->peer_recv[tid];
     if (tid == 0) blocked_s = ep->blocked;
     __syncthreads();
-    for (int i = blockIdx.x * 8 + warp; i < S; i += gridDim.x * 8) {
+    // slots at or past offsets[E] belong to pairs with a bad expert id: not sent
+    const int n_valid = min(S, off_s[E]);
+    for (int i = blockIdx.x * 8 + warp; i < n_valid; i += gridDim.x * 8) {
         int lo = 0, hi = E;                          // largest v with off_s[v] <= i
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -181,11 +187,11 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__
 }
 
 // which: 1 = rows arrived from every rank, 2 = expert outputs returned by every rank.
-__global__ void ep_wait_kernel(EpDev *ep, int which, uint32_t epoch, int *err)
+__global__ void ep_wait_kernel(EpDev *ep, int which, uint32_t epoch, int *err, uint64_t limit_ns)
 {
     const int lane = threadIdx.x;
     EpShared *mine = ep->peer_shared[ep->me];
-    if (lane < ep->G) ep_wait_flag(which == 1 ? &mine->row_flag[lane] : &mine->ret_flag[lane], epoch, err);
+    if (lane < ep->G) ep_wait_flag(which == 1 ? &mine->row_flag[lane] : &mine->ret_flag[lane], epoch, err, limit_ns);
 }
 
 __global__ void ep_signal_kernel(EpDev *ep, uint32_t epoch)
@@ -315,7 +321,7 @@ cudaError_t launch_ep_counts(void *ctx, const int *offsets, uint32_t epoch, int 
 {
     EpHost *p = static_cast<EpHost *>(ctx);
     if (!p->opened) return cudaErrorInvalidValue;
-    ep_counts_kernel<<<1, 256, 0, st>>>(p->dev, offsets, epoch, err);
+    ep_counts_kernel<<<1, 256, 0, st>>>(p->dev, offsets, epoch, err, g_ep_wait_ns);
     return cudaGetLastError();
 }
 
@@ -336,7 +342,7 @@ cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaS
 {
     EpHost *p = static_cast<EpHost *>(ctx);
     if (!p->opened || (which != 1 && which != 2)) return cudaErrorInvalidValue;
-    ep_wait_kernel<<<1, 32, 0, st>>>(p->dev, which, epoch, err);
+    ep_wait_kernel<<<1, 32, 0, st>>>(p->dev, which, epoch, err, g_ep_wait_ns);
     return cudaGetLastError();
 }
 

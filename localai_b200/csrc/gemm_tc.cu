@@ -85,6 +85,8 @@ struct TcArgs {
     __nv_bfloat16 *out_bf16;//             out_bf16[row * ld_out + n]
     long long ld_out;
     const float *row_scale; // plain mode, optional: out *= row_scale[row]
+    int out_t;              // plain mode, f32: store transposed, out[n * ld_out + row]
+                            // (the [rows][tokens] layout of the reference's matmul)
     __nv_bfloat16 *act;     // gate/up mode: act[row * ld_act + f]
     long long ld_act;
     // plain mode, optional: expert-parallel return.  Row r of group g (a run
@@ -529,6 +531,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                                        part * 8) = o;
                         }
                     }
+                } else if (a.out_t) {
+                    // lane = weight row n0 + lane; v[j] = activation row row0 + j: each
+                    // lane stores its 32 consecutive outputs (128 contiguous bytes)
+                    float *dst = a.out + (long long)(c.nt * TC_BM + 32 * ew + lane) * a.ld_out + row0;
+                    if (nrow == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+                        for (int q4 = 0; q4 < 8; ++q4)
+                            reinterpret_cast<float4 *>(dst)[q4] =
+                                make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
+                                            __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nrow) dst[j] = __uint_as_float(v[j]);
+                    }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) stg[j * TC_STG_STRIDE + lane] = __uint_as_float(v[j]);
@@ -714,16 +731,20 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
                                int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
-                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret)
+                               int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret,
+                               bool out_t)
 {
     if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
+    // transposed output: plain f32 mode only, no row scale, no peer return
+    if (out_t && (up_offset >= 0 || !out || out_bf16 || row_scale || ep_ret || ld_out < 1)) return cudaErrorInvalidValue;
     if (ep_ret && (up_offset >= 0 || groups > EP_MAX_EXPERTS)) return cudaErrorInvalidValue;
     // the epilogue stores 16-byte vectors along output rows
     if (up_offset >= 0 && ((reinterpret_cast<uintptr_t>(act) & 15) || ld_act % 8)) return cudaErrorInvalidValue;
-    if (up_offset < 0 && !ep_ret &&
+    if (up_offset < 0 && !ep_ret && !out_t &&
         (out_bf16 ? ((reinterpret_cast<uintptr_t>(out_bf16) & 15) || ld_out % 8)
                   : ((reinterpret_cast<uintptr_t>(out) & 15) || ld_out % 4)))
         return cudaErrorInvalidValue;
+    if (out_t && (reinterpret_cast<uintptr_t>(out) & 3)) return cudaErrorInvalidValue;
     if (ep_ret && ld_out % 8) return cudaErrorInvalidValue;
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
@@ -760,6 +781,7 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     a.out_bf16 = out_bf16;
     a.ld_out = ld_out;
     a.row_scale = row_scale;
+    a.out_t = out_t ? 1 : 0;
     a.act = act;
     a.ld_act = ld_act;
     a.ep_ret = ep_ret;

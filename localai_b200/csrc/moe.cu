@@ -284,6 +284,8 @@ __global__ void __launch_bounds__(256) moe_assign_kernel(const int *__restrict__
             slot_of[gi] = slot;
             token_of[slot] = (int)(gi / k);
             slot_w[slot] = wts[gi];
+        } else if (valid) {
+            slot_of[i0 + item] = -1;       // a pair with a bad expert id owns no slot
         }
         __syncthreads();
         for (int i = tid; i < 8 * E; i += 256) wcnt[i] = 0;
@@ -291,34 +293,57 @@ __global__ void __launch_bounds__(256) moe_assign_kernel(const int *__restrict__
     }
 }
 
+// Source token of slot row ``row``, or -1 when the row must not be read: rows
+// at or past ``n_valid`` (*n_valid = the dispatch's offsets[E]; slots past it
+// belong to pairs with a bad expert id and were never assigned) and token ids
+// outside [0, T) (recorded in the error word).
+__device__ __forceinline__ int gather_token(const int *__restrict__ token_of, long long row,
+                                            const int *__restrict__ n_valid, int T, int *err)
+{
+    if (n_valid && row >= __ldg(n_valid)) return -1;
+    const int t = token_of[row];
+    if (t < 0 || t >= T) {
+        if ((threadIdx.x & 31) == 0) atomicExch(err, ERR_BAD_INDEX);
+        return -1;
+    }
+    return t;
+}
+
 // out[slot, :] = h[token_of[slot], :] (f32, for the GEMV decode path); one warp per row.
-__global__ void moe_gather_f32_kernel(const float *__restrict__ h, const int *__restrict__ token_of, long long S, int D,
-                                      float *__restrict__ out)
+__global__ void moe_gather_f32_kernel(const float *__restrict__ h, int T, const int *__restrict__ token_of,
+                                      long long S, int D, float *__restrict__ out, int *err)
 {
     const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= S) return;
-    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)token_of[row] * D);
+    const int t = gather_token(token_of, row, nullptr, T, err);
+    if (t < 0) return;
+    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)t * D);
     float4 *dst = reinterpret_cast<float4 *>(out + row * D);
     for (int c = lane; c < D / 4; c += 32) dst[c] = __ldg(src + c);
 }
 
-cudaError_t launch_moe_gather_f32(const float *h, const int *token_of, int S, int D, float *out, cudaStream_t st)
+cudaError_t launch_moe_gather_f32(const float *h, int T, const int *token_of, int S, int D, float *out, int *err,
+                                  cudaStream_t st)
 {
-    if (S < 1 || D < 4 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    if (S < 1 || T < 1 || D < 4 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
         return cudaErrorInvalidValue;
-    moe_gather_f32_kernel<<<(unsigned)(((long long)S * 32 + 255) / 256), 256, 0, st>>>(h, token_of, S, D, out);
+    moe_gather_f32_kernel<<<(unsigned)(((long long)S * 32 + 255) / 256), 256, 0, st>>>(h, T, token_of, S, D, out,
+                                                                                       err);
     return cudaGetLastError();
 }
 
-// xperm[slot, :] = bf16(h[token_of[slot], :]); one warp per slot row.
-__global__ void moe_gather_kernel(const float *__restrict__ h, const int *__restrict__ token_of, long long S, int D,
-                                  __nv_bfloat16 *__restrict__ xperm)
+// xperm[slot, :] = bf16(h[token_of[slot], :]) for slots below offsets[E]; one warp per slot row.
+__global__ void moe_gather_kernel(const float *__restrict__ h, int T, const int *__restrict__ token_of, long long S,
+                                  const int *__restrict__ n_valid, int D, __nv_bfloat16 *__restrict__ xperm, int *err)
 {
     const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= S) return;
-    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)token_of[row] * D);
+    const int t = gather_token(token_of, row, n_valid, T, err);
+    if (t < 0) return;
+    const float4 *src = reinterpret_cast<const float4 *>(h + (long long)t * D);
     uint2 *dst = reinterpret_cast<uint2 *>(xperm + row * D);
     for (int c = lane; c < D / 4; c += 32) {
         const float4 v = __ldg(src + c);
@@ -340,8 +365,9 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *p, long long i)
                        __uint_as_float(u.y & 0xffff0000u));
 }
 
+// A slot outside [0, n_rows) (a pair with a bad expert id, slot -1) adds nothing.
 template <typename RowT>
-__global__ void moe_combine_kernel(const RowT *__restrict__ out, const int *__restrict__ slot_of,
+__global__ void moe_combine_kernel(const RowT *__restrict__ out, long long n_rows, const int *__restrict__ slot_of,
                                    const float *__restrict__ slot_w, int T, int k, int D, float *__restrict__ y)
 {
     const int t = blockIdx.x;
@@ -350,6 +376,7 @@ __global__ void moe_combine_kernel(const RowT *__restrict__ out, const int *__re
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; ++j) {
             const int slot = slot_of[(long long)t * k + j];
+            if (slot < 0 || slot >= n_rows) continue;
             const float4 v = load4(out, (long long)slot * (D / 4) + c);
             const float wj = slot_w ? __ldg(slot_w + slot) : 1.0f;
             acc.x = fmaf(wj, v.x, acc.x); acc.y = fmaf(wj, v.y, acc.y);
@@ -460,14 +487,18 @@ cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, 
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st)
 {
-    if (T < 1 || k < 1 || E < 1 || E > 4096 || (xperm && D % 4)) return cudaErrorInvalidValue;
+    if (T < 1 || k < 1 || E < 1 || E > 4096) return cudaErrorInvalidValue;
+    // the gather reads h with 16-byte loads and writes xperm with 8-byte stores
+    if (xperm && (D < 4 || D % 4 || (reinterpret_cast<uintptr_t>(h) & 15) || (reinterpret_cast<uintptr_t>(xperm) & 7)))
+        return cudaErrorInvalidValue;
     const int nblk = moe_num_blocks(T);
     moe_count_kernel<<<nblk, 256, E * sizeof(int), st>>>(ids, T, k, E, block_counts, err);
     moe_scan_kernel<<<1, 256, E * sizeof(int), st>>>(block_counts, nblk, E, base, offsets);
     moe_assign_kernel<<<nblk, 256, 9 * E * sizeof(int), st>>>(ids, wts, T, k, E, base, slot_of, token_of, slot_w);
     if (xperm) {
         const long long S = (long long)T * k;
-        moe_gather_kernel<<<(unsigned)((S * 32 + 255) / 256), 256, 0, st>>>(h, token_of, S, D, xperm);
+        moe_gather_kernel<<<(unsigned)((S * 32 + 255) / 256), 256, 0, st>>>(h, T, token_of, S, offsets + E, D, xperm,
+                                                                            err);
     }
     return cudaGetLastError();
 }
@@ -485,29 +516,24 @@ cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, 
 // rejected on the host.  The array occupies 256 KB + 256 B on every GPU that
 // loads the library until the process exits.  Every call shares it and it
 // keeps the previous call's contents; nothing in it has to start at zero,
-// because each call writes every count and base entry it later reads (the
-// error word is the only cumulative field, set on a bad expert id).  Calls
-// that overlap on the GPU (different streams, or different host threads
-// without ordering) race on the array.
+// because each call writes every count and base entry it later reads.  The
+// error word (set on a bad expert id or token index) is cumulative: it is read
+// and cleared by b200q_check_device_error together with the library's
+// per-device error word.  Calls that overlap on the GPU (different streams, or
+// different host threads without ordering) race on the array.
 constexpr int NOALLOC_DISPATCH_MAX = 32768;
+constexpr int NOALLOC_ERR_WORD = 2 * NOALLOC_DISPATCH_MAX;
 static __device__ __align__(256) int g_noalloc_dispatch_scratch[2 * NOALLOC_DISPATCH_MAX + 64];
 
-// Device address of the array, looked up once per device (with that device
-// current) on the first call made on it.
-cudaError_t noalloc_dispatch_scratch(int **ptr)
+// Device address of the array on the current device.  Looked up on every
+// call (cheap, allocates nothing), so a device reset or a reload of the
+// library's module never leaves a stale address behind.
+static cudaError_t noalloc_dispatch_scratch(int **ptr)
 {
-    static int *addr[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_dispatch_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!addr[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_dispatch_scratch);
-        if (e != cudaSuccess) return e;
-        addr[dev] = static_cast<int *>(p);
-    }
-    *ptr = addr[dev];
+    *ptr = static_cast<int *>(p);
     return cudaSuccess;
 }
 
@@ -520,22 +546,39 @@ cudaError_t launch_moe_dispatch_noalloc(const int *ids, const float *wts, int T,
     cudaError_t e = noalloc_dispatch_scratch(&scratch);
     if (e != cudaSuccess) return e;
     int *block_counts = scratch, *base = scratch + NOALLOC_DISPATCH_MAX;
-    int *err = scratch + 2 * NOALLOC_DISPATCH_MAX;
+    int *err = scratch + NOALLOC_ERR_WORD;
     return launch_moe_dispatch(ids, wts, T, k, E, h, D, block_counts, base, offsets, slot_of, token_of, slot_w, xperm,
                                err, st);
 }
 
+// Reads and clears the allocation-free dispatch's error word on the current
+// device (synchronous; no allocation).  *code = 0 when no error was recorded.
+cudaError_t noalloc_dispatch_take_error(int *code)
+{
+    *code = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(code, g_noalloc_dispatch_scratch, sizeof(int),
+                                         NOALLOC_ERR_WORD * sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess || *code == 0) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_noalloc_dispatch_scratch, &zero, sizeof(int), NOALLOC_ERR_WORD * sizeof(int),
+                              cudaMemcpyHostToDevice);
+}
+
 int noalloc_dispatch_max() { return NOALLOC_DISPATCH_MAX; }
 
-cudaError_t launch_moe_combine(const void *out, bool out_bf16, const int *slot_of, const float *slot_w, int T, int k,
-                               int D, float *y, cudaStream_t st)
+// n_rows: rows of ``out`` (slots at or past it are skipped like unassigned ones).
+cudaError_t launch_moe_combine(const void *out, bool out_bf16, long long n_rows, const int *slot_of,
+                               const float *slot_w, int T, int k, int D, float *y, cudaStream_t st)
 {
-    if (T < 1 || k < 1 || D % 4) return cudaErrorInvalidValue;
+    if (T < 1 || k < 1 || D < 4 || D % 4 || n_rows < 1 || (reinterpret_cast<uintptr_t>(y) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & (out_bf16 ? 7 : 15)))
+        return cudaErrorInvalidValue;
     if (out_bf16)
-        moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(out), slot_of, slot_w,
-                                                             T, k, D, y);
+        moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(out), n_rows, slot_of,
+                                                             slot_w, T, k, D, y);
     else
-        moe_combine_kernel<float><<<T, 256, 0, st>>>(static_cast<const float *>(out), slot_of, slot_w, T, k, D, y);
+        moe_combine_kernel<float><<<T, 256, 0, st>>>(static_cast<const float *>(out), n_rows, slot_of, slot_w, T, k,
+                                                     D, y);
     return cudaGetLastError();
 }
 

@@ -296,7 +296,7 @@ class DeviceGGUF:
         if x.ggml_type in (GGML_F32, GGML_F16):
             m = w.view(torch.float32 if x.ggml_type == GGML_F32 else torch.float16).reshape(rows, cols).float()
             return X @ m.T
-        return ops.gemv(w, X, x.ggml_type, rows, cols)
+        return ops.matmul(w, X, x.ggml_type, rows, cols)
 
     def matvec(self, name, vector):
         """W @ x (engine/gguf_parser.py:194-288): numpy in -> numpy out, CUDA

@@ -205,8 +205,8 @@ class QuantMoE:
         S, dev = token_of.numel(), h.device
         G = self.E_held if n_groups is None else n_groups
         xs = torch.empty((S, self.D), dtype=torch.float32, device=dev)
-        _lib.check(self.lib.b200q_moe_gather_f32_dev(h.data_ptr(), token_of.data_ptr(), S, self.D, xs.data_ptr(),
-                                                     _stream()))
+        _lib.check(self.lib.b200q_moe_gather_f32_dev(h.data_ptr(), h.shape[0], token_of.data_ptr(), S, self.D,
+                                                     xs.data_ptr(), _stream()))
         gu = torch.empty((S, 2 * self.F), dtype=torch.float32, device=dev)
         active = max(1, min(G, S))
         _lib.check(self.lib.b200q_gemv_grouped_dev(

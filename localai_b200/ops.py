@@ -79,6 +79,36 @@ def gemv(w: torch.Tensor, x: torch.Tensor, ggml_type: int, rows: int, cols: int,
     return out.reshape(rows) if squeeze else out
 
 
+def tensor_core_min_tokens() -> int:
+    """Token count from which batched quantised matmuls use the tensor cores
+    (the library setting shared with the localai_*_matmul entry points)."""
+    return int(_lib.load().b200q_matmul_tensor_core_min_tokens(-1))
+
+
+def tensor_core_shape_ok(ggml_type: int, rows: int, cols: int) -> bool:
+    """Q4_K/Q6_K/Q8_0 weights the tensor-core GEMM can stream as packed rows."""
+    if ggml_type not in (8, 12, 14) or rows % 128 or cols % 64 or cols % BLOCK[ggml_type][0]:
+        return False
+    return row_bytes(ggml_type, cols) % 16 == 0
+
+
+def matmul(w: torch.Tensor, x: torch.Tensor, ggml_type: int, rows: int, cols: int) -> torch.Tensor:
+    """f32 [tokens, rows] = x @ W^T for f32 x [tokens, cols]: the tensor-core
+    GEMM (bf16 operands, f32 accumulation) for batches of at least
+    ``tensor_core_min_tokens()`` tokens on supported weights, else the f32 GEMV."""
+    _check_weights(w, ggml_type, rows, cols)
+    x2 = x.reshape(-1, cols)
+    T = x2.shape[0]
+    nmin = tensor_core_min_tokens()
+    if nmin <= 0 or T < nmin or not tensor_core_shape_ok(ggml_type, rows, cols) or w.data_ptr() % 16:
+        return gemv(w, x2, ggml_type, rows, cols)
+    if x2.dtype != torch.float32 or not x2.is_cuda:
+        raise ValueError('x must be a CUDA float32 tensor with cols columns')
+    off = torch.tensor([0, T], dtype=torch.int32, device=x2.device)
+    return gemm_quant(x2.contiguous().to(torch.bfloat16), w, off, k=cols, n_feat=rows, w_rows_per_group=rows,
+                      ggml_type=ggml_type, out_dtype=torch.float32)
+
+
 def check_device_error() -> None:
     """Synchronise and raise if a kernel reported a timed-out wait or bad index."""
     code = _lib.load().b200q_check_device_error()

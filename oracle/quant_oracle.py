@@ -38,6 +38,10 @@ is the single f32 subtraction of the Q4_K/Q5_K minimum term.
 """
 from __future__ import annotations
 
+import ctypes
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
 import numpy as np
 
 # (values per block, bytes per block) -- engine/dequant.py:6-9
@@ -185,15 +189,48 @@ def dequantize(raw, t, shape):
     return _DECODERS[t](blocks).reshape(shape)
 
 
+_C_ORACLE = None
+
+
+def _c_oracle():
+    """The C restatement (oracle/quant_oracle.c, built by ``make -C oracle``),
+    or None when it is not built.  tests/test_oracle.py checks that its decode
+    equals ``dequantize`` bit for bit."""
+    global _C_ORACLE
+    if _C_ORACLE is None:
+        so = Path(__file__).resolve().parent / '_build' / 'liboracle.so'
+        _C_ORACLE = ctypes.CDLL(str(so)) if so.exists() else False
+    return _C_ORACLE or None
+
+
+def dequantize_fast(raw, t, shape):
+    """``dequantize`` through the C restatement when it is built (same f32
+    bits, several times faster on large matrices; releases the GIL), else the
+    NumPy restatement."""
+    lib = _c_oracle()
+    if lib is None or t not in MATVEC_TYPES:
+        return dequantize(raw, t, shape)
+    block, nbytes = block_layout(t)
+    n = int(np.prod(shape, dtype=np.int64))
+    if n % block:
+        raise ValueError(f'{n} elements is not divisible by block size {block}')
+    buf = np.frombuffer(raw, dtype=np.uint8, count=(n // block) * nbytes)
+    out = np.empty(n, np.float32)
+    if lib.oracle_dequant(t, buf.ctypes.data_as(ctypes.c_void_p), out.ctypes.data_as(ctypes.c_void_p),
+                          ctypes.c_longlong(n // block)) != 0:
+        raise ValueError(f'C oracle cannot decode type {t}')
+    return out.reshape(shape)
+
+
 def matvec_f64(raw, t, rows, cols, x):
     """``dequantize(raw) @ x`` in float64: the GEMV parity oracle."""
-    w = dequantize(raw, t, (rows, cols)).astype(np.float64)
+    w = dequantize_fast(raw, t, (rows, cols)).astype(np.float64)
     return w @ np.asarray(x, np.float64)
 
 
 def matmul_f64(raw, t, rows, cols, vectors):
     """[tokens, cols] x W[rows, cols]^T in float64 -> [tokens, rows]."""
-    w = dequantize(raw, t, (rows, cols)).astype(np.float64)
+    w = dequantize_fast(raw, t, (rows, cols)).astype(np.float64)
     return np.asarray(vectors, np.float64) @ w.T
 
 
@@ -256,21 +293,32 @@ def expert_ffn_f64(gate_up_raw, down_raw, t_gu, t_dn, d_model, d_ff, d_ff_padded
     return matmul_f64(down_raw, t_dn, d_model, d_ff_padded, act)
 
 
-def moe_forward_f64(h, ids, weights, experts, t_gu, t_dn, d_model, d_ff, d_ff_padded):
-    """Weighted combine over the selected experts, in fixed k order.
+def moe_forward_f64(h, ids, weights, experts, t_gu, t_dn, d_model, d_ff, d_ff_padded, workers=1):
+    """Weighted combine over the selected experts.
 
-    ``experts[e] = (gate_up_raw, down_raw)``.  Tokens are grouped per expert
-    (each expert's product runs once over its tokens), then
-    ``y[t] = sum_j w[t,j] * out_e(t)`` with j ascending.
+    ``experts[e] = (gate_up_raw, down_raw)`` (a list, dict or callable).
+    Tokens are grouped per expert (each expert's product runs once over its
+    tokens), then ``y[t] = sum_j w[t,j] * out_e(t)``.  ``workers`` > 1 runs the
+    experts' products in threads; the sum is still taken in expert order.
     """
     h = np.atleast_2d(np.asarray(h, np.float32))
     T, k = ids.shape
     y = np.zeros((T, d_model), np.float64)
-    for e in np.unique(ids):
+    get = experts if callable(experts) else experts.__getitem__
+
+    def one(e):
         # a token selects an expert at most once, so ``rows`` is duplicate-free
         rows, slots = np.nonzero(ids == e)
-        out = expert_ffn_f64(experts[e][0], experts[e][1], t_gu, t_dn,
-                             d_model, d_ff, d_ff_padded, h[rows])
+        gu, dn = get(int(e))
+        return rows, slots, expert_ffn_f64(gu, dn, t_gu, t_dn, d_model, d_ff, d_ff_padded, h[rows])
+
+    uniq = np.unique(ids)
+    if workers > 1:
+        with ThreadPoolExecutor(max_workers=workers) as ex:
+            results = list(ex.map(one, uniq))
+    else:
+        results = [one(e) for e in uniq]
+    for rows, slots, out in results:
         y[rows] += out * weights[rows, slots].astype(np.float64)[:, None]
     return y
 

@@ -18,6 +18,12 @@ from localai_b200.moe import QuantMoE
 
 pytestmark = pytest.mark.gpu
 
+# Routing decisions may differ from float64 ones only where the oracle's k-th
+# and (k+1)-th probabilities are closer than this (the router's f32 dot
+# products move a logit by ~1e-6, a probability by less; 2e-6 leaves a
+# twentyfold allowance and is far below the typical margin).
+ROUTE_MARGIN = 2e-6
+
 
 def make_layer(rng, E, D, F, k, renorm=True, router_bias=None, sel_bias=None):
     F_pad = (F + 255) // 256 * 256
@@ -125,9 +131,20 @@ def test_layer_matches_oracle(E, D, F, k, T):
     ops.check_device_error()
     logits, ids, w = layer.route(torch.from_numpy(h).cuda())
     ids, w = ids.cpu().numpy(), w.cpu().numpy()
-    # the GPU routing agrees with the oracle on float64 logits except at near-ties
-    ref_ids, _ = o.route_topk((h.astype(np.float64) @ wr.T.astype(np.float64)).astype(np.float32), k)
-    assert np.mean(np.all(np.sort(ids, 1) == np.sort(ref_ids, 1), axis=1)) > 0.97
+    # the top-k kernel is bit-exact on the GPU's own logits
+    assert np.array_equal(ids, o.route_topk(logits.cpu().numpy(), k)[0])
+    # against float64 logits the GPU's selected set may differ only where the
+    # oracle's k-th and (k+1)-th probabilities are within ROUTE_MARGIN
+    lg64 = h.astype(np.float64) @ wr.T.astype(np.float64)
+    p64 = np.exp(lg64 - lg64.max(axis=1, keepdims=True))
+    p64 /= p64.sum(axis=1, keepdims=True)
+    order = np.argsort(-p64, axis=1, kind='stable')
+    differ = np.nonzero(np.any(np.sort(ids, 1) != np.sort(order[:, :k], 1), axis=1))[0]
+    if k < E:
+        margin = p64[differ, order[differ, k - 1]] - p64[differ, order[differ, k]]
+        assert np.all(margin <= ROUTE_MARGIN), (differ, margin)
+    else:
+        assert differ.size == 0
     experts = [(gate_up[e], down[e]) for e in range(E)]
     ref = o.moe_forward_f64(h, ids, w, experts, 12, 12, D, F, F_pad)
     assert o.normwise_rel_err(y.cpu().numpy(), ref) < 1e-2

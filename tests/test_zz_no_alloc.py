@@ -76,3 +76,31 @@ def test_noalloc_dispatch_rejects_oversize_call():
                                             torch.cuda.current_stream().cuda_stream)
     assert st == _lib.B200Q_EINVAL
     assert b'static scratch limit' in lib.b200q_last_error()
+
+
+def test_noalloc_dispatch_reports_bad_expert_id():
+    """A bad expert id through the allocation-free entry point is reported by
+    b200q_check_device_error (the error word lives in the static array) and
+    the call otherwise equals the regular dispatch."""
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    assert lib.b200q_check_device_error() == 0
+    T, k, E, D = 300, 2, 8, 128
+    g = torch.Generator(device='cuda')
+    g.manual_seed(11)
+    ids = torch.topk(torch.rand((T, E), generator=g, device='cuda'), k, dim=1).indices.to(torch.int32)
+    ids[17, 1] = E + 3
+    ids = ids.contiguous()
+    w = torch.rand((T, k), generator=g, device='cuda')
+    h = torch.randn((T, D), generator=g, device='cuda')
+    ref = _dispatch(lib, ids, w, h, E, noalloc=False)
+    assert lib.b200q_check_device_error() == 2
+    got = _dispatch(lib, ids, w, h, E, noalloc=True)
+    assert lib.b200q_check_device_error() == 2
+    assert lib.b200q_check_device_error() == 0
+    n = T * k - 1
+    assert int(got[0][-1]) == n and int(got[1][17 * k + 1]) == -1
+    for i, (r, x) in enumerate(zip(ref, got)):
+        if i in (2, 3, 4):                   # token_of, slot_w, xperm: the unassigned tail is not written
+            r, x = r[:n], x[:n]
+        assert torch.equal(r, x)
