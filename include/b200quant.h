@@ -252,6 +252,13 @@ int b200q_check_device_error(void);
  * and the most CTAs per SM in the grid (0 = as many as fit); 0 (-1 for the
  * last) keeps the current value. */
 void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas_per_sm);
+/* Batch-1 Q4_K GEMV on the integer tensor cores (used by b200q_gemv_dev and
+ * the localai_q4k_matvec drop-in when the weights are 16-byte aligned):
+ * enable (1) or disable (0; -1 keeps), super-blocks per warp per pipeline
+ * stage (1..3, 0 = automatic), stages per warp (0 = as many as fit in half an
+ * SM's shared memory) and CTAs of one launch per SM (1 or 2; with 1 the other
+ * slot runs the next launch's weight stream); -1 keeps a setting. */
+void b200q_gemv_mma_tuning(int enable, int sb_per_warp, int stages, int ctas_per_sm);
 
 /* Number of kernel launches made by this library since load. */
 long long b200q_launch_count(void);

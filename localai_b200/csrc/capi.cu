@@ -21,6 +21,8 @@ cudaError_t launch_dequant_bf16(int type, const void *raw, __nv_bfloat16 *out, l
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st);
 void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm);
+void gemv_set_mma(bool on);
+void gemv_mma_set_tuning(int spw, int stages, int ctas_per_sm);
 cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
                               cudaStream_t st);
 cudaError_t launch_moe_topk(const float *logits, const float *sel_bias, int T, int E, int k, int renorm, int *ids,
@@ -697,6 +699,13 @@ B200Q_API void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
     gemv_set_tuning(stage_bytes, stages, rows_per_group, ctas_per_sm);
+}
+
+B200Q_API void b200q_gemv_mma_tuning(int enable, int sb_per_warp, int stages, int ctas_per_sm)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (enable >= 0) gemv_set_mma(enable != 0);
+    gemv_mma_set_tuning(sb_per_warp, stages, ctas_per_sm);
 }
 
 B200Q_API long long b200q_launch_count(void) { return g_launches; }

@@ -661,6 +661,26 @@ static PFN_encodeTiled get_encode()
     return fn;
 }
 
+// Raw bytes [rows, row_bytes] seen as uint16 elements, box [box_bytes x box_rows],
+// no swizzle, out-of-range elements read as zero (used by the batch-1 GEMV).
+cudaError_t make_map_u16_rows(CUtensorMap *m, const void *ptr, long long rows, long long row_bytes, int box_bytes,
+                              int box_rows)
+{
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || row_bytes % 16 || box_bytes % 16 || box_bytes / 2 > 256 ||
+        box_rows < 1 || box_rows > 256)
+        return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(box_bytes / 2), (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // bf16 [rows, cols] row-major, box [64 cols x box_rows], 128-byte swizzle.
 static cudaError_t make_map_bf16(CUtensorMap *m, const void *ptr, long long rows, long long cols, int box_rows)
 {

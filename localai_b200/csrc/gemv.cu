@@ -710,6 +710,8 @@ static int g_stage_target = 48 * 1024;
 static int g_stages = 3;
 static int g_rpg_max = 4;
 static int g_ctas_per_sm = 0;     // 0 = as many as fit
+static bool g_use_mma = true;     // batch-1 Q4_K on the integer tensor cores
+void gemv_set_mma(bool on) { g_use_mma = on; }
 void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm)
 {
     if (stage_target_bytes > 0) g_stage_target = stage_target_bytes;
@@ -864,11 +866,18 @@ static cudaError_t launch_gemv_chunk(int type, const void *w, const float *x, fl
 // of the block size, or rows too wide for the register budget).  Token
 // batches whose quantised activations do not fit in shared memory next to the
 // weight pipeline are processed in chunks of tokens (one launch each).
+bool gemv_mma_supported(int type, const void *w, int rows, int cols, int tokens);
+cudaError_t launch_gemv_mma(const void *w, const float *x, float *y, long long ys_r, int rows, int cols, int *err,
+                            int num_sms, cudaStream_t st);
+
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st)
 {
     const int vals = type_vals(type), bytes = type_bytes(type);
     if (!bytes || rows < 1 || tokens < 1 || cols < vals || cols % vals) return cudaErrorInvalidValue;
+    // batch-1 Q4_K: the integer-tensor-core kernel (gemv_mma.cu)
+    if (g_use_mma && gemv_mma_supported(type, w, rows, cols, tokens) && !(reinterpret_cast<uintptr_t>(x) & 15))
+        return launch_gemv_mma(w, x, y, ys_r, rows, cols, err, num_sms, st);
     const int units = (cols / vals) * ((vals == 256) ? 4 : 1);
     const size_t per_tok = (size_t)units * ((vals == 256) ? XPackWords<16>::N : XPackWords<8>::N) * 4;
     int chunk = (int)std::max<size_t>(1, (96 * 1024) / per_tok);
