@@ -259,6 +259,13 @@ void b200q_gemv_tuning(int stage_bytes, int stages, int rows_per_group, int ctas
  * SM's shared memory) and CTAs of one launch per SM (1 or 2; with 1 the other
  * slot runs the next launch's weight stream); -1 keeps a setting. */
 void b200q_gemv_mma_tuning(int enable, int sb_per_warp, int stages, int ctas_per_sm);
+/* Tensor-core grouped GEMM (b200q_gemm_q4k_dev, b200q_gemm_dev, the batched
+ * localai_*_matmul drop-ins, the MoE and expert-parallel layers): 1 (default)
+ * runs every tile on a pair of SMs (tcgen05 cta_group::2, M = 256 weight rows
+ * x N = 256 activation rows, each SM loading half of the activation tile);
+ * 0 runs one tile per SM (M = 128); -1 keeps the mode.  Results are
+ * identical.  Returns the number of SM pairs the last pair launch used. */
+int b200q_gemm_pair_mode(int on);
 
 /* Number of kernel launches made by this library since load. */
 long long b200q_launch_count(void);

@@ -65,6 +65,7 @@ SIGNATURES = {
     'b200q_check_device_error': (_i, []),
     'b200q_gemv_tuning': (None, [_i, _i, _i, _i]),
     'b200q_gemv_mma_tuning': (None, [_i, _i, _i, _i]),
+    'b200q_gemm_pair_mode': (_i, [_i]),
     'b200q_launch_count': (_ll, []),
     'b200q_dequant_row_dev': (_i, [_i, _vp, _ll, _i, _vp, _i, _i, _vp, _vp]),
     'b200q_add_rmsnorm_dev': (_i, [_vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp, _vp]),

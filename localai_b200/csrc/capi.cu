@@ -22,6 +22,8 @@ cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long 
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st);
 void gemv_set_tuning(int stage_target_bytes, int stages, int rpg_max, int ctas_per_sm);
 void gemv_set_mma(bool on);
+void tc_gemm_set_pair(bool on);
+int tc_gemm_pairs_used();
 void gemv_mma_set_tuning(int spw, int stages, int ctas_per_sm);
 cudaError_t launch_moe_router(const float *h, const float *wr, const float *bias, float *logits, int T, int E, int D,
                               cudaStream_t st);
@@ -706,6 +708,13 @@ B200Q_API void b200q_gemv_mma_tuning(int enable, int sb_per_warp, int stages, in
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (enable >= 0) gemv_set_mma(enable != 0);
     gemv_mma_set_tuning(sb_per_warp, stages, ctas_per_sm);
+}
+
+B200Q_API int b200q_gemm_pair_mode(int on)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (on >= 0) tc_gemm_set_pair(on != 0);
+    return tc_gemm_pairs_used();
 }
 
 B200Q_API long long b200q_launch_count(void) { return g_launches; }

@@ -69,15 +69,21 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// A waiting warp is suspended in hardware until the phase completes or the
+// hint (ns) runs out, instead of spinning: spinning warps compete with the
+// producers and the MMA issuer for the barrier unit and for issue slots.
+#ifndef MBAR_SUSPEND_NS
+#define MBAR_SUSPEND_NS 1000000u
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(MBAR_SUSPEND_NS)
         : "memory");
     return ok != 0;
 }
@@ -96,7 +102,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *er
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+        if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
             atomicExch(err, ERR_WAIT_TIMEOUT);
             return false;
         }

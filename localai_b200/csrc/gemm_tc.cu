@@ -52,6 +52,14 @@ constexpr int TC_BK = 64;               // K per stage (bf16, 128 bytes)
 #endif
 constexpr int TC_A_STAGES = TC_A_STAGES_CFG;     // dequantised weight tiles (dequant warps -> MMA)
 constexpr int TC_B_STAGES = TC_B_STAGES_CFG;     // activation tiles (TMA -> MMA)
+// CTA-pair mode: a B stage holds half the activation rows (16 KB), so more
+// stages fit; A and B stages are released together by ONE MMA commit per
+// K-step (a second commit per 4 MMAs costs ~15% of the tensor pipe's rate).
+#ifndef TC_PAIR_STAGES_CFG
+#define TC_PAIR_STAGES_CFG 4
+#endif
+constexpr int TC_PAIR_A_STAGES = TC_PAIR_STAGES_CFG;
+constexpr int TC_PAIR_B_STAGES = TC_PAIR_STAGES_CFG;
 // Raw weight chunks (one 256-value run of blocks per row, 4 K-steps), TMA ->
 // dequant warps.  The box of each type is 16-byte sized: Q4_K 144 B (a
 // super-block), Q8_0 272 B (8 blocks, as 136 uint16), Q6_K 240 B (as 120
@@ -136,6 +144,108 @@ __device__ __forceinline__ void umma_commit(uint32_t bar)
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) forms.  The pair is a cluster of two CTAs on
+// two SMs; the even CTA issues the MMAs, which read A (weight rows) and B
+// (activation rows) from both CTAs' shared memory at the same offsets and
+// write each CTA's half of M into that CTA's tensor memory.
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA ``rank`` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier given by its cluster address (this CTA's or the peer's).
+#ifndef TC_PAIR_CLUSTER_SCOPE
+#define TC_PAIR_CLUSTER_SCOPE 0
+#endif
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cbar)
+{
+#if TC_PAIR_CLUSTER_SCOPE
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+#else
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+#endif
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+#if TC_PAIR_CLUSTER_SCOPE
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+#else
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+#endif
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(MBAR_SUSPEND_NS)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (as mbar_wait) with cluster-scope acquire: for barriers that
+// the peer CTA arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *err)
+{
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+            atomicExch(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+// TMA tile load into this CTA's shared memory whose completion (bytes) is
+// signalled on an mbarrier of either CTA of the pair (cluster address).  No
+// multicast: each CTA loads its own rows.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t cbar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cbar)
+        : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at offset ``bar`` in both CTAs of the pair when
+// every pair MMA issued so far completes (a completion signal, not a load).
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar)
+{
+    const uint16_t mask = 3;
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"(mask)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 {
@@ -179,9 +289,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
 
 __device__ __forceinline__ float silu_ref(float g)
 {
-    // engine/zaya.py:305: g / (1 + exp(-clip(g, -80, 80)))
+    // engine/zaya.py:305: g / (1 + exp(-clip(g, -80, 80))).  The hardware
+    // exponential and approximate division (a few ulp of f32) are far below
+    // the bf16 rounding of the stored result, and keep the epilogue's issue
+    // slots for the mainloop.
     const float c = fminf(fmaxf(g, -80.f), 80.f);
-    return g / (1.0f + expf(-c));
+    return __fdividef(g, 1.0f + __expf(-c));
 }
 
 // ---------------------------------------------------------------- dequant
@@ -333,30 +446,45 @@ __device__ __forceinline__ TileCoord tile_coord(int t, const int *tile_pref, con
     return c;
 }
 
-template <int WT>
+// PAIR = false: one CTA per tile, MMA M = 128 weight rows x N <= 256
+// activation rows.  PAIR = true: a cluster of two CTAs per tile
+// (tcgen05 cta_group::2), M = 256 weight rows (128 dequantised by each CTA)
+// x N <= 256 activation rows (N/2 loaded by each CTA): every SM reads only
+// half of the activation tile from shared memory, which halves the operand
+// traffic that bounds the one-CTA form.  Barriers of the pair: the even CTA
+// ("leader") owns full_a (16 dequant warps of both CTAs arrive), full_b (both
+// CTAs' TMA bytes) and acc_empty (8 epilogue warps); the MMA commits arrive on
+// empty_a / empty_b / acc_full in both CTAs.
+template <int WT, bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                    const TcArgs a)
 {
     constexpr int TC_RAW_STAGES = TcW<WT>::RAW;
+    constexpr int A_ST = PAIR ? TC_PAIR_A_STAGES : TC_A_STAGES;
+    constexpr int B_ST = PAIR ? TC_PAIR_B_STAGES : TC_B_STAGES;
+    constexpr int B_BYTES = PAIR ? TC_B_BYTES / 2 : TC_B_BYTES;       // activation rows loaded by this CTA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-aligned base for the swizzled tiles
     const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
     const uint32_t sA = base;
-    const uint32_t sB = sA + TC_A_STAGES * TC_A_BYTES;
-    const uint32_t sRaw = sB + TC_B_STAGES * TC_B_BYTES;
+    const uint32_t sB = sA + A_ST * TC_A_BYTES;
+    const uint32_t sRaw = sB + B_ST * B_BYTES;
     const uint32_t raw_stage_bytes = (uint32_t)(TC_BM * a.raw_chunk_bytes);
     const uint32_t sStg = (sRaw + TC_RAW_STAGES * raw_stage_bytes + 15u) & ~15u;
     const uint32_t sBar = sStg + 4 * TC_STG_BYTES;
-    const uint32_t full_a = sBar;                             // [A]        8 dequant warps
-    const uint32_t empty_a = full_a + 8 * TC_A_STAGES;        // [A]        MMA commit
-    const uint32_t full_b = empty_a + 8 * TC_A_STAGES;        // [B]        TMA tx
-    const uint32_t empty_b = full_b + 8 * TC_B_STAGES;        // [B]        MMA commit
-    const uint32_t raw_full = empty_b + 8 * TC_B_STAGES;      // [RAW]      TMA tx
+    const uint32_t full_a = sBar;                             // [A]        dequant warps
+    const uint32_t empty_a = full_a + 8 * A_ST;               // [A]        MMA commit
+    const uint32_t full_b = empty_a + 8 * A_ST;               // [B]        TMA tx
+    const uint32_t empty_b = full_b + 8 * B_ST;               // [B]        MMA commit
+    const uint32_t raw_full = empty_b + 8 * B_ST;             // [RAW]      TMA tx
     const uint32_t raw_empty = raw_full + 8 * TC_RAW_STAGES;  // [RAW]      8 dequant warps
     const uint32_t acc_full = raw_empty + 8 * TC_RAW_STAGES;  // [2]        MMA commit
-    const uint32_t acc_empty = acc_full + 16;                 // [2]        4 epilogue warps
+    const uint32_t acc_empty = acc_full + 16;                 // [2]        epilogue warps
     const uint32_t tmem_slot = acc_empty + 16;
+    // the barrier that releases a B stage: its own (one CTA) or the shared A/B one (pair)
+    const uint32_t empty_ab = PAIR ? empty_a : empty_b;
+    static_assert(!PAIR || A_ST == B_ST, "pair mode releases A and B stages with one commit");
     __shared__ int tile_pref[TC_MAX_GROUPS + 1];
     __shared__ int row_off_s[TC_MAX_GROUPS + 1];
     __shared__ int group_w_s[TC_MAX_GROUPS];
@@ -367,13 +495,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ksteps = a.k / TC_BK;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    // the leader's copy of a barrier (cluster address); the CTA's own in one-CTA mode
+    auto lead = [&](uint32_t bar) -> uint32_t { return PAIR ? mapa_shared(bar, 0) : bar; };
+    // work units: tiles (one CTA) or pair tiles (two CTAs, 2 weight tiles each)
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int nunits = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int n_units_w = PAIR ? (a.n_tiles + 1) / 2 : a.n_tiles;    // weight-row units per group
 
     if (tid == 0) {
-        for (int s = 0; s < TC_A_STAGES; ++s) {
-            mbar_init(full_a + 8 * s, 8);
+        for (int s = 0; s < A_ST; ++s) {
+            mbar_init(full_a + 8 * s, PAIR ? 16 : 8);
             mbar_init(empty_a + 8 * s, 1);
         }
-        for (int s = 0; s < TC_B_STAGES; ++s) {
+        for (int s = 0; s < B_ST; ++s) {
             mbar_init(full_b + 8 * s, 1);
             mbar_init(empty_b + 8 * s, 1);
         }
@@ -383,7 +518,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(acc_full + 8 * s, 1);
-            mbar_init(acc_empty + 8 * s, 4);
+            mbar_init(acc_empty + 8 * s, PAIR ? 8 : 4);
         }
         mbar_fence_init();
     }
@@ -397,7 +532,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int g = 0; g < a.groups; ++g) {
                 tile_pref[g] = acc;
                 const int m = row_off_s[g + 1] - row_off_s[g];
-                acc += (m > 0 ? (m + TC_BN - 1) / TC_BN : 0) * a.n_tiles;
+                acc += (m > 0 ? (m + TC_BN - 1) / TC_BN : 0) * n_units_w;
             }
             tile_pref[a.groups] = acc;
         }
@@ -411,25 +546,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) ret_G = G;
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 512);
+            tmem_relinquish();
+        }
         tc_fence_before();
     }
     __syncthreads();
+    if (PAIR) cluster_sync_all();        // the peer's barriers are initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = lds32(tmem_slot);
     const int total_tiles = tile_pref[a.groups];
     const bool gate_up = a.up_offset >= 0;
     bool ok = true;
+    // this CTA's weight tile of a unit, clamped for loads (an odd tile count
+    // leaves the peer of the last pair without rows: it computes a copy of the
+    // leader's and stores nothing)
+    auto cta_nt = [&](int nt_unit) { return PAIR ? 2 * nt_unit + (int)rank : nt_unit; };
+    // activation rows per CTA in pair mode: half the tile's valid rows, rounded up to 16
+    auto pair_half = [&](int rows) { return min(TC_BN / 2, (((rows + 1) >> 1) + 15) & ~15); };
 
     if (warp == 0) {
         // ------------------------------------------------ raw weight producer (TMA)
         if (lane == 0) {
             const int nchunks = (ksteps + 3) / 4;
             int rq = 0;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
-                const int wrow0 = group_w_s[c.g] * a.w_rows_per_group + (gate_up ? c.nt * 64 : c.nt * TC_BM);
+            for (int t = unit; t < total_tiles && ok; t += nunits) {
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
+                const int nt = min(cta_nt(c.nt), a.n_tiles - 1);
+                const int wrow0 = group_w_s[c.g] * a.w_rows_per_group + (gate_up ? nt * 64 : nt * TC_BM);
                 const int wrow1 = gate_up ? wrow0 + a.up_offset : wrow0 + 64;
                 for (int rc = 0; rc < nchunks; ++rc, ++rq) {
                     const int rs = rq % TC_RAW_STAGES;
@@ -447,45 +595,71 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ------------------------------------------------ activation producer (TMA)
         if (lane == 0) {
             int q = 0;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
-                const int xrow = row_off_s[c.g] + c.m0;
+            for (int t = unit; t < total_tiles && ok; t += nunits) {
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
+                const int xrow = row_off_s[c.g] + c.m0 + (PAIR ? (int)rank * pair_half(c.rows) : 0);
                 for (int ks = 0; ks < ksteps; ++ks, ++q) {
-                    const int s = q % TC_B_STAGES;
-                    if (q >= TC_B_STAGES && !mbar_wait(empty_b + 8 * s, ((q / TC_B_STAGES) + 1) & 1, a.err)) { ok = false; break; }
-                    mbar_arrive_expect_tx(full_b + 8 * s, TC_B_BYTES);
-                    tma_load_2d(sB + s * TC_B_BYTES, &map_x, ks * TC_BK, xrow, full_b + 8 * s);
+                    const int s = q % B_ST;
+                    if (q >= B_ST && !mbar_wait(empty_ab + 8 * s, ((q / B_ST) + 1) & 1, a.err)) { ok = false; break; }
+                    if (PAIR) {
+                        if (rank == 0) mbar_arrive_expect_tx(full_b + 8 * s, 2 * B_BYTES);
+                        tma_load_2d_pair(sB + s * B_BYTES, &map_x, ks * TC_BK, xrow, lead(full_b + 8 * s));
+                    } else {
+                        mbar_arrive_expect_tx(full_b + 8 * s, B_BYTES);
+                        tma_load_2d(sB + s * B_BYTES, &map_x, ks * TC_BK, xrow, full_b + 8 * s);
+                    }
                 }
             }
+            // pair: every MMA completion signal for this CTA's stages has landed before it leaves
+            if (PAIR && ok)
+                for (int u = max(0, q - B_ST); u < q; ++u)
+                    if (!mbar_wait(empty_ab + 8 * (u % B_ST), (u / B_ST) & 1, a.err)) break;
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------ MMA issuer (the leader's lane 0)
+        if (lane == 0 && rank == 0) {
             int q = 0, acc = 0;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
-                // N of this tile's MMAs: its valid activation rows rounded up to 16
-                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
-                const uint32_t idesc = idesc_bf16(TC_BM, min(TC_BN, (c.rows + 15) & ~15));
+            for (int t = unit; t < total_tiles && ok; t += nunits, ++acc) {
+                // N of this tile's MMAs: its valid activation rows rounded up to 16 (pair: 2 x half)
+                const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
+                const uint32_t idesc = PAIR ? idesc_bf16(2 * TC_BM, 2 * pair_half(c.rows))
+                                            : idesc_bf16(TC_BM, min(TC_BN, (c.rows + 15) & ~15));
                 const int ab = acc & 1;
-                if (acc >= 2 && !mbar_wait(acc_empty + 8 * ab, ((acc >> 1) + 1) & 1, a.err)) { ok = false; break; }
+                if (acc >= 2 && !(PAIR ? mbar_wait_cluster(acc_empty + 8 * ab, ((acc >> 1) + 1) & 1, a.err)
+                                       : mbar_wait(acc_empty + 8 * ab, ((acc >> 1) + 1) & 1, a.err))) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(ab * TC_BN);
                 for (int ks = 0; ks < ksteps; ++ks) {
-                    const int sa = q % TC_A_STAGES, sb = q % TC_B_STAGES;
-                    if (!mbar_wait(full_b + 8 * sb, (q / TC_B_STAGES) & 1, a.err)) { ok = false; break; }
-                    if (!mbar_wait(full_a + 8 * sa, (q / TC_A_STAGES) & 1, a.err)) { ok = false; break; }
+                    const int sa = q % A_ST, sb = q % B_ST;
+                    if (PAIR) {
+                        if (!mbar_wait_cluster(full_b + 8 * sb, (q / B_ST) & 1, a.err)) { ok = false; break; }
+                        if (!mbar_wait_cluster(full_a + 8 * sa, (q / A_ST) & 1, a.err)) { ok = false; break; }
+                    } else {
+                        if (!mbar_wait(full_b + 8 * sb, (q / B_ST) & 1, a.err)) { ok = false; break; }
+                        if (!mbar_wait(full_a + 8 * sa, (q / A_ST) & 1, a.err)) { ok = false; break; }
+                    }
                     tc_fence_after();
-                    const uint32_t as = sA + sa * TC_A_BYTES, bs = sB + sb * TC_B_BYTES;
+                    const uint32_t as = sA + sa * TC_A_BYTES, bs = sB + sb * B_BYTES;
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk)
-                        umma_bf16(d_tmem, sw128_desc(as + 32 * kk), sw128_desc(bs + 32 * kk), idesc,
-                                  (ks > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(empty_a + 8 * sa);
-                    umma_commit(empty_b + 8 * sb);
+                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                        if (PAIR)
+                            umma_bf16_pair(d_tmem, sw128_desc(as + 32 * kk), sw128_desc(bs + 32 * kk), idesc,
+                                           (ks > 0 || kk > 0) ? 1u : 0u);
+                        else
+                            umma_bf16(d_tmem, sw128_desc(as + 32 * kk), sw128_desc(bs + 32 * kk), idesc,
+                                      (ks > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    if (PAIR) {
+                        umma_commit_pair_both(empty_a + 8 * sa);        // releases A and B stage sa == sb
+                    } else {
+                        umma_commit(empty_a + 8 * sa);
+                        umma_commit(empty_b + 8 * sb);
+                    }
                     ++q;
                 }
                 if (!ok) break;
-                umma_commit(acc_full + 8 * ab);
+                if (PAIR) umma_commit_pair_both(acc_full + 8 * ab);
+                else umma_commit(acc_full + 8 * ab);
             }
         }
     } else if (warp >= 4 && warp < 8) {
@@ -493,13 +667,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int ew = warp - 4;
         float *stg = reinterpret_cast<float *>(smem_raw + (sStg - smem_addr(smem_raw)) + ew * TC_STG_BYTES);
         int acc = 0;
-        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++acc) {
-            const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, a.n_tiles);
+        for (int t = unit; t < total_tiles && ok; t += nunits, ++acc) {
+            const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
+            const int nt = cta_nt(c.nt);
+            const bool store = nt < a.n_tiles;
             const int ab = acc & 1;
             if (!mbar_wait(acc_full + 8 * ab, (acc >> 1) & 1, a.err)) { ok = false; break; }
             tc_fence_after();
             const long long row_base = row_off_s[c.g] + c.m0;
-            for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            for (int ch = 0; ch < TC_BN / 32 && store; ++ch) {
                 if (ch * 32 >= c.rows) break;                       // warp-uniform
                 uint32_t v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * ew) << 16) + (uint32_t)(ab * TC_BN + 32 * ch), v);
@@ -527,14 +703,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             const float4 x1 = *reinterpret_cast<const float4 *>(src + 4);
                             const uint4 o = make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w),
                                                        pack_bf16(x1.x, x1.y), pack_bf16(x1.z, x1.w));
-                            *reinterpret_cast<uint4 *>(a.act + (row0 + r) * a.ld_act + c.nt * 64 + 16 * ew +
+                            *reinterpret_cast<uint4 *>(a.act + (row0 + r) * a.ld_act + nt * 64 + 16 * ew +
                                                        part * 8) = o;
                         }
                     }
                 } else if (a.out_t) {
                     // lane = weight row n0 + lane; v[j] = activation row row0 + j: each
                     // lane stores its 32 consecutive outputs (128 contiguous bytes)
-                    float *dst = a.out + (long long)(c.nt * TC_BM + 32 * ew + lane) * a.ld_out + row0;
+                    float *dst = a.out + (long long)(nt * TC_BM + 32 * ew + lane) * a.ld_out + row0;
                     if (nrow == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
                         for (int q4 = 0; q4 < 8; ++q4)
@@ -550,7 +726,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) stg[j * TC_STG_STRIDE + lane] = __uint_as_float(v[j]);
                     __syncwarp();
-                    const int n0 = c.nt * TC_BM + 32 * ew;
+                    const int n0 = nt * TC_BM + 32 * ew;
                     if (a.out_bf16 || a.ep_ret) {
 #pragma unroll
                         for (int it = 0; it < 4; ++it) {
@@ -596,7 +772,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+            if (lane == 0) {
+                if (PAIR) mbar_arrive_cluster(lead(acc_empty + 8 * ab));
+                else mbar_arrive(acc_empty + 8 * ab);
+            }
         }
         if (a.ep_ret) __threadfence_system();        // peer stores complete before the signal
     } else if (warp >= 8) {
@@ -608,12 +787,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int raw_r = gate_up ? ((l < 16) ? 16 * ew + (l & 15) : 64 + 16 * ew + (l & 15)) : r;
         int q = 0, rq = 0;
         uint4 hdr = make_uint4(0, 0, 0, 0);
-        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        for (int t = unit; t < total_tiles && ok; t += nunits) {
             for (int ks = 0; ks < ksteps && ok; ++ks) {
                 const int rs = rq % TC_RAW_STAGES;
                 if ((ks & 3) == 0 && !mbar_wait(raw_full + 8 * rs, (rq / TC_RAW_STAGES) & 1, a.err)) { ok = false; break; }
-                const int s = q % TC_A_STAGES;
-                if (q >= TC_A_STAGES && !mbar_wait(empty_a + 8 * s, ((q / TC_A_STAGES) + 1) & 1, a.err)) { ok = false; break; }
+                const int s = q % A_ST;
+                if (q >= A_ST && !mbar_wait(empty_a + 8 * s, ((q / A_ST) + 1) & 1, a.err)) { ok = false; break; }
                 const uint32_t raw_row = sRaw + rs * raw_stage_bytes + (uint32_t)(raw_r * a.raw_chunk_bytes);
                 const uint32_t a_row = sA + s * TC_A_BYTES + (uint32_t)(r * 128);
                 if (WT == T_Q4_K) {
@@ -624,7 +803,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 else dequant_q8_0_half(raw_row, ks & 3, h, a_row, r);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(full_a + 8 * s);
+                if (lane == 0) {
+                    if (PAIR) mbar_arrive_cluster(lead(full_a + 8 * s));
+                    else mbar_arrive(full_a + 8 * s);
+                }
                 ++q;
                 if ((ks & 3) == 3 || ks == ksteps - 1) {
                     __syncwarp();
@@ -633,12 +815,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
         }
+        // pair: every MMA completion signal for this CTA's A stages has landed before it leaves
+        if (PAIR && ok && warp == 8 && lane == 0)
+            for (int u = max(0, q - A_ST); u < q; ++u)
+                if (!mbar_wait(empty_a + 8 * (u % A_ST), (u / A_ST) & 1, a.err)) break;
     }
 
     __syncthreads();
+    if (PAIR) cluster_sync_all();        // neither CTA leaves while the other may still touch its memory
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 512);
+        if (PAIR) tmem_dealloc_pair(tmem_base, 512);
+        else tmem_dealloc(tmem_base, 512);
     }
 }
 
@@ -719,25 +907,61 @@ static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int WT>
+template <int WT, bool PAIR>
 static size_t tc_gemm_smem_bytes()
 {
-    return 1024 + (size_t)TC_A_STAGES * TC_A_BYTES + (size_t)TC_B_STAGES * TC_B_BYTES +
+    const int a_st = PAIR ? TC_PAIR_A_STAGES : TC_A_STAGES, b_st = PAIR ? TC_PAIR_B_STAGES : TC_B_STAGES;
+    return 1024 + (size_t)a_st * TC_A_BYTES + (size_t)b_st * (PAIR ? TC_B_BYTES / 2 : TC_B_BYTES) +
            (size_t)TcW<WT>::RAW * TC_BM * TcW<WT>::CHUNK + 16 + 4 * TC_STG_BYTES + 256;
 }
 
-template <int WT>
-static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const TcArgs &a, int grid, cudaStream_t st)
+// CTA pairs (tcgen05 cta_group::2) by default; b200q_gemm_pair_mode(0) selects
+// the one-CTA form of the same kernel.
+static bool g_tc_pair = true;
+static int g_tc_pairs_used = 0;        // CTA pairs of the last pair-mode launch
+void tc_gemm_set_pair(bool on) { g_tc_pair = on; }
+int tc_gemm_pairs_used() { return g_tc_pairs_used; }
+
+template <int WT, bool PAIR>
+static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const TcArgs &a, int num_sms, int max_ctas,
+                             cudaStream_t st)
 {
     static bool attr = false;
-    const size_t smem = tc_gemm_smem_bytes<WT>();
+    static int max_pairs = 0;
+    const size_t smem = tc_gemm_smem_bytes<WT, PAIR>();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    if (PAIR) {
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+    }
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
         if (e != cudaSuccess) return e;
+        if (PAIR) {
+            // pairs that can be resident at once (one CTA per SM; the SMs of a pair share a GPC)
+            cfg.gridDim = dim3(2 * (num_sms / 2));
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<WT, PAIR>, &cfg);
+            if (e != cudaSuccess) return e;
+            max_pairs = n;
+        }
         attr = true;
     }
-    tc_gemm_kernel<WT><<<grid, TC_THREADS, smem, st>>>(mx, mw, a);
-    return cudaGetLastError();
+    int units = PAIR ? std::min(num_sms / 2, max_pairs) : num_sms;
+    if (max_ctas > 0) units = std::min(units, PAIR ? std::max(1, max_ctas / 2) : max_ctas);
+    if (units < 1) return cudaErrorInvalidConfiguration;
+    cfg.gridDim = dim3(PAIR ? 2 * units : units);
+    if (PAIR) g_tc_pairs_used = units;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WT, PAIR>, mx, mw, a);
 }
 
 // Grouped GEMM, Q4_K / Q6_K / Q8_0 weights.
@@ -783,7 +1007,8 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
                               : wtype == T_Q6_K ? ((long long)k + 255) / 256 * 210 : ((long long)k + 31) / 32 * 34;
     if (row_bytes < min_bytes) return cudaErrorInvalidValue;
     CUtensorMap mx, mw;
-    cudaError_t e = make_map_bf16(&mx, x, x_rows, k, TC_BN);
+    const bool pair = g_tc_pair;
+    cudaError_t e = make_map_bf16(&mx, x, x_rows, k, pair ? TC_BN / 2 : TC_BN);
     if (e != cudaSuccess) return e;
     e = make_map_raw(&mw, w, (long long)(group_w ? n_weight_groups : groups) * w_rows_per_group, row_bytes, chunk,
                      elem);
@@ -806,11 +1031,14 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     a.ld_act = ld_act;
     a.ep_ret = ep_ret;
     a.err = err;
-    int grid = num_sms;
-    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-    if (wtype == T_Q4_K) return tc_launch<T_Q4_K>(mx, mw, a, grid, st);
-    if (wtype == T_Q6_K) return tc_launch<T_Q6_K>(mx, mw, a, grid, st);
-    return tc_launch<T_Q8_0>(mx, mw, a, grid, st);
+    if (pair) {
+        if (wtype == T_Q4_K) return tc_launch<T_Q4_K, true>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q6_K) return tc_launch<T_Q6_K, true>(mx, mw, a, num_sms, max_ctas, st);
+        return tc_launch<T_Q8_0, true>(mx, mw, a, num_sms, max_ctas, st);
+    }
+    if (wtype == T_Q4_K) return tc_launch<T_Q4_K, false>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q6_K) return tc_launch<T_Q6_K, false>(mx, mw, a, num_sms, max_ctas, st);
+    return tc_launch<T_Q8_0, false>(mx, mw, a, num_sms, max_ctas, st);
 }
 
 } // namespace b200q
