@@ -34,6 +34,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 E, D, F, K_TOP, T_TOTAL = 64, 4096, 1408, 8, 16384
+T_HEADLINE = T_TOTAL          # the configured token count (--tokens may change T_TOTAL)
 F_PAD = 1536
 Q4K_BLOCK = 144
 WORKLOAD = 'moe_q4k_d4096_e64_f1408_top8_t16384_zipf1.1'
@@ -482,7 +483,8 @@ def decode_probe(torch, hbm_peak, prompt_len=2048, new_tokens=128):
 
 def moe_q6k_probe(torch, synth):
     """Configuration 3: Q6_K MoE, D=2048, E=16, F=1024, top-2, T = 1, 64, 4096
-    (two layer copies, 165 MB, cycled in a CUDA graph)."""
+    (four layer copies, 330 MB of expert weights = more than twice the L2,
+    cycled in a CUDA graph)."""
     from localai_b200.moe import QuantMoE
     E3, D3, F3, k3 = 16, 2048, 1024, 2
     rng = np.random.default_rng(3)
@@ -490,7 +492,7 @@ def moe_q6k_probe(torch, synth):
     gu = b''.join(synth.q6_k(rng, 2 * F3, D3) for _ in range(E3))
     dn = b''.join(synth.q6_k(rng, D3, F3) for _ in range(E3))
     wr3 = torch.from_numpy(rng.normal(0, 0.02, size=(E3, D3)).astype(np.float32)).cuda()
-    layers = [QuantMoE(wr3, dev(gu), dev(dn), d_model=D3, d_ff=F3, top_k=k3, ggml_type=14) for _ in range(2)]
+    layers = [QuantMoE(wr3, dev(gu), dev(dn), d_model=D3, d_ff=F3, top_k=k3, ggml_type=14) for _ in range(4)]
     res = {}
     for T in (1, 64, 4096):
         h3 = torch.randn(T, D3, device='cuda')
@@ -654,11 +656,14 @@ def main():
         gemm_ms = g0.elapsed_time(g1) / gemm_reps
         flops = 2.0 * slots * (2 * F) * D
         achieved = flops / (gemm_ms * 1e-3) / 1e12
+        # DRAM bytes of one full-size gate/up launch, from the committed ncu
+        # capture (only meaningful for the full token count)
         traffic = None
-        if PROFILE_TRAFFIC.exists():
+        if PROFILE_TRAFFIC.exists() and T_TOTAL == T_HEADLINE:
             for line in PROFILE_TRAFFIC.read_text().splitlines():
                 if line.startswith('traffic_bytes_per_launch:'):
                     traffic = float(line.split(':', 1)[1].split()[0])
+        algo_bytes = gate_up.numel() + slots * D * 2 + slots * F * 2
         # the down GEMM alone as well (same kernel, plain bf16 epilogue, K = 1408)
         out_dn = torch.empty((slots, D), dtype=torch.bfloat16, device=dev)
         down_call = lambda: ops.gemm_q4k(act, down, offsets, k=F, n_feat=D, w_rows_per_group=D, out=out_dn,
@@ -674,7 +679,7 @@ def main():
         down_flops = 2.0 * slots * D * F
         roof = {'kernel': 'tc_gemm_q4k_kernel (gate/up, fused SiLU*up)', 'bound': 'tensor',
                 'achieved': round(achieved, 1), 'peak': tc_burst, 'unit': 'TFLOP/s',
-                'frac': round(achieved / tc_burst, 3), 'traffic': traffic,
+                'frac': round(achieved / tc_burst, 3), 'traffic': traffic, 'algorithmic_bytes': int(algo_bytes),
                 'peak_source': f'{peak_src} bf16 (burst; kernel timed alone)',
                 'flops_per_launch': flops, 'ms_per_launch': round(gemm_ms, 4),
                 'down_gemm': {'ms_per_launch': round(down_ms, 4), 'flops_per_launch': down_flops,

@@ -172,6 +172,11 @@ int b200q_gemv_grouped_dev(int ggml_type, const void *w, long long w_group_strid
  * h has h_rows rows: a row whose token is outside [0, h_rows) is left
  * unwritten and the device error word set (B200Q_EINDEX). */
 int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *token_of, int S, int D, float *out, void *stream);
+/* out[s, :] = h_bf16[token_of[s], :] for s < S (bf16 rows of D values,
+ * D % 8 == 0, both 16-byte aligned); same index contract as
+ * b200q_moe_gather_f32_dev. */
+int b200q_moe_gather_bf16_dev(const void *h_bf16, int h_rows, const int *token_of, int S, int D, void *out,
+                              void *stream);
 /* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
  * weights.  w_row_bytes is the byte distance between weight rows (0: packed
  * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed
@@ -202,6 +207,12 @@ size_t b200q_moe_route_workspace_bytes(int T, int E, int D);
 int b200q_moe_route_dev(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E, int D,
                         int k, int renormalize, float *logits, int *ids, float *w, void *workspace,
                         size_t workspace_bytes, void *stream);
+/* b200q_moe_route_dev that also writes h_bf16 [T, D] = bf16(h) (8-byte
+ * aligned), converted while the router stages h (the rows the tensor-core
+ * experts read, gathered by b200q_moe_gather_bf16_dev). */
+int b200q_moe_route_bf16_dev(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E,
+                             int D, int k, int renormalize, float *logits, int *ids, float *w, void *workspace,
+                             size_t workspace_bytes, void *h_bf16, void *stream);
 /* Scratch rows needed by b200q_moe_dispatch_dev: block_counts and base are
  * int32 [b200q_moe_num_blocks(T) * E]. */
 int b200q_moe_num_blocks(int T);

@@ -52,6 +52,7 @@ SIGNATURES = {
     'b200q_gemv_grouped_max_tokens': (_i, [_i, _i]),
     'b200q_gemv_grouped_dev': (_i, [_i, _vp, _ll, _ll, _i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
     'b200q_moe_gather_f32_dev': (_i, [_vp, _i, _vp, _i, _i, _vp, _vp]),
+    'b200q_moe_gather_bf16_dev': (_i, [_vp, _i, _vp, _i, _i, _vp, _vp]),
     'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
                             _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
@@ -59,6 +60,7 @@ SIGNATURES = {
     'b200q_moe_num_blocks': (_i, [_i]),
     'b200q_moe_route_workspace_bytes': (_sz, [_i, _i, _i]),
     'b200q_moe_route_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
+    'b200q_moe_route_bf16_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     'b200q_moe_dispatch_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_dispatch_noalloc_dev': (_i, [_vp, _vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     'b200q_moe_combine_dev': (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),

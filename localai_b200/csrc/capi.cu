@@ -33,7 +33,7 @@ int moe_num_blocks(int T);
 size_t moe_route_workspace_bytes(int T, int E, int D, int num_sms);
 cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E,
                              int D, int k, int renorm, float *logits, int *ids, float *wts, float *ws,
-                             size_t ws_bytes, int num_sms, cudaStream_t st);
+                             size_t ws_bytes, int num_sms, cudaStream_t st, __nv_bfloat16 *hb = nullptr);
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
@@ -95,6 +95,8 @@ cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int 
                           unsigned long long *key, int num_sms, cudaStream_t st);
 cudaError_t launch_moe_gather_f32(const float *h, int T, const int *token_of, int S, int D, float *out, int *err,
                                   cudaStream_t st);
+cudaError_t launch_moe_gather_bf16(const __nv_bfloat16 *h, int T, const int *token_of, int S, int D,
+                                   __nv_bfloat16 *out, int *err, cudaStream_t st);
 cudaError_t launch_zaya_router_prep(const float *x, const float *prev, const float *w_eda, const float *norm_w, int T,
                                     int R, float eps, float *state, float *out, cudaStream_t st);
 cudaError_t launch_gelu(float *x, long long n, int num_sms, cudaStream_t st);
@@ -586,6 +588,19 @@ B200Q_API int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *to
                        "gather_f32");
 }
 
+B200Q_API int b200q_moe_gather_bf16_dev(const void *h_bf16, int h_rows, const int *token_of, int S, int D, void *out,
+                                        void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h_bf16 || !token_of || !out) return set_status(B200Q_EINVAL, "gather_bf16: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_moe_gather_bf16(static_cast<const __nv_bfloat16 *>(h_bf16), h_rows, token_of, S, D,
+                                              static_cast<__nv_bfloat16 *>(out), di->err, (cudaStream_t)stream),
+                       "gather_bf16");
+}
+
 B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,
                                    int D, void *stream)
 {
@@ -626,6 +641,21 @@ B200Q_API int b200q_moe_route_dev(const float *h, const float *wr, const float *
     return cuda_status(launch_moe_route(h, wr, bias, sel_bias, T, E, D, k, renormalize, logits, ids, w,
                                         static_cast<float *>(workspace), workspace_bytes, di->sms,
                                         (cudaStream_t)stream),
+                       "route");
+}
+
+B200Q_API int b200q_moe_route_bf16_dev(const float *h, const float *wr, const float *bias, const float *sel_bias,
+                                       int T, int E, int D, int k, int renormalize, float *logits, int *ids, float *w,
+                                       void *workspace, size_t workspace_bytes, void *h_bf16, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h || !wr || !logits || !ids || !w || !h_bf16) return set_status(B200Q_EINVAL, "route: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += 2;
+    return cuda_status(launch_moe_route(h, wr, bias, sel_bias, T, E, D, k, renormalize, logits, ids, w,
+                                        static_cast<float *>(workspace), workspace_bytes, di->sms,
+                                        (cudaStream_t)stream, static_cast<__nv_bfloat16 *>(h_bf16)),
                        "route");
 }
 

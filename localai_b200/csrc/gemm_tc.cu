@@ -439,9 +439,12 @@ __device__ __forceinline__ TileCoord tile_coord(int t, const int *tile_pref, con
     c.g = lo;
     const int local = t - tile_pref[lo];
     const int mrows = row_off[lo + 1] - row_off[lo];
-    const int mt = (mrows + TC_BN - 1) / TC_BN;
-    c.nt = local / mt;
-    c.m0 = (local % mt) * TC_BN;
+    // activation-row-tile major: the CTAs (pairs) running at the same time
+    // share a few activation row tiles and one expert's weight tiles, so both
+    // stay in L2 (weight-tile major made a large expert's rows, e.g. 140 MB,
+    // stream from DRAM once per weight tile)
+    c.m0 = (local / n_tiles) * TC_BN;
+    c.nt = local % n_tiles;
     c.rows = min(TC_BN, mrows - c.m0);
     return c;
 }

@@ -36,9 +36,12 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src
 }
 
 // Double-buffered (cp.async) tiles: [buf][h | w][64 rows][RT_BK + RT_PAD].
+// With ``hb`` the CTAs of the first expert tile also write bf16(h) for their
+// token and K range from the staged tile (the routed rows the tensor-core
+// experts gather, converted while h passes through shared memory anyway).
 __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict__ h, const float *__restrict__ wr,
                                                          const float *__restrict__ bias, float *__restrict__ out,
-                                                         int T, int E, int D, int kchunk)
+                                                         int T, int E, int D, int kchunk, __nv_bfloat16 *__restrict__ hb)
 {
     extern __shared__ __align__(16) float rsm[];
     const int tid = threadIdx.x;
@@ -73,6 +76,18 @@ __global__ void __launch_bounds__(256) moe_router_kernel(const float *__restrict
         }
         __syncthreads();
         const float *hs = rsm + buf * 2 * RT_TILE, *ws = hs + RT_TILE;
+        if (hb && blockIdx.y == 0) {
+            for (int i = tid; i < RT_TOK * RT_BK / 4; i += 256) {
+                const int r = i / (RT_BK / 4), c = (i % (RT_BK / 4)) * 4;
+                const int t = t0 + r, kk = k0 + c;
+                if (t < T && kk < kend) {
+                    const float4 v = *reinterpret_cast<const float4 *>(hs + r * (RT_BK + RT_PAD) + c);
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+                    *reinterpret_cast<uint2 *>(hb + (long long)t * D + kk) =
+                        make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+                }
+            }
+        }
         const int cb = slice * (RT_BK / 4);
 #pragma unroll 2
         for (int c = cb; c < cb + RT_BK / 4; c += 4) {
@@ -334,6 +349,41 @@ cudaError_t launch_moe_gather_f32(const float *h, int T, const int *token_of, in
     return cudaGetLastError();
 }
 
+// out[s, :] = h[token_of[s], :] for bf16 rows (D % 8 == 0, 16-byte aligned);
+// one warp per row, four 16-byte loads in flight per lane.
+__global__ void moe_gather_bf16_kernel(const __nv_bfloat16 *__restrict__ h, int T, const int *__restrict__ token_of,
+                                       long long S, int D, __nv_bfloat16 *__restrict__ out, int *err)
+{
+    const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= S) return;
+    const int t = gather_token(token_of, row, nullptr, T, err);
+    if (t < 0) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(h + (long long)t * D);
+    uint4 *dst = reinterpret_cast<uint4 *>(out + row * D);
+    const int n = D / 8;
+    int c = lane;
+    for (; c + 96 < n; c += 128) {
+        const uint4 v0 = __ldg(src + c), v1 = __ldg(src + c + 32), v2 = __ldg(src + c + 64), v3 = __ldg(src + c + 96);
+        dst[c] = v0;
+        dst[c + 32] = v1;
+        dst[c + 64] = v2;
+        dst[c + 96] = v3;
+    }
+    for (; c < n; c += 32) dst[c] = __ldg(src + c);
+}
+
+cudaError_t launch_moe_gather_bf16(const __nv_bfloat16 *h, int T, const int *token_of, int S, int D,
+                                   __nv_bfloat16 *out, int *err, cudaStream_t st)
+{
+    if (S < 1 || T < 1 || D < 8 || D % 8 || (reinterpret_cast<uintptr_t>(h) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    moe_gather_bf16_kernel<<<(unsigned)(((long long)S * 32 + 255) / 256), 256, 0, st>>>(h, T, token_of, S, D, out,
+                                                                                        err);
+    return cudaGetLastError();
+}
+
 // xperm[slot, :] = bf16(h[token_of[slot], :]) for slots below offsets[E]; one warp per slot row.
 __global__ void moe_gather_kernel(const float *__restrict__ h, int T, const int *__restrict__ token_of, long long S,
                                   const int *__restrict__ n_valid, int D, __nv_bfloat16 *__restrict__ xperm, int *err)
@@ -390,7 +440,7 @@ __global__ void moe_combine_kernel(const RowT *__restrict__ out, long long n_row
 static size_t router_smem() { return (size_t)4 * RT_TILE * sizeof(float); }
 
 static cudaError_t router_launch(const float *h, const float *wr, const float *bias, float *out, int T, int E, int D,
-                                 int nsplit, cudaStream_t st)
+                                 int nsplit, cudaStream_t st, __nv_bfloat16 *hb = nullptr)
 {
     static bool attr = false;
     if (!attr) {
@@ -401,7 +451,7 @@ static cudaError_t router_launch(const float *h, const float *wr, const float *b
     }
     const int kchunk = ((D + nsplit - 1) / nsplit + RT_BK - 1) / RT_BK * RT_BK;
     dim3 grid((T + RT_TOK - 1) / RT_TOK, (E + RT_EXP - 1) / RT_EXP, nsplit);
-    moe_router_kernel<<<grid, 256, router_smem(), st>>>(h, wr, bias, out, T, E, D, kchunk);
+    moe_router_kernel<<<grid, 256, router_smem(), st>>>(h, wr, bias, out, T, E, D, kchunk, hb);
     return cudaGetLastError();
 }
 
@@ -457,20 +507,21 @@ size_t moe_route_workspace_bytes(int T, int E, int D, int num_sms)
 // split across CTAs.
 cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias, const float *sel_bias, int T, int E,
                              int D, int k, int renorm, float *logits, int *ids, float *wts, float *ws,
-                             size_t ws_bytes, int num_sms, cudaStream_t st)
+                             size_t ws_bytes, int num_sms, cudaStream_t st, __nv_bfloat16 *hb)
 {
     if (!router_args_ok(h, wr, T, E, D) || E > 256 || k < 1 || k > 32 || k > E) return cudaErrorInvalidValue;
+    if (hb && (reinterpret_cast<uintptr_t>(hb) & 7)) return cudaErrorInvalidValue;
     int s = moe_route_splits(T, E, D, num_sms);
     if (s > 1 && (!ws || ws_bytes < (size_t)s * T * E * sizeof(float))) s = 1;
     const int threads = 256, grid = (int)(((long long)T * 32 + threads - 1) / threads);
     cudaError_t e;
     if (s == 1) {
-        e = router_launch(h, wr, bias, logits, T, E, D, 1, st);
+        e = router_launch(h, wr, bias, logits, T, E, D, 1, st, hb);
         if (e != cudaSuccess) return e;
         topk_dispatch(E, grid, threads, st, (const float *)logits, sel_bias, T, E, k, renorm, ids, wts, 0,
                       (const float *)nullptr, (float *)nullptr);
     } else {
-        e = router_launch(h, wr, nullptr, ws, T, E, D, s, st);
+        e = router_launch(h, wr, nullptr, ws, T, E, D, s, st, hb);
         if (e != cudaSuccess) return e;
         topk_dispatch(E, grid, threads, st, (const float *)ws, sel_bias, T, E, k, renorm, ids, wts, s, bias, logits);
     }

@@ -4,12 +4,13 @@ The reference block (engine/zaya.py:274-307, ``ZayaModel._moe``) routes one
 token at a time to one expert and runs two GEMVs on it.  ``QuantMoE`` runs the
 same block batched over T tokens and generalised to top-k:
 
-    logits = h @ Wr^T (+ router bias)             b200q_moe_router_dev
-    p = softmax(logits); top-k of p (+ sel bias)  b200q_moe_topk_dev
-    stable counting sort of (token, j) by expert  b200q_moe_dispatch_dev
-    act = SiLU(gate x) * (up x)  per expert       b200q_gemm_q4k_dev (gate/up mode, tcgen05)
-    out = w_slot * (down act)    per expert       b200q_gemm_q4k_dev (plain mode, tcgen05; bf16 rows)
-    y[t] = sum_j out[slot(t, j)]                  b200q_moe_combine_dev
+    logits = h @ Wr^T (+ router bias), hb = bf16(h)   b200q_moe_route_bf16_dev
+    p = softmax(logits); top-k of p (+ sel bias)      (same call)
+    stable counting sort of (token, j) by expert      b200q_moe_dispatch_dev
+    xperm[slot] = hb[token_of[slot]]                  b200q_moe_gather_bf16_dev
+    act = SiLU(gate x) * (up x)  per expert           b200q_gemm_dev (gate/up mode, tcgen05)
+    out = w_slot * (down act)    per expert           b200q_gemm_dev (plain mode, tcgen05; bf16 rows)
+    y[t] = sum_j out[slot(t, j)]                      b200q_moe_combine_dev
 
 Expert weights are raw GGUF Q4_K, Q6_K or Q8_0 tensors in ZAYA's layout:
 ``gate_up`` [E, 2F, D] (gate rows first, then up rows, as
@@ -117,8 +118,9 @@ class QuantMoE:
                                self.lib.b200q_gemv_grouped_max_tokens(ggml_type, self.F_pad))
 
     # -- stages ---------------------------------------------------------------
-    def route(self, h: torch.Tensor):
-        """Router logits, top-k expert ids and routing weights."""
+    def route(self, h: torch.Tensor, hb: torch.Tensor | None = None):
+        """Router logits, top-k expert ids and routing weights; with ``hb``
+        (bf16 [T, D]) also hb = bf16(h)."""
         T = h.shape[0]
         dev = h.device
         logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
@@ -126,12 +128,17 @@ class QuantMoE:
         w = torch.empty((T, self.k), dtype=torch.float32, device=dev)
         nws = self.lib.b200q_moe_route_workspace_bytes(T, self.E, self.D)
         ws = torch.empty(nws // 4, dtype=torch.float32, device=dev) if nws else None
-        _lib.check(self.lib.b200q_moe_route_dev(
-            h.data_ptr(), self.router_w.data_ptr(),
-            None if self.router_bias is None else self.router_bias.data_ptr(),
-            None if self.sel_bias is None else self.sel_bias.data_ptr(),
-            T, self.E, self.D, self.k, self.renorm, logits.data_ptr(), ids.data_ptr(), w.data_ptr(),
-            None if ws is None else ws.data_ptr(), nws, _stream()))
+        args = (h.data_ptr(), self.router_w.data_ptr(),
+                None if self.router_bias is None else self.router_bias.data_ptr(),
+                None if self.sel_bias is None else self.sel_bias.data_ptr(),
+                T, self.E, self.D, self.k, self.renorm, logits.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                None if ws is None else ws.data_ptr(), nws)
+        if hb is None:
+            _lib.check(self.lib.b200q_moe_route_dev(*args, _stream()))
+        else:
+            if hb.dtype != torch.bfloat16 or hb.shape != (T, self.D) or not hb.is_contiguous():
+                raise ValueError('hb must be a contiguous bf16 [T, d_model] tensor')
+            _lib.check(self.lib.b200q_moe_route_bf16_dev(*args, hb.data_ptr(), _stream()))
         return logits, ids, w
 
     def topk(self, logits: torch.Tensor):
@@ -164,6 +171,14 @@ class QuantMoE:
             scratch[0].data_ptr(), scratch[1].data_ptr(), offsets.data_ptr(), slot_of.data_ptr(),
             token_of.data_ptr(), slot_w.data_ptr(), None if xperm is None else xperm.data_ptr(), _stream()))
         return offsets, slot_of, token_of, slot_w, xperm
+
+    def gather_bf16(self, hb: torch.Tensor, token_of: torch.Tensor) -> torch.Tensor:
+        """xperm[s] = hb[token_of[s]] (bf16 rows grouped by expert)."""
+        S = token_of.numel()
+        xperm = torch.empty((S, self.D), dtype=torch.bfloat16, device=hb.device)
+        _lib.check(self.lib.b200q_moe_gather_bf16_dev(hb.data_ptr(), hb.shape[0], token_of.data_ptr(), S, self.D,
+                                                      xperm.data_ptr(), _stream()))
+        return xperm
 
     def experts(self, xperm: torch.Tensor, offsets: torch.Tensor, slot_w: torch.Tensor | None, *,
                 group_w: torch.Tensor | None = None, out_dtype=torch.bfloat16, max_ctas: int = 0):
@@ -230,14 +245,17 @@ class QuantMoE:
         if h.dtype != torch.float32 or not h.is_cuda or h.dim() != 2 or h.shape[1] != self.D:
             raise ValueError('h must be a CUDA f32 [T, d_model] tensor')
         h = h.contiguous()
-        _, ids, w = self.route(h)
-        if h.shape[0] * self.k <= self.small_slots:
+        T = h.shape[0]
+        if T * self.k <= self.small_slots:
+            _, ids, w = self.route(h)
             offsets, slot_of, token_of, slot_w, _ = self.dispatch(h, ids, w, gather=False)
             out = self.experts_small(h, offsets, token_of)
-            return self.combine(out, slot_of, h.shape[0], slot_w)
-        offsets, slot_of, _, slot_w, xperm = self.dispatch(h, ids, w)
-        out = self.experts(xperm, offsets, slot_w)
-        return self.combine(out, slot_of, h.shape[0])
+            return self.combine(out, slot_of, T, slot_w)
+        hb = torch.empty((T, self.D), dtype=torch.bfloat16, device=h.device)
+        _, ids, w = self.route(h, hb)
+        offsets, slot_of, token_of, slot_w, _ = self.dispatch(h, ids, w, gather=False)
+        out = self.experts(self.gather_bf16(hb, token_of), offsets, slot_w)
+        return self.combine(out, slot_of, T)
 
     def forward_host(self, h_host: torch.Tensor, y_host: torch.Tensor | None = None, chunks: int = 4,
                      device=None) -> torch.Tensor:
