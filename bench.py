@@ -64,9 +64,9 @@ def set_tokens(n):
     WORKLOAD = f'moe_q4k_d4096_e64_f1408_top8_t{n}_zipf1.1'
 
 
-def hidden_states(torch, device, t0, t1):
+def hidden_states(torch, device, t0, t1, seed=1001):
     g = torch.Generator(device=device)
-    g.manual_seed(1001)
+    g.manual_seed(seed)
     h = torch.randn((T_TOTAL, D), generator=g, device=device, dtype=torch.float32)
     return h[t0:t1].contiguous()
 
@@ -552,12 +552,13 @@ def main():
     t0, t1 = rank * T_loc, (rank + 1) * T_loc
     h = hidden_states(torch, dev, t0, t1)
 
-    # expert placement: LPT on the routing loads of the full token set (setup, untimed)
+    # expert placement: LPT on the routing loads of a calibration batch (same
+    # distribution, different seed from the timed tokens; setup, untimed)
     if world > 1:
         probe = QuantMoE.__new__(QuantMoE)
         probe.E, probe.D, probe.k, probe.renorm, probe.sel_bias = E, D, K_TOP, 1, None
         probe.router_w, probe.router_bias, probe.lib = wr, bias, lib
-        _, ids_all, _ = probe.route(hidden_states(torch, dev, 0, T_TOTAL))
+        _, ids_all, _ = probe.route(hidden_states(torch, dev, 0, T_TOTAL, seed=4242))
         loads = torch.bincount(ids_all.reshape(-1).long(), minlength=E).cpu().numpy()
         owner, local = lpt_placement(loads, world)
         mine = [int(e) for e in np.nonzero(owner == rank)[0]]

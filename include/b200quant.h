@@ -284,7 +284,10 @@ long long b200q_launch_count(void);
 /* ---- Expert-parallel exchange over NVLink peer memory (no reference
  * counterpart: the reference runs the MoE block in one CPU process).  One
  * context per rank (one process per GPU); every rank makes the same calls in
- * the same order with the same epoch (1, 2, ... per layer call).
+ * the same order with the same epoch (1, 2, ... per layer call), or with
+ * epoch 0 in every call: the count exchange then advances a device-side
+ * counter that the later calls of the layer call read (no per-call host
+ * argument, so a layer call can be captured in a CUDA graph and replayed).
  *   b200q_ep_create        allocate this rank's exchange region (counts inbox,
  *                          flags, receive rows bf16 [max_recv_rows, d_model],
  *                          return rows bf16 [max_send_rows, d_model]);
@@ -322,6 +325,10 @@ const int *b200q_ep_group_offsets(void *ep);
 int b200q_ep_exchange_counts_dev(void *ep, const int *offsets, unsigned int epoch, void *stream);
 int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int *token_of, const int *offsets, int slots,
                            unsigned int epoch, void *stream);
+/* b200q_ep_send_rows_dev from bf16 rows (h_bf16 [T, D], 16-byte aligned, e.g.
+ * the copy b200q_moe_route_bf16_dev writes): the rows are copied as they are. */
+int b200q_ep_send_rows_bf16_dev(void *ep, const void *h_bf16, int T, const int *token_of, const int *offsets,
+                                int slots, unsigned int epoch, void *stream);
 int b200q_ep_experts_dev(void *ep, int ggml_type, const void *gate_up, long long gate_up_row_bytes,
                          const void *down, long long down_row_bytes, int d_ff, void *act, unsigned int epoch,
                          int max_ctas, void *stream);

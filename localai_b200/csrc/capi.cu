@@ -67,7 +67,7 @@ long long ep_cap_send(void *ctx);
 int ep_local_experts(void *ctx);
 int ep_d_model(void *ctx);
 cudaError_t launch_ep_counts(void *ctx, const int *offsets, uint32_t epoch, int *err, cudaStream_t st);
-cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const int *offsets, int S, int T,
+cudaError_t launch_ep_send(void *ctx, const void *h, bool h_bf16, const int *token_of, const int *offsets, int S, int T,
                            uint32_t epoch, int *err, int num_sms, cudaStream_t st);
 cudaError_t launch_ep_wait(void *ctx, int which, uint32_t epoch, int *err, cudaStream_t st);
 cudaError_t launch_ep_signal(void *ctx, uint32_t epoch, cudaStream_t st);
@@ -809,7 +809,20 @@ B200Q_API int b200q_ep_send_rows_dev(void *ep, const float *h, int T, const int 
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_ep_send(ep, h, token_of, offsets, slots, T, epoch, di->err, di->sms,
+    return cuda_status(launch_ep_send(ep, h, false, token_of, offsets, slots, T, epoch, di->err, di->sms,
+                                      (cudaStream_t)stream),
+                       "ep_send_rows");
+}
+
+B200Q_API int b200q_ep_send_rows_bf16_dev(void *ep, const void *h_bf16, int T, const int *token_of,
+                                          const int *offsets, int slots, unsigned int epoch, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !h_bf16 || !token_of || !offsets) return set_status(B200Q_EINVAL, "ep_send_rows: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_ep_send(ep, h_bf16, true, token_of, offsets, slots, T, epoch, di->err, di->sms,
                                       (cudaStream_t)stream),
                        "ep_send_rows");
 }

@@ -15,6 +15,11 @@
 // All waits are bounded (g_ep_wait_ns); a wait that runs out sets the device
 // error word and the kernel returns, so the host sees an error instead of a
 // hang.
+//
+// Epochs: an epoch argument of 0 means "the device-side counter": the count
+// exchange advances it (ep->epoch + 1) and the later kernels of the call read
+// it, so a whole layer call can be captured once in a CUDA graph and
+// replayed.  A nonzero argument is used as given (and stored as the counter).
 #include "common.cuh"
 #include "ep.cuh"
 
@@ -61,6 +66,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
     const int tid = threadIdx.x;
     const int G = ep->G, me = ep->me, El = ep->E_loc, E = G * El;
     EpShared *mine = ep->peer_shared[me];
+    epoch = epoch ? epoch : ep->epoch + 1;           // every thread reads the counter before it is advanced
     for (int v = tid; v < E; v += blockDim.x) {
         const int c = offsets[v + 1] - offsets[v];
         for (int d = 0; d < G; ++d) ep->peer_shared[d]->inbox[me][v] = c;
@@ -72,6 +78,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
     }
     __threadfence_system();
     __syncthreads();
+    if (tid == 0) ep->epoch = epoch;
     if (tid < G) st_release_sys(&ep->peer_shared[tid]->cnt_flag[me], epoch);
     if (tid < G && !ep_wait_flag(&mine->cnt_flag[tid], epoch, err, limit_ns)) ok_s = 0;
     __syncthreads();
@@ -130,7 +137,10 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
     if (tid == 0) ep->blocked = blocked_s;
 }
 
-__global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__restrict__ h,
+// Source rows f32 (converted to bf16 on the way) or already bf16 (the
+// router's copy of h: a plain 16-byte copy, four loads in flight per lane).
+template <typename TIn>
+__global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const TIn *__restrict__ h,
                                                       const int *__restrict__ token_of,
                                                       const int *__restrict__ offsets, int S, int T, uint32_t epoch,
                                                       int *err)
@@ -147,7 +157,12 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__
     __syncthreads();
     // slots at or past offsets[E] belong to pairs with a bad expert id: not sent
     const int n_valid = min(S, off_s[E]);
-    for (int i = blockIdx.x * 8 + warp; i < n_valid; i += gridDim.x * 8) {
+    // start with the rows for rank me + 1 (then me + 2, ...; my own last), so
+    // that the ranks' first stores go to different destinations instead of
+    // all of them filling rank 0's receive buffer first
+    const int start = n_valid ? off_s[((me + 1) % G) * El] % n_valid : 0;
+    for (int j = blockIdx.x * 8 + warp; j < n_valid; j += gridDim.x * 8) {
+        const int i = j + start < n_valid ? j + start : j + start - n_valid;
         int lo = 0, hi = E;                          // largest v with off_s[v] <= i
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -160,8 +175,24 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__
             if (lane == 0) atomicExch(err, ERR_BAD_INDEX);
             continue;
         }
-        const float *src = h + (long long)t * D;
         __nv_bfloat16 *dst = peer_s[d] + (long long)(dst_s[lo] + (i - off_s[lo])) * D;
+        if constexpr (sizeof(TIn) == 2) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(h + (long long)t * D);
+            uint4 *d16 = reinterpret_cast<uint4 *>(dst);
+            const int n = D / 8;
+            int c = lane;
+            for (; c + 96 < n; c += 128) {
+                const uint4 v0 = __ldg(src + c), v1 = __ldg(src + c + 32), v2 = __ldg(src + c + 64),
+                            v3 = __ldg(src + c + 96);
+                d16[c] = v0;
+                d16[c + 32] = v1;
+                d16[c + 64] = v2;
+                d16[c + 96] = v3;
+            }
+            for (; c < n; c += 32) d16[c] = __ldg(src + c);
+            continue;
+        }
+        const float *src = reinterpret_cast<const float *>(h) + (long long)t * D;
         for (int c = lane * 8; c < D; c += 256) {
             const float4 a = __ldg(reinterpret_cast<const float4 *>(src + c));
             const float4 b = __ldg(reinterpret_cast<const float4 *>(src + c + 4));
@@ -181,7 +212,8 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpDev *ep, const float *__
         const unsigned old = atomicAdd(&ep->done, 1u);
         if (old == gridDim.x - 1) {
             __threadfence_system();
-            for (int d = 0; d < G; ++d) st_release_sys(&ep->peer_shared[d]->row_flag[me], epoch);
+            const uint32_t e = epoch ? epoch : ep->epoch;
+            for (int d = 0; d < G; ++d) st_release_sys(&ep->peer_shared[d]->row_flag[me], e);
         }
     }
 }
@@ -191,6 +223,7 @@ __global__ void ep_wait_kernel(EpDev *ep, int which, uint32_t epoch, int *err, u
 {
     const int lane = threadIdx.x;
     EpShared *mine = ep->peer_shared[ep->me];
+    epoch = epoch ? epoch : ep->epoch;
     if (lane < ep->G) ep_wait_flag(which == 1 ? &mine->row_flag[lane] : &mine->ret_flag[lane], epoch, err, limit_ns);
 }
 
@@ -198,6 +231,7 @@ __global__ void ep_signal_kernel(EpDev *ep, uint32_t epoch)
 {
     __threadfence_system();
     const int lane = threadIdx.x;
+    epoch = epoch ? epoch : ep->epoch;
     if (lane < ep->G) st_release_sys(&ep->peer_shared[lane]->ret_flag[ep->me], epoch);
 }
 
@@ -325,8 +359,8 @@ cudaError_t launch_ep_counts(void *ctx, const int *offsets, uint32_t epoch, int 
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const int *offsets, int S, int T,
-                           uint32_t epoch, int *err, int num_sms, cudaStream_t st)
+cudaError_t launch_ep_send(void *ctx, const void *h, bool h_bf16, const int *token_of, const int *offsets, int S,
+                           int T, uint32_t epoch, int *err, int num_sms, cudaStream_t st)
 {
     EpHost *p = static_cast<EpHost *>(ctx);
     if (!p->opened || S < 0 || (long long)S > p->cap_send || (reinterpret_cast<uintptr_t>(h) & 15))
@@ -334,7 +368,12 @@ cudaError_t launch_ep_send(void *ctx, const float *h, const int *token_of, const
     int grid = (S + 7) / 8;
     if (grid > num_sms * 8) grid = num_sms * 8;
     if (grid < 1) grid = 1;
-    ep_send_kernel<<<grid, 256, 0, st>>>(p->dev, h, token_of, offsets, S, T, epoch, err);
+    if (h_bf16)
+        ep_send_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p->dev, static_cast<const __nv_bfloat16 *>(h), token_of,
+                                                             offsets, S, T, epoch, err);
+    else
+        ep_send_kernel<float><<<grid, 256, 0, st>>>(p->dev, static_cast<const float *>(h), token_of, offsets, S, T,
+                                                     epoch, err);
     return cudaGetLastError();
 }
 

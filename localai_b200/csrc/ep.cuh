@@ -33,6 +33,7 @@ struct EpDev {
     int G, me, E_loc, D;
     long long cap_recv, cap_send;
     unsigned int done;                        // CTAs of the send kernel that finished
+    uint32_t epoch;                           // epoch of the current call (device-side counter)
     int blocked;                              // bit d: rank d's receive buffer would overflow
     // Receive layout (expert-major, source-minor), rebuilt by every count exchange:
     int grp_off[EP_MAX_EXPERTS + 1];          // [E_loc + 1] rows of local expert e start here

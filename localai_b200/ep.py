@@ -30,7 +30,10 @@ Two transports carry steps 3-5:
   kernel gathers each routed row as bf16 straight into its owner's receive
   buffer (expert-major, so each local expert is one GEMM group), and the down
   GEMM's epilogue stores each output row straight into its source rank's
-  return buffer.  Needs peer access between all ranks' GPUs.
+  return buffer.  Needs peer access between all ranks' GPUs.  The call's
+  epoch lives on the device, so with ``graph=True`` (default) a layer call is
+  captured once per token count in a CUDA graph and replayed (no per-call
+  host work between the kernels).
 """
 from __future__ import annotations
 
@@ -80,7 +83,7 @@ class EPMoE:
     """
 
     def __init__(self, layer: QuantMoE, owner, local, group=None, *, transport: str = 'nccl',
-                 max_tokens: int | None = None):
+                 max_tokens: int | None = None, graph: bool = True):
         self.layer = layer
         self.group = group
         self.G = dist.get_world_size(group)
@@ -98,6 +101,8 @@ class EPMoE:
             raise ValueError("transport must be 'nccl' or 'p2p'")
         self.transport = transport
         self.ctx = None
+        self.use_graph = graph
+        self._graphs = {}
         if transport == 'p2p':
             if max_tokens is None or max_tokens < 1:
                 raise ValueError('the p2p transport needs max_tokens (tokens per rank per call)')
@@ -122,12 +127,12 @@ class EPMoE:
         _lib.check(lib.b200q_ep_open(ctx, handles))
         dist.barrier(group=self.group)
         self.act = torch.empty((cap_recv, L.F), dtype=torch.bfloat16, device=dev)
-        self.epoch = 0
 
     def close(self):
         """Release the p2p exchange region (collective: every rank calls it)."""
         if self.ctx is not None:
             torch.cuda.synchronize()
+            self._graphs.clear()
             dist.barrier(group=self.group)
             _lib.check(self.layer.lib.b200q_ep_destroy(self.ctx))
             self.ctx = None
@@ -144,10 +149,10 @@ class EPMoE:
                 ev.record()
                 marks.append((name, ev))
 
-        self.epoch = (self.epoch + 1) & 0xffffffff
-        ep = self.epoch
+        ep = 0                      # device-side epoch: advanced by the count exchange
         mark('start')
-        _, ids, w = L.route(h)
+        hb = torch.empty((T, L.D), dtype=torch.bfloat16, device=dev)
+        _, ids, w = L.route(h, hb)
         mark('route')
         vids = self.virt[ids.long()]
         offsets, slot_of, token_of, slot_w, _ = L.dispatch(h, vids, w, gather=False)
@@ -155,8 +160,8 @@ class EPMoE:
         st = _stream()
         _lib.check(lib.b200q_ep_exchange_counts_dev(self.ctx, offsets.data_ptr(), ep, st))
         mark('counts')
-        _lib.check(lib.b200q_ep_send_rows_dev(self.ctx, h.data_ptr(), T, token_of.data_ptr(), offsets.data_ptr(),
-                                              T * L.k, ep, st))
+        _lib.check(lib.b200q_ep_send_rows_bf16_dev(self.ctx, hb.data_ptr(), T, token_of.data_ptr(),
+                                                   offsets.data_ptr(), T * L.k, ep, st))
         mark('send')
         _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride, L.down.data_ptr(),
                                             L.dn_stride, L.F, self.act.data_ptr(), ep, 0, st))
@@ -187,8 +192,33 @@ class EPMoE:
         of chunks."""
         return pipelined_host_forward(self.forward, h_host, y_host, chunks, self.layer.router_w.device)
 
+    def _forward_graph(self, h: torch.Tensor) -> torch.Tensor:
+        """p2p layer call through a CUDA graph captured on the first call for
+        this token count (every rank captures at the same call)."""
+        T = h.shape[0]
+        entry = self._graphs.get(T)
+        if entry is None:
+            static_h = torch.empty_like(h)
+            side = torch.cuda.Stream(h.device)
+            side.wait_stream(torch.cuda.current_stream(h.device))
+            with torch.cuda.stream(side):
+                static_h.copy_(h)
+                self._forward_p2p(static_h)          # eager call: allocations settle (all ranks alike)
+            torch.cuda.current_stream(h.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                y_static = self._forward_p2p(static_h)
+            entry = (graph, static_h, y_static)
+            self._graphs[T] = entry
+        graph, static_h, y_static = entry
+        static_h.copy_(h)
+        graph.replay()
+        return y_static.clone()
+
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         if self.transport == 'p2p':
+            if self.use_graph:
+                return self._forward_graph(h.contiguous())
             return self._forward_p2p(h.contiguous())
         L = self.layer
         T, dev = h.shape[0], h.device

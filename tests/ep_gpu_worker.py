@@ -64,6 +64,17 @@ def main():
         d = float((y_p - y_ep).abs().max())
         print(f'rank {rank}: p2p call {it} vs nccl max |diff| {d:.3e}', flush=True)
         good = good and d == 0.0
+    # the captured graph reads new inputs (same token count, other values)
+    other = shard.flip(0).contiguous()
+    d = float((p2p(other) - ep(other)).abs().max())
+    print(f'rank {rank}: p2p replay on new inputs vs nccl max |diff| {d:.3e}', flush=True)
+    good = good and d == 0.0
+    # the eager (non-graph) p2p path alternates with the graph replays
+    p2p_eager = EPMoE(part, owner, local, transport='p2p', max_tokens=n, graph=False)
+    d = float((p2p_eager(shard) - y_ep).abs().max())
+    print(f'rank {rank}: p2p eager vs nccl max |diff| {d:.3e}', flush=True)
+    good = good and d == 0.0
+    p2p_eager.close()
     m = n - 3 - rank                        # ragged: a different token count on every rank
     y_p = p2p(shard[:m])
     y_n = ep(shard[:m])
