@@ -177,11 +177,13 @@ int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *token_of, in
  * b200q_moe_gather_f32_dev. */
 int b200q_moe_gather_bf16_dev(const void *h_bf16, int h_rows, const int *token_of, int S, int D, void *out,
                               void *stream);
-/* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q6_K (14) or Q8_0 (8)
- * weights.  w_row_bytes is the byte distance between weight rows (0: packed
- * rows of k values); it must be a multiple of 16, so Q6_K rows whose packed
- * size is not (k not a multiple of 2048) need a padded copy.  Q6_K needs k a
- * multiple of 256 when rows are packed; every type needs k a multiple of 64. */
+/* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q5_K (13), Q6_K (14),
+ * Q8_0 (8) or Q4_0 (2) weights.  w_row_bytes is the byte distance between
+ * weight rows (0: packed rows of k values); it must be a multiple of 16, so
+ * rows whose packed size is not (Q6_K with k not a multiple of 2048, Q8_0
+ * with k not a multiple of 256, Q4_0 with k not a multiple of 256) need a
+ * padded copy.  Q6_K needs k a multiple of 256 when rows are packed; every
+ * type needs k a multiple of 64. */
 int b200q_gemm_dev(int ggml_type, const void *x_bf16, long long x_rows, int k, const void *w, long long w_row_bytes,
                    int groups, int w_rows_per_group, int up_offset, int n_feat, const int *row_off,
                    const int *group_w, int n_weight_groups, void *out, int out_is_bf16, long long ld_out,

@@ -229,11 +229,11 @@ static const uint8_t *lookup_registered(const uint8_t *raw, size_t n)
 // 0 keeps every call on the GEMV.
 static int g_tc_min_tokens = 32;
 
-// Q4_K/Q6_K/Q8_0 weights whose packed rows are whole 16-byte units (the GEMM
-// streams them with TMA), a multiple of 128 rows and of 64 columns.
+// Q4_K/Q5_K/Q6_K/Q8_0/Q4_0 weights whose packed rows are whole 16-byte units
+// (the GEMM streams them with TMA), a multiple of 128 rows and of 64 columns.
 static bool tc_matmul_shape_ok(int type, const void *wdev, int rows, int cols)
 {
-    if (type != T_Q4_K && type != T_Q6_K && type != T_Q8_0) return false;
+    if (type != T_Q4_K && type != T_Q5_K && type != T_Q6_K && type != T_Q8_0 && type != T_Q4_0) return false;
     if (rows % 128 || cols % 64 || (reinterpret_cast<uintptr_t>(wdev) & 15)) return false;
     const long long rb = (long long)(cols / type_vals(type)) * type_bytes(type);
     return rb % 16 == 0;

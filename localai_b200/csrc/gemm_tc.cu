@@ -62,11 +62,14 @@ constexpr int TC_PAIR_A_STAGES = TC_PAIR_STAGES_CFG;
 constexpr int TC_PAIR_B_STAGES = TC_PAIR_STAGES_CFG;
 // Raw weight chunks (one 256-value run of blocks per row, 4 K-steps), TMA ->
 // dequant warps.  The box of each type is 16-byte sized: Q4_K 144 B (a
-// super-block), Q8_0 272 B (8 blocks, as 136 uint16), Q6_K 240 B (as 120
-// uint16) -- an aligned window around the 210-byte super-block, whose start
-// within the window is (chunk * 210) mod 16.
+// super-block), Q5_K 176 B, Q4_0 144 B (8 blocks of 18 B), Q8_0 272 B (8
+// blocks, as 136 uint16), Q6_K 240 B (as 120 uint16) -- an aligned window
+// around the 210-byte super-block, whose start within the window is
+// (chunk * 210) mod 16.
 template <int WT> struct TcW;
 template <> struct TcW<T_Q4_K> { static constexpr int CHUNK = 144, RAW = 4, ELEM = 1; };
+template <> struct TcW<T_Q5_K> { static constexpr int CHUNK = 176, RAW = 3, ELEM = 1; };
+template <> struct TcW<T_Q4_0> { static constexpr int CHUNK = 144, RAW = 4, ELEM = 1; };
 template <> struct TcW<T_Q6_K> { static constexpr int CHUNK = 240, RAW = 2, ELEM = 2; };
 template <> struct TcW<T_Q8_0> { static constexpr int CHUNK = 272, RAW = 2, ELEM = 2; };
 constexpr int TC_THREADS = 512;
@@ -336,6 +339,44 @@ __device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, const uint4 h
     }
 }
 
+// Q5_K (engine/dequant.py:122-145): as Q4_K with a fifth bit per value, bit
+// g of qh[j] for value j of sub-block g; q = 0..31 still fits the f = 0.5 +
+// q/256 byte trick.  Block layout: d, dmin, scales[12], qh[32], qs[128].
+__device__ __forceinline__ void dequant_q5k_half(uint32_t raw_row, const uint4 hdr, int p, int h, uint32_t a_row,
+                                                 int r)
+{
+    const uint4 q0 = lds128(raw_row + 48 + 32 * p), q1 = lds128(raw_row + 64 + 32 * p);
+    const uint4 h0 = lds128(raw_row + 16), h1 = lds128(raw_row + 32);
+    const uint32_t sp = k_scales_packed(hdr, p);
+    const uint32_t sc = (sp >> (8 * h)) & 0xffu, mn = (sp >> (8 * (2 + h))) & 0xffu;
+    const float s = h2f(hdr.x) * (float)sc;            // exact
+    const float m = h2f(hdr.x >> 16) * (float)mn;      // exact
+    const float A = 256.0f * s, B = -(128.0f * s + m);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const int g = 2 * p + h;                            // sub-block
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const uint32_t wd = w[2 * c + ww];
+            const uint32_t nib = h ? ((wd >> 4) & 0x0F0F0F0Fu) : (wd & 0x0F0F0F0Fu);
+            const uint32_t q = nib | (((qh[2 * c + ww] >> g) & 0x01010101u) << 4);
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                v[b] = fmaf(A, __uint_as_float(__byte_perm(q, 0x3F000000u, 0x7044u | (uint32_t)(b << 8))), B);
+            o[2 * ww] = pack_bf16(v[0], v[1]);
+            o[2 * ww + 1] = pack_bf16(v[2], v[3]);
+        }
+        const uint32_t chunk = (uint32_t)(4 * h + c);
+        const uint32_t dst = a_row + ((chunk ^ (uint32_t)(r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                     : "memory");
+    }
+}
+
 // N consecutive 32-bit words of shared memory starting at an even address.
 template <int N>
 __device__ __forceinline__ void lds_run_a2(uint32_t addr, uint32_t (&w)[N])
@@ -390,6 +431,34 @@ __device__ __forceinline__ void dequant_q6k_half(uint32_t blk, int p, int h, uin
 #pragma unroll
             for (int b = 0; b < 4; ++b)       // 2^23 + q - (2^23 + 32) = q - 32, exact
                 v[b] = sc * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388640.0f);
+            o[2 * ww] = pack_bf16(v[0], v[1]);
+            o[2 * ww + 1] = pack_bf16(v[2], v[3]);
+        }
+        sts_a_chunk(a_row, r, 4 * h + c, o);
+    }
+}
+
+// Q4_0 (engine/dequant.py:62-67): K-step p, half h = block 2p+h of the
+// 8-block chunk (18-byte blocks at even addresses): value j < 16 = d *
+// (low nibble of qs[j] - 8), j >= 16 = d * (high nibble of qs[j-16] - 8),
+// exact in f32 and rounded once to bf16.
+__device__ __forceinline__ void dequant_q4_0_half(uint32_t chunk, int p, int h, uint32_t a_row, int r)
+{
+    const uint32_t blk = chunk + 18u * (uint32_t)(2 * p + h);
+    const float d = h2f(lds_u16(blk));
+    uint32_t qs[4];
+    lds_run_a2<4>(blk + 2, qs);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {                      // 8 K columns: qs[8(c&1) ..], low (c < 2) or high nibbles
+        uint32_t o[4];
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const uint32_t wd = qs[2 * (c & 1) + ww];
+            const uint32_t q = c < 2 ? (wd & 0x0F0F0F0Fu) : ((wd >> 4) & 0x0F0F0F0Fu);
+            float v[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b)       // 2^23 + q - (2^23 + 8) = q - 8, exact
+                v[b] = d * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388616.0f);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }
@@ -588,7 +657,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint32_t dst = sRaw + rs * raw_stage_bytes;
                     mbar_arrive_expect_tx(raw_full + 8 * rs, raw_stage_bytes);
                     // box start (in map elements): 16-byte aligned, see TcW
-                    const int xb = WT == T_Q4_K ? rc * 144 : WT == T_Q8_0 ? rc * 136 : ((rc * 210) & ~15) >> 1;
+                    const int xb = (WT == T_Q4_K || WT == T_Q4_0) ? rc * 144 : WT == T_Q5_K ? rc * 176
+                                 : WT == T_Q8_0 ? rc * 136 : ((rc * 210) & ~15) >> 1;
                     tma_load_2d(dst, &map_w, xb, wrow0, raw_full + 8 * rs);
                     tma_load_2d(dst + 64 * a.raw_chunk_bytes, &map_w, xb, wrow1, raw_full + 8 * rs);
                 }
@@ -801,6 +871,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (WT == T_Q4_K) {
                     if ((ks & 3) == 0) hdr = lds128(raw_row);
                     dequant_q4k_half(raw_row, hdr, ks & 3, h, a_row, r);
+                } else if (WT == T_Q5_K) {
+                    if ((ks & 3) == 0) hdr = lds128(raw_row);
+                    dequant_q5k_half(raw_row, hdr, ks & 3, h, a_row, r);
+                } else if (WT == T_Q4_0) {
+                    dequant_q4_0_half(raw_row, ks & 3, h, a_row, r);
                 }
                 else if (WT == T_Q6_K) dequant_q6k_half(raw_row + (uint32_t)(((ks >> 2) * 210) & 15), ks & 3, h, a_row, r);
                 else dequant_q8_0_half(raw_row, ks & 3, h, a_row, r);
@@ -996,17 +1071,24 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
     if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
-    if (wtype != T_Q4_K && wtype != T_Q6_K && wtype != T_Q8_0) return cudaErrorInvalidValue;
-    if (wtype != T_Q8_0 && w_row_bytes == 0 && k % 256 && wtype != T_Q4_K) return cudaErrorInvalidValue;
-    const int chunk = wtype == T_Q4_K ? TcW<T_Q4_K>::CHUNK : wtype == T_Q6_K ? TcW<T_Q6_K>::CHUNK : TcW<T_Q8_0>::CHUNK;
-    const int elem = wtype == T_Q4_K ? 1 : 2;
+    if (wtype != T_Q4_K && wtype != T_Q5_K && wtype != T_Q4_0 && wtype != T_Q6_K && wtype != T_Q8_0)
+        return cudaErrorInvalidValue;
+    if (wtype == T_Q6_K && w_row_bytes == 0 && k % 256) return cudaErrorInvalidValue;
+    const int chunk = wtype == T_Q4_K ? TcW<T_Q4_K>::CHUNK : wtype == T_Q5_K ? TcW<T_Q5_K>::CHUNK
+                    : wtype == T_Q4_0 ? TcW<T_Q4_0>::CHUNK : wtype == T_Q6_K ? TcW<T_Q6_K>::CHUNK
+                    : TcW<T_Q8_0>::CHUNK;
+    const int elem = (wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q4_0) ? 1 : 2;
     long long row_bytes = w_row_bytes;
     if (row_bytes == 0) {
         // packed rows (Q4_K rows hold whole super-blocks: k rounded up to 256)
         row_bytes = wtype == T_Q4_K ? ((long long)k + 255) / 256 * 144
+                  : wtype == T_Q5_K ? ((long long)k + 255) / 256 * 176
+                  : wtype == T_Q4_0 ? ((long long)k + 31) / 32 * 18
                   : wtype == T_Q6_K ? (long long)k / 256 * 210 : (long long)k / 32 * 34;
     }
     const long long min_bytes = wtype == T_Q4_K ? ((long long)k + 255) / 256 * 144
+                              : wtype == T_Q5_K ? ((long long)k + 255) / 256 * 176
+                              : wtype == T_Q4_0 ? ((long long)k + 31) / 32 * 18
                               : wtype == T_Q6_K ? ((long long)k + 255) / 256 * 210 : ((long long)k + 31) / 32 * 34;
     if (row_bytes < min_bytes) return cudaErrorInvalidValue;
     CUtensorMap mx, mw;
@@ -1036,10 +1118,14 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     a.err = err;
     if (pair) {
         if (wtype == T_Q4_K) return tc_launch<T_Q4_K, true>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q5_K) return tc_launch<T_Q5_K, true>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q4_0) return tc_launch<T_Q4_0, true>(mx, mw, a, num_sms, max_ctas, st);
         if (wtype == T_Q6_K) return tc_launch<T_Q6_K, true>(mx, mw, a, num_sms, max_ctas, st);
         return tc_launch<T_Q8_0, true>(mx, mw, a, num_sms, max_ctas, st);
     }
     if (wtype == T_Q4_K) return tc_launch<T_Q4_K, false>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q5_K) return tc_launch<T_Q5_K, false>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q4_0) return tc_launch<T_Q4_0, false>(mx, mw, a, num_sms, max_ctas, st);
     if (wtype == T_Q6_K) return tc_launch<T_Q6_K, false>(mx, mw, a, num_sms, max_ctas, st);
     return tc_launch<T_Q8_0, false>(mx, mw, a, num_sms, max_ctas, st);
 }

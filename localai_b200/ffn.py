@@ -23,7 +23,7 @@ from . import _lib, ops
 from .moe import _stream
 
 SUPPORTED_GEMV = (2, 8, 12, 13, 14)
-SUPPORTED_GEMM = (8, 12, 14)
+SUPPORTED_GEMM = (2, 8, 12, 13, 14)
 
 
 class QuantFFN:
@@ -51,7 +51,7 @@ class QuantFFN:
         """16-byte-row copies for the tensor-core path (made once, if needed)."""
         if self._gemm_w is None:
             if self.t_gu not in SUPPORTED_GEMM or self.t_dn not in SUPPORTED_GEMM:
-                raise NotImplementedError('the tensor-core path supports Q4_K, Q6_K and Q8_0')
+                raise NotImplementedError('the tensor-core path supports Q4_0, Q8_0, Q4_K, Q5_K and Q6_K')
             gu, s_gu = ops.pad_rows(self.gate_up, 2 * self.F, ops.packed_row_bytes(self.t_gu, self.D))
             dn, s_dn = ops.pad_rows(self.down, self.D, ops.packed_row_bytes(self.t_dn, self.F))
             self._gemm_w = (gu, s_gu, dn, s_dn)

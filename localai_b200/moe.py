@@ -12,7 +12,7 @@ same block batched over T tokens and generalised to top-k:
     out = w_slot * (down act)    per expert           b200q_gemm_dev (plain mode, tcgen05; bf16 rows)
     y[t] = sum_j out[slot(t, j)]                      b200q_moe_combine_dev
 
-Expert weights are raw GGUF Q4_K, Q6_K or Q8_0 tensors in ZAYA's layout:
+Expert weights are raw GGUF Q4_K, Q5_K, Q6_K, Q8_0 or Q4_0 tensors in ZAYA's layout:
 ``gate_up`` [E, 2F, D] (gate rows first, then up rows, as
 ``np.split(packed, 2)`` reads them, engine/zaya.py:304) and ``down``
 [E, D, F_pad] with F_pad the next multiple of the type's block (256 for the
@@ -27,7 +27,7 @@ import torch
 from . import _lib
 from .ops import packed_row_bytes, pad_rows
 
-Q4_K, Q6_K, Q8_0 = 12, 14, 8
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K = 2, 8, 12, 13, 14
 
 
 def _stream():
@@ -87,14 +87,16 @@ class QuantMoE:
                  d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
                  sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K,
                  local_experts: int | None = None):
-        if ggml_type not in (Q4_K, Q6_K, Q8_0):
-            raise NotImplementedError('the tensor-core expert path supports Q4_K, Q6_K and Q8_0 expert weights')
-        if d_ff % 64 or d_model % 128 or (ggml_type != Q8_0 and d_model % 256):
+        if ggml_type not in (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K):
+            raise NotImplementedError('the tensor-core expert path supports Q4_0, Q8_0, Q4_K, Q5_K and Q6_K '
+                                      'expert weights')
+        small_blk = ggml_type in (Q4_0, Q8_0)
+        if d_ff % 64 or d_model % 128 or (not small_blk and d_model % 256):
             raise ValueError('d_ff must be a multiple of 64 and d_model of 128 (256 for K-quants)')
         self.E = router_w.shape[0]
         self.D, self.F, self.k = d_model, d_ff, top_k
         self.type = ggml_type
-        blk = 32 if ggml_type == Q8_0 else 256
+        blk = 32 if small_blk else 256
         self.F_pad = (d_ff + blk - 1) // blk * blk
         self.router_w = router_w.contiguous().float()
         self.router_bias = None if router_bias is None else router_bias.contiguous().float()

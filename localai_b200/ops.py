@@ -86,8 +86,8 @@ def tensor_core_min_tokens() -> int:
 
 
 def tensor_core_shape_ok(ggml_type: int, rows: int, cols: int) -> bool:
-    """Q4_K/Q6_K/Q8_0 weights the tensor-core GEMM can stream as packed rows."""
-    if ggml_type not in (8, 12, 14) or rows % 128 or cols % 64 or cols % BLOCK[ggml_type][0]:
+    """Q4_0/Q8_0/Q4_K/Q5_K/Q6_K weights the tensor-core GEMM can stream as packed rows."""
+    if ggml_type not in (2, 8, 12, 13, 14) or rows % 128 or cols % 64 or cols % BLOCK[ggml_type][0]:
         return False
     return row_bytes(ggml_type, cols) % 16 == 0
 
@@ -117,13 +117,17 @@ def check_device_error() -> None:
 
 
 def packed_row_bytes(ggml_type: int, k: int) -> int:
-    """Bytes of one GGUF row of k values (Q4_K rows rounded up to whole super-blocks)."""
+    """Bytes of one GGUF row of k values (rounded up to whole blocks)."""
     if ggml_type == 12:
         return (k + 255) // 256 * 144
+    if ggml_type == 13:
+        return (k + 255) // 256 * 176
     if ggml_type == 14:
         return (k + 255) // 256 * 210
     if ggml_type == 8:
         return (k + 31) // 32 * 34
+    if ggml_type == 2:
+        return (k + 31) // 32 * 18
     raise ValueError(f'unsupported ggml type {ggml_type} for the tensor-core path')
 
 
@@ -145,7 +149,7 @@ def gemm_quant(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, 
                act: torch.Tensor | None = None, group_w: torch.Tensor | None = None, n_weight_groups: int = 0,
                out_dtype=torch.float32, max_ctas: int = 0) -> torch.Tensor:
     """Grouped tensor-core GEMM with in-kernel dequantisation of Q4_K (12),
-    Q6_K (14) or Q8_0 (8) weights.
+    Q5_K (13), Q6_K (14), Q8_0 (8) or Q4_0 (2) weights.
 
     ``x_bf16`` [rows, k] bf16 activations; group g owns rows
     ``row_off[g]:row_off[g+1]`` (int32 CUDA tensor, groups+1 entries) and the

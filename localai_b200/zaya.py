@@ -14,15 +14,31 @@ Router chain (all f32, one row per token):
 Route E is the learned skip route: the token's output is its block input
 times p[E].  Otherwise the output is the selected expert's quantised FFN
 (``QuantMoE``'s tensor-core path) times p[e].  The linear layers run on the
-library's f32 linear kernel (the router kernel), the rest on its element-
-and row-wise kernels; nothing falls back to the CPU.
+library's f32 linear kernel (the router kernel) for f32/f16 weights, or on
+the quantised GEMV (f32 accumulation) for GGUF block-quantised weights -- the
+reference calls ``self._matvec`` on whatever type the checkpoint stores
+(engine/zaya.py:279-289, engine/model.py:42-80, which also adds a
+``<name>.bias`` tensor when the file has one); the rest runs on the library's
+element- and row-wise kernels; nothing falls back to the CPU.
 """
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import torch
 
-from . import _lib
+from . import _lib, ops
 from .moe import QuantMoE, _stream
+
+QUANT_TYPES = (2, 8, 12, 13, 14)      # Q4_0, Q8_0, Q4_K, Q5_K, Q6_K
+
+
+class QuantMatrix(NamedTuple):
+    """A [rows, cols] matrix kept as raw GGUF blocks on the device."""
+    raw: torch.Tensor                 # CUDA uint8
+    ggml_type: int
+    rows: int
+    cols: int
 
 
 def _f32(t):
@@ -33,27 +49,85 @@ def _f32(t):
     return t.contiguous().float()
 
 
+def _weight(w):
+    """f32 CUDA tensor, or a QuantMatrix of a supported block type."""
+    if isinstance(w, QuantMatrix):
+        if w.ggml_type not in QUANT_TYPES:
+            raise ValueError(f'router weights of GGML type {w.ggml_type} are not supported')
+        if w.raw.dtype != torch.uint8 or not w.raw.is_cuda:
+            raise ValueError('QuantMatrix.raw must be a CUDA uint8 tensor')
+        ops._check_weights(w.raw, w.ggml_type, w.rows, w.cols)
+        return w
+    return _f32(w)
+
+
+def _shape(w):
+    return (w.rows, w.cols) if isinstance(w, QuantMatrix) else tuple(w.shape)
+
+
 class ZayaRouter:
+    """Router chain of one ZAYA MoE layer.  Each of ``w_in``, ``w_gate``,
+    ``w_mlp2``, ``w_mlp4`` is an f32/f16 CUDA matrix or a ``QuantMatrix``
+    (raw GGUF blocks, as a checkpoint stores them); ``from_gguf`` builds the
+    router of layer ``layer`` from a ``DeviceGGUF`` by the reference's tensor
+    names."""
+
     def __init__(self, w_in, w_gate, w_mlp2, w_mlp4, norm_w, route_bias, *, b_in=None, b_gate=None, b_mlp2=None,
                  b_mlp4=None, w_eda=None, eps: float = 1e-5):
-        self.w = [_f32(w_in), _f32(w_gate), _f32(w_mlp2), _f32(w_mlp4)]
+        self.w = [_weight(w_in), _weight(w_gate), _weight(w_mlp2), _weight(w_mlp4)]
         self.b = [_f32(b_in), _f32(b_gate), _f32(b_mlp2), _f32(b_mlp4)]
+        shapes = [_shape(w) for w in self.w]
         for i in range(1, 4):
-            if self.w[i].shape[1] != self.w[i - 1].shape[0]:
+            if shapes[i][1] != shapes[i - 1][0]:
                 raise ValueError('router layer shapes do not chain')
-        self.D, self.R = self.w[0].shape[1], self.w[0].shape[0]
-        self.n_routes = self.w[3].shape[0]                 # experts + 1 (skip)
-        for w in self.w:
-            if w.shape[1] % 4:
+        self.D, self.R = shapes[0][1], shapes[0][0]
+        self.n_routes = shapes[3][0]                       # experts + 1 (skip)
+        for w, shp in zip(self.w, shapes):
+            if not isinstance(w, QuantMatrix) and shp[1] % 4:
                 raise ValueError('router input widths must be multiples of 4')
+        for b, shp in zip(self.b, shapes):
+            if b is not None and b.numel() != shp[0]:
+                raise ValueError("router bias length must match its layer's output rows")
         self.norm_w = _f32(norm_w)
         self.route_bias = _f32(route_bias)
         self.w_eda = _f32(w_eda)
         self.eps = float(eps)
         self.lib = _lib.load()
 
+    @classmethod
+    def from_gguf(cls, gguf, layer: int, eps: float = 1e-5):
+        """Router of MoE layer ``layer`` from a DeviceGGUF, by the names
+        engine/zaya.py:278-293 reads (F32/F16 tensors as f32 matrices,
+        block-quantised ones kept raw; ``<name>.bias`` added when present)."""
+        p = f'blk.{layer}.'
+
+        def mat(name):
+            x = gguf.tensors[name]
+            if x.ggml_type in QUANT_TYPES:
+                rows, cols = x.shape
+                return QuantMatrix(gguf.raw(name), x.ggml_type, rows, cols)
+            return gguf.tensor_dev(name)
+
+        def vec(name):
+            return gguf.tensor_dev(name).reshape(-1) if name in gguf.tensors else None
+
+        def bias(name):
+            return vec(name[:-6] + 'bias')
+
+        names = [p + 'ffn_gate_inp.weight', p + 'ffn_gate.weight', p + 'zaya_router_mlp2.weight',
+                 p + 'zaya_router_mlp4.weight']
+        return cls(*[mat(n) for n in names], vec(p + 'ffn_norm.weight'), vec(p + 'zaya_router_biases.weight'),
+                   b_in=bias(names[0]), b_gate=bias(names[1]), b_mlp2=bias(names[2]), b_mlp4=bias(names[3]),
+                   w_eda=vec(p + 'zaya_router_eda.weight'), eps=eps)
+
     def _linear(self, x, i):
         w, b = self.w[i], self.b[i]
+        if isinstance(w, QuantMatrix):
+            # f32-accurate quantised GEMV (routing decisions need f32, not the bf16 tensor-core path)
+            y = ops.gemv(w.raw, x.contiguous(), w.ggml_type, w.rows, w.cols)
+            if b is not None:
+                y += b
+            return y
         y = torch.empty((x.shape[0], w.shape[0]), dtype=torch.float32, device=x.device)
         _lib.check(self.lib.b200q_moe_router_dev(x.data_ptr(), w.data_ptr(), None if b is None else b.data_ptr(),
                                                  y.data_ptr(), x.shape[0], w.shape[0], w.shape[1], _stream()))

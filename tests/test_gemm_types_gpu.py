@@ -1,12 +1,13 @@
-"""GPU tests of the tensor-core grouped GEMM on Q6_K and Q8_0 weights, and of
+"""GPU tests of the tensor-core grouped GEMM on Q6_K, Q8_0, Q5_K and Q4_0 weights, and of
 the Q6_K MoE block of the benchmark's configuration 3 (D=2048, E=16,
 F=1024, top-2; T = 1, 64, 4096).
 
 References as for Q4_K: the f32 product of the same bf16-rounded operands
 (normwise <= 5e-4: a few weights may sit one bf16 ulp apart) and the float64
 oracle ``dequantize(raw) @ x`` (normwise <= 1e-2, the bf16 tensor-core bar).
-Q6_K rows of 1024 values (840 B) are not 16-byte sized and go through
-``ops.pad_rows`` exactly as ``QuantMoE`` does.
+Q6_K rows of 1024 values (840 B) and Q4_0 rows of 640 values (360 B) are
+not 16-byte sized and go through ``ops.pad_rows`` exactly as ``QuantMoE``
+does.
 """
 import numpy as np
 import pytest
@@ -20,6 +21,8 @@ pytestmark = pytest.mark.gpu
 
 
 def weights(rng, t, rows, k, full_scales=False):
+    if t in (13, 2):                    # Q5_K / Q4_0: random block bytes, small fp16 scales
+        return synth.make(rng, t, rows, k)
     if t == 14:
         raw = synth.q6_k(rng, rows, k)
         if full_scales:                 # int8 scales over the whole range, incl. -128 and 127
@@ -39,7 +42,8 @@ def ref_bf16(raw, t, rows, k, x_bf16):
 
 
 @pytest.mark.parametrize('t,k,full', [(14, 2048, False), (14, 1024, False), (14, 512, True), (8, 512, False),
-                                      (8, 1024, False)])
+                                      (8, 1024, False), (13, 2048, False), (13, 1024, False), (2, 512, False),
+                                      (2, 768, False), (2, 640, False)])
 def test_plain_grouped(t, k, full):
     rng = np.random.default_rng(t * 100 + k)
     n = 256
@@ -68,7 +72,7 @@ def test_plain_grouped(t, k, full):
         assert o.normwise_rel_err(out[a:b].cpu().numpy(), ref64) < 1e-2
 
 
-@pytest.mark.parametrize('t,k', [(14, 1024), (8, 768)])
+@pytest.mark.parametrize('t,k', [(14, 1024), (8, 768), (13, 1024), (2, 512)])
 def test_gate_up(t, k):
     rng = np.random.default_rng(t + k)
     f = 128
@@ -124,3 +128,26 @@ def test_config3_q6k_moe(T):
     experts = [(gate_up[e], down[e]) for e in range(16)]
     ref = o.moe_forward_f64(h[sample], ids[sample], w[sample], experts, 14, 14, 2048, 1024, 1024)
     assert o.normwise_rel_err(y.cpu().numpy()[sample], ref) < 1e-2
+
+
+@pytest.mark.parametrize('t', [13, 2])
+def test_moe_layer_q5k_q4_0(t):
+    """The MoE layer on Q5_K and Q4_0 experts (tensor-core path) against the
+    float64 oracle with the GPU's routing."""
+    rng = np.random.default_rng(500 + t)
+    E, D, F, k, T = 8, 1024, 256, 2, 600
+    gate_up = [synth.make(rng, t, 2 * F, D) for _ in range(E)]
+    down = [synth.make(rng, t, D, F) for _ in range(E)]
+    wr = rng.normal(0, D ** -0.5, size=(E, D)).astype(np.float32)
+    cat = lambda parts: torch.frombuffer(bytearray(b''.join(parts)), dtype=torch.uint8).cuda()
+    layer = QuantMoE(torch.from_numpy(wr).cuda(), cat(gate_up), cat(down), d_model=D, d_ff=F, top_k=k,
+                     ggml_type=t)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    hd = torch.from_numpy(h).cuda()
+    assert T * k > layer.small_slots
+    y = layer(hd)
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    _, ids, w = layer.route(hd)
+    ref = o.moe_forward_f64(h, ids.cpu().numpy(), w.cpu().numpy(), list(zip(gate_up, down)), t, t, D, F, F)
+    assert o.normwise_rel_err(y.cpu().numpy(), ref) < 1e-2

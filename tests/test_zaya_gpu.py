@@ -70,3 +70,51 @@ def test_zaya_skip_route_dominates():
     assert bool((ids == 8).all())
     ref = h * w.cpu().numpy()
     assert o.normwise_rel_err(y.cpu().numpy(), ref) < 5e-3      # bf16 rows
+
+
+def test_zaya_router_quantised_weights(tmp_path):
+    """Router matrices stored block-quantised, as a ZAYA checkpoint may hold
+    them (engine/zaya.py:279-289 calls _matvec on any tensor type): the
+    quantised GEMV path against the f32 oracle run on the dequantised
+    matrices, built directly and through a GGUF file (from_gguf, with a
+    ``.bias`` tensor on the first projection)."""
+    from localai_b200.gguf import DeviceGGUF, write_gguf
+    from localai_b200.zaya import QuantMatrix
+    rng = np.random.default_rng(11)
+    E, D, R, R2, R3, T = 8, 512, 256, 256, 128, 200
+    raws = {'w_in': (synth.q8_0(rng, R, D), 8, R, D), 'w_gate': (synth.q4_k(rng, R2, R), 12, R2, R),
+            'w_mlp2': (synth.q6_k(rng, R3, R2), 14, R3, R2)}
+    deq = {k: o.dequantize(v[0], v[1], (v[2], v[3])) for k, v in raws.items()}
+    f = lambda *shape, s=1.0: rng.normal(0, s, size=shape).astype(np.float32)
+    w_mlp4, norm_w = f(E + 1, R3, s=2 * R3 ** -0.5), (1 + f(R, s=0.1)).astype(np.float32)
+    bias = np.concatenate([f(E, s=0.02), [0.08]]).astype(np.float32)
+    b_in, w_eda = f(R, s=0.1), f(R, s=0.5)
+    cu = lambda a: torch.from_numpy(a).cuda()
+    qm = {k: QuantMatrix(torch.frombuffer(bytearray(v[0]), dtype=torch.uint8).cuda(), v[1], v[2], v[3])
+          for k, v in raws.items()}
+    direct = ZayaRouter(qm['w_in'], qm['w_gate'], qm['w_mlp2'], cu(w_mlp4), cu(norm_w), cu(bias), b_in=cu(b_in),
+                        w_eda=cu(w_eda), eps=1e-5)
+    path = tmp_path / 'router.gguf'
+    p = 'blk.3.'
+    write_gguf(path, {'general.architecture': 'zaya'},
+               {p + 'ffn_gate_inp.weight': (raws['w_in'][0], 8, (R, D)),
+                p + 'ffn_gate_inp.bias': (b_in.tobytes(), 0, (R,)),
+                p + 'ffn_gate.weight': (raws['w_gate'][0], 12, (R2, R)),
+                p + 'zaya_router_mlp2.weight': (raws['w_mlp2'][0], 14, (R3, R2)),
+                p + 'zaya_router_mlp4.weight': (w_mlp4.astype(np.float16).tobytes(), 1, (E + 1, R3)),
+                p + 'ffn_norm.weight': (norm_w.tobytes(), 0, (R,)),
+                p + 'zaya_router_biases.weight': (bias.tobytes(), 0, (E + 1,)),
+                p + 'zaya_router_eda.weight': (w_eda.tobytes(), 0, (R,))})
+    from_file = ZayaRouter.from_gguf(DeviceGGUF(path), 3)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    prev = rng.normal(size=(T, R)).astype(np.float32)
+    for router, mlp4 in ((direct, w_mlp4), (from_file, w_mlp4.astype(np.float16).astype(np.float32))):
+        ids, w, state = router(cu(h), cu(prev))
+        torch.cuda.synchronize()
+        r_e, r_w, _, r_state = o.zaya_router_f32(h, deq['w_in'], deq['w_gate'], deq['w_mlp2'], mlp4, norm_w, bias,
+                                                  1e-5, prev=prev, w_eda=w_eda, b_in=b_in)
+        assert o.normwise_rel_err(state.cpu().numpy(), r_state) < 1e-5
+        g_e, g_w = ids.cpu().numpy()[:, 0], w.cpu().numpy()[:, 0]
+        assert np.mean(g_e == r_e) >= 0.97
+        same = g_e == r_e
+        np.testing.assert_allclose(g_w[same], r_w[same], rtol=1e-4, atol=1e-6)
