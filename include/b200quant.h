@@ -374,6 +374,17 @@ int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int rotary, floa
                       float *k_cache, float *v_cache, int max_seq, void *stream);
 int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T, int H,
                            int KV, int hd, int max_seq, void *out_bf16, void *stream);
+/* b200q_attn_prefill_dev on the tensor cores (tcgen05: bf16 operands, f32
+ * accumulation, P in bf16), hd = 128: the rotated queries and the cache rows
+ * 0 .. *pos + T - 1 are first copied as bf16 into ``scratch``
+ * (b200q_attn_prefill_tc_scratch_bytes bytes, 16-byte aligned), then one CTA
+ * per (head, 128 queries) runs the causal softmax attention over 128-key
+ * blocks.  Same contract for positions and errors as b200q_attn_prefill_dev;
+ * out 16-byte aligned. */
+size_t b200q_attn_prefill_tc_scratch_bytes(int T, int H, int KV, int hd, int max_seq);
+int b200q_attn_prefill_tc_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T,
+                              int H, int KV, int hd, int max_seq, void *scratch, size_t scratch_bytes, void *out_bf16,
+                              void *stream);
 size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq);
 int b200q_attn_decode_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H, int KV,
                           int hd, int max_seq, float *scratch, float *out, void *stream);

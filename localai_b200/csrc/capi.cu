@@ -88,6 +88,10 @@ cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary,
                            float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
                                 int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st);
+size_t attn_prefill_tc_scratch_bytes(int T, int H, int KV, int hd, int max_seq);
+cudaError_t launch_attn_prefill_tc(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
+                                   int KV, int hd, int max_seq, void *scratch, size_t scratch_bytes,
+                                   __nv_bfloat16 *out, int *err, int num_sms, cudaStream_t st);
 size_t attn_scratch_floats(int H, int hd, int max_seq);
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
                                int max_seq, float *part, float *out, cudaStream_t st);
@@ -937,6 +941,27 @@ B200Q_API int b200q_argmax_dev(const float *logits, int V, int *token, int *pos,
     return cuda_status(launch_argmax(logits, V, token, pos, out_tokens, max_tokens, key, di->sms,
                                      (cudaStream_t)stream),
                        "argmax");
+}
+
+B200Q_API size_t b200q_attn_prefill_tc_scratch_bytes(int T, int H, int KV, int hd, int max_seq)
+{
+    return attn_prefill_tc_scratch_bytes(T, H, KV, hd, max_seq);
+}
+
+B200Q_API int b200q_attn_prefill_tc_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos,
+                                        int T, int H, int KV, int hd, int max_seq, void *scratch,
+                                        size_t scratch_bytes, void *out_bf16, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!qkv || !k_cache || !v_cache || !pos || !out_bf16 || !scratch)
+        return set_status(B200Q_EINVAL, "attn_prefill_tc: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    g_launches += 2;
+    return cuda_status(launch_attn_prefill_tc(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq, scratch,
+                                              scratch_bytes, static_cast<__nv_bfloat16 *>(out_bf16), di->err, di->sms,
+                                              (cudaStream_t)stream),
+                       "attn_prefill_tc");
 }
 
 B200Q_API int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T,

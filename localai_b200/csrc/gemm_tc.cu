@@ -34,6 +34,7 @@
 // 16 gate rows and the 16 matching up rows (lanes l and l+16).
 #include "common.cuh"
 #include "ep.cuh"
+#include "tcgen05.cuh"
 
 #include <cuda.h>
 #include <algorithm>
@@ -107,188 +108,6 @@ struct TcArgs {
     const EpDev *ep_ret;
     int *err;
 };
-
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols)
-{
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
-{
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, f32 accumulation.
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t accumulate)
-{
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrive (once) on an mbarrier when every MMA issued so far by this thread completes.
-__device__ __forceinline__ void umma_commit(uint32_t bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// ---- CTA-pair (cta_group::2) forms.  The pair is a cluster of two CTAs on
-// two SMs; the even CTA issues the MMAs, which read A (weight rows) and B
-// (activation rows) from both CTAs' shared memory at the same offsets and
-// write each CTA's half of M into that CTA's tensor memory.
-__device__ __forceinline__ uint32_t cluster_rank()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Address of the same shared-memory offset in CTA ``rank`` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
-{
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all()
-{
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Arrive on an mbarrier given by its cluster address (this CTA's or the peer's).
-#ifndef TC_PAIR_CLUSTER_SCOPE
-#define TC_PAIR_CLUSTER_SCOPE 0
-#endif
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cbar)
-{
-#if TC_PAIR_CLUSTER_SCOPE
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
-#else
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
-#endif
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-#if TC_PAIR_CLUSTER_SCOPE
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-#else
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-#endif
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(MBAR_SUSPEND_NS)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (as mbar_wait) with cluster-scope acquire: for barriers that
-// the peer CTA arrives on.
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *err)
-{
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
-            atomicExch(err, ERR_WAIT_TIMEOUT);
-            return false;
-        }
-    }
-}
-// TMA tile load into this CTA's shared memory whose completion (bytes) is
-// signalled on an mbarrier of either CTA of the pair (cluster address).  No
-// multicast: each CTA loads its own rows.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t cbar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cbar)
-        : "memory");
-}
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate)
-{
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrive once on the mbarrier at offset ``bar`` in both CTAs of the pair when
-// every pair MMA issued so far completes (a completion signal, not a load).
-__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar)
-{
-    const uint16_t mask = 3;
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-                 ::"r"(bar), "h"(mask)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols)
-{
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
-{
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// 32 lanes x 32 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
-{
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (stride byte offset), leading byte offset 16 (unused by the
-// swizzled K-major form), descriptor version 1 (sm100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem)
-{
-    uint64_t d = 0;
-    d |= (uint64_t)((smem & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
-
-// Instruction descriptor: kind::f16, A = B = bf16 (K-major), D = f32, M x N.
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n)
-{
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
-{
-    __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&p);
-}
 
 __device__ __forceinline__ float silu_ref(float g)
 {
@@ -948,7 +767,7 @@ cudaError_t make_map_u16_rows(CUtensorMap *m, const void *ptr, long long rows, l
 }
 
 // bf16 [rows, cols] row-major, box [64 cols x box_rows], 128-byte swizzle.
-static cudaError_t make_map_bf16(CUtensorMap *m, const void *ptr, long long rows, long long cols, int box_rows)
+cudaError_t make_map_bf16(CUtensorMap *m, const void *ptr, long long rows, long long cols, int box_rows)
 {
     PFN_encodeTiled enc = get_encode();
     if (!enc) return cudaErrorNotSupported;

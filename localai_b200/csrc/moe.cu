@@ -415,6 +415,56 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *p, long long i)
                        __uint_as_float(u.y & 0xffff0000u));
 }
 
+// bf16 rows, k <= 32: the token's slots and weights read once into shared
+// memory, then each thread sums 8 consecutive values of every routed row
+// (16-byte loads, the k loads of a chunk issued before their FMAs); the sum
+// keeps the fixed j order, so results equal moe_combine_kernel's bit for bit.
+// A slot outside [0, n_rows) adds nothing.
+__global__ void __launch_bounds__(256) moe_combine_bf16x8_kernel(const __nv_bfloat16 *__restrict__ out,
+                                                                 long long n_rows, const int *__restrict__ slot_of,
+                                                                 const float *__restrict__ slot_w, int T, int k, int D,
+                                                                 float *__restrict__ y)
+{
+    __shared__ long long row_s[32];
+    __shared__ float w_s[32];
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    if (threadIdx.x < k) {
+        const int slot = slot_of[(long long)t * k + threadIdx.x];
+        const bool ok = slot >= 0 && slot < n_rows;
+        row_s[threadIdx.x] = ok ? (long long)slot * (D / 8) : -1;
+        w_s[threadIdx.x] = ok ? (slot_w ? __ldg(slot_w + slot) : 1.0f) : 0.f;
+    }
+    __syncthreads();
+    const uint4 *src = reinterpret_cast<const uint4 *>(out);
+    for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int j0 = 0; j0 < k; j0 += 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const int j = j0 + jj;
+                v[jj] = (j < k && row_s[j] >= 0) ? __ldg(src + row_s[j] + c) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const int j = j0 + jj;
+                if (j >= k || row_s[j] < 0) continue;
+                const float wj = w_s[j];
+                const uint32_t u[4] = {v[jj].x, v[jj].y, v[jj].z, v[jj].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    acc[2 * e] = fmaf(wj, __uint_as_float(u[e] << 16), acc[2 * e]);
+                    acc[2 * e + 1] = fmaf(wj, __uint_as_float(u[e] & 0xffff0000u), acc[2 * e + 1]);
+                }
+            }
+        }
+        float4 *dst = reinterpret_cast<float4 *>(y + (long long)t * D) + 2 * c;
+        dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
 // A slot outside [0, n_rows) (a pair with a bad expert id, slot -1) adds nothing.
 template <typename RowT>
 __global__ void moe_combine_kernel(const RowT *__restrict__ out, long long n_rows, const int *__restrict__ slot_of,
@@ -624,7 +674,10 @@ cudaError_t launch_moe_combine(const void *out, bool out_bf16, long long n_rows,
     if (T < 1 || k < 1 || D < 4 || D % 4 || n_rows < 1 || (reinterpret_cast<uintptr_t>(y) & 15) ||
         (reinterpret_cast<uintptr_t>(out) & (out_bf16 ? 7 : 15)))
         return cudaErrorInvalidValue;
-    if (out_bf16)
+    if (out_bf16 && D % 8 == 0 && k <= 32 && !(reinterpret_cast<uintptr_t>(out) & 15))
+        moe_combine_bf16x8_kernel<<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(out), n_rows, slot_of,
+                                                     slot_w, T, k, D, y);
+    else if (out_bf16)
         moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(out), n_rows, slot_of,
                                                              slot_w, T, k, D, y);
     else

@@ -25,7 +25,8 @@ each step.
 engine/model.py:118-170): embedding rows, then per layer RMSNorm (bf16 out),
 the tensor-core GEMMs (QKV, O, gate/up with fused SiLU*up, down) over all
 prompt rows, RoPE and the KV-cache store for every row, and causal
-grouped-query attention (``b200q_attn_prefill_dev``); the last row goes
+grouped-query attention (on the tensor cores, ``b200q_attn_prefill_tc_dev``,
+for head dim 128; else the f32 ``b200q_attn_prefill_dev``); the last row goes
 through the output head and argmax like a decode step, so decoding continues
 from there.  bf16 tensor-core operands: logits within 1e-2 of the f32 path.
 """
@@ -180,6 +181,11 @@ class QuantLlama:
         act = torch.empty((T, c.d_ff), dtype=torch.bfloat16, device=dev)
         Dn = torch.empty((T, c.d_model), dtype=torch.float32, device=dev)
         off = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        # head dim 128: causal attention on the tensor cores (bf16 staging copies in scratch)
+        scratch = None
+        if hd == 128:
+            nb = lib.b200q_attn_prefill_tc_scratch_bytes(T, c.n_heads, c.n_kv_heads, hd, c.max_seq)
+            scratch = torch.empty(nb, dtype=torch.uint8, device=dev)
         delta = None
         for li, L in enumerate(self.layers):
             _lib.check(lib.b200q_add_rmsnorm_dev(X.data_ptr(), None if delta is None else delta.data_ptr(),
@@ -191,8 +197,15 @@ class QuantLlama:
             kc, vc = self.k_cache[li], self.v_cache[li]
             _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
                                              self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), c.max_seq, st))
-            _lib.check(lib.b200q_attn_prefill_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.pos.data_ptr(),
-                                                  T, c.n_heads, c.n_kv_heads, hd, c.max_seq, attb.data_ptr(), st))
+            if scratch is not None:
+                _lib.check(lib.b200q_attn_prefill_tc_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                         self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd,
+                                                         c.max_seq, scratch.data_ptr(), scratch.numel(),
+                                                         attb.data_ptr(), st))
+            else:
+                _lib.check(lib.b200q_attn_prefill_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                      self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, c.max_seq,
+                                                      attb.data_ptr(), st))
             wo, so, to = self._gemm_w(('o', li), L['o'], c.d_model, c.d_model)
             ops.gemm_quant(attb, wo, off, k=c.d_model, n_feat=c.d_model, w_rows_per_group=c.d_model, ggml_type=to,
                            w_row_bytes=so, out=O)

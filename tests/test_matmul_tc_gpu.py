@@ -1,6 +1,6 @@
 """The reference's batched matmul boundary on the tensor cores.
 
-``localai_{q4k,q6k,q8_0}_matmul`` (engine/native_quant.cpp:754-768, the
+``localai_{q4k,q5k,q6k,q8_0,q4_0}_matmul`` (engine/native_quant.cpp:749-768, the
 prefill path decoded_matmul_row :620-703) called through ctypes with host
 buffers -- exactly as engine/native_quant.py:130-156 does -- and
 ``DeviceGGUF.matmul`` (engine/gguf_parser.py:290-331) run the tcgen05 GEMM for
@@ -26,7 +26,8 @@ def _launches():
 
 @pytest.mark.parametrize('t,rows,cols,tokens', [(12, 14336, 4096, 512), (12, 4096, 14336, 512),
                                                 (14, 1024, 2048, 333), (8, 1024, 4096, 77),
-                                                (12, 256, 1536, 32), (8, 128, 256, 300)])
+                                                (12, 256, 1536, 32), (8, 128, 256, 300),
+                                                (13, 512, 2048, 100), (2, 256, 1024, 64)])
 def test_drop_in_matmul_on_tensor_cores(t, rows, cols, tokens):
     lib = _lib.load()
     assert lib.b200q_matmul_tensor_core_min_tokens(-1) == 32
@@ -46,7 +47,7 @@ def test_threshold_and_ineligible_shapes_use_the_gemv():
     rng = np.random.default_rng(9)
     cases = [(12, 200, 1024, 64),        # rows not a multiple of 128
              (14, 128, 1024, 64),        # Q6_K rows of 840 bytes (not whole 16-byte units)
-             (13, 256, 1024, 64),        # Q5_K: GEMV only
+             (2, 128, 1056, 64),         # Q4_0 rows of 594 bytes (not whole 16-byte units)
              (12, 256, 1024, 31)]        # below the threshold
     for t, rows, cols, tokens in cases:
         raw = synth.make(rng, t, rows, cols)

@@ -117,4 +117,8 @@ def test_zaya_router_quantised_weights(tmp_path):
         g_e, g_w = ids.cpu().numpy()[:, 0], w.cpu().numpy()[:, 0]
         assert np.mean(g_e == r_e) >= 0.97
         same = g_e == r_e
-        np.testing.assert_allclose(g_w[same], r_w[same], rtol=1e-4, atol=1e-6)
+        # the quantised layers run on the GEMV (fixed-point activations, f32
+        # accumulation across blocks) instead of numpy's f32 matmul: one token
+        # of 200 was measured 7e-4 apart; the reference's own Q4_K kernel is
+        # 5e-3 off (int8 activations)
+        np.testing.assert_allclose(g_w[same], r_w[same], rtol=2e-3, atol=1e-6)
