@@ -511,6 +511,9 @@ def main():
     ap.add_argument('--cpu-tokens', type=int, default=2048, help='token sample of the CPU baseline')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-gemv', action='store_true')
+    ap.add_argument('--ep-unfused', action='store_true',
+                    help='N > 1, p2p: separate send kernel before the expert GEMMs instead of the '
+                         'exchange fused into the gate/up GEMM')
     ap.add_argument('--transport', default='p2p', choices=['p2p', 'nccl'],
                     help='expert-parallel exchange (N > 1): NVLink peer memory or NCCL all-to-all')
     ap.add_argument('--phases', action='store_true',
@@ -571,7 +574,8 @@ def main():
     del parts
     layer = QuantMoE(wr, gate_up, down, d_model=D, d_ff=F, top_k=K_TOP, router_bias=bias, renormalize=True,
                      local_experts=len(mine))
-    step = EPMoE(layer, owner, local, transport=args.transport, max_tokens=T_loc) if world > 1 else layer
+    step = (EPMoE(layer, owner, local, transport=args.transport, max_tokens=T_loc, fused=not args.ep_unfused)
+            if world > 1 else layer)
 
     def barrier():
         if world > 1:
@@ -596,6 +600,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     n0 = lib.b200q_launch_count()
+    g0_launches = getattr(step, 'graph_launches', 0)
     t_start = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -604,7 +609,7 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     t_end = time.time()
-    launches = lib.b200q_launch_count() - n0
+    launches = lib.b200q_launch_count() - n0 + getattr(step, 'graph_launches', 0) - g0_launches
     barrier()
     clocks = sampler.stop(t_start, t_end) if sampler else None
     ms = e0.elapsed_time(e1) / args.steps
@@ -714,7 +719,9 @@ def main():
                 'config': {'workload': WORKLOAD, 'hidden': D, 'experts': E, 'intermediate': F, 'top_k': K_TOP,
                            'tokens': T_TOTAL, 'weights': 'Q4_K', 'router': 'f32 + Zipf(1.1) bias',
                            'parallelism': f'ep{world}' if world > 1 else 'single',
-                           'ep_transport': args.transport if world > 1 else None,
+                           'ep_transport': (args.transport + ('' if args.ep_unfused or args.transport != 'p2p'
+                                                              else ', exchange fused into the gate/up GEMM'))
+                                           if world > 1 else None,
                            'l2': 'inputs larger than L2 (641 MB expert weights, 256 MB hidden states)'},
                 'roofline': roof, 'cpu_baseline': cpu,
                 'e2e': {'value': e2e_value, 'unit': 'tokens/s', 'h2d_bytes_per_step': T_TOTAL * D * 4,

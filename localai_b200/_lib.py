@@ -91,6 +91,8 @@ SIGNATURES = {
     'b200q_ep_send_rows_dev': (_i, [_vp, _vp, _i, _vp, _vp, _i, _u32, _vp]),
     'b200q_ep_send_rows_bf16_dev': (_i, [_vp, _vp, _i, _vp, _vp, _i, _u32, _vp]),
     'b200q_ep_experts_dev': (_i, [_vp, _i, _vp, _ll, _vp, _ll, _i, _vp, _u32, _i, _vp]),
+    'b200q_ep_dispatch_experts_dev': (_i, [_vp, _i, _vp, _ll, _vp, _ll, _i, _vp, _vp, _i, _vp, _vp, _i, _u32, _i,
+                                           _vp]),
     'b200q_ep_combine_dev': (_i, [_vp, _vp, _vp, _i, _i, _vp, _u32, _vp]),
 }
 

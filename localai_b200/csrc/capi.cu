@@ -51,7 +51,7 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
                                int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret,
-                               bool out_t = false);
+                               bool out_t = false, const EpPush *push = nullptr);
 cudaError_t ep_create(int G, int me, int E_loc, int D, long long cap_send, long long cap_recv, void **out);
 cudaError_t ep_ipc_handle(void *ctx, void *handle64);
 size_t ep_ipc_handle_bytes();
@@ -858,6 +858,45 @@ B200Q_API int b200q_ep_experts_dev(void *ep, int ggml_type, const void *gate_up,
     if (e == cudaSuccess) e = launch_ep_signal(ep, epoch, st);
     g_launches += 4;
     return cuda_status(e, "ep_experts");
+}
+
+B200Q_API int b200q_ep_dispatch_experts_dev(void *ep, int ggml_type, const void *gate_up, long long gate_up_row_bytes,
+                                            const void *down, long long down_row_bytes, int d_ff, void *act,
+                                            const void *h_bf16, int T, const int *token_of, const int *offsets,
+                                            int slots, unsigned int epoch, int max_ctas, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!ep || !gate_up || !down || !act || !h_bf16 || !token_of || !offsets)
+        return set_status(B200Q_EINVAL, "ep_dispatch_experts: null pointer");
+    if (d_ff < 64 || d_ff % 64) return set_status(B200Q_EINVAL, "ep_dispatch_experts: d_ff must be a multiple of 64");
+    if (T < 0 || slots < 0 || (long long)slots > ep_cap_send(ep))
+        return set_status(B200Q_EINVAL, "ep_dispatch_experts: more slots than max_send_rows");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int El = ep_local_experts(ep), D = ep_d_model(ep);
+    const long long cap = ep_cap_recv(ep);
+    const int *grp = ep_group_offsets(ep);
+    EpPush push;
+    push.ep = ep_dev(ep);
+    push.h = static_cast<const __nv_bfloat16 *>(h_bf16);
+    push.token_of = token_of;
+    push.offsets = offsets;
+    push.S = slots;
+    push.T = T;
+    push.epoch = epoch;
+    push.wait_ns = ep_wait_ns();
+    cudaError_t e = launch_tc_gemm(ggml_type, static_cast<const __nv_bfloat16 *>(ep_recv_rows(ep)), cap, D, gate_up,
+                                   gate_up_row_bytes, El, 2 * d_ff, d_ff, d_ff, grp, nullptr, El, nullptr, nullptr, 0,
+                                   nullptr, static_cast<__nv_bfloat16 *>(act), d_ff, di->err, di->sms, max_ctas, st,
+                                   nullptr, false, &push);
+    if (e == cudaSuccess)
+        e = launch_tc_gemm(ggml_type, static_cast<const __nv_bfloat16 *>(act), cap, d_ff, down, down_row_bytes, El, D,
+                           -1, D, grp, nullptr, El, nullptr, nullptr, D, nullptr, nullptr, 0, di->err, di->sms,
+                           max_ctas, st, ep_dev(ep));
+    if (e == cudaSuccess) e = launch_ep_signal(ep, epoch, st);
+    g_launches += 3;
+    return cuda_status(e, "ep_dispatch_experts");
 }
 
 B200Q_API int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int T, int k, float *y,

@@ -31,32 +31,7 @@ namespace b200q {
 // with b200q_ep_set_wait_limit_ns; passed to each waiting kernel at launch.
 static unsigned long long g_ep_wait_ns = 5000000000ull;
 void ep_set_wait_ns(unsigned long long ns) { g_ep_wait_ns = ns ? ns : 5000000000ull; }
-
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v)
-{
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
-{
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Wait until *flag has reached ``epoch`` (wrap-safe comparison), for at most
-// limit_ns nanoseconds (and 2^30 polls).
-__device__ bool ep_wait_flag(const uint32_t *flag, uint32_t epoch, int *err, uint64_t limit_ns)
-{
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if ((int)(ld_acquire_sys(flag) - epoch) >= 0) return true;
-        if ((it & 63) == 63 && (global_timer_ns() - t0 > limit_ns || it > (1u << 30))) {
-            atomicExch(err, ERR_WAIT_TIMEOUT);
-            return false;
-        }
-        __nanosleep(100);
-    }
-}
+unsigned long long ep_wait_ns() { return g_ep_wait_ns; }
 
 __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__restrict__ offsets, uint32_t epoch,
                                                         int *err, uint64_t limit_ns)
@@ -71,6 +46,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
         const int c = offsets[v + 1] - offsets[v];
         for (int d = 0; d < G; ++d) ep->peer_shared[d]->inbox[me][v] = c;
     }
+    for (int e = tid; e < El; e += blockDim.x) ep->chunk_done[e] = 0;
     if (tid == 0) {
         ep->done = 0;
         ok_s = 1;

@@ -9,6 +9,7 @@
 // under a time limit.  Flags carry the call's epoch (1, 2, ...), so nothing
 // is ever reset between calls.
 #pragma once
+#include "common.cuh"
 #include <cstdint>
 #include <cuda_bf16.h>
 
@@ -23,6 +24,9 @@ struct EpShared {
     uint32_t ret_flag[EP_MAX_RANKS];    // owner s has written my expert outputs back
     uint32_t pad[64 - 3 * EP_MAX_RANKS];
     int inbox[EP_MAX_RANKS][EP_MAX_EXPERTS];   // [source][virtual expert] row counts
+    // dispatch fused into the gate/up GEMM: chunk_flag[s * E_loc + e] = epoch
+    // once source s has stored every row it sends for my local expert e
+    uint32_t chunk_flag[EP_MAX_EXPERTS];
 };
 
 // Device-resident tables of one rank (not shared).
@@ -33,6 +37,7 @@ struct EpDev {
     int G, me, E_loc, D;
     long long cap_recv, cap_send;
     unsigned int done;                        // CTAs of the send kernel that finished
+    unsigned int chunk_done[EP_MAX_EXPERTS];  // fused dispatch: push warps done with local expert e's rows
     uint32_t epoch;                           // epoch of the current call (device-side counter)
     int blocked;                              // bit d: rank d's receive buffer would overflow
     // Receive layout (expert-major, source-minor), rebuilt by every count exchange:
@@ -43,5 +48,49 @@ struct EpDev {
     // in rank d's receive buffer.
     int dst_off[EP_MAX_EXPERTS];
 };
+
+// Expert-parallel dispatch fused into the gate/up grouped GEMM: while the
+// GEMM runs, one warp of every CTA stores this rank's routed rows into their
+// owners' receive buffers, and each GEMM tile waits only for the rows of its
+// own local expert (chunk_flag) instead of for the whole exchange.
+struct EpPush {
+    const EpDev *ep;            // this rank's device tables
+    const __nv_bfloat16 *h;     // bf16 [T, D] token rows (the router's copy of h)
+    const int *token_of;        // [S] token of each routed slot, dispatch (virtual expert) order
+    const int *offsets;         // [G * E_loc + 1] first slot of each virtual expert
+    int S, T;
+    uint32_t epoch;             // 0: the device-side counter
+    unsigned long long wait_ns; // limit of each wait on a peer's flag
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until *flag has reached ``epoch`` (wrap-safe comparison), for at most
+// limit_ns nanoseconds (and 2^30 polls); on time-out the error word is set.
+__device__ __forceinline__ bool ep_wait_flag(const uint32_t *flag, uint32_t epoch, int *err, uint64_t limit_ns)
+{
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if ((int)(ld_acquire_sys(flag) - epoch) >= 0) return true;
+        if ((it & 63) == 63 && (global_timer_ns() - t0 > limit_ns || it > (1u << 30))) {
+            atomicExch(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+        __nanosleep(100);
+    }
+}
+#endif
+
+unsigned long long ep_wait_ns();
 
 } // namespace b200q

@@ -38,6 +38,7 @@
 
 #include <cuda.h>
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 namespace b200q {
@@ -106,6 +107,9 @@ struct TcArgs {
     // return buffer at row ret_base[g*G + s] + (r - run_off[g*G + s]), through
     // the peer mapping, instead of into out/out_bf16.
     const EpDev *ep_ret;
+    // gate/up mode, optional: expert-parallel dispatch fused into the GEMM
+    // (push.ep != nullptr; row_off is then the receive layout's grp_off)
+    EpPush push;
     int *err;
 };
 
@@ -310,6 +314,67 @@ __device__ __forceinline__ void dequant_q8_0_half(uint32_t chunk, int p, int h, 
     }
 }
 
+// ---------------------------------------------------------------- fused dispatch
+// One warp (w of NW, one per CTA) of this rank's share of the expert-parallel
+// exchange: every routed slot i (dispatch order, virtual expert v = d * E_loc +
+// e owned by rank d) is the bf16 row h[token_of[i]], stored into rank d's
+// receive buffer at row dst_off[v] + (i - offsets[v]) -- the layout the count
+// exchange built (expert-major, source-minor).  Rows go out chunk by chunk of
+// destination-local expert e (e = 0, 1, ...; within a chunk the destinations
+// in the order me+1, me+2, ..., so that the ranks' stores spread over the
+// receivers); after a chunk each warp fences and counts itself in, and the
+// last one raises chunk_flag[me * E_loc + e] at every rank.  A receiver's
+// GEMM tile of local expert e waits for that flag from all G sources only.
+__device__ __forceinline__ void ep_push_rows(const EpPush &pp, int w, int NW, int lane, int *err)
+{
+    const EpDev *ep = pp.ep;
+    const int G = ep->G, me = ep->me, El = ep->E_loc, D = ep->D;
+    const uint32_t epoch = pp.epoch ? pp.epoch : ep->epoch;
+    const int blocked = ep->blocked;
+    const int n_valid = min(pp.S, __ldg(pp.offsets + G * El));   // slots past offsets[E]: bad expert ids, not sent
+    const int n16 = D / 8;                                          // 16-byte pieces per row
+    for (int e = 0; e < El; ++e) {
+        int acc = 0;                                                // rows of this chunk before the run
+        for (int dd = 1; dd <= G; ++dd) {
+            const int d = (me + dd) % G;
+            const int v = d * El + e;
+            const int lo = min(__ldg(pp.offsets + v), n_valid), hi = min(__ldg(pp.offsets + v + 1), n_valid);
+            if (hi > lo && !((blocked >> d) & 1)) {
+                uint4 *dst0 = reinterpret_cast<uint4 *>(ep->peer_recv[d] + (long long)ep->dst_off[v] * D);
+                for (int i = lo + ((w - acc) % NW + NW) % NW; i < hi; i += NW) {
+                    const int t = __ldg(pp.token_of + i);
+                    if (t < 0 || t >= pp.T) {
+                        if (lane == 0) atomicExch(err, ERR_BAD_INDEX);
+                        continue;
+                    }
+                    const uint4 *src = reinterpret_cast<const uint4 *>(pp.h + (long long)t * D);
+                    uint4 *dst = dst0 + (long long)(i - lo) * n16;
+                    int c = lane;
+                    for (; c + 15 * 32 < n16; c += 16 * 32) {          // a 4096-wide row: 16 loads in flight
+                        uint4 r[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) r[u] = __ldg(src + c + 32 * u);
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) dst[c + 32 * u] = r[u];
+                    }
+                    for (; c < n16; c += 32) dst[c] = __ldg(src + c);
+                }
+            }
+            acc += hi - lo;
+        }
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+            const unsigned old = atomicAdd(const_cast<unsigned *>(&ep->chunk_done[e]), 1u);
+            if (old == (unsigned)NW - 1) {
+                __threadfence_system();
+                for (int d = 0; d < G; ++d) st_release_sys(&ep->peer_shared[d]->chunk_flag[me * El + e], epoch);
+            }
+        }
+        __syncwarp();
+    }
+}
+
 // ---------------------------------------------------------------- kernel
 struct TileCoord {
     int g, nt, m0, rows;    // group, weight-row tile, first activation row (local), valid rows
@@ -486,9 +551,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 3) {
         // ------------------------------------------------ activation producer (TMA)
         if (lane == 0) {
-            int q = 0;
+            int q = 0, ready = -1;
+            const EpDev *pep = a.push.ep;
+            const uint32_t pepoch = pep ? (a.push.epoch ? a.push.epoch : pep->epoch) : 0u;
             for (int t = unit; t < total_tiles && ok; t += nunits) {
                 const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
+                if (pep && c.g > ready) {
+                    // fused dispatch: every source's rows of this local expert have landed
+                    const EpShared *mine = pep->peer_shared[pep->me];
+                    for (int s = 0; s < pep->G && ok; ++s)
+                        ok = ep_wait_flag(&mine->chunk_flag[s * pep->E_loc + c.g], pepoch, a.err, a.push.wait_ns);
+                    if (!ok) break;
+                    fence_proxy_async_global();
+                    ready = c.g;
+                }
                 const int xrow = row_off_s[c.g] + c.m0 + (PAIR ? (int)rank * pair_half(c.rows) : 0);
                 for (int ks = 0; ks < ksteps; ++ks, ++q) {
                     const int s = q % B_ST;
@@ -670,6 +746,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         if (a.ep_ret) __threadfence_system();        // peer stores complete before the signal
+    } else if (warp == 2) {
+        // ------------------------------------------------ fused dispatch (push warp)
+        if (a.push.ep) ep_push_rows(a.push, (int)blockIdx.x, (int)gridDim.x, lane, a.err);
     } else if (warp >= 8) {
         // ------------------------------------------------ dequantisers
         const int dt = tid - 256;                   // 0..255
@@ -873,7 +952,7 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
                                const int *group_w, int n_weight_groups, float *out, __nv_bfloat16 *out_bf16,
                                long long ld_out, const float *row_scale, __nv_bfloat16 *act, long long ld_act,
                                int *err, int num_sms, int max_ctas, cudaStream_t st, const EpDev *ep_ret,
-                               bool out_t)
+                               bool out_t, const EpPush *push)
 {
     if (k < TC_BK || k % TC_BK) return cudaErrorInvalidValue;
     // transposed output: plain f32 mode only, no row scale, no peer return
@@ -887,6 +966,10 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
         return cudaErrorInvalidValue;
     if (out_t && (reinterpret_cast<uintptr_t>(out) & 3)) return cudaErrorInvalidValue;
     if (ep_ret && ld_out % 8) return cudaErrorInvalidValue;
+    // fused dispatch: gate/up mode over the receive buffer, bf16 rows of 16-byte pieces
+    if (push && (up_offset < 0 || !push->ep || !push->h || !push->token_of || !push->offsets || push->S < 0 ||
+                 push->T < 0 || (reinterpret_cast<uintptr_t>(push->h) & 15) || groups > EP_MAX_EXPERTS))
+        return cudaErrorInvalidValue;
     if (groups < 1 || groups > TC_MAX_GROUPS || x_rows < 1) return cudaErrorInvalidValue;
     const bool gu = up_offset >= 0;
     if (gu ? (n_feat % 64) : (n_feat % TC_BM)) return cudaErrorInvalidValue;
@@ -934,6 +1017,8 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     a.act = act;
     a.ld_act = ld_act;
     a.ep_ret = ep_ret;
+    if (push) a.push = *push;
+    else std::memset(&a.push, 0, sizeof(a.push));
     a.err = err;
     if (pair) {
         if (wtype == T_Q4_K) return tc_launch<T_Q4_K, true>(mx, mw, a, num_sms, max_ctas, st);

@@ -83,7 +83,7 @@ class EPMoE:
     """
 
     def __init__(self, layer: QuantMoE, owner, local, group=None, *, transport: str = 'nccl',
-                 max_tokens: int | None = None, graph: bool = True):
+                 max_tokens: int | None = None, graph: bool = True, fused: bool = True):
         self.layer = layer
         self.group = group
         self.G = dist.get_world_size(group)
@@ -102,6 +102,12 @@ class EPMoE:
         self.transport = transport
         self.ctx = None
         self.use_graph = graph
+        # library kernels launched by graph replays (the library's own launch
+        # counter sees only the capture)
+        self.graph_launches = 0
+        # p2p: the row exchange runs inside the gate/up GEMM (push warps, per-expert
+        # arrival flags); False: a separate send kernel, then the GEMMs
+        self.fused = fused
         self._graphs = {}
         if transport == 'p2p':
             if max_tokens is None or max_tokens < 1:
@@ -160,12 +166,19 @@ class EPMoE:
         st = _stream()
         _lib.check(lib.b200q_ep_exchange_counts_dev(self.ctx, offsets.data_ptr(), ep, st))
         mark('counts')
-        _lib.check(lib.b200q_ep_send_rows_bf16_dev(self.ctx, hb.data_ptr(), T, token_of.data_ptr(),
-                                                   offsets.data_ptr(), T * L.k, ep, st))
-        mark('send')
-        _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride, L.down.data_ptr(),
-                                            L.dn_stride, L.F, self.act.data_ptr(), ep, 0, st))
-        mark('experts')
+        if self.fused:
+            # rows stored into the owners' buffers by the gate/up GEMM's own push warps
+            _lib.check(lib.b200q_ep_dispatch_experts_dev(
+                self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride, L.down.data_ptr(), L.dn_stride, L.F,
+                self.act.data_ptr(), hb.data_ptr(), T, token_of.data_ptr(), offsets.data_ptr(), T * L.k, ep, 0, st))
+            mark('send+experts')
+        else:
+            _lib.check(lib.b200q_ep_send_rows_bf16_dev(self.ctx, hb.data_ptr(), T, token_of.data_ptr(),
+                                                       offsets.data_ptr(), T * L.k, ep, st))
+            mark('send')
+            _lib.check(lib.b200q_ep_experts_dev(self.ctx, L.type, L.gate_up.data_ptr(), L.gu_stride,
+                                                L.down.data_ptr(), L.dn_stride, L.F, self.act.data_ptr(), ep, 0, st))
+            mark('experts')
         y = torch.empty((T, L.D), dtype=torch.float32, device=dev)
         _lib.check(lib.b200q_ep_combine_dev(self.ctx, slot_of.data_ptr(), slot_w.data_ptr(), T, L.k, y.data_ptr(),
                                             ep, st))
@@ -206,13 +219,16 @@ class EPMoE:
                 self._forward_p2p(static_h)          # eager call: allocations settle (all ranks alike)
             torch.cuda.current_stream(h.device).wait_stream(side)
             graph = torch.cuda.CUDAGraph()
+            n0 = self.layer.lib.b200q_launch_count()
             with torch.cuda.graph(graph):
                 y_static = self._forward_p2p(static_h)
-            entry = (graph, static_h, y_static)
+            n_kernels = self.layer.lib.b200q_launch_count() - n0      # library kernels in the graph
+            entry = (graph, static_h, y_static, n_kernels)
             self._graphs[T] = entry
-        graph, static_h, y_static = entry
+        graph, static_h, y_static, n_kernels = entry
         static_h.copy_(h)
         graph.replay()
+        self.graph_launches += n_kernels
         return y_static.clone()
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:

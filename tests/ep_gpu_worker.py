@@ -69,12 +69,16 @@ def main():
     d = float((p2p(other) - ep(other)).abs().max())
     print(f'rank {rank}: p2p replay on new inputs vs nccl max |diff| {d:.3e}', flush=True)
     good = good and d == 0.0
-    # the eager (non-graph) p2p path alternates with the graph replays
-    p2p_eager = EPMoE(part, owner, local, transport='p2p', max_tokens=n, graph=False)
-    d = float((p2p_eager(shard) - y_ep).abs().max())
-    print(f'rank {rank}: p2p eager vs nccl max |diff| {d:.3e}', flush=True)
-    good = good and d == 0.0
-    p2p_eager.close()
+    # the eager (non-graph) p2p paths alternate with the graph replays: rows
+    # stored by the gate/up GEMM's push warps (fused), or by a separate send
+    # kernel before the GEMMs
+    for fused in (True, False):
+        p2p_eager = EPMoE(part, owner, local, transport='p2p', max_tokens=n, graph=False, fused=fused)
+        for it in range(2):
+            d = float((p2p_eager(shard) - y_ep).abs().max())
+            print(f'rank {rank}: p2p eager (fused={fused}) call {it} vs nccl max |diff| {d:.3e}', flush=True)
+            good = good and d == 0.0
+        p2p_eager.close()
     m = n - 3 - rank                        # ragged: a different token count on every rank
     y_p = p2p(shard[:m])
     y_n = ep(shard[:m])

@@ -94,6 +94,32 @@ def test_fused_route_split_and_unsplit(T, E, D):
         assert torch.equal(plain, logits)
 
 
+@pytest.mark.parametrize('T,E,D', [(2048, 64, 4096), (16384, 64, 4096), (1000, 40, 1056), (129, 64, 4096),
+                                   (64, 64, 4096)])
+def test_router_accuracy_and_bf16_copy(T, E, D):
+    """Router logits within 1e-6 of the float64 product relative to the
+    largest logit, at the headline shape (16384 tokens, one pass) and split
+    K (few tokens), and the bf16 copy of h written on the way equals bf16(h)."""
+    from localai_b200 import _lib
+    rng = np.random.default_rng(T + E)
+    layer = QuantMoE.__new__(QuantMoE)
+    layer.lib = _lib.load()
+    layer.E, layer.D, layer.k, layer.renorm = E, D, 4, 1
+    wr = rng.normal(0, 1 / np.sqrt(D), size=(E, D)).astype(np.float32)
+    bias = rng.normal(scale=0.1, size=E).astype(np.float32)
+    layer.router_w = torch.from_numpy(wr).cuda()
+    layer.router_bias = torch.from_numpy(bias).cuda()
+    layer.sel_bias = None
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    hd = torch.from_numpy(h).cuda()
+    hb = torch.empty((T, D), dtype=torch.bfloat16, device='cuda')
+    logits, ids, w = layer.route(hd, hb)
+    ref = h.astype(np.float64) @ wr.T.astype(np.float64) + bias
+    err = np.abs(logits.cpu().numpy().astype(np.float64) - ref).max() / np.abs(ref).max()
+    assert err < 1e-6, err
+    assert torch.equal(hb, hd.to(torch.bfloat16))
+
+
 def test_router_logits_and_dispatch():
     rng = np.random.default_rng(3)
     E, D, F, k, T = 16, 512, 128, 4, 1000
