@@ -315,52 +315,83 @@ __device__ __forceinline__ void dequant_q8_0_half(uint32_t chunk, int p, int h, 
 }
 
 // ---------------------------------------------------------------- fused dispatch
-// One warp (w of NW, one per CTA) of this rank's share of the expert-parallel
-// exchange: every routed slot i (dispatch order, virtual expert v = d * E_loc +
-// e owned by rank d) is the bf16 row h[token_of[i]], stored into rank d's
-// receive buffer at row dst_off[v] + (i - offsets[v]) -- the layout the count
-// exchange built (expert-major, source-minor).  Rows go out chunk by chunk of
+// The expert-parallel exchange inside the gate/up GEMM (TcArgs::push).  Warp 2
+// of every CTA (idle in the plain GEMM) is a push warp; w of NW = gridDim.x.
+// Every routed slot i (dispatch order, virtual expert v = d * E_loc + e owned
+// by rank d) is the bf16 row h[token_of[i]], stored into rank d's receive
+// buffer at row dst_off[v] + (i - offsets[v]) -- the layout the count exchange
+// built (expert-major, source-minor).  Rows go out chunk by chunk of
 // destination-local expert e (e = 0, 1, ...; within a chunk the destinations
-// in the order me+1, me+2, ..., so that the ranks' stores spread over the
-// receivers); after a chunk each warp fences and counts itself in, and the
-// last one raises chunk_flag[me * E_loc + e] at every rank.  A receiver's
-// GEMM tile of local expert e waits for that flag from all G sources only.
-__device__ __forceinline__ void ep_push_rows(const EpPush &pp, int w, int NW, int lane, int *err)
+// me+1, me+2, ..., so that the ranks' stores spread over the receivers); the
+// rows of a run are dealt round-robin over the push warps.
+// The copy engine is the SM's bulk-copy unit, not the warp's registers: lane 0
+// loads a row (pieces of at most TC_PUSH_ROW bytes) into one slot of a small
+// shared-memory ring (1-D bulk load, completion on the slot's mbarrier) and
+// stores it to the owner with a 1-D bulk store; up to TC_PUSH_NB stores are in
+// flight.  A few instructions per 8 KB row, so the push hardly competes with
+// the GEMM warps for issue slots (a register copy loop did: ~300 GB/s).
+// After a chunk the warp waits for its stores to complete, fences (system
+// scope) and counts itself into chunk_done[e]; the last one raises
+// chunk_flag[me * E_loc + e] at every rank.  A receiver's GEMM tile of local
+// expert e waits for that flag from all G sources only.
+constexpr int TC_PUSH_NB = 3;          // ring slots
+constexpr int TC_PUSH_ROW = 8192;      // bytes per slot (a 4096-wide bf16 row)
+
+__device__ __forceinline__ void ep_push_rows(const EpPush &pp, int w, int NW, int lane, int *err, uint32_t ring,
+                                             uint32_t bars)
 {
     const EpDev *ep = pp.ep;
     const int G = ep->G, me = ep->me, El = ep->E_loc, D = ep->D;
     const uint32_t epoch = pp.epoch ? pp.epoch : ep->epoch;
     const int blocked = ep->blocked;
     const int n_valid = min(pp.S, __ldg(pp.offsets + G * El));   // slots past offsets[E]: bad expert ids, not sent
-    const int n16 = D / 8;                                          // 16-byte pieces per row
+    const uint32_t row_bytes = 2u * (uint32_t)D;
+    uint32_t k = 0;                     // transfers issued by this warp: slot k % NB, use k / NB
+    bool ok = true;
     for (int e = 0; e < El; ++e) {
-        int acc = 0;                                                // rows of this chunk before the run
+        int acc = 0;                    // rows of this chunk before the run
         for (int dd = 1; dd <= G; ++dd) {
             const int d = (me + dd) % G;
             const int v = d * El + e;
             const int lo = min(__ldg(pp.offsets + v), n_valid), hi = min(__ldg(pp.offsets + v + 1), n_valid);
-            if (hi > lo && !((blocked >> d) & 1)) {
-                uint4 *dst0 = reinterpret_cast<uint4 *>(ep->peer_recv[d] + (long long)ep->dst_off[v] * D);
-                for (int i = lo + ((w - acc) % NW + NW) % NW; i < hi; i += NW) {
-                    const int t = __ldg(pp.token_of + i);
+            const int first = lo + ((w - acc) % NW + NW) % NW;          // my rows: first, first + NW, ...
+            const int cnt = (hi > first && !((blocked >> d) & 1)) ? (hi - first + NW - 1) / NW : 0;
+            char *dst0 = reinterpret_cast<char *>(ep->peer_recv[d]) + (long long)ep->dst_off[v] * row_bytes;
+            for (int jb = 0; jb < cnt && ok; jb += 32) {
+                const int tl = jb + lane < cnt ? __ldg(pp.token_of + first + (jb + lane) * NW) : 0;
+                const int nb = min(32, cnt - jb);
+                for (int u = 0; u < nb; ++u) {
+                    const int t = __shfl_sync(0xffffffffu, tl, u);
+                    if (lane != 0 || !ok) continue;
                     if (t < 0 || t >= pp.T) {
-                        if (lane == 0) atomicExch(err, ERR_BAD_INDEX);
+                        atomicExch(err, ERR_BAD_INDEX);
                         continue;
                     }
-                    const uint4 *src = reinterpret_cast<const uint4 *>(pp.h + (long long)t * D);
-                    uint4 *dst = dst0 + (long long)(i - lo) * n16;
-                    int c = lane;
-                    for (; c + 15 * 32 < n16; c += 16 * 32) {          // a 4096-wide row: 16 loads in flight
-                        uint4 r[16];
-#pragma unroll
-                        for (int u = 0; u < 16; ++u) r[u] = __ldg(src + c + 32 * u);
-#pragma unroll
-                        for (int u = 0; u < 16; ++u) dst[c + 32 * u] = r[u];
+                    const char *src = reinterpret_cast<const char *>(pp.h) + (long long)t * row_bytes;
+                    char *dst = dst0 + (long long)(first + (jb + u) * NW - lo) * row_bytes;
+                    for (uint32_t off = 0; off < row_bytes && ok; off += TC_PUSH_ROW, ++k) {
+                        const uint32_t n = min((uint32_t)TC_PUSH_ROW, row_bytes - off);
+                        const uint32_t slot = k % TC_PUSH_NB, bar = bars + 8u * slot;
+                        const uint32_t buf = ring + slot * (uint32_t)TC_PUSH_ROW;
+                        if (k >= TC_PUSH_NB) bulk_wait_read<TC_PUSH_NB - 1>();   // the slot's last store has read it
+                        mbar_arrive_expect_tx(bar, n);
+                        bulk_g2s(buf, src + off, n, bar);
+                        if (!mbar_wait(bar, (k / TC_PUSH_NB) & 1u, err)) {
+                            ok = false;
+                            break;
+                        }
+                        bulk_s2g(dst + off, buf, n);
+                        bulk_commit();
                     }
-                    for (; c < n16; c += 32) dst[c] = __ldg(src + c);
                 }
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             }
             acc += hi - lo;
+        }
+        if (!ok) break;                 // receivers then time out on this chunk and report it
+        if (lane == 0) {
+            bulk_wait_all();            // this chunk's stores have landed
+            fence_proxy_async_global();
         }
         __threadfence_system();
         __syncwarp();
@@ -373,6 +404,7 @@ __device__ __forceinline__ void ep_push_rows(const EpPush &pp, int w, int NW, in
         }
         __syncwarp();
     }
+    if (lane == 0) bulk_wait_all();     // nothing in flight when the warp leaves
 }
 
 // ---------------------------------------------------------------- kernel
@@ -411,14 +443,16 @@ __device__ __forceinline__ TileCoord tile_coord(int t, const int *tile_pref, con
 // ("leader") owns full_a (16 dequant warps of both CTAs arrive), full_b (both
 // CTAs' TMA bytes) and acc_empty (8 epilogue warps); the MMA commits arrive on
 // empty_a / empty_b / acc_full in both CTAs.
-template <int WT, bool PAIR>
+// PUSH = true: the fused expert-parallel dispatch (TcArgs::push) -- one A/B
+// stage fewer, which leaves room for the push warp's ring.
+template <int WT, bool PAIR, bool PUSH>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                    const TcArgs a)
 {
     constexpr int TC_RAW_STAGES = TcW<WT>::RAW;
-    constexpr int A_ST = PAIR ? TC_PAIR_A_STAGES : TC_A_STAGES;
-    constexpr int B_ST = PAIR ? TC_PAIR_B_STAGES : TC_B_STAGES;
+    constexpr int A_ST = PAIR ? (PUSH ? TC_PAIR_A_STAGES - 1 : TC_PAIR_A_STAGES) : TC_A_STAGES;
+    constexpr int B_ST = PAIR ? (PUSH ? TC_PAIR_B_STAGES - 1 : TC_PAIR_B_STAGES) : (PUSH ? TC_B_STAGES - 1 : TC_B_STAGES);
     constexpr int B_BYTES = PAIR ? TC_B_BYTES / 2 : TC_B_BYTES;       // activation rows loaded by this CTA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-aligned base for the swizzled tiles
@@ -428,7 +462,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t sRaw = sB + B_ST * B_BYTES;
     const uint32_t raw_stage_bytes = (uint32_t)(TC_BM * a.raw_chunk_bytes);
     const uint32_t sStg = (sRaw + TC_RAW_STAGES * raw_stage_bytes + 15u) & ~15u;
-    const uint32_t sBar = sStg + 4 * TC_STG_BYTES;
+    const uint32_t sPush = (sStg + 4 * TC_STG_BYTES + 127u) & ~127u;        // push ring (PUSH only)
+    const uint32_t sBar = PUSH ? sPush + TC_PUSH_NB * TC_PUSH_ROW : sStg + 4 * TC_STG_BYTES;
     const uint32_t full_a = sBar;                             // [A]        dequant warps
     const uint32_t empty_a = full_a + 8 * A_ST;               // [A]        MMA commit
     const uint32_t full_b = empty_a + 8 * A_ST;               // [B]        TMA tx
@@ -438,6 +473,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t acc_full = raw_empty + 8 * TC_RAW_STAGES;  // [2]        MMA commit
     const uint32_t acc_empty = acc_full + 16;                 // [2]        epilogue warps
     const uint32_t tmem_slot = acc_empty + 16;
+    const uint32_t push_bar = tmem_slot + 8;                  // [TC_PUSH_NB] push ring loads (PUSH only)
     // the barrier that releases a B stage: its own (one CTA) or the shared A/B one (pair)
     const uint32_t empty_ab = PAIR ? empty_a : empty_b;
     static_assert(!PAIR || A_ST == B_ST, "pair mode releases A and B stages with one commit");
@@ -476,6 +512,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(acc_full + 8 * s, 1);
             mbar_init(acc_empty + 8 * s, PAIR ? 8 : 4);
         }
+        if (PUSH)
+            for (int s = 0; s < TC_PUSH_NB; ++s) mbar_init(push_bar + 8 * s, 1);
         mbar_fence_init();
     }
     // tile prefix over groups (every CTA computes the same table)
@@ -552,7 +590,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ------------------------------------------------ activation producer (TMA)
         if (lane == 0) {
             int q = 0, ready = -1;
-            const EpDev *pep = a.push.ep;
+            const EpDev *pep = PUSH ? a.push.ep : nullptr;
             const uint32_t pepoch = pep ? (a.push.epoch ? a.push.epoch : pep->epoch) : 0u;
             for (int t = unit; t < total_tiles && ok; t += nunits) {
                 const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
@@ -748,7 +786,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (a.ep_ret) __threadfence_system();        // peer stores complete before the signal
     } else if (warp == 2) {
         // ------------------------------------------------ fused dispatch (push warp)
-        if (a.push.ep) ep_push_rows(a.push, (int)blockIdx.x, (int)gridDim.x, lane, a.err);
+        if (PUSH && a.push.ep) ep_push_rows(a.push, (int)blockIdx.x, (int)gridDim.x, lane, a.err, sPush, push_bar);
     } else if (warp >= 8) {
         // ------------------------------------------------ dequantisers
         const int dt = tid - 256;                   // 0..255
@@ -883,12 +921,14 @@ static cudaError_t make_map_raw(CUtensorMap *m, const void *ptr, long long rows,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int WT, bool PAIR>
+template <int WT, bool PAIR, bool PUSH>
 static size_t tc_gemm_smem_bytes()
 {
-    const int a_st = PAIR ? TC_PAIR_A_STAGES : TC_A_STAGES, b_st = PAIR ? TC_PAIR_B_STAGES : TC_B_STAGES;
+    const int a_st = PAIR ? (PUSH ? TC_PAIR_A_STAGES - 1 : TC_PAIR_A_STAGES) : TC_A_STAGES;
+    const int b_st = PAIR ? (PUSH ? TC_PAIR_B_STAGES - 1 : TC_PAIR_B_STAGES) : (PUSH ? TC_B_STAGES - 1 : TC_B_STAGES);
     return 1024 + (size_t)a_st * TC_A_BYTES + (size_t)b_st * (PAIR ? TC_B_BYTES / 2 : TC_B_BYTES) +
-           (size_t)TcW<WT>::RAW * TC_BM * TcW<WT>::CHUNK + 16 + 4 * TC_STG_BYTES + 256;
+           (size_t)TcW<WT>::RAW * TC_BM * TcW<WT>::CHUNK + 16 + 4 * TC_STG_BYTES + 256 +
+           (PUSH ? 128 + (size_t)TC_PUSH_NB * TC_PUSH_ROW + 8 * TC_PUSH_NB : 0);
 }
 
 // CTA pairs (tcgen05 cta_group::2) by default; b200q_gemm_pair_mode(0) selects
@@ -898,13 +938,13 @@ static int g_tc_pairs_used = 0;        // CTA pairs of the last pair-mode launch
 void tc_gemm_set_pair(bool on) { g_tc_pair = on; }
 int tc_gemm_pairs_used() { return g_tc_pairs_used; }
 
-template <int WT, bool PAIR>
+template <int WT, bool PAIR, bool PUSH>
 static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const TcArgs &a, int num_sms, int max_ctas,
                              cudaStream_t st)
 {
     static bool attr = false;
     static int max_pairs = 0;
-    const size_t smem = tc_gemm_smem_bytes<WT, PAIR>();
+    const size_t smem = tc_gemm_smem_bytes<WT, PAIR, PUSH>();
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
     cfg.blockDim = dim3(TC_THREADS);
@@ -919,14 +959,14 @@ static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const
         cfg.numAttrs = 1;
     }
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WT, PAIR, PUSH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
         if (PAIR) {
             // pairs that can be resident at once (one CTA per SM; the SMs of a pair share a GPC)
             cfg.gridDim = dim3(2 * (num_sms / 2));
             int n = 0;
-            e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<WT, PAIR>, &cfg);
+            e = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<WT, PAIR, PUSH>, &cfg);
             if (e != cudaSuccess) return e;
             max_pairs = n;
         }
@@ -937,7 +977,25 @@ static cudaError_t tc_launch(const CUtensorMap &mx, const CUtensorMap &mw, const
     if (units < 1) return cudaErrorInvalidConfiguration;
     cfg.gridDim = dim3(PAIR ? 2 * units : units);
     if (PAIR) g_tc_pairs_used = units;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WT, PAIR>, mx, mw, a);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<WT, PAIR, PUSH>, mx, mw, a);
+}
+
+template <bool PUSH>
+static cudaError_t tc_launch_type(int wtype, bool pair, const CUtensorMap &mx, const CUtensorMap &mw, const TcArgs &a,
+                                  int num_sms, int max_ctas, cudaStream_t st)
+{
+    if (pair) {
+        if (wtype == T_Q4_K) return tc_launch<T_Q4_K, true, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q5_K) return tc_launch<T_Q5_K, true, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q4_0) return tc_launch<T_Q4_0, true, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+        if (wtype == T_Q6_K) return tc_launch<T_Q6_K, true, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+        return tc_launch<T_Q8_0, true, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+    }
+    if (wtype == T_Q4_K) return tc_launch<T_Q4_K, false, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q5_K) return tc_launch<T_Q5_K, false, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q4_0) return tc_launch<T_Q4_0, false, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+    if (wtype == T_Q6_K) return tc_launch<T_Q6_K, false, PUSH>(mx, mw, a, num_sms, max_ctas, st);
+    return tc_launch<T_Q8_0, false, PUSH>(mx, mw, a, num_sms, max_ctas, st);
 }
 
 // Grouped GEMM, Q4_K / Q6_K / Q8_0 weights.
@@ -1020,18 +1078,8 @@ cudaError_t launch_tc_gemm(int wtype, const __nv_bfloat16 *x, long long x_rows, 
     if (push) a.push = *push;
     else std::memset(&a.push, 0, sizeof(a.push));
     a.err = err;
-    if (pair) {
-        if (wtype == T_Q4_K) return tc_launch<T_Q4_K, true>(mx, mw, a, num_sms, max_ctas, st);
-        if (wtype == T_Q5_K) return tc_launch<T_Q5_K, true>(mx, mw, a, num_sms, max_ctas, st);
-        if (wtype == T_Q4_0) return tc_launch<T_Q4_0, true>(mx, mw, a, num_sms, max_ctas, st);
-        if (wtype == T_Q6_K) return tc_launch<T_Q6_K, true>(mx, mw, a, num_sms, max_ctas, st);
-        return tc_launch<T_Q8_0, true>(mx, mw, a, num_sms, max_ctas, st);
-    }
-    if (wtype == T_Q4_K) return tc_launch<T_Q4_K, false>(mx, mw, a, num_sms, max_ctas, st);
-    if (wtype == T_Q5_K) return tc_launch<T_Q5_K, false>(mx, mw, a, num_sms, max_ctas, st);
-    if (wtype == T_Q4_0) return tc_launch<T_Q4_0, false>(mx, mw, a, num_sms, max_ctas, st);
-    if (wtype == T_Q6_K) return tc_launch<T_Q6_K, false>(mx, mw, a, num_sms, max_ctas, st);
-    return tc_launch<T_Q8_0, false>(mx, mw, a, num_sms, max_ctas, st);
+    if (push) return tc_launch_type<true>(wtype, pair, mx, mw, a, num_sms, max_ctas, st);
+    return tc_launch_type<false>(wtype, pair, mx, mw, a, num_sms, max_ctas, st);
 }
 
 } // namespace b200q
