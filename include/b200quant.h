@@ -301,7 +301,8 @@ long long b200q_launch_count(void);
  *                          rank's slots sorted by (owner rank, local expert)
  *                          (b200q_moe_dispatch_dev on virtual expert ids);
  *   b200q_ep_send_rows_dev gather h[token_of[slot]] as bf16 into the owner's
- *                          receive buffer (expert-major, source-minor);
+ *                          receive buffer (expert-major; in a group the
+ *                          receiver's own rows first, then ranks r+1, ...);
  *   b200q_ep_experts_dev   wait for all ranks' rows, gate/up then down on the
  *                          local experts (weights as for b200q_gemm_dev: type,
  *                          row strides, 0 = packed); the down GEMM stores each output row

@@ -5,8 +5,9 @@
 //                      rank's inbox, raise cnt_flag there, wait for all G
 //                      inboxes, then build the receive and send layouts;
 //   ep_send_kernel     gather my routed rows (f32 -> bf16) and store each one
-//                      directly into its owner's receive buffer, expert-major
-//                      and source-minor, then raise row_flag at every rank;
+//                      directly into its owner's receive buffer (expert-major;
+//                      in a group the owner's own rows first, then ranks
+//                      owner+1, ...), then raise row_flag at every rank;
 //   ep_wait_kernel     wait for row_flag (before the GEMMs) or ret_flag
 //                      (before the combine) from all G ranks;
 //   (gate/up GEMM on the received rows; down GEMM whose epilogue stores each
@@ -46,7 +47,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
         const int c = offsets[v + 1] - offsets[v];
         for (int d = 0; d < G; ++d) ep->peer_shared[d]->inbox[me][v] = c;
     }
-    for (int e = tid; e < El; e += blockDim.x) ep->chunk_done[e] = 0;
+    for (int r = tid; r < EP_MAX_ROUNDS; r += blockDim.x) ep->round_done[r] = 0;
     if (tid == 0) {
         ep->done = 0;
         ok_s = 1;
@@ -62,7 +63,12 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
         // no layout: send nothing, receive nothing
         for (int i = tid; i <= El; i += blockDim.x) ep->grp_off[i] = 0;
         for (int i = tid; i <= E; i += blockDim.x) ep->run_off[i] = 0;
-        if (tid == 0) ep->blocked = (1 << G) - 1;
+        if (tid == 0) {
+            ep->blocked = (1 << G) - 1;
+            ep->rounds = 0;
+            ep->rt = 1;
+            ep->r0 = 1;
+        }
         return;
     }
     for (int i = tid; i < G * E; i += blockDim.x) cnt[i / E][i % E] = __ldcg(&mine->inbox[i / E][i % E]);
@@ -81,25 +87,29 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
     const bool me_blocked = (blocked_s >> me) & 1;
     const int vme = me * El;
     for (int i = tid; i < E; i += blockDim.x) {
-        // receive runs: i = e * G + s
+        // receive runs: i = e * G + j, the j-th run of group e, from source
+        // (me + j) % G -- every group starts with this rank's own rows, so that
+        // the first row tiles of every rank are fed by local copies and the
+        // sources' shares of a rank's early tiles rotate with the rank
         {
-            const int e = i / G, s = i % G;
+            const int e = i / G, j = i % G, s = (me + j) % G;
             int r = 0;
             for (int e2 = 0; e2 < e; ++e2)
                 for (int s2 = 0; s2 < G; ++s2) r += cnt[s2][vme + e2];
-            for (int s2 = 0; s2 < s; ++s2) r += cnt[s2][vme + e];
+            for (int j2 = 0; j2 < j; ++j2) r += cnt[(me + j2) % G][vme + e];
             ep->run_off[i] = me_blocked ? 0 : r;
             int b = 0;
             for (int v = 0; v < vme + e; ++v) b += cnt[s][v];
             ep->ret_base[i] = b;
         }
-        // send runs: i = d * El + e (virtual expert)
+        // send runs: i = d * El + e (virtual expert): my run is the
+        // ((me - d) mod G)-th of rank d's group e
         {
             const int d = i / El, e = i % El;
             int r = 0;
             for (int e2 = 0; e2 < e; ++e2)
                 for (int s2 = 0; s2 < G; ++s2) r += cnt[s2][d * El + e2];
-            for (int s2 = 0; s2 < me; ++s2) r += cnt[s2][i];
+            for (int j2 = 0; j2 < (me - d + G) % G; ++j2) r += cnt[(d + j2) % G][i];
             ep->dst_off[i] = r;
         }
     }
@@ -110,7 +120,33 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpDev *ep, const int *__
         ep->grp_off[e] = me_blocked ? 0 : r;
         if (e == El) ep->run_off[E] = me_blocked ? 0 : r;
     }
-    if (tid == 0) ep->blocked = blocked_s;
+    // every rank's group row offsets and row-tile bases (the fused exchange's
+    // rounds); all ranks compute the same tables from the same counts
+    if (tid < G) {
+        const int d = tid;
+        int rows = 0, tiles = 0;
+        for (int g = 0; g <= El; ++g) {
+            ep->dgrp_off[d * (El + 1) + g] = rows;
+            ep->dtile[d * (El + 1) + g] = tiles;
+            if (g == El) break;
+            int m = 0;
+            for (int s2 = 0; s2 < G; ++s2) m += cnt[s2][d * El + g];
+            rows += m;
+            tiles += (m + EP_TILE_ROWS - 1) / EP_TILE_ROWS;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        ep->blocked = blocked_s;
+        int qmax = 0;
+        for (int d = 0; d < G; ++d) qmax = max(qmax, ep->dtile[d * (El + 1) + El]);
+        const int rt = max(1, (qmax + EP_ROUNDS_TARGET - 1) / EP_ROUNDS_TARGET);
+        const int r0 = min(rt, EP_FIRST_ROUND);
+        ep->rt = rt;
+        ep->r0 = r0;
+        // <= 1 + EP_ROUNDS_TARGET + 1 <= EP_MAX_ROUNDS
+        ep->rounds = qmax == 0 ? 0 : qmax <= r0 ? 1 : 1 + (qmax - r0 + rt - 1) / rt;
+    }
 }
 
 // Source rows f32 (converted to bf16 on the way) or already bf16 (the

@@ -3,6 +3,8 @@
 //
 // Each rank owns one exchange region, mapped by every other rank:
 //   [EpShared header | recv rows bf16 [cap_recv, D] | return rows bf16 [cap_send, D]]
+// Receive rows are expert-major; inside an expert's group the runs of the
+// sources follow the order me, me+1, ... (the receiver's own rows first).
 // Senders write straight into the receiver's region (plain stores through the
 // peer mapping; no TMA, no multicast) and raise per-source flags with release
 // stores at system scope; receivers poll their own flags with acquire loads
@@ -17,6 +19,13 @@ namespace b200q {
 
 constexpr int EP_MAX_RANKS = 8;
 constexpr int EP_MAX_EXPERTS = 256;     // G * experts-per-rank
+// Fused exchange: every receiver's rows are cut into GEMM row tiles of
+// EP_TILE_ROWS (group by group) and the tiles into at most EP_ROUNDS_TARGET
+// (+1) rounds of equal tile counts; a source announces each round once its
+// rows of that round have landed at every receiver.
+constexpr int EP_TILE_ROWS = 256;
+constexpr int EP_ROUNDS_TARGET = 16;
+constexpr int EP_MAX_ROUNDS = 32;
 
 struct EpShared {
     uint32_t cnt_flag[EP_MAX_RANKS];    // source s's routing counts have arrived
@@ -24,9 +33,9 @@ struct EpShared {
     uint32_t ret_flag[EP_MAX_RANKS];    // owner s has written my expert outputs back
     uint32_t pad[64 - 3 * EP_MAX_RANKS];
     int inbox[EP_MAX_RANKS][EP_MAX_EXPERTS];   // [source][virtual expert] row counts
-    // dispatch fused into the gate/up GEMM: chunk_flag[s * E_loc + e] = epoch
-    // once source s has stored every row it sends for my local expert e
-    uint32_t chunk_flag[EP_MAX_EXPERTS];
+    // dispatch fused into the gate/up GEMM: round_flag[s][r] = epoch once
+    // source s has stored every row it sends for my row tiles of round r
+    uint32_t round_flag[EP_MAX_RANKS][EP_MAX_ROUNDS];
 };
 
 // Device-resident tables of one rank (not shared).
@@ -37,22 +46,31 @@ struct EpDev {
     int G, me, E_loc, D;
     long long cap_recv, cap_send;
     unsigned int done;                        // CTAs of the send kernel that finished
-    unsigned int chunk_done[EP_MAX_EXPERTS];  // fused dispatch: push warps done with local expert e's rows
+    unsigned int round_done[EP_MAX_ROUNDS];   // fused dispatch: push warps done with round r
     uint32_t epoch;                           // epoch of the current call (device-side counter)
     int blocked;                              // bit d: rank d's receive buffer would overflow
-    // Receive layout (expert-major, source-minor), rebuilt by every count exchange:
+    // Receive layout (expert-major; within a group the sources in the order
+    // me, me+1, ...), rebuilt by every count exchange:
     int grp_off[EP_MAX_EXPERTS + 1];          // [E_loc + 1] rows of local expert e start here
-    int run_off[EP_MAX_EXPERTS + 1];          // [e * G + s] rows from source s for expert e
-    int ret_base[EP_MAX_EXPERTS];             // [e * G + s] first slot of that run in s's slot order
+    int run_off[EP_MAX_EXPERTS + 1];          // [e * G + j] rows from source (me + j) % G for expert e
+    int ret_base[EP_MAX_EXPERTS];             // [e * G + j] first slot of that run in its source's slot order
     // Send layout: rows of my virtual expert v = d * E_loc + e start at dst_off[v]
     // in rank d's receive buffer.
     int dst_off[EP_MAX_EXPERTS];
+    // Every rank's receive layout, for the fused exchange's rounds: rank d's
+    // group g (local expert) starts at row dgrp_off[d * (E_loc + 1) + g] and at
+    // row tile dtile[d * (E_loc + 1) + g] (tiles of EP_TILE_ROWS, group by
+    // group); a round is rt consecutive tiles, rounds = ceil(max tiles / rt).
+    int dgrp_off[EP_MAX_EXPERTS + EP_MAX_RANKS];
+    int dtile[EP_MAX_EXPERTS + EP_MAX_RANKS];
+    int rt, rounds;
 };
 
 // Expert-parallel dispatch fused into the gate/up grouped GEMM: while the
 // GEMM runs, one warp of every CTA stores this rank's routed rows into their
-// owners' receive buffers, and each GEMM tile waits only for the rows of its
-// own local expert (chunk_flag) instead of for the whole exchange.
+// owners' receive buffers, round by round of the receivers' row tiles, and
+// each GEMM tile waits only for its own round (round_flag) instead of for the
+// whole exchange.
 struct EpPush {
     const EpDev *ep;            // this rank's device tables
     const __nv_bfloat16 *h;     // bf16 [T, D] token rows (the router's copy of h)

@@ -102,10 +102,11 @@ struct TcArgs {
                             // (the [rows][tokens] layout of the reference's matmul)
     __nv_bfloat16 *act;     // gate/up mode: act[row * ld_act + f]
     long long ld_act;
-    // plain mode, optional: expert-parallel return.  Row r of group g (a run
-    // of rows received from source rank s) is stored as bf16 into rank s's
-    // return buffer at row ret_base[g*G + s] + (r - run_off[g*G + s]), through
-    // the peer mapping, instead of into out/out_bf16.
+    // plain mode, optional: expert-parallel return.  Row r of group g, in the
+    // j-th run of that group (rows received from source rank s = (me + j) % G),
+    // is stored as bf16 into rank s's return buffer at row ret_base[g*G + j] +
+    // (r - run_off[g*G + j]), through the peer mapping, instead of into
+    // out/out_bf16.
     const EpDev *ep_ret;
     // gate/up mode, optional: expert-parallel dispatch fused into the GEMM
     // (push.ep != nullptr; row_off is then the receive layout's grp_off)
@@ -317,23 +318,25 @@ __device__ __forceinline__ void dequant_q8_0_half(uint32_t chunk, int p, int h, 
 // ---------------------------------------------------------------- fused dispatch
 // The expert-parallel exchange inside the gate/up GEMM (TcArgs::push).  Warp 2
 // of every CTA (idle in the plain GEMM) is a push warp; w of NW = gridDim.x.
-// Every routed slot i (dispatch order, virtual expert v = d * E_loc + e owned
+// Every routed slot i (dispatch order, virtual expert v = d * E_loc + g owned
 // by rank d) is the bf16 row h[token_of[i]], stored into rank d's receive
 // buffer at row dst_off[v] + (i - offsets[v]) -- the layout the count exchange
-// built (expert-major, source-minor).  Rows go out chunk by chunk of
-// destination-local expert e (e = 0, 1, ...; within a chunk the destinations
-// me+1, me+2, ..., so that the ranks' stores spread over the receivers); the
-// rows of a run are dealt round-robin over the push warps.
+// built (expert-major; the sources of a group in the order d, d+1, ...).
+// Order: round by round of the receivers' GEMM row tiles (the count exchange
+// cuts every rank's rows into tiles of EP_TILE_ROWS, group by group, and the
+// tiles into rounds: a short first one, then rounds of rt tiles).  In round r each source stores, for
+// every receiver d (d = me+1, me+2, ...: the ranks' stores spread over the
+// receivers), its rows that fall in d's tiles [r * rt, (r+1) * rt); so the
+// receivers' first tiles fill first, whatever the sizes of the experts.  The
+// rows of a round are dealt round-robin over the push warps.
 // The copy engine is the SM's bulk-copy unit, not the warp's registers: lane 0
 // loads a row (pieces of at most TC_PUSH_ROW bytes) into one slot of a small
 // shared-memory ring (1-D bulk load, completion on the slot's mbarrier) and
 // stores it to the owner with a 1-D bulk store; up to TC_PUSH_NB stores are in
-// flight.  A few instructions per 8 KB row, so the push hardly competes with
-// the GEMM warps for issue slots (a register copy loop did: ~300 GB/s).
-// After a chunk the warp waits for its stores to complete, fences (system
-// scope) and counts itself into chunk_done[e]; the last one raises
-// chunk_flag[me * E_loc + e] at every rank.  A receiver's GEMM tile of local
-// expert e waits for that flag from all G sources only.
+// flight.  After a round the warp waits for its stores to complete, fences
+// (system scope) and counts itself into round_done[r]; the last one raises
+// round_flag[me][r] at every rank.  A receiver's GEMM tile waits for its
+// round's flag from all G sources only.
 constexpr int TC_PUSH_NB = 3;          // ring slots
 constexpr int TC_PUSH_ROW = 8192;      // bytes per slot (a 4096-wide bf16 row)
 
@@ -343,63 +346,77 @@ __device__ __forceinline__ void ep_push_rows(const EpPush &pp, int w, int NW, in
     const EpDev *ep = pp.ep;
     const int G = ep->G, me = ep->me, El = ep->E_loc, D = ep->D;
     const uint32_t epoch = pp.epoch ? pp.epoch : ep->epoch;
-    const int blocked = ep->blocked;
+    const int blocked = ep->blocked, r0t = ep->r0, rt = ep->rt, rounds = ep->rounds;
     const int n_valid = min(pp.S, __ldg(pp.offsets + G * El));   // slots past offsets[E]: bad expert ids, not sent
     const uint32_t row_bytes = 2u * (uint32_t)D;
     uint32_t k = 0;                     // transfers issued by this warp: slot k % NB, use k / NB
     bool ok = true;
-    for (int e = 0; e < El; ++e) {
-        int acc = 0;                    // rows of this chunk before the run
+    for (int r = 0; r < rounds; ++r) {
+        const int q0 = ep_round_first_tile(r, r0t, rt), q1 = ep_round_first_tile(r + 1, r0t, rt);
+        int acc = 0;                    // rows of this round before the current segment
         for (int dd = 1; dd <= G; ++dd) {
             const int d = (me + dd) % G;
-            const int v = d * El + e;
-            const int lo = min(__ldg(pp.offsets + v), n_valid), hi = min(__ldg(pp.offsets + v + 1), n_valid);
-            const int first = lo + ((w - acc) % NW + NW) % NW;          // my rows: first, first + NW, ...
-            const int cnt = (hi > first && !((blocked >> d) & 1)) ? (hi - first + NW - 1) / NW : 0;
-            char *dst0 = reinterpret_cast<char *>(ep->peer_recv[d]) + (long long)ep->dst_off[v] * row_bytes;
-            for (int jb = 0; jb < cnt && ok; jb += 32) {
-                const int tl = jb + lane < cnt ? __ldg(pp.token_of + first + (jb + lane) * NW) : 0;
-                const int nb = min(32, cnt - jb);
-                for (int u = 0; u < nb; ++u) {
-                    const int t = __shfl_sync(0xffffffffu, tl, u);
-                    if (lane != 0 || !ok) continue;
-                    if (t < 0 || t >= pp.T) {
-                        atomicExch(err, ERR_BAD_INDEX);
-                        continue;
-                    }
-                    const char *src = reinterpret_cast<const char *>(pp.h) + (long long)t * row_bytes;
-                    char *dst = dst0 + (long long)(first + (jb + u) * NW - lo) * row_bytes;
-                    for (uint32_t off = 0; off < row_bytes && ok; off += TC_PUSH_ROW, ++k) {
-                        const uint32_t n = min((uint32_t)TC_PUSH_ROW, row_bytes - off);
-                        const uint32_t slot = k % TC_PUSH_NB, bar = bars + 8u * slot;
-                        const uint32_t buf = ring + slot * (uint32_t)TC_PUSH_ROW;
-                        if (k >= TC_PUSH_NB) bulk_wait_read<TC_PUSH_NB - 1>();   // the slot's last store has read it
-                        mbar_arrive_expect_tx(bar, n);
-                        bulk_g2s(buf, src + off, n, bar);
-                        if (!mbar_wait(bar, (k / TC_PUSH_NB) & 1u, err)) {
-                            ok = false;
-                            break;
+            if ((blocked >> d) & 1) continue;
+            const int *tb = ep->dtile + d * (El + 1), *gr = ep->dgrp_off + d * (El + 1);
+            for (int g = 0; g < El; ++g) {
+                const int t0 = tb[g], t1 = tb[g + 1];
+                if (t1 <= q0 || t0 >= q1) continue;
+                // d's rows of this round in group g, and my run there
+                const int r0 = gr[g] + EP_TILE_ROWS * max(q0 - t0, 0);
+                const int r1 = min(gr[g] + EP_TILE_ROWS * (q1 - t0), gr[g + 1]);
+                const int v = d * El + g;
+                const int so = min(__ldg(pp.offsets + v), n_valid);
+                const int nv = min(__ldg(pp.offsets + v + 1), n_valid) - so;
+                const int base = ep->dst_off[v];
+                const int lo = max(r0, base), hi = min(r1, base + nv);        // rows in d's buffer
+                if (hi <= lo) continue;
+                const int first = lo + ((w - acc) % NW + NW) % NW;          // my rows: first, first + NW, ...
+                const int cnt = hi > first ? (hi - first + NW - 1) / NW : 0;
+                char *dst0 = reinterpret_cast<char *>(ep->peer_recv[d]);
+                for (int jb = 0; jb < cnt && ok; jb += 32) {
+                    const int tl = jb + lane < cnt ? __ldg(pp.token_of + so + (first + (jb + lane) * NW - base)) : 0;
+                    const int nb = min(32, cnt - jb);
+                    for (int u = 0; u < nb; ++u) {
+                        const int t = __shfl_sync(0xffffffffu, tl, u);
+                        if (lane != 0 || !ok) continue;
+                        if (t < 0 || t >= pp.T) {
+                            atomicExch(err, ERR_BAD_INDEX);
+                            continue;
                         }
-                        bulk_s2g(dst + off, buf, n);
-                        bulk_commit();
+                        const char *src = reinterpret_cast<const char *>(pp.h) + (long long)t * row_bytes;
+                        char *dst = dst0 + (long long)(first + (jb + u) * NW) * row_bytes;
+                        for (uint32_t off = 0; off < row_bytes && ok; off += TC_PUSH_ROW, ++k) {
+                            const uint32_t n = min((uint32_t)TC_PUSH_ROW, row_bytes - off);
+                            const uint32_t slot = k % TC_PUSH_NB, bar = bars + 8u * slot;
+                            const uint32_t buf = ring + slot * (uint32_t)TC_PUSH_ROW;
+                            if (k >= TC_PUSH_NB) bulk_wait_read<TC_PUSH_NB - 1>();   // the slot's last store has read it
+                            mbar_arrive_expect_tx(bar, n);
+                            bulk_g2s(buf, src + off, n, bar);
+                            if (!mbar_wait(bar, (k / TC_PUSH_NB) & 1u, err)) {
+                                ok = false;
+                                break;
+                            }
+                            bulk_s2g(dst + off, buf, n);
+                            bulk_commit();
+                        }
                     }
+                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                 }
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                acc += hi - lo;
             }
-            acc += hi - lo;
         }
-        if (!ok) break;                 // receivers then time out on this chunk and report it
+        if (!ok) break;                 // receivers then time out on this round and report it
         if (lane == 0) {
-            bulk_wait_all();            // this chunk's stores have landed
+            bulk_wait_all();            // this round's stores have landed
             fence_proxy_async_global();
         }
         __threadfence_system();
         __syncwarp();
         if (lane == 0) {
-            const unsigned old = atomicAdd(const_cast<unsigned *>(&ep->chunk_done[e]), 1u);
+            const unsigned old = atomicAdd(const_cast<unsigned *>(&ep->round_done[r]), 1u);
             if (old == (unsigned)NW - 1) {
                 __threadfence_system();
-                for (int d = 0; d < G; ++d) st_release_sys(&ep->peer_shared[d]->chunk_flag[me * El + e], epoch);
+                for (int d = 0; d < G; ++d) st_release_sys(&ep->peer_shared[d]->round_flag[me][r], epoch);
             }
         }
         __syncwarp();
@@ -477,6 +494,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // the barrier that releases a B stage: its own (one CTA) or the shared A/B one (pair)
     const uint32_t empty_ab = PAIR ? empty_a : empty_b;
     static_assert(!PAIR || A_ST == B_ST, "pair mode releases A and B stages with one commit");
+    static_assert(TC_BN == EP_TILE_ROWS, "the fused exchange's rounds are made of GEMM row tiles");
     __shared__ int tile_pref[TC_MAX_GROUPS + 1];
     __shared__ int row_off_s[TC_MAX_GROUPS + 1];
     __shared__ int group_w_s[TC_MAX_GROUPS];
@@ -536,7 +554,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int G = ep->G, nrun = a.groups * G;
         for (int i = lane; i <= nrun; i += 32) ret_run_s[i] = ep->run_off[i];
         for (int i = lane; i < nrun; i += 32) ret_base_s[i] = ep->ret_base[i];
-        if (lane < G) ret_peer_s[lane] = ep->peer_ret[lane];
+        if (lane < G) ret_peer_s[lane] = ep->peer_ret[(ep->me + lane) % G];     // by run position
         if (lane == 0) ret_G = G;
     }
     if (warp == 1) {
@@ -594,14 +612,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t pepoch = pep ? (a.push.epoch ? a.push.epoch : pep->epoch) : 0u;
             for (int t = unit; t < total_tiles && ok; t += nunits) {
                 const TileCoord c = tile_coord(t, tile_pref, row_off_s, a.groups, n_units_w);
-                if (pep && c.g > ready) {
-                    // fused dispatch: every source's rows of this local expert have landed
-                    const EpShared *mine = pep->peer_shared[pep->me];
-                    for (int s = 0; s < pep->G && ok; ++s)
-                        ok = ep_wait_flag(&mine->chunk_flag[s * pep->E_loc + c.g], pepoch, a.err, a.push.wait_ns);
-                    if (!ok) break;
-                    fence_proxy_async_global();
-                    ready = c.g;
+                if (pep) {
+                    // fused dispatch: every source's rows of this tile's round have landed
+                    const int rnd = ep_round_of_tile(pep->dtile[pep->me * (pep->E_loc + 1) + c.g] + c.m0 / EP_TILE_ROWS,
+                                                     pep->r0, pep->rt);
+                    if (rnd > ready) {
+                        const EpShared *mine = pep->peer_shared[pep->me];
+                        for (int s = 0; s < pep->G && ok; ++s)
+                            ok = ep_wait_flag(&mine->round_flag[s][rnd], pepoch, a.err, a.push.wait_ns);
+                        if (!ok) break;
+                        fence_proxy_async_global();
+                        ready = rnd;
+                    }
                 }
                 const int xrow = row_off_s[c.g] + c.m0 + (PAIR ? (int)rank * pair_half(c.rows) : 0);
                 for (int ks = 0; ks < ksteps; ++ks, ++q) {
