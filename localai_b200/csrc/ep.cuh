@@ -20,12 +20,19 @@ namespace b200q {
 constexpr int EP_MAX_RANKS = 8;
 constexpr int EP_MAX_EXPERTS = 256;     // G * experts-per-rank
 // Fused exchange: every receiver's rows are cut into GEMM row tiles of
-// EP_TILE_ROWS (group by group) and the tiles into at most EP_ROUNDS_TARGET
-// (+1) rounds of equal tile counts; a source announces each round once its
-// rows of that round have landed at every receiver.
+// EP_TILE_ROWS (group by group) and the tiles into rounds: a first round of
+// at most EP_FIRST_ROUND tiles (about what the GEMM's first wave of tiles
+// reads), then rounds of rt tiles, at most EP_ROUNDS_TARGET + 2 in all; a
+// source announces each round once its rows of that round have landed at
+// every receiver.
 constexpr int EP_TILE_ROWS = 256;
 constexpr int EP_ROUNDS_TARGET = 16;
+constexpr int EP_FIRST_ROUND = 8;
 constexpr int EP_MAX_ROUNDS = 32;
+
+// Round of row tile q (EpDev::r0, rt) and first tile of round r.
+__host__ __device__ inline int ep_round_of_tile(int q, int r0, int rt) { return q < r0 ? 0 : 1 + (q - r0) / rt; }
+__host__ __device__ inline int ep_round_first_tile(int r, int r0, int rt) { return r == 0 ? 0 : r0 + (r - 1) * rt; }
 
 struct EpShared {
     uint32_t cnt_flag[EP_MAX_RANKS];    // source s's routing counts have arrived
@@ -60,10 +67,11 @@ struct EpDev {
     // Every rank's receive layout, for the fused exchange's rounds: rank d's
     // group g (local expert) starts at row dgrp_off[d * (E_loc + 1) + g] and at
     // row tile dtile[d * (E_loc + 1) + g] (tiles of EP_TILE_ROWS, group by
-    // group); a round is rt consecutive tiles, rounds = ceil(max tiles / rt).
+    // group); round 0 is tiles [0, r0), round r > 0 tiles
+    // [r0 + (r-1) rt, r0 + r rt); ``rounds`` covers the largest layout.
     int dgrp_off[EP_MAX_EXPERTS + EP_MAX_RANKS];
     int dtile[EP_MAX_EXPERTS + EP_MAX_RANKS];
-    int rt, rounds;
+    int r0, rt, rounds;
 };
 
 // Expert-parallel dispatch fused into the gate/up grouped GEMM: while the
