@@ -177,6 +177,12 @@ int b200q_moe_gather_f32_dev(const float *h, int h_rows, const int *token_of, in
  * b200q_moe_gather_f32_dev. */
 int b200q_moe_gather_bf16_dev(const void *h_bf16, int h_rows, const int *token_of, int S, int D, void *out,
                               void *stream);
+/* The same rows by token: out[slot_of[t * k + j]] = h_bf16[t] for every pair
+ * with a slot (slot_of >= 0; slot_of as b200q_moe_dispatch_dev writes it,
+ * [T * k]); each row is read once and stored k times (k <= 32).  A slot at or
+ * past S sets the device error word. */
+int b200q_moe_scatter_bf16_dev(const void *h_bf16, int T, const int *slot_of, int k, int S, int d_model, void *out,
+                               void *stream);
 /* Grouped GEMM as b200q_gemm_q4k_dev for Q4_K (12), Q5_K (13), Q6_K (14),
  * Q8_0 (8) or Q4_0 (2) weights.  w_row_bytes is the byte distance between
  * weight rows (0: packed rows of k values); it must be a multiple of 16, so

@@ -53,6 +53,7 @@ SIGNATURES = {
     'b200q_gemv_grouped_dev': (_i, [_i, _vp, _ll, _ll, _i, _vp, _vp, _vp, _ll, _i, _i, _i, _i, _i, _vp]),
     'b200q_moe_gather_f32_dev': (_i, [_vp, _i, _vp, _i, _i, _vp, _vp]),
     'b200q_moe_gather_bf16_dev': (_i, [_vp, _i, _vp, _i, _i, _vp, _vp]),
+    'b200q_moe_scatter_bf16_dev': (_i, [_vp, _i, _vp, _i, _i, _i, _vp, _vp]),
     'b200q_gemm_dev': (_i, [_i, _vp, _ll, _i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _ll, _vp, _vp, _ll,
                             _i, _vp]),
     'b200q_moe_router_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),

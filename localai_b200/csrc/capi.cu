@@ -37,6 +37,8 @@ cudaError_t launch_moe_route(const float *h, const float *wr, const float *bias,
 cudaError_t launch_moe_dispatch(const int *ids, const float *wts, int T, int k, int E, const float *h, int D,
                                 int *block_counts, int *base, int *offsets, int *slot_of, int *token_of,
                                 float *slot_w, __nv_bfloat16 *xperm, int *err, cudaStream_t st);
+cudaError_t launch_moe_scatter_bf16(const __nv_bfloat16 *h, int T, const int *slot_of, int k, int S, int D,
+                                    __nv_bfloat16 *out, int *err, cudaStream_t st);
 cudaError_t launch_moe_combine(const void *out, bool out_bf16, long long n_rows, const int *slot_of,
                                const float *slot_w, int T, int k,
                                int D, float *y, cudaStream_t st);
@@ -603,6 +605,19 @@ B200Q_API int b200q_moe_gather_bf16_dev(const void *h_bf16, int h_rows, const in
     return cuda_status(launch_moe_gather_bf16(static_cast<const __nv_bfloat16 *>(h_bf16), h_rows, token_of, S, D,
                                               static_cast<__nv_bfloat16 *>(out), di->err, (cudaStream_t)stream),
                        "gather_bf16");
+}
+
+B200Q_API int b200q_moe_scatter_bf16_dev(const void *h_bf16, int T, const int *slot_of, int k, int S, int D, void *out,
+                                         void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!h_bf16 || !slot_of || !out) return set_status(B200Q_EINVAL, "scatter_bf16: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_moe_scatter_bf16(static_cast<const __nv_bfloat16 *>(h_bf16), T, slot_of, k, S, D,
+                                               static_cast<__nv_bfloat16 *>(out), di->err, (cudaStream_t)stream),
+                       "scatter_bf16");
 }
 
 B200Q_API int b200q_moe_router_dev(const float *h, const float *wr, const float *bias, float *logits, int T, int E,

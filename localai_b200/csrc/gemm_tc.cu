@@ -149,10 +149,11 @@ __device__ __forceinline__ void dequant_q4k_half(uint32_t raw_row, const uint4 h
         for (int ww = 0; ww < 2; ++ww) {
             const uint32_t wd = w[2 * c + ww];
             const uint32_t nib = h ? ((wd >> 4) & 0x0F0F0F0Fu) : (wd & 0x0F0F0F0Fu);
-            float v[4];
+            float f[4], v[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-                v[b] = fmaf(A, __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7044u | (uint32_t)(b << 8))), B);
+            for (int b = 0; b < 4; ++b) f[b] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7044u | (uint32_t)(b << 8)));
+            ffma2(v[0], v[1], A, A, f[0], f[1], B, B);           // two values per instruction
+            ffma2(v[2], v[3], A, A, f[2], f[3], B, B);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }

@@ -384,6 +384,52 @@ cudaError_t launch_moe_gather_bf16(const __nv_bfloat16 *h, int T, const int *tok
     return cudaGetLastError();
 }
 
+// The same rows written the other way round: out[slot_of[t*k + j], :] =
+// h[t, :] for every token t and j < k whose pair owns a slot (slot_of >= 0).
+// One warp per token reads its row once (16 loads of 16 bytes in flight per
+// lane for a 4096-wide row) and stores it k times, so the source rows cross
+// the memory system once instead of k times (k <= 32).  A slot at or past S
+// is an error and is skipped.
+__global__ void moe_scatter_bf16_kernel(const __nv_bfloat16 *__restrict__ h, int T, const int *__restrict__ slot_of,
+                                        int k, long long S, int D, __nv_bfloat16 *__restrict__ out, int *err)
+{
+    const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    int mine = lane < k ? __ldg(slot_of + t * k + lane) : -1;
+    if (mine >= S) {
+        atomicExch(err, ERR_BAD_INDEX);
+        mine = -1;
+    }
+    const uint4 *src = reinterpret_cast<const uint4 *>(h + t * D);
+    const int n = D / 8;
+    for (int c0 = 0; c0 < n; c0 += 16 * 32) {
+        uint4 r[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+            if (c0 + 32 * u + lane < n) r[u] = __ldg(src + c0 + 32 * u + lane);
+        for (int j = 0; j < k; ++j) {
+            const int slot = __shfl_sync(0xffffffffu, mine, j);
+            if (slot < 0) continue;                                   // warp-uniform
+            uint4 *dst = reinterpret_cast<uint4 *>(out + (long long)slot * D);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (c0 + 32 * u + lane < n) dst[c0 + 32 * u + lane] = r[u];
+        }
+    }
+}
+
+cudaError_t launch_moe_scatter_bf16(const __nv_bfloat16 *h, int T, const int *slot_of, int k, int S, int D,
+                                    __nv_bfloat16 *out, int *err, cudaStream_t st)
+{
+    if (S < 1 || T < 1 || k < 1 || k > 32 || D < 8 || D % 8 || (reinterpret_cast<uintptr_t>(h) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    moe_scatter_bf16_kernel<<<(unsigned)(((long long)T * 32 + 255) / 256), 256, 0, st>>>(h, T, slot_of, k, S, D, out,
+                                                                                        err);
+    return cudaGetLastError();
+}
+
 // xperm[slot, :] = bf16(h[token_of[slot], :]) for slots below offsets[E]; one warp per slot row.
 __global__ void moe_gather_kernel(const float *__restrict__ h, int T, const int *__restrict__ token_of, long long S,
                                   const int *__restrict__ n_valid, int D, __nv_bfloat16 *__restrict__ xperm, int *err)

@@ -7,7 +7,7 @@ same block batched over T tokens and generalised to top-k:
     logits = h @ Wr^T (+ router bias), hb = bf16(h)   b200q_moe_route_bf16_dev
     p = softmax(logits); top-k of p (+ sel bias)      (same call)
     stable counting sort of (token, j) by expert      b200q_moe_dispatch_dev
-    xperm[slot] = hb[token_of[slot]]                  b200q_moe_gather_bf16_dev
+    xperm[slot_of[t, j]] = hb[t]                      b200q_moe_scatter_bf16_dev
     act = SiLU(gate x) * (up x)  per expert           b200q_gemm_dev (gate/up mode, tcgen05)
     out = w_slot * (down act)    per expert           b200q_gemm_dev (plain mode, tcgen05; bf16 rows)
     y[t] = sum_j out[slot(t, j)]                      b200q_moe_combine_dev
@@ -174,6 +174,14 @@ class QuantMoE:
             token_of.data_ptr(), slot_w.data_ptr(), None if xperm is None else xperm.data_ptr(), _stream()))
         return offsets, slot_of, token_of, slot_w, xperm
 
+    def scatter_bf16(self, hb: torch.Tensor, slot_of: torch.Tensor, S: int) -> torch.Tensor:
+        """xperm[slot_of[t, j]] = hb[t]: the rows of gather_bf16, each token row
+        read once and stored k times."""
+        xperm = torch.empty((S, self.D), dtype=torch.bfloat16, device=hb.device)
+        _lib.check(self.lib.b200q_moe_scatter_bf16_dev(hb.data_ptr(), hb.shape[0], slot_of.data_ptr(), self.k, S,
+                                                       self.D, xperm.data_ptr(), _stream()))
+        return xperm
+
     def gather_bf16(self, hb: torch.Tensor, token_of: torch.Tensor) -> torch.Tensor:
         """xperm[s] = hb[token_of[s]] (bf16 rows grouped by expert)."""
         S = token_of.numel()
@@ -256,7 +264,9 @@ class QuantMoE:
         hb = torch.empty((T, self.D), dtype=torch.bfloat16, device=h.device)
         _, ids, w = self.route(h, hb)
         offsets, slot_of, token_of, slot_w, _ = self.dispatch(h, ids, w, gather=False)
-        out = self.experts(self.gather_bf16(hb, token_of), offsets, slot_w)
+        xperm = (self.scatter_bf16(hb, slot_of, token_of.numel()) if self.k <= 32
+                 else self.gather_bf16(hb, token_of))
+        out = self.experts(xperm, offsets, slot_w)
         return self.combine(out, slot_of, T)
 
     def forward_host(self, h_host: torch.Tensor, y_host: torch.Tensor | None = None, chunks: int = 4,

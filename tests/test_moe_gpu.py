@@ -120,6 +120,29 @@ def test_router_accuracy_and_bf16_copy(T, E, D):
     assert torch.equal(hb, hd.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize('T,E,k,D', [(16384, 64, 8, 4096), (1000, 16, 4, 512), (77, 8, 8, 8200)])
+def test_scatter_equals_gather(T, E, k, D):
+    """b200q_moe_scatter_bf16_dev (each token row read once, stored k times)
+    fills the same rows as b200q_moe_gather_bf16_dev, bit for bit; D = 8200
+    exercises the partial last chunk of the row loop."""
+    from localai_b200 import _lib
+    rng = np.random.default_rng(T + k)
+    layer = QuantMoE.__new__(QuantMoE)
+    layer.lib = _lib.load()
+    layer.E, layer.D, layer.k = E, D, k
+    ids = torch.from_numpy(np.argsort(rng.random((T, E)), axis=1)[:, :k].astype(np.int32)).cuda()
+    w = torch.rand((T, k), device='cuda')
+    hb = torch.randn((T, D), device='cuda').to(torch.bfloat16)
+    offsets, slot_of, token_of, slot_w, _ = layer.dispatch(hb, ids, w, gather=False)
+    a = layer.gather_bf16(hb, token_of)
+    b = layer.scatter_bf16(hb, slot_of, token_of.numel())
+    torch.cuda.synchronize()
+    n = int(offsets[-1])
+    assert n == T * k
+    assert torch.equal(a[:n], b[:n])
+    assert layer.lib.b200q_check_device_error() == 0
+
+
 def test_router_logits_and_dispatch():
     rng = np.random.default_rng(3)
     E, D, F, k, T = 16, 512, 128, 4, 1000
