@@ -188,10 +188,11 @@ __device__ __forceinline__ void dequant_q5k_half(uint32_t raw_row, const uint4 h
             const uint32_t wd = w[2 * c + ww];
             const uint32_t nib = h ? ((wd >> 4) & 0x0F0F0F0Fu) : (wd & 0x0F0F0F0Fu);
             const uint32_t q = nib | (((qh[2 * c + ww] >> g) & 0x01010101u) << 4);
-            float v[4];
+            float f[4], v[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-                v[b] = fmaf(A, __uint_as_float(__byte_perm(q, 0x3F000000u, 0x7044u | (uint32_t)(b << 8))), B);
+            for (int b = 0; b < 4; ++b) f[b] = __uint_as_float(__byte_perm(q, 0x3F000000u, 0x7044u | (uint32_t)(b << 8)));
+            ffma2(v[0], v[1], A, A, f[0], f[1], B, B);
+            ffma2(v[2], v[3], A, A, f[2], f[3], B, B);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }
@@ -252,10 +253,12 @@ __device__ __forceinline__ void dequant_q6k_half(uint32_t blk, int p, int h, uin
             const uint32_t nib = hi_nib ? ((ql[wi] >> 4) & 0x0F0F0F0Fu) : (ql[wi] & 0x0F0F0F0Fu);
             const uint32_t q = nib | (((qh[wi] >> sh) & 0x03030303u) << 4);
             const float sc = wi < 4 ? s0 : s1;
-            float v[4];
+            float f[4], v[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b)       // 2^23 + q - (2^23 + 32) = q - 32, exact
-                v[b] = sc * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388640.0f);
+                f[b] = __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b));
+            fsubmul2(v[0], v[1], sc, f[0], f[1], 8388640.0f);
+            fsubmul2(v[2], v[3], sc, f[2], f[3], 8388640.0f);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }
@@ -280,10 +283,12 @@ __device__ __forceinline__ void dequant_q4_0_half(uint32_t chunk, int p, int h, 
         for (int ww = 0; ww < 2; ++ww) {
             const uint32_t wd = qs[2 * (c & 1) + ww];
             const uint32_t q = c < 2 ? (wd & 0x0F0F0F0Fu) : ((wd >> 4) & 0x0F0F0F0Fu);
-            float v[4];
+            float f[4], v[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b)       // 2^23 + q - (2^23 + 8) = q - 8, exact
-                v[b] = d * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388616.0f);
+                f[b] = __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b));
+            fsubmul2(v[0], v[1], d, f[0], f[1], 8388616.0f);
+            fsubmul2(v[2], v[3], d, f[2], f[3], 8388616.0f);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }
@@ -305,10 +310,12 @@ __device__ __forceinline__ void dequant_q8_0_half(uint32_t chunk, int p, int h, 
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
             const uint32_t q = qs[2 * c + ww] ^ 0x80808080u;   // int8 + 128
-            float v[4];
+            float f[4], v[4];
 #pragma unroll
             for (int b = 0; b < 4; ++b)       // 2^23 + (q + 128) - (2^23 + 128) = q, exact
-                v[b] = d * (__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388736.0f);
+                f[b] = __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540u | (uint32_t)b));
+            fsubmul2(v[0], v[1], d, f[0], f[1], 8388736.0f);
+            fsubmul2(v[2], v[3], d, f[2], f[3], 8388736.0f);
             o[2 * ww] = pack_bf16(v[0], v[1]);
             o[2 * ww + 1] = pack_bf16(v[2], v[3]);
         }

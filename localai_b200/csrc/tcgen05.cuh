@@ -216,6 +216,16 @@ __device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, 
         : "=f"(d0), "=f"(d1)
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
+// d = s * (x - c) for two values (packed f32x2 add and multiply; each lane
+// rounds exactly as the scalar x - c then s * that).
+__device__ __forceinline__ void fsubmul2(float &d0, float &d1, float s, float x0, float x1, float c)
+{
+    asm("{\n\t.reg .b64 rx, rc, rs, rd;\n\t"
+        "mov.b64 rx, {%2, %3};\n\tmov.b64 rc, {%4, %4};\n\tmov.b64 rs, {%5, %5};\n\t"
+        "add.rn.f32x2 rd, rx, rc;\n\tmul.rn.f32x2 rd, rs, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(x0), "f"(x1), "f"(-c), "f"(s));
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi)
 {
     __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
