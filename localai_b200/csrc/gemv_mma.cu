@@ -272,15 +272,24 @@ __global__ void __launch_bounds__(GM_THREADS, 2) gemv_q4k_mma_kernel(const __gri
     if (lane == 0)
         for (int i = 0; i < a.stages; ++i) issue_next();
 
-    // ---- quantise x into the fragment tables (x may come from the previous kernel)
-    pdl_wait();
+    // tile counters zeroed before any warp can finish a tile (shared memory,
+    // not the previous kernel's output: done before the dependency wait)
     for (int i = threadIdx.x; i < a.max_tiles; i += GM_THREADS) cnt[i] = 0;
-    for (int b0 = warp; b0 < a.nsb; b0 += 4 * GM_NW) {
+    __syncthreads();
+
+    // ---- quantise x into the fragment tables (x may come from the previous kernel).
+    // A warp reads only the super-blocks it owns (c * csb + warp * SPW + i of
+    // every chunk c), so each warp quantises exactly those and starts on its
+    // weights without waiting for the other warps.
+    pdl_wait();
+    const int nown = a.nchunk * SPW;
+    auto owned = [&](int j) { return (j / SPW) * csb + warp * SPW + j % SPW; };
+    for (int j0 = 0; j0 < nown; j0 += 4) {
         float4 v[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int b = b0 + i * GM_NW;
-            if (b < a.nsb) {
+            const int b = owned(j0 + i);
+            if (j0 + i < nown && b < a.nsb) {
                 const float4 *p = reinterpret_cast<const float4 *>(a.x + (long long)b * 256 + 8 * lane);
                 v[i][0] = __ldg(p);
                 v[i][1] = __ldg(p + 1);
@@ -288,13 +297,13 @@ __global__ void __launch_bounds__(GM_THREADS, 2) gemv_q4k_mma_kernel(const __gri
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int b = b0 + i * GM_NW;
-            if (b < a.nsb)                                             // warp-uniform condition
+            const int b = owned(j0 + i);
+            if (j0 + i < nown && b < a.nsb)                          // warp-uniform condition
                 gm_quantize_sb(v[i], b, reinterpret_cast<uint32_t *>(smem + (xb - sbase)),
                                reinterpret_cast<float *>(smem + (xs - sbase)), lane);
         }
     }
-    __syncthreads();
+    __syncwarp();
 
     const int g = lane >> 2, t = lane & 3;
     // selection masks: column pair i of a set belongs to sub-block i of that set
