@@ -344,10 +344,12 @@ int b200q_ep_experts_dev(void *ep, int ggml_type, const void *gate_up, long long
 /* The exchange fused into the gate/up GEMM (replaces b200q_ep_send_rows_bf16_dev
  * + b200q_ep_experts_dev after b200q_ep_exchange_counts_dev): one warp of every
  * GEMM CTA stores this rank's routed rows h_bf16[token_of[slot]] into their
- * owners' receive buffers, one destination-local expert at a time, and each
- * GEMM tile waits only until every rank has stored the rows of its own local
- * expert, so the NVLink transfer overlaps the tensor-core work.  Same
- * arguments and results as the two calls it replaces (bit-identical). */
+ * owners' receive buffers with bulk copies, round by round of the receivers'
+ * GEMM row tiles, and each GEMM tile waits only until every rank has stored
+ * the rows of its own round, so the NVLink transfer overlaps the tensor-core
+ * work.  Same arguments and results as the two calls it replaces
+ * (bit-identical).  All CTAs of the launch must be resident together (the
+ * grid is sized so); a wait that runs out sets the device error word. */
 int b200q_ep_dispatch_experts_dev(void *ep, int ggml_type, const void *gate_up, long long gate_up_row_bytes,
                                   const void *down, long long down_row_bytes, int d_ff, void *act,
                                   const void *h_bf16, int T, const int *token_of, const int *offsets, int slots,
