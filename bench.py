@@ -518,7 +518,7 @@ def main():
                     help='expert-parallel exchange (N > 1): NVLink peer memory or NCCL all-to-all')
     ap.add_argument('--phases', action='store_true',
                     help='N > 1, p2p: add per-rank stage times of one layer call ("ep_phases")')
-    ap.add_argument('--e2e-chunks', type=str, default='1,2,4,8',
+    ap.add_argument('--e2e-chunks', type=str, default='1,2,3,4,6,8',
                     help='token chunk counts tried for the end-to-end leg (PCIe copies overlapped with '
                          'compute); the fastest is reported')
     ap.add_argument('--tokens', type=int, default=T_TOTAL,

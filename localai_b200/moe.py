@@ -34,6 +34,21 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+def chunk_bounds(T: int, chunks: int) -> list[int]:
+    """Token boundaries of the chunks of pipelined_host_forward.  The first
+    chunk's upload and the last chunk's download overlap nothing, so with
+    three or more chunks those two are half the size of the others; no chunk
+    is empty."""
+    chunks = max(1, min(chunks, T))
+    wts = [1.0] * chunks
+    if chunks >= 3:
+        wts[0] = wts[-1] = 0.5
+    acc = [0.0]
+    for wv in wts:
+        acc.append(acc[-1] + wv)
+    return sorted({int(round(T * a / acc[-1])) for a in acc})
+
+
 def pipelined_host_forward(fn, h_host: torch.Tensor, y_host: torch.Tensor | None, chunks: int, device):
     """y_host = fn(h) for host (pinned) f32 h_host [T, D], in ``chunks`` token
     chunks: the host->device copy of chunk c+1 and the device->host copy of
@@ -45,8 +60,8 @@ def pipelined_host_forward(fn, h_host: torch.Tensor, y_host: torch.Tensor | None
     T, D = h_host.shape
     if y_host is None:
         y_host = torch.empty((T, D), dtype=torch.float32, pin_memory=True)
-    chunks = max(1, min(chunks, T))
-    bounds = [T * c // chunks for c in range(chunks + 1)]
+    bounds = chunk_bounds(T, chunks)
+    chunks = len(bounds) - 1
     rows = max(bounds[c + 1] - bounds[c] for c in range(chunks))
     comp = torch.cuda.current_stream(device)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)

@@ -14,7 +14,7 @@ import torch
 
 from oracle import quant_oracle as o
 from localai_b200 import synth
-from localai_b200.moe import QuantMoE
+from localai_b200.moe import QuantMoE, chunk_bounds
 
 pytestmark = pytest.mark.gpu
 
@@ -219,6 +219,6 @@ def test_forward_host_equals_chunked_forward(chunks):
     h = torch.from_numpy(rng.normal(size=(T, D)).astype(np.float32)).pin_memory()
     y = layer.forward_host(h, chunks=chunks)
     torch.cuda.synchronize()
-    bounds = [T * c // chunks for c in range(chunks + 1)]
+    bounds = chunk_bounds(T, chunks)
     ref = torch.cat([layer(h[a:b].cuda()).cpu() for a, b in zip(bounds[:-1], bounds[1:])])
     assert torch.equal(y, ref)
