@@ -590,7 +590,17 @@ int moe_route_splits(int T, int E, int D, int num_sms)
     const long long ctas = (long long)((T + RT_TOK - 1) / RT_TOK) * ((E + RT_EXP - 1) / RT_EXP);
     int s = 1;
     while (s < 32 && ctas * s < 2LL * num_sms && (D / RT_BK) >= 2 * s) s *= 2;
-    return s;
+    // one CTA per SM (the tiles take most of shared memory): among up to two
+    // more doublings, the split whose last wave of CTAs is fullest (at most
+    // 16 K tiles per split, the partials stay small next to h)
+    auto waste = [&](int sp) {
+        const long long n = ctas * sp, waves = (n + num_sms - 1) / num_sms;
+        return (double)(waves * num_sms) / (double)n;
+    };
+    int best = s;
+    for (int sp = 2 * s; sp <= 4 * s && sp <= 32 && (D / RT_BK) >= 2 * sp && ctas * sp <= 8LL * num_sms; sp *= 2)
+        if (waste(sp) < waste(best) - 0.05) best = sp;
+    return best;
 }
 
 size_t moe_route_workspace_bytes(int T, int E, int D, int num_sms)
