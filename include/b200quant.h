@@ -370,7 +370,12 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *   b200q_rope_kv_dev       rows t < T of qkv = [q H*hd | k KV*hd | v KV*hd]
  *                           at positions *pos + t: adjacent-pair RoPE of q and
  *                           k over the first ``rotary`` dims, then k, v stored
- *                           at cache[*pos + t] (cache layout [max_seq][KV][hd])
+ *                           at cache[*pos + t] (cache layout [max_seq][KV][hd]);
+ *                           pair j turns at pos * base^(-j / (rotary / 2))
+ *   b200q_rope_kv_freq_dev  the same with pair j turning at pos * inv_freq[j]
+ *                           (device f32 [rotary / 2]: RoPE scaling -- llama3
+ *                           frequency interpolation or linear, engine/model.py
+ *                           :200-214 -- is a table computed once on the host)
  *   b200q_attn_prefill_dev  causal attention of T query rows (positions
  *                           *pos + t, q from the rotated qkv rows) over cache
  *                           positions 0 .. *pos + t; out bf16 [T][H*hd]; if
@@ -392,6 +397,8 @@ int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, i
                           void *h_bf16, void *stream);
 int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
                       float *k_cache, float *v_cache, int max_seq, void *stream);
+int b200q_rope_kv_freq_dev(float *qkv, int T, int H, int KV, int hd, int rotary, const float *inv_freq,
+                           const int *pos, float *k_cache, float *v_cache, int max_seq, void *stream);
 int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T, int H,
                            int KV, int hd, int max_seq, void *out_bf16, void *stream);
 /* b200q_attn_prefill_dev on the tensor cores (tcgen05: bf16 operands, f32

@@ -94,15 +94,16 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
 
 // qkv = [q (H*hd) | k (KV*hd) | v (KV*hd)]: rotate q and k in place over the
 // first ``rotary`` dims (adjacent pairs, engine/model.py:205-217):
-// inv_j = 1 / base^(j / half), angle = pos * inv_j; and store the rotated k
+// inv_j = 1 / base^(j / half) (or inv_freq[j] when a table is given),
+// angle = pos * inv_j; and store the rotated k
 // and v of every row into the caches (layout [max_seq][KV][hd], as the
 // reference's KVCache).  Rows t of qkv (row stride (H + 2 KV) * hd) are
 // positions *pos_p + t.  Work items of one row: H*half q pairs, KV*half k
 // pairs (rotated, then stored), KV*(hd - rotary) unrotated k values and KV*hd
 // v values (both only stored).
 __global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd, int rotary, float base,
-                               const int *__restrict__ pos_p, float *__restrict__ kc, float *__restrict__ vc,
-                               int max_seq, int *err)
+                               const float *__restrict__ inv_freq, const int *__restrict__ pos_p,
+                               float *__restrict__ kc, float *__restrict__ vc, int max_seq, int *err)
 {
     pdl_enter();
     const int pos0 = *pos_p;
@@ -125,7 +126,8 @@ __global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, in
             const bool is_k = r >= nq;
             if (is_k) r -= nq;
             const int hh = r / half, j = r % half;
-            const float inv = 1.0f / powf(base, (float)j / (float)half);
+            // a given frequency table (RoPE scaling: llama3 interpolation, linear) or base^(-j/half)
+            const float inv = inv_freq ? __ldg(inv_freq + j) : 1.0f / powf(base, (float)j / (float)half);
             const float ang = (float)(pos0 + t) * inv;
             const float c = cosf(ang), s = sinf(ang);
             const long long off = (long long)((is_k ? H : 0) + hh) * hd + 2 * j;
@@ -574,16 +576,16 @@ cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int
     return launch_pdl(add_rmsnorm_kernel, dim3(T), dim3(NORM_THREADS), 0, st, x, delta, w, D, eps, h, hb);
 }
 
-cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
-                           float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st)
+cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const float *inv_freq,
+                           const int *pos, float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st)
 {
     if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 2 || rotary < 0 || rotary > hd || rotary % 2 || max_seq < 1)
         return cudaErrorInvalidValue;
     const long long items = (long long)T * ((long long)(H + KV) * (rotary / 2) + (long long)KV * (hd - rotary) +
                                             (long long)KV * hd);
     const long long g = std::min(8LL * num_sms, (items + 255) / 256);
-    return launch_pdl(rope_kv_kernel, dim3((unsigned)g), dim3(256), 0, st, qkv, T, H, KV, hd, rotary, base, pos, kc,
-                      vc, max_seq, err);
+    return launch_pdl(rope_kv_kernel, dim3((unsigned)g), dim3(256), 0, st, qkv, T, H, KV, hd, rotary, base, inv_freq,
+                      pos, kc, vc, max_seq, err);
 }
 
 size_t attn_scratch_floats(int H, int hd, int max_seq)

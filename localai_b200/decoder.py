@@ -1,7 +1,7 @@
 """Greedy decode of the reference's Llama decoder on the GPU.
 
-``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama', no RoPE
-scaling) runs one token through every layer with NumPy and the native
+``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama', RoPE
+plain or scaled: llama3 / linear) runs one token through every layer with NumPy and the native
 quantised matvecs.  ``QuantLlama`` keeps every weight on the device in its raw
 GGUF form and runs one token per *step*:
 
@@ -52,10 +52,45 @@ class LlamaConfig:
     rope_dim: int | None = None       # default: head_dim
     eps: float = 1e-5
     max_seq: int = 2048
+    # RoPE scaling, as the GGUF keys {arch}.rope.scaling.* (engine/model.py:
+    # 21-26): 'none', 'llama3' (Llama 3.1/3.2 frequency interpolation) or
+    # 'linear' (angles divided by the factor); only applied for factor > 1
+    rope_scaling: str = 'none'
+    rope_factor: float = 1.0
+    rope_orig_ctx: int = 8192
+    rope_low_freq: float = 1.0
+    rope_high_freq: float = 4.0
 
     @property
     def head_dim(self) -> int:
         return self.d_model // self.n_heads
+
+
+def rope_inv_freq(cfg: LlamaConfig, rotary: int):
+    """Per-pair RoPE frequencies with the configured scaling, or None for
+    plain base^(-j / half).  float32 arithmetic in the order of the reference
+    (engine/model.py:199-214): llama3 keeps the high-frequency pairs, divides
+    the low-frequency ones by the factor and blends the band between; linear
+    divides every angle by the factor (folded into the frequency here)."""
+    import numpy as np
+    kind = cfg.rope_scaling.lower()
+    if kind not in ('none', 'llama3', 'linear'):
+        raise ValueError(f'unsupported RoPE scaling {cfg.rope_scaling!r}')
+    half = rotary // 2
+    if kind == 'none' or cfg.rope_factor <= 1.0 or half == 0:
+        return None
+    f32 = np.float32
+    inv = (f32(1.0) / (f32(cfg.rope_base) ** (np.arange(half, dtype=f32) / f32(max(half, 1))))).astype(f32)
+    fac = f32(cfg.rope_factor)
+    if kind == 'linear':
+        return (inv / fac).astype(f32)
+    orig, lo, hi = f32(cfg.rope_orig_ctx), f32(cfg.rope_low_freq), f32(cfg.rope_high_freq)
+    wavelength = (f32(2.0 * np.pi) / np.maximum(inv, f32(1e-12))).astype(f32)
+    low_wl = orig / max(lo, f32(1e-6))
+    high_wl = orig / max(hi, f32(1e-6))
+    smooth = ((orig / np.maximum(wavelength, f32(1e-12)) - lo) / max(hi - lo, f32(1e-6))).astype(f32)
+    blended = ((f32(1.0) - smooth) * (inv / fac) + smooth * inv).astype(f32)
+    return np.where(wavelength > low_wl, inv / fac, np.where(wavelength < high_wl, inv, blended)).astype(f32)
 
 
 class QuantLlama:
@@ -75,6 +110,8 @@ class QuantLlama:
         self.rotary -= self.rotary % 2
         dev = weights['output_norm'].device
         self.dev = dev
+        inv = rope_inv_freq(c, self.rotary)
+        self.inv_freq = None if inv is None else torch.from_numpy(inv).to(dev)
         self.emb, self.t_emb = weights['token_embd']
         self.out_w, self.t_out = weights['output']
         self.out_norm = weights['output_norm'].float().contiguous()
@@ -114,6 +151,18 @@ class QuantLlama:
         self.graph = None
 
     # -- one step -------------------------------------------------------------
+    def _rope(self, qkv, T, kc, vc, st):
+        """RoPE of T rows of qkv at positions pos.. and their k/v cache store
+        (a frequency table when RoPE scaling is configured)."""
+        c, lib, hd = self.cfg, self.lib, self.cfg.head_dim
+        if self.inv_freq is None:
+            _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
+                                             self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), c.max_seq, st))
+        else:
+            _lib.check(lib.b200q_rope_kv_freq_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary,
+                                                  self.inv_freq.data_ptr(), self.pos.data_ptr(), kc.data_ptr(),
+                                                  vc.data_ptr(), c.max_seq, st))
+
     def _gemv(self, w, x, y, rows, cols):
         raw, t = w
         _lib.check(self.lib.b200q_gemv_dev(t, raw.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 1, rows, 1,
@@ -131,9 +180,7 @@ class QuantLlama:
                                                  None, st))
             self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            _lib.check(lib.b200q_rope_kv_dev(self.qkv.data_ptr(), 1, c.n_heads, c.n_kv_heads, hd, self.rotary,
-                                             c.rope_base, self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                             c.max_seq, st))
+            self._rope(self.qkv, 1, kc, vc, st)
             _lib.check(lib.b200q_attn_decode_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                                  self.pos.data_ptr(), c.n_heads, c.n_kv_heads, hd, c.max_seq,
                                                  self.scratch.data_ptr(), self.att.data_ptr(), st))
@@ -195,8 +242,7 @@ class QuantLlama:
             ops.gemm_quant(Hb, wq, off, k=c.d_model, n_feat=nq, w_rows_per_group=nq, ggml_type=tq, w_row_bytes=sq,
                            out=qkv)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
-                                             self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), c.max_seq, st))
+            self._rope(qkv, T, kc, vc, st)
             if scratch is not None:
                 _lib.check(lib.b200q_attn_prefill_tc_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                                          self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd,

@@ -383,6 +383,27 @@ def zaya_moe_f64(h, expert, weight, experts, t_gu, t_dn, d_model, d_ff, d_ff_pad
     return y
 
 
+def rope_inv_f64(cfg, half):
+    """Per-pair RoPE frequencies in float64 (engine/model.py:199-214): plain
+    base^(-j/half); 'llama3' keeps wavelengths below orig/high, divides those
+    above orig/low by the factor and blends linearly in between; 'linear'
+    divides by the factor (the reference divides the angle, the same up to
+    rounding)."""
+    inv = 1.0 / (cfg['rope_base'] ** (np.arange(half, dtype=np.float64) / max(half, 1)))
+    kind = str(cfg.get('rope_scaling', 'none')).lower()
+    fac = float(cfg.get('rope_factor', 1.0))
+    if kind == 'none' or fac <= 1.0:
+        return inv
+    if kind == 'linear':
+        return inv / fac
+    orig = float(cfg.get('rope_orig_ctx', 8192))
+    lo, hi = float(cfg.get('rope_low_freq', 1.0)), float(cfg.get('rope_high_freq', 4.0))
+    wl = 2.0 * np.pi / inv
+    smooth = (orig / wl - lo) / (hi - lo)
+    mid = (1.0 - smooth) * inv / fac + smooth * inv
+    return np.where(wl > orig / lo, inv / fac, np.where(wl < orig / hi, inv, mid))
+
+
 def llama_decode_f64(w, cfg, tokens):
     """Logits after each token of ``tokens`` (positions 0, 1, ...), float64.
 
@@ -390,7 +411,9 @@ def llama_decode_f64(w, cfg, tokens):
     'layers': [{'attn_q': [H*hd, D], 'attn_k': [KV*hd, D], 'attn_v',
     'attn_output': [D, D], 'ffn_gate': [F, D], 'ffn_up', 'ffn_down': [D, F],
     'attn_norm': [D], 'ffn_norm': [D]}]} as float arrays; ``cfg`` with
-    n_heads, n_kv_heads, rope_base, eps (and optional rope_dim).
+    n_heads, n_kv_heads, rope_base, eps (and optional rope_dim, and RoPE
+    scaling: rope_scaling 'llama3' / 'linear' with rope_factor, rope_orig_ctx,
+    rope_low_freq, rope_high_freq -- engine/model.py:199-214).
     """
     H, KV = cfg['n_heads'], cfg['n_kv_heads']
     D = w['token_embd'].shape[1]
@@ -406,7 +429,7 @@ def llama_decode_f64(w, cfg, tokens):
     out = []
     for pos, tok in enumerate(tokens):
         x = w['token_embd'][tok].astype(np.float64)
-        inv = 1.0 / (cfg['rope_base'] ** (np.arange(half, dtype=np.float64) / max(half, 1)))
+        inv = rope_inv_f64(cfg, half)
         ang = pos * inv
         c, s_ = np.cos(ang), np.sin(ang)
 

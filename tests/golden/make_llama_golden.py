@@ -1,6 +1,6 @@
 """Generate tests/golden/llama_decode_golden.npz by running the reference's own
 ``LlamaModel.forward`` (engine/model.py:174-240) token by token on a tiny
-stub model with f32 weights.
+stub model with f32 weights, plain RoPE and with llama3 / linear RoPE scaling.
 
 The stub supplies what ``forward`` touches: ``gguf`` (``metadata``,
 ``tensors``, ``find``), ``w`` and ``mat`` (a plain f32 ``x @ W.T``, standing in
@@ -60,8 +60,18 @@ def main(ref_root):
     m.mat = lambda x, name: (np.asarray(x, np.float32) @ T[name].T).astype(np.float32)
     tokens = [3, 17, 42, 5, 0, 49, 8]
     logits = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
+    # RoPE scaling (engine/model.py:199-214): llama3 interpolation with a short
+    # original context, so that the 8 frequency pairs fall in all three bands
+    # (kept, blended, divided), and linear; same weights and tokens
+    scaled = {}
+    for kind, fac in (('llama3', 8.0), ('linear', 4.0)):
+        m.rope_scaling_type, m.rope_scaling_factor = kind, fac
+        m.rope_original_context, m.rope_low_freq, m.rope_high_freq = 64, 1.0, 4.0
+        m.cache = KVCache(NL, KV, hd, 32)
+        scaled['logits_' + kind] = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
     out = Path(__file__).resolve().parent / 'llama_decode_golden.npz'
-    np.savez_compressed(out, logits=logits, tokens=np.array(tokens), **{k.replace('.', '_'): v for k, v in T.items()})
+    np.savez_compressed(out, logits=logits, tokens=np.array(tokens), **scaled,
+                        **{k.replace('.', '_'): v for k, v in T.items()})
     print('wrote', out)
 
 

@@ -17,7 +17,7 @@ from localai_b200.decoder import LlamaConfig, QuantLlama
 pytestmark = pytest.mark.gpu
 
 
-def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64):
+def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None):
     gen = {8: synth.q8_0, 12: synth.q4_k}[t]
     dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
     hd = D // H
@@ -39,9 +39,10 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64):
     ref_w = {'token_embd': o.dequantize(raw['token_embd'], 8, (V, D)).astype(np.float64),
              'output': o.dequantize(raw['output'], t, (V, D)).astype(np.float64), 'output_norm': on,
              'layers': layers_ref}
+    sc = scaling or {}
     cfg = LlamaConfig(n_layers=NL, d_model=D, n_heads=H, n_kv_heads=KV, d_ff=F, vocab=V, rope_base=10000.0,
-                      eps=1e-5, max_seq=max_seq)
-    return QuantLlama(weights, cfg), ref_w, {'n_heads': H, 'n_kv_heads': KV, 'rope_base': 10000.0, 'eps': 1e-5}
+                      eps=1e-5, max_seq=max_seq, **sc)
+    return QuantLlama(weights, cfg), ref_w, {'n_heads': H, 'n_kv_heads': KV, 'rope_base': 10000.0, 'eps': 1e-5, **sc}
 
 
 @pytest.mark.parametrize('t', [8, 12])
@@ -119,6 +120,32 @@ def test_prefill_matches_oracle_then_decode_continues(t):
         torch.cuda.synchronize()
         err = o.normwise_rel_err(model.logits.cpu().numpy(), ref[len(prompt) + i])
         assert err < 3e-2, ('decode step after prefill', i, err)
+
+
+@pytest.mark.parametrize('kind,fac', [('llama3', 8.0), ('linear', 4.0)])
+def test_rope_scaling_decode_and_prefill_match_oracle(kind, fac):
+    """RoPE scaling (engine/model.py:199-214) through the frequency-table
+    kernel: decode logits within 1e-3 of the float64 oracle at every position
+    (a short original context puts the 32 frequency pairs in all three llama3
+    bands), and the tensor-core prefill within 3e-2."""
+    rng = np.random.default_rng(61)
+    scaling = dict(rope_scaling=kind, rope_factor=fac, rope_orig_ctx=64, rope_low_freq=1.0, rope_high_freq=4.0)
+    model, ref_w, cfg = build(rng, 12, max_seq=96, scaling=scaling)
+    assert model.inv_freq is not None
+    tokens = [int(v) for v in rng.integers(0, 300, size=40)]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    plain = o.llama_decode_f64(ref_w, {k: cfg[k] for k in ('n_heads', 'n_kv_heads', 'rope_base', 'eps')}, tokens)
+    assert o.normwise_rel_err(plain[-1], ref[-1]) > 1e-2          # the scaling matters at these positions
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    model.reset()
+    model.prefill(tokens)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
 
 
 @pytest.mark.parametrize('T,rotary', [(1, 64), (5, 32), (3, 0)])

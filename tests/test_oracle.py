@@ -254,3 +254,27 @@ def test_llama_decode_oracle_matches_reference_golden():
     cfg = {'n_heads': 4, 'n_kv_heads': 2, 'rope_base': 10000.0, 'eps': 1e-5}
     got = o.llama_decode_f64(w, cfg, list(d['tokens']))
     assert o.normwise_rel_err(got, d['logits'].astype(np.float64)) < 1e-5
+    # RoPE scaling (engine/model.py:199-214): llama3 interpolation and linear
+    for kind, fac in (('llama3', 8.0), ('linear', 4.0)):
+        sc = dict(cfg, rope_scaling=kind, rope_factor=fac, rope_orig_ctx=64, rope_low_freq=1.0, rope_high_freq=4.0)
+        got = o.llama_decode_f64(w, sc, list(d['tokens']))
+        ref = d['logits_' + kind].astype(np.float64)
+        assert o.normwise_rel_err(got, ref) < 1e-5, kind
+        assert o.normwise_rel_err(ref, d['logits'].astype(np.float64)) > 1e-2     # the scaling changes the logits
+
+
+def test_rope_frequency_table_matches_oracle():
+    """localai_b200.decoder.rope_inv_freq (float32, uploaded for the RoPE
+    kernel) against the oracle's float64 frequencies, all three llama3 bands
+    and linear, within f32 rounding."""
+    from localai_b200.decoder import LlamaConfig, rope_inv_freq
+    for kind, fac, base, rot in (('llama3', 8.0, 500000.0, 128), ('llama3', 8.0, 10000.0, 16),
+                                 ('linear', 4.0, 10000.0, 64)):
+        c = LlamaConfig(n_layers=1, d_model=32 * rot, n_heads=32, n_kv_heads=8, d_ff=64, vocab=8, rope_base=base,
+                        rope_scaling=kind, rope_factor=fac, rope_orig_ctx=64 if rot == 16 else 8192)
+        got = rope_inv_freq(c, rot).astype(np.float64)
+        ref = o.rope_inv_f64({'rope_base': base, 'rope_scaling': kind, 'rope_factor': fac,
+                              'rope_orig_ctx': c.rope_orig_ctx, 'rope_low_freq': 1.0, 'rope_high_freq': 4.0}, rot // 2)
+        np.testing.assert_allclose(got, ref, rtol=2e-6)
+    plain = LlamaConfig(n_layers=1, d_model=64, n_heads=1, n_kv_heads=1, d_ff=64, vocab=8)
+    assert rope_inv_freq(plain, 64) is None
