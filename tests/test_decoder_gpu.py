@@ -127,15 +127,15 @@ def test_rope_scaling_decode_and_prefill_match_oracle(kind, fac):
     """RoPE scaling (engine/model.py:199-214) through the frequency-table
     kernel: decode logits within 1e-3 of the float64 oracle at every position
     (a short original context puts the 32 frequency pairs in all three llama3
-    bands), and the tensor-core prefill within 3e-2."""
+    bands), and the tensor-core prefill within 3e-2.  (These random weights
+    make the logits insensitive to RoPE; the kernel's rotation itself is
+    checked against the table in test_rope_kv_freq_table.)"""
     rng = np.random.default_rng(61)
     scaling = dict(rope_scaling=kind, rope_factor=fac, rope_orig_ctx=64, rope_low_freq=1.0, rope_high_freq=4.0)
     model, ref_w, cfg = build(rng, 12, max_seq=96, scaling=scaling)
     assert model.inv_freq is not None
     tokens = [int(v) for v in rng.integers(0, 300, size=40)]
     ref = o.llama_decode_f64(ref_w, cfg, tokens)
-    plain = o.llama_decode_f64(ref_w, {k: cfg[k] for k in ('n_heads', 'n_kv_heads', 'rope_base', 'eps')}, tokens)
-    assert o.normwise_rel_err(plain[-1], ref[-1]) > 1e-2          # the scaling matters at these positions
     model.reset()
     for p, tok in enumerate(tokens):
         model.set_token(tok)
@@ -146,6 +146,45 @@ def test_rope_scaling_decode_and_prefill_match_oracle(kind, fac):
     model.prefill(tokens)
     torch.cuda.synchronize()
     assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
+@pytest.mark.parametrize('kind,fac', [('llama3', 8.0), ('linear', 4.0)])
+def test_rope_kv_freq_table(kind, fac):
+    """b200q_rope_kv_freq_dev: pair j of q and k turns by pos * inv_freq[j]
+    (the scaled table of rope_inv_freq), not by base^(-j/half); k and v land
+    in the caches."""
+    from localai_b200 import _lib, ops
+    from localai_b200.decoder import rope_inv_freq
+    rng = np.random.default_rng(7)
+    H, KV, hd, T, max_seq, p0 = 4, 2, 64, 3, 64, 40
+    c = LlamaConfig(n_layers=1, d_model=H * hd, n_heads=H, n_kv_heads=KV, d_ff=64, vocab=8, rope_base=10000.0,
+                    rope_scaling=kind, rope_factor=fac, rope_orig_ctx=64)
+    inv = rope_inv_freq(c, hd)
+    plain = 1.0 / 10000.0 ** (np.arange(hd // 2) / (hd // 2))
+    assert np.abs(inv - plain).max() > 1e-2 * plain.max()
+    qkv = rng.normal(size=(T, (H + 2 * KV) * hd)).astype(np.float32)
+    ref = qkv.astype(np.float64).copy()
+    for t in range(T):
+        ang = (p0 + t) * inv.astype(np.float64)
+        cs, sn = np.cos(ang), np.sin(ang)
+        for hh in range(H + KV):
+            a = ref[t, hh * hd:(hh + 1) * hd]
+            e, od = a[0::2].copy(), a[1::2].copy()
+            a[0::2], a[1::2] = e * cs - od * sn, e * sn + od * cs
+    kc = torch.zeros((max_seq, KV * hd), device='cuda')
+    vc = torch.zeros((max_seq, KV * hd), device='cuda')
+    qd = torch.from_numpy(qkv).cuda()
+    pos = torch.tensor([p0], dtype=torch.int32, device='cuda')
+    invd = torch.from_numpy(inv).cuda()
+    lib = _lib.load()
+    _lib.check(lib.b200q_rope_kv_freq_dev(qd.data_ptr(), T, H, KV, hd, hd, invd.data_ptr(), pos.data_ptr(),
+                                          kc.data_ptr(), vc.data_ptr(), max_seq,
+                                          torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    ops.check_device_error()
+    np.testing.assert_allclose(qd.cpu().numpy(), ref, rtol=0, atol=5e-5)
+    np.testing.assert_allclose(kc[p0:p0 + T].cpu().numpy(), ref[:, H * hd:(H + KV) * hd], rtol=0, atol=5e-5)
+    np.testing.assert_allclose(vc[p0:p0 + T].cpu().numpy(), ref[:, (H + KV) * hd:], rtol=0, atol=0)
 
 
 @pytest.mark.parametrize('T,rotary', [(1, 64), (5, 32), (3, 0)])
