@@ -372,10 +372,18 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *                           k over the first ``rotary`` dims, then k, v stored
  *                           at cache[*pos + t] (cache layout [max_seq][KV][hd]);
  *                           pair j turns at pos * base^(-j / (rotary / 2))
- *   b200q_rope_kv_freq_dev  the same with pair j turning at pos * inv_freq[j]
- *                           (device f32 [rotary / 2]: RoPE scaling -- llama3
- *                           frequency interpolation or linear, engine/model.py
- *                           :200-214 -- is a table computed once on the host)
+ *   b200q_rope_kv_ex_dev    the same with pair j turning at pos * inv_freq[j]
+ *                           when inv_freq is given (device f32 [rotary / 2]:
+ *                           RoPE scaling -- llama3 frequency interpolation or
+ *                           linear, engine/model.py:200-214 -- is a table
+ *                           computed once on the host), and with neox != 0
+ *                           the pairs (j, j + rotary/2) of Qwen2/Qwen3
+ *                           instead of adjacent ones (engine/model.py:212-221)
+ *   b200q_qkv_bias_norm_dev before RoPE: qkv rows += bias (optional,
+ *                           [(H + 2 KV) * hd], Qwen2's biased projections),
+ *                           then every q / k head RMS-normalised with the
+ *                           per-head weights q_norm / k_norm (optional, [hd],
+ *                           Qwen3); hd a multiple of 32 up to 256
  *   b200q_attn_prefill_dev  causal attention of T query rows (positions
  *                           *pos + t, q from the rotated qkv rows) over cache
  *                           positions 0 .. *pos + t; out bf16 [T][H*hd]; if
@@ -397,8 +405,10 @@ int b200q_add_rmsnorm_dev(float *x, const float *delta, const float *w, int T, i
                           void *h_bf16, void *stream);
 int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const int *pos,
                       float *k_cache, float *v_cache, int max_seq, void *stream);
-int b200q_rope_kv_freq_dev(float *qkv, int T, int H, int KV, int hd, int rotary, const float *inv_freq,
-                           const int *pos, float *k_cache, float *v_cache, int max_seq, void *stream);
+int b200q_rope_kv_ex_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const float *inv_freq,
+                         int neox, const int *pos, float *k_cache, float *v_cache, int max_seq, void *stream);
+int b200q_qkv_bias_norm_dev(float *qkv, int T, int H, int KV, int hd, const float *bias, const float *q_norm,
+                            const float *k_norm, float eps, void *stream);
 int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T, int H,
                            int KV, int hd, int max_seq, void *out_bf16, void *stream);
 /* b200q_attn_prefill_dev on the tensor cores (tcgen05: bf16 operands, f32

@@ -73,7 +73,8 @@ SIGNATURES = {
     'b200q_dequant_row_dev': (_i, [_i, _vp, _ll, _i, _vp, _i, _i, _vp, _vp]),
     'b200q_add_rmsnorm_dev': (_i, [_vp, _vp, _vp, _i, _i, ctypes.c_float, _vp, _vp, _vp]),
     'b200q_rope_kv_dev': (_i, [_vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _vp, _i, _vp]),
-    'b200q_rope_kv_freq_dev': (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
+    'b200q_rope_kv_ex_dev': (_i, [_vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _i, _vp, _vp, _vp, _i, _vp]),
+    'b200q_qkv_bias_norm_dev': (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_float, _vp]),
     'b200q_attn_prefill_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
     'b200q_attn_prefill_tc_scratch_bytes': (_sz, [_i, _i, _i, _i, _i]),
     'b200q_attn_prefill_tc_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp, _vp]),

@@ -87,7 +87,10 @@ cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, i
 cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int T, int D, float eps, float *h,
                                __nv_bfloat16 *hb, cudaStream_t st);
 cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const float *inv_freq,
-                           const int *pos, float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st);
+                           int neox, const int *pos, float *kc, float *vc, int max_seq, int *err, int num_sms,
+                           cudaStream_t st);
+cudaError_t launch_qkv_bias_norm(float *qkv, int T, int H, int KV, int hd, const float *bias, const float *qn,
+                                 const float *kn, float eps, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
                                 int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st);
 size_t attn_prefill_tc_scratch_bytes(int T, int H, int KV, int hd, int max_seq);
@@ -963,22 +966,35 @@ B200Q_API int b200q_rope_kv_dev(float *qkv, int T, int H, int KV, int hd, int ro
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, base, nullptr, pos, k_cache, v_cache, max_seq,
+    return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, base, nullptr, 0, pos, k_cache, v_cache, max_seq,
                                       di->err, di->sms, (cudaStream_t)stream),
                        "rope_kv");
 }
 
-B200Q_API int b200q_rope_kv_freq_dev(float *qkv, int T, int H, int KV, int hd, int rotary, const float *inv_freq,
-                                     const int *pos, float *k_cache, float *v_cache, int max_seq, void *stream)
+B200Q_API int b200q_rope_kv_ex_dev(float *qkv, int T, int H, int KV, int hd, int rotary, float base,
+                                   const float *inv_freq, int neox, const int *pos, float *k_cache, float *v_cache,
+                                   int max_seq, void *stream)
 {
     std::lock_guard<std::recursive_mutex> g(g_lock);
-    if (!qkv || !inv_freq || !pos || !k_cache || !v_cache) return set_status(B200Q_EINVAL, "rope_kv_freq: null pointer");
+    if (!qkv || !pos || !k_cache || !v_cache) return set_status(B200Q_EINVAL, "rope_kv_ex: null pointer");
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, 0.f, inv_freq, pos, k_cache, v_cache, max_seq,
+    return cuda_status(launch_rope_kv(qkv, T, H, KV, hd, rotary, base, inv_freq, neox, pos, k_cache, v_cache, max_seq,
                                       di->err, di->sms, (cudaStream_t)stream),
-                       "rope_kv_freq");
+                       "rope_kv_ex");
+}
+
+B200Q_API int b200q_qkv_bias_norm_dev(float *qkv, int T, int H, int KV, int hd, const float *bias, const float *q_norm,
+                                      const float *k_norm, float eps, void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!qkv) return set_status(B200Q_EINVAL, "qkv_bias_norm: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_qkv_bias_norm(qkv, T, H, KV, hd, bias, q_norm, k_norm, eps, (cudaStream_t)stream),
+                       "qkv_bias_norm");
 }
 
 B200Q_API size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq)

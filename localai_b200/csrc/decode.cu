@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float *__rest
 // pairs (rotated, then stored), KV*(hd - rotary) unrotated k values and KV*hd
 // v values (both only stored).
 __global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd, int rotary, float base,
-                               const float *__restrict__ inv_freq, const int *__restrict__ pos_p,
+                               const float *__restrict__ inv_freq, int neox, const int *__restrict__ pos_p,
                                float *__restrict__ kc, float *__restrict__ vc, int max_seq, int *err)
 {
     pdl_enter();
@@ -130,14 +130,16 @@ __global__ void rope_kv_kernel(float *__restrict__ qkv, int T, int H, int KV, in
             const float inv = inv_freq ? __ldg(inv_freq + j) : 1.0f / powf(base, (float)j / (float)half);
             const float ang = (float)(pos0 + t) * inv;
             const float c = cosf(ang), s = sinf(ang);
-            const long long off = (long long)((is_k ? H : 0) + hh) * hd + 2 * j;
-            const float e = qr[off], o = qr[off + 1];
+            // pair j: dims (2j, 2j+1) (llama) or (j, j + half) (NeoX split halves, qwen2/qwen3)
+            const int de = neox ? j : 2 * j, dodd = neox ? j + half : 2 * j + 1;
+            const long long hb = (long long)((is_k ? H : 0) + hh) * hd;
+            const float e = qr[hb + de], o = qr[hb + dodd];
             const float e2 = e * c - o * s, o2 = e * s + o * c;
-            qr[off] = e2;
-            qr[off + 1] = o2;
+            qr[hb + de] = e2;
+            qr[hb + dodd] = o2;
             if (is_k) {
-                kcr[hh * hd + 2 * j] = e2;
-                kcr[hh * hd + 2 * j + 1] = o2;
+                kcr[hh * hd + de] = e2;
+                kcr[hh * hd + dodd] = o2;
             }
         } else if (r < nq + nk + nkr) {                  // k beyond the rotary dims
             r -= nq + nk;
@@ -576,8 +578,59 @@ cudaError_t launch_add_rmsnorm(float *x, const float *delta, const float *w, int
     return launch_pdl(add_rmsnorm_kernel, dim3(T), dim3(NORM_THREADS), 0, st, x, delta, w, D, eps, h, hb);
 }
 
+// Before RoPE, per row t < T of qkv = [q H*hd | k KV*hd | v KV*hd]: add the
+// projection bias (when given: [(H + 2 KV) * hd], engine/model.py:73-79, the
+// biased Q/K/V of Qwen2), then RMS-normalise every q head and every k head
+// over its hd values with the per-head weights q_norm / k_norm (when given:
+// [hd], Qwen3, engine/model.py:188-192: x / sqrt(mean(x^2) + eps) * w).  One
+// warp per (row, head); hd <= 256, a multiple of 32.
+__global__ void qkv_bias_norm_kernel(float *__restrict__ qkv, int T, int H, int KV, int hd,
+                                     const float *__restrict__ bias, const float *__restrict__ qn,
+                                     const float *__restrict__ kn, float eps)
+{
+    pdl_enter();
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nh = H + 2 * KV;
+    if (wid >= (long long)T * nh) return;
+    const int t = (int)(wid / nh), hh = (int)(wid % nh);
+    float *a = qkv + ((long long)t * nh + hh) * hd;
+    const float *b = bias ? bias + (long long)hh * hd : nullptr;
+    const float *g = hh < H ? qn : hh < H + KV ? kn : nullptr;
+    const int per = hd / 32;
+    float v[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+        if (u < per) {
+            v[u] = a[lane + 32 * u] + (b ? __ldg(b + lane + 32 * u) : 0.f);
+            ss += v[u] * v[u];
+        }
+    if (g) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = 1.0f / sqrtf(ss / (float)hd + eps);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (u < per) v[u] = v[u] * r * __ldg(g + lane + 32 * u);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+        if (u < per) a[lane + 32 * u] = v[u];
+}
+
+cudaError_t launch_qkv_bias_norm(float *qkv, int T, int H, int KV, int hd, const float *bias, const float *qn,
+                                 const float *kn, float eps, cudaStream_t st)
+{
+    if (T < 1 || H < 1 || KV < 1 || hd < 32 || hd > 256 || hd % 32) return cudaErrorInvalidValue;
+    const long long warps = (long long)T * (H + 2 * KV);
+    return launch_pdl(qkv_bias_norm_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st, qkv, T, H,
+                      KV, hd, bias, qn, kn, eps);
+}
+
 cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary, float base, const float *inv_freq,
-                           const int *pos, float *kc, float *vc, int max_seq, int *err, int num_sms, cudaStream_t st)
+                           int neox, const int *pos, float *kc, float *vc, int max_seq, int *err, int num_sms,
+                           cudaStream_t st)
 {
     if (T < 1 || H < 1 || KV < 1 || H % KV || hd < 2 || rotary < 0 || rotary > hd || rotary % 2 || max_seq < 1)
         return cudaErrorInvalidValue;
@@ -585,7 +638,7 @@ cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary,
                                             (long long)KV * hd);
     const long long g = std::min(8LL * num_sms, (items + 255) / 256);
     return launch_pdl(rope_kv_kernel, dim3((unsigned)g), dim3(256), 0, st, qkv, T, H, KV, hd, rotary, base, inv_freq,
-                      pos, kc, vc, max_seq, err);
+                      neox ? 1 : 0, pos, kc, vc, max_seq, err);
 }
 
 size_t attn_scratch_floats(int H, int hd, int max_seq)

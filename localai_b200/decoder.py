@@ -1,7 +1,8 @@
 """Greedy decode of the reference's Llama decoder on the GPU.
 
-``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama', RoPE
-plain or scaled: llama3 / linear) runs one token through every layer with NumPy and the native
+``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama' / 'qwen2' /
+'qwen3', RoPE plain or scaled: llama3 / linear) runs one token through every
+layer with NumPy and the native
 quantised matvecs.  ``QuantLlama`` keeps every weight on the device in its raw
 GGUF form and runs one token per *step*:
 
@@ -60,6 +61,11 @@ class LlamaConfig:
     rope_orig_ctx: int = 8192
     rope_low_freq: float = 1.0
     rope_high_freq: float = 4.0
+    # 'llama' (adjacent RoPE pairs) or 'qwen2' / 'qwen3' (split-half NeoX pairs,
+    # engine/model.py:212-221); Qwen2 layers may carry q/k/v biases and Qwen3
+    # layers per-head q/k norms (the optional 'attn_{q,k,v}_bias' and
+    # 'attn_{q,k}_norm' entries of a layer's weights)
+    arch: str = 'llama'
 
     @property
     def head_dim(self) -> int:
@@ -112,6 +118,9 @@ class QuantLlama:
         self.dev = dev
         inv = rope_inv_freq(c, self.rotary)
         self.inv_freq = None if inv is None else torch.from_numpy(inv).to(dev)
+        if c.arch not in ('llama', 'qwen2', 'qwen3'):
+            raise ValueError(f'unsupported architecture {c.arch!r}')
+        self.neox = c.arch != 'llama'
         self.emb, self.t_emb = weights['token_embd']
         self.out_w, self.t_out = weights['output']
         self.out_norm = weights['output_norm'].float().contiguous()
@@ -128,6 +137,10 @@ class QuantLlama:
                 'down': lw['ffn_down'],
                 'attn_norm': lw['attn_norm'].float().contiguous(),
                 'ffn_norm': lw['ffn_norm'].float().contiguous(),
+                'qkv_bias': (torch.cat([lw['attn_q_bias'], lw['attn_k_bias'], lw['attn_v_bias']]).float().contiguous()
+                             if 'attn_q_bias' in lw else None),
+                'q_norm': lw['attn_q_norm'].float().contiguous() if 'attn_q_norm' in lw else None,
+                'k_norm': lw['attn_k_norm'].float().contiguous() if 'attn_k_norm' in lw else None,
             })
         f32 = dict(dtype=torch.float32, device=dev)
         kvd = c.n_kv_heads * hd
@@ -151,17 +164,23 @@ class QuantLlama:
         self.graph = None
 
     # -- one step -------------------------------------------------------------
-    def _rope(self, qkv, T, kc, vc, st):
-        """RoPE of T rows of qkv at positions pos.. and their k/v cache store
-        (a frequency table when RoPE scaling is configured)."""
+    def _rope(self, qkv, T, kc, vc, st, L=None):
+        """Optional q/k/v bias and per-head q/k norms (layer L), then RoPE of T
+        rows of qkv at positions pos.. and their k/v cache store (a frequency
+        table when RoPE scaling is configured; split-half pairs for Qwen)."""
         c, lib, hd = self.cfg, self.lib, self.cfg.head_dim
-        if self.inv_freq is None:
+        if L is not None and (L['qkv_bias'] is not None or L['q_norm'] is not None or L['k_norm'] is not None):
+            ptr = lambda t: None if t is None else t.data_ptr()
+            _lib.check(lib.b200q_qkv_bias_norm_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, ptr(L['qkv_bias']),
+                                                   ptr(L['q_norm']), ptr(L['k_norm']), c.eps, st))
+        if self.inv_freq is None and not self.neox:
             _lib.check(lib.b200q_rope_kv_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
                                              self.pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), c.max_seq, st))
         else:
-            _lib.check(lib.b200q_rope_kv_freq_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary,
-                                                  self.inv_freq.data_ptr(), self.pos.data_ptr(), kc.data_ptr(),
-                                                  vc.data_ptr(), c.max_seq, st))
+            _lib.check(lib.b200q_rope_kv_ex_dev(qkv.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, self.rotary, c.rope_base,
+                                                None if self.inv_freq is None else self.inv_freq.data_ptr(),
+                                                1 if self.neox else 0, self.pos.data_ptr(), kc.data_ptr(),
+                                                vc.data_ptr(), c.max_seq, st))
 
     def _gemv(self, w, x, y, rows, cols):
         raw, t = w
@@ -180,7 +199,7 @@ class QuantLlama:
                                                  None, st))
             self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            self._rope(self.qkv, 1, kc, vc, st)
+            self._rope(self.qkv, 1, kc, vc, st, L)
             _lib.check(lib.b200q_attn_decode_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                                  self.pos.data_ptr(), c.n_heads, c.n_kv_heads, hd, c.max_seq,
                                                  self.scratch.data_ptr(), self.att.data_ptr(), st))
@@ -242,7 +261,7 @@ class QuantLlama:
             ops.gemm_quant(Hb, wq, off, k=c.d_model, n_feat=nq, w_rows_per_group=nq, ggml_type=tq, w_row_bytes=sq,
                            out=qkv)
             kc, vc = self.k_cache[li], self.v_cache[li]
-            self._rope(qkv, T, kc, vc, st)
+            self._rope(qkv, T, kc, vc, st, L)
             if scratch is not None:
                 _lib.check(lib.b200q_attn_prefill_tc_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                                          self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd,

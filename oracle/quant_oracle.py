@@ -413,7 +413,11 @@ def llama_decode_f64(w, cfg, tokens):
     'attn_norm': [D], 'ffn_norm': [D]}]} as float arrays; ``cfg`` with
     n_heads, n_kv_heads, rope_base, eps (and optional rope_dim, and RoPE
     scaling: rope_scaling 'llama3' / 'linear' with rope_factor, rope_orig_ctx,
-    rope_low_freq, rope_high_freq -- engine/model.py:199-214).
+    rope_low_freq, rope_high_freq -- engine/model.py:199-214; arch 'qwen2' /
+    'qwen3': split-half RoPE pairs, engine/model.py:212-221).  A layer may add
+    'attn_q_bias' / 'attn_k_bias' / 'attn_v_bias' (projection biases,
+    engine/model.py:73-79) and 'attn_q_norm' / 'attn_k_norm' (per-head RMSNorm
+    weights [hd], engine/model.py:188-192).
     """
     H, KV = cfg['n_heads'], cfg['n_kv_heads']
     D = w['token_embd'].shape[1]
@@ -422,7 +426,8 @@ def llama_decode_f64(w, cfg, tokens):
     rotary -= rotary % 2
     half = rotary // 2
     eps = cfg['eps']
-    norm = lambda x, g: x * (1.0 / np.sqrt(np.mean(x * x) + eps)) * g
+    norm = lambda x, g: x * (1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)) * g
+    neox = cfg.get('arch', 'llama') != 'llama'
     nl = len(w['layers'])
     kc = [[] for _ in range(nl)]
     vc = [[] for _ in range(nl)]
@@ -435,16 +440,30 @@ def llama_decode_f64(w, cfg, tokens):
 
         def rope(a):
             z = a.copy()
-            e, o = a[:, 0:rotary:2].copy(), a[:, 1:rotary:2].copy()
-            z[:, 0:rotary:2] = e * c - o * s_
-            z[:, 1:rotary:2] = e * s_ + o * c
+            if neox:
+                e, o = a[:, :half].copy(), a[:, half:rotary].copy()
+                z[:, :half] = e * c - o * s_
+                z[:, half:rotary] = e * s_ + o * c
+            else:
+                e, o = a[:, 0:rotary:2].copy(), a[:, 1:rotary:2].copy()
+                z[:, 0:rotary:2] = e * c - o * s_
+                z[:, 1:rotary:2] = e * s_ + o * c
             return z
+
+        def proj(L, name, h, heads):
+            y = L[name] @ h
+            if name + '_bias' in L:
+                y = y + L[name + '_bias']
+            y = y.reshape(heads, hd)
+            if name + '_norm' in L:
+                y = norm(y, L[name + '_norm'])
+            return y
         for li, L in enumerate(w['layers']):
             pre = x
             h = norm(x, L['attn_norm'])
-            q = rope((L['attn_q'] @ h).reshape(H, hd))
-            k = rope((L['attn_k'] @ h).reshape(KV, hd))
-            v = (L['attn_v'] @ h).reshape(KV, hd)
+            q = rope(proj(L, 'attn_q', h, H))
+            k = rope(proj(L, 'attn_k', h, KV))
+            v = proj(L, 'attn_v', h, KV)
             kc[li].append(k)
             vc[li].append(v)
             ks, vs = np.stack(kc[li]), np.stack(vc[li])          # [L, KV, hd]

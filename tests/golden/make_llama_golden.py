@@ -1,6 +1,7 @@
 """Generate tests/golden/llama_decode_golden.npz by running the reference's own
 ``LlamaModel.forward`` (engine/model.py:174-240) token by token on a tiny
-stub model with f32 weights, plain RoPE and with llama3 / linear RoPE scaling.
+stub model with f32 weights, plain RoPE and with llama3 / linear RoPE scaling,
+and in the Qwen2 / Qwen3 layouts.
 
 The stub supplies what ``forward`` touches: ``gguf`` (``metadata``,
 ``tensors``, ``find``), ``w`` and ``mat`` (a plain f32 ``x @ W.T``, standing in
@@ -69,9 +70,43 @@ def main(ref_root):
         m.rope_original_context, m.rope_low_freq, m.rope_high_freq = 64, 1.0, 4.0
         m.cache = KVCache(NL, KV, hd, 32)
         scaled['logits_' + kind] = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
+    # Qwen layouts (engine/model.py:184-221): split-half RoPE pairs; qwen3 with
+    # per-head q/k RMSNorm weights and its FFN norm named post_attention_norm,
+    # qwen2 with q/k/v projection biases (added by the reference's own
+    # _mat_impl, which these runs use instead of the plain stub matvec)
+    extra = {}
+    for l in range(NL):
+        p = f'blk.{l}.'
+        extra[p + 'attn_q_norm.weight'] = (1 + f(hd, sc=0.2)).astype(np.float32)
+        extra[p + 'attn_k_norm.weight'] = (1 + f(hd, sc=0.2)).astype(np.float32)
+        extra[p + 'post_attention_norm.weight'] = T[p + 'ffn_norm.weight']
+        extra[p + 'attn_q.bias'] = f(H * hd, sc=0.5)
+        extra[p + 'attn_k.bias'] = f(KV * hd, sc=0.5)
+        extra[p + 'attn_v.bias'] = f(KV * hd, sc=0.5)
+    m.rope_scaling_type, m.rope_scaling_factor = 'none', 1.0
+    for arch in ('qwen3', 'qwen2'):
+        keep = (lambda n: 'bias' not in n) if arch == 'qwen3' else (lambda n: 'norm' not in n or 'attn_norm' in n)
+        TT = dict(T, **{k: v for k, v in extra.items() if keep(k) and not (arch == 'qwen2' and 'post_attention' in k)})
+
+        class GQ(GG):
+            tensors = dict.fromkeys(TT)
+
+            def find(self, *names):
+                for n in names:
+                    if n in TT:
+                        return n
+                return None
+
+        m.gguf = GQ()
+        m.arch = arch
+        m.cache = KVCache(NL, KV, hd, 32)
+        m.w = lambda name, TT=TT: TT[name]
+        m.mat = lambda x, name: LlamaModel._mat_impl(m, np.asarray(x, np.float32), name).astype(np.float32)
+        scaled['logits_' + arch] = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
     out = Path(__file__).resolve().parent / 'llama_decode_golden.npz'
     np.savez_compressed(out, logits=logits, tokens=np.array(tokens), **scaled,
-                        **{k.replace('.', '_'): v for k, v in T.items()})
+                        **{k.replace('.', '_'): v for k, v in T.items()},
+                        **{k.replace('.', '_'): v for k, v in extra.items()})
     print('wrote', out)
 
 

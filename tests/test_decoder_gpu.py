@@ -17,7 +17,7 @@ from localai_b200.decoder import LlamaConfig, QuantLlama
 pytestmark = pytest.mark.gpu
 
 
-def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None):
+def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None, arch='llama'):
     gen = {8: synth.q8_0, 12: synth.q4_k}[t]
     dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
     hd = D // H
@@ -31,6 +31,13 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None
                  'ffn_norm': (1 + rng.normal(0, 0.1, D)).astype(np.float32)}
         shapes = {'attn_q': (H * hd, D), 'attn_k': (KV * hd, D), 'attn_v': (KV * hd, D), 'attn_output': (D, D),
                   'ffn_gate': (F, D), 'ffn_up': (F, D), 'ffn_down': (D, F)}
+        if arch == 'qwen3':                                           # per-head q/k RMSNorm weights
+            norms.update({'attn_q_norm': (1 + rng.normal(0, 0.2, hd)).astype(np.float32),
+                          'attn_k_norm': (1 + rng.normal(0, 0.2, hd)).astype(np.float32)})
+        if arch == 'qwen2':                                           # q/k/v projection biases
+            norms.update({'attn_q_bias': rng.normal(0, 0.5, H * hd).astype(np.float32),
+                          'attn_k_bias': rng.normal(0, 0.5, KV * hd).astype(np.float32),
+                          'attn_v_bias': rng.normal(0, 0.5, KV * hd).astype(np.float32)})
         layers_dev.append({**{k: (dev(v), t) for k, v in L.items()}, **{k: torch.from_numpy(v).cuda() for k, v in norms.items()}})
         layers_ref.append({**{k: o.dequantize(v, t, shapes[k]).astype(np.float64) for k, v in L.items()}, **norms})
     on = (1 + rng.normal(0, 0.1, D)).astype(np.float32)
@@ -41,8 +48,9 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None
              'layers': layers_ref}
     sc = scaling or {}
     cfg = LlamaConfig(n_layers=NL, d_model=D, n_heads=H, n_kv_heads=KV, d_ff=F, vocab=V, rope_base=10000.0,
-                      eps=1e-5, max_seq=max_seq, **sc)
-    return QuantLlama(weights, cfg), ref_w, {'n_heads': H, 'n_kv_heads': KV, 'rope_base': 10000.0, 'eps': 1e-5, **sc}
+                      eps=1e-5, max_seq=max_seq, arch=arch, **sc)
+    return QuantLlama(weights, cfg), ref_w, {'n_heads': H, 'n_kv_heads': KV, 'rope_base': 10000.0, 'eps': 1e-5,
+                                             'arch': arch, **sc}
 
 
 @pytest.mark.parametrize('t', [8, 12])
@@ -148,9 +156,58 @@ def test_rope_scaling_decode_and_prefill_match_oracle(kind, fac):
     assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
 
 
+@pytest.mark.parametrize('arch', ['qwen2', 'qwen3'])
+def test_qwen_layouts_decode_and_prefill_match_oracle(arch):
+    """Qwen2 (q/k/v projection biases) and Qwen3 (per-head q/k RMSNorm), both
+    with split-half RoPE pairs (engine/model.py:184-221): decode logits within
+    1e-3 of the float64 oracle, prefill within 3e-2, greedy tokens equal."""
+    rng = np.random.default_rng(71 if arch == 'qwen2' else 72)
+    model, ref_w, cfg = build(rng, 12, max_seq=96, arch=arch)
+    assert model.neox
+    tokens = [int(v) for v in rng.integers(0, 300, size=24)]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    assert model.tokens[:len(tokens)].cpu().tolist() == [int(np.argmax(r)) for r in ref]
+    model.reset()
+    model.prefill(tokens)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
+@pytest.mark.parametrize('H,KV,hd', [(4, 2, 64), (2, 1, 128)])
+def test_qkv_bias_norm_kernel(H, KV, hd):
+    """b200q_qkv_bias_norm_dev: bias added to every q/k/v value, then each q
+    and k head RMS-normalised with its weights; v heads only biased."""
+    from localai_b200 import _lib
+    rng = np.random.default_rng(H + hd)
+    T, eps = 3, 1e-6
+    n = (H + 2 * KV) * hd
+    qkv = rng.normal(size=(T, n)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    qn, kn = rng.normal(1, 0.2, hd).astype(np.float32), rng.normal(1, 0.2, hd).astype(np.float32)
+    ref = (qkv.astype(np.float64) + bias).reshape(T, H + 2 * KV, hd)
+    for hh in range(H + KV):
+        g = qn if hh < H else kn
+        a = ref[:, hh]
+        ref[:, hh] = a / np.sqrt(np.mean(a * a, axis=-1, keepdims=True) + eps) * g
+    d = torch.from_numpy(qkv).cuda()
+    t = lambda a: torch.from_numpy(a).cuda()
+    bd, qd, kd = t(bias), t(qn), t(kn)
+    lib = _lib.load()
+    _lib.check(lib.b200q_qkv_bias_norm_dev(d.data_ptr(), T, H, KV, hd, bd.data_ptr(), qd.data_ptr(), kd.data_ptr(),
+                                           eps, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(d.cpu().numpy(), ref.reshape(T, n), rtol=0, atol=2e-5)
+
+
 @pytest.mark.parametrize('kind,fac', [('llama3', 8.0), ('linear', 4.0)])
 def test_rope_kv_freq_table(kind, fac):
-    """b200q_rope_kv_freq_dev: pair j of q and k turns by pos * inv_freq[j]
+    """b200q_rope_kv_ex_dev: pair j of q and k turns by pos * inv_freq[j]
     (the scaled table of rope_inv_freq), not by base^(-j/half); k and v land
     in the caches."""
     from localai_b200 import _lib, ops
@@ -177,9 +234,9 @@ def test_rope_kv_freq_table(kind, fac):
     pos = torch.tensor([p0], dtype=torch.int32, device='cuda')
     invd = torch.from_numpy(inv).cuda()
     lib = _lib.load()
-    _lib.check(lib.b200q_rope_kv_freq_dev(qd.data_ptr(), T, H, KV, hd, hd, invd.data_ptr(), pos.data_ptr(),
-                                          kc.data_ptr(), vc.data_ptr(), max_seq,
-                                          torch.cuda.current_stream().cuda_stream))
+    _lib.check(lib.b200q_rope_kv_ex_dev(qd.data_ptr(), T, H, KV, hd, hd, 10000.0, invd.data_ptr(), 0,
+                                        pos.data_ptr(), kc.data_ptr(), vc.data_ptr(), max_seq,
+                                        torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     ops.check_device_error()
     np.testing.assert_allclose(qd.cpu().numpy(), ref, rtol=0, atol=5e-5)

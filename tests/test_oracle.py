@@ -261,6 +261,23 @@ def test_llama_decode_oracle_matches_reference_golden():
         ref = d['logits_' + kind].astype(np.float64)
         assert o.normwise_rel_err(got, ref) < 1e-5, kind
         assert o.normwise_rel_err(ref, d['logits'].astype(np.float64)) > 1e-2     # the scaling changes the logits
+    # Qwen layouts (engine/model.py:184-221): split-half RoPE pairs; qwen3 with
+    # per-head q/k norms, qwen2 with q/k/v projection biases
+    for arch in ('qwen3', 'qwen2'):
+        lw = []
+        for l in range(NL):
+            L = dict(w['layers'][l])
+            if arch == 'qwen3':
+                L['attn_q_norm'] = d[f'blk_{l}_attn_q_norm_weight']
+                L['attn_k_norm'] = d[f'blk_{l}_attn_k_norm_weight']
+            else:
+                for n in ('q', 'k', 'v'):
+                    L[f'attn_{n}_bias'] = d[f'blk_{l}_attn_{n}_bias']
+            lw.append(L)
+        got = o.llama_decode_f64(dict(w, layers=lw), dict(cfg, arch=arch), list(d['tokens']))
+        ref = d['logits_' + arch].astype(np.float64)
+        assert o.normwise_rel_err(got, ref) < 1e-5, arch
+        assert o.normwise_rel_err(ref, d['logits'].astype(np.float64)) > 1e-2
 
 
 def test_rope_frequency_table_matches_oracle():
