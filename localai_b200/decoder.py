@@ -2,8 +2,8 @@
 
 ``engine/model.py:174-240`` (``LlamaModel.forward``, arch 'llama' / 'qwen2' /
 'qwen3', RoPE plain or scaled: llama3 / linear) runs one token through every
-layer with NumPy and the native
-quantised matvecs.  ``QuantLlama`` keeps every weight on the device in its raw
+layer with NumPy and the native quantised matvecs.  ``QuantLlama`` keeps
+every weight on the device in its raw
 GGUF form and runs one token per *step*:
 
     x = emb[token]                                  b200q_dequant_row_dev
