@@ -870,9 +870,75 @@ bool gemv_mma_supported(int type, const void *w, int rows, int cols, int tokens)
 cudaError_t launch_gemv_mma(const void *w, const float *x, float *y, long long ys_r, int rows, int cols, int *err,
                             int num_sms, cudaStream_t st);
 
+// Unquantised weights (GGML F32 = 0, F16 = 1; engine/gguf_parser.py:180-288
+// takes those through NumPy): y[t * ys_t + r * ys_r] = sum_c W[r, c] x[t, c],
+// f32 accumulation.  One warp per row and up to 8 tokens per pass: the row
+// streams once per pass with 16-byte loads (8 halves or 4 floats per lane per
+// load), x rows come from L1/L2.  cols a multiple of 8.
+template <typename TW>
+__global__ void __launch_bounds__(256) gemv_dense_kernel(const TW *__restrict__ w, const float *__restrict__ x,
+                                                         float *__restrict__ y, long long ys_t, long long ys_r,
+                                                         int rows, int cols, int tokens)
+{
+    const long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const TW *wr = w + r * cols;
+    for (int t0 = 0; t0 < tokens; t0 += 8) {
+        const int nt = min(8, tokens - t0);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int c = lane * 8; c < cols; c += 256) {
+            float wv[8];
+            if constexpr (sizeof(TW) == 2) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4 *>(wr + c));
+                const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    wv[2 * i] = h2f(uw[i]);
+                    wv[2 * i + 1] = h2f(uw[i] >> 16);
+                }
+            } else {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(wr + c));
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(wr + c + 4));
+                wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+                wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (t >= nt) break;
+                const float *xr = x + (long long)(t0 + t) * cols + c;
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(xr));
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(xr + 4));
+                acc[t] = fmaf(wv[0], a.x, fmaf(wv[1], a.y, fmaf(wv[2], a.z, fmaf(wv[3], a.w, acc[t]))));
+                acc[t] = fmaf(wv[4], b.x, fmaf(wv[5], b.y, fmaf(wv[6], b.z, fmaf(wv[7], b.w, acc[t]))));
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float v = acc[t];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && t < nt) y[(t0 + t) * ys_t + r * ys_r] = v;
+        }
+    }
+}
+
 cudaError_t launch_gemv(int type, const void *w, const float *x, float *y, long long ys_t, long long ys_r, int rows,
                         int cols, int tokens, int *err, int num_sms, cudaStream_t st)
 {
+    if (type == 0 || type == 1) {
+        if (rows < 1 || tokens < 1 || cols < 8 || cols % 8 || (reinterpret_cast<uintptr_t>(w) & 15) ||
+            (reinterpret_cast<uintptr_t>(x) & 15))
+            return cudaErrorInvalidValue;
+        const unsigned grid = (unsigned)(((long long)rows * 32 + 255) / 256);
+        if (type == 1)
+            gemv_dense_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half *>(w), x, y, ys_t, ys_r, rows,
+                                                            cols, tokens);
+        else
+            gemv_dense_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(w), x, y, ys_t, ys_r, rows, cols,
+                                                           tokens);
+        return cudaGetLastError();
+    }
     const int vals = type_vals(type), bytes = type_bytes(type);
     if (!bytes || rows < 1 || tokens < 1 || cols < vals || cols % vals) return cudaErrorInvalidValue;
     // batch-1 Q4_K: the integer-tensor-core kernel (gemv_mma.cu)

@@ -294,8 +294,11 @@ class DeviceGGUF:
             raise ValueError(f'{name}: expected {cols} input columns, got {X.shape[-1]}')
         w = self.device_tensors[name]
         if x.ggml_type in (GGML_F32, GGML_F16):
+            if X.shape[0] <= 16 and cols % 8 == 0 and w.data_ptr() % 16 == 0:
+                # a few tokens (decode): the library's dense GEMV streams the f16/f32 rows once
+                return ops.gemv(w, X.contiguous(), x.ggml_type, rows, cols)
             m = w.view(torch.float32 if x.ggml_type == GGML_F32 else torch.float16).reshape(rows, cols).float()
-            return X @ m.T
+            return X @ m.T                      # prompt-sized batches: a plain library GEMM
         return ops.matmul(w, X, x.ggml_type, rows, cols)
 
     def matvec(self, name, vector):

@@ -10,6 +10,8 @@ import torch
 from . import _lib
 
 BLOCK = {2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+# unquantised GGML types the GEMV also takes: bytes per value (F32, F16)
+DENSE = {0: 4, 1: 2}
 
 
 def _stream():
@@ -17,6 +19,8 @@ def _stream():
 
 
 def row_bytes(ggml_type: int, cols: int) -> int:
+    if ggml_type in DENSE:
+        return cols * DENSE[ggml_type]
     vals, nbytes = BLOCK[ggml_type]
     if cols % vals:
         raise ValueError(f'cols={cols} not a multiple of block {vals}')
@@ -24,7 +28,7 @@ def row_bytes(ggml_type: int, cols: int) -> int:
 
 
 def _check_weights(w: torch.Tensor, ggml_type: int, rows: int, cols: int):
-    if ggml_type not in BLOCK:
+    if ggml_type not in BLOCK and ggml_type not in DENSE:
         raise ValueError(f'unsupported GGML type {ggml_type}')
     if not w.is_cuda or w.dtype != torch.uint8:
         raise ValueError('weights must be a CUDA uint8 tensor of raw GGUF blocks')
@@ -60,7 +64,9 @@ def gemv(w: torch.Tensor, x: torch.Tensor, ggml_type: int, rows: int, cols: int,
     """y = x @ W^T with f32 accumulation.
 
     ``x`` is f32 [cols] or [tokens, cols]; the result is [rows] or
-    [tokens, rows].  Suited to decode (1 token) and small batches.
+    [tokens, rows].  Suited to decode (1 token) and small batches.  Besides
+    the block-quantised types, F32 (0) and F16 (1) rows are taken (cols a
+    multiple of 8, 16-byte aligned).
     """
     _check_weights(w, ggml_type, rows, cols)
     squeeze = x.dim() == 1
