@@ -395,6 +395,10 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  *                           b200q_attn_decode_scratch_floats floats; hd a
  *                           multiple of 4 up to 128, H / KV <= 8, q and the
  *                           caches 16-byte aligned
+ *   b200q_attn_decode_ex_dev, b200q_attn_prefill_ex_dev  the same with a
+ *                           sliding window (engine/model.py:222): a query at
+ *                           position p sees positions max(0, p + 1 - window)
+ *                           .. p (window 0: all)
  *   b200q_argmax_dev        *token = argmax(logits) (first index on ties);
  *                           with pos: out_tokens[*pos] = token, ++*pos;
  *                           key: optional zero-initialised 64-bit device word
@@ -411,6 +415,8 @@ int b200q_qkv_bias_norm_dev(float *qkv, int T, int H, int KV, int hd, const floa
                             const float *k_norm, float eps, void *stream);
 int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T, int H,
                            int KV, int hd, int max_seq, void *out_bf16, void *stream);
+int b200q_attn_prefill_ex_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos, int T,
+                              int H, int KV, int hd, int max_seq, int window, void *out_bf16, void *stream);
 /* b200q_attn_prefill_dev on the tensor cores (tcgen05: bf16 operands, f32
  * accumulation, P in bf16), hd = 128: the rotated queries and the cache rows
  * 0 .. *pos + T - 1 are first copied as bf16 into ``scratch``
@@ -425,6 +431,8 @@ int b200q_attn_prefill_tc_dev(const float *qkv, const float *k_cache, const floa
 size_t b200q_attn_decode_scratch_floats(int H, int hd, int max_seq);
 int b200q_attn_decode_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H, int KV,
                           int hd, int max_seq, float *scratch, float *out, void *stream);
+int b200q_attn_decode_ex_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos, int H, int KV,
+                             int hd, int max_seq, int window, float *scratch, float *out, void *stream);
 int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
                      unsigned long long *key, void *stream);
 

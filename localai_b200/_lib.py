@@ -76,10 +76,12 @@ SIGNATURES = {
     'b200q_rope_kv_ex_dev': (_i, [_vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _i, _vp, _vp, _vp, _i, _vp]),
     'b200q_qkv_bias_norm_dev': (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_float, _vp]),
     'b200q_attn_prefill_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    'b200q_attn_prefill_ex_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     'b200q_attn_prefill_tc_scratch_bytes': (_sz, [_i, _i, _i, _i, _i]),
     'b200q_attn_prefill_tc_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp, _vp]),
     'b200q_attn_decode_scratch_floats': (_sz, [_i, _i, _i]),
     'b200q_attn_decode_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    'b200q_attn_decode_ex_dev': (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     'b200q_argmax_dev': (_i, [_vp, _i, _vp, _vp, _vp, _i, _vp, _vp]),
     'b200q_ep_create': (_i, [_i, _i, _i, _i, _ll, _ll, ctypes.POINTER(_vp)]),
     'b200q_ep_handle_bytes': (_sz, []),

@@ -92,14 +92,14 @@ cudaError_t launch_rope_kv(float *qkv, int T, int H, int KV, int hd, int rotary,
 cudaError_t launch_qkv_bias_norm(float *qkv, int T, int H, int KV, int hd, const float *bias, const float *qn,
                                  const float *kn, float eps, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
-                                int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st);
+                                int KV, int hd, int max_seq, int window, __nv_bfloat16 *out, int *err, cudaStream_t st);
 size_t attn_prefill_tc_scratch_bytes(int T, int H, int KV, int hd, int max_seq);
 cudaError_t launch_attn_prefill_tc(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
                                    int KV, int hd, int max_seq, void *scratch, size_t scratch_bytes,
                                    __nv_bfloat16 *out, int *err, int num_sms, cudaStream_t st);
 size_t attn_scratch_floats(int H, int hd, int max_seq);
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
-                               int max_seq, float *part, float *out, cudaStream_t st);
+                               int max_seq, int window, float *part, float *out, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
                           unsigned long long *key, int num_sms, cudaStream_t st);
 cudaError_t launch_moe_gather_f32(const float *h, int T, const int *token_of, int S, int D, float *out, int *err,
@@ -1008,9 +1008,21 @@ B200Q_API int b200q_attn_decode_dev(const float *q, const float *k_cache, const 
     std::lock_guard<std::recursive_mutex> g(g_lock);
     if (!q || !k_cache || !v_cache || !pos || !scratch || !out) return set_status(B200Q_EINVAL, "attn: null pointer");
     g_launches += 2;
-    return cuda_status(launch_attn_decode(q, k_cache, v_cache, pos, H, KV, hd, max_seq, scratch, out,
+    return cuda_status(launch_attn_decode(q, k_cache, v_cache, pos, H, KV, hd, max_seq, 0, scratch, out,
                                           (cudaStream_t)stream),
                        "attn_decode");
+}
+
+B200Q_API int b200q_attn_decode_ex_dev(const float *q, const float *k_cache, const float *v_cache, const int *pos,
+                                       int H, int KV, int hd, int max_seq, int window, float *scratch, float *out,
+                                       void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!q || !k_cache || !v_cache || !pos || !scratch || !out) return set_status(B200Q_EINVAL, "attn: null pointer");
+    g_launches += 2;
+    return cuda_status(launch_attn_decode(q, k_cache, v_cache, pos, H, KV, hd, max_seq, window, scratch, out,
+                                          (cudaStream_t)stream),
+                       "attn_decode_ex");
 }
 
 B200Q_API int b200q_argmax_dev(const float *logits, int V, int *token, int *pos, int *out_tokens, int max_tokens,
@@ -1055,7 +1067,21 @@ B200Q_API int b200q_attn_prefill_dev(const float *qkv, const float *k_cache, con
     DevInfo *di = nullptr;
     if (current_device_info(&di) != B200Q_OK) return g_status;
     ++g_launches;
-    return cuda_status(launch_attn_prefill(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq,
+    return cuda_status(launch_attn_prefill(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq, 0,
                                            static_cast<__nv_bfloat16 *>(out_bf16), di->err, (cudaStream_t)stream),
                        "attn_prefill");
+}
+
+B200Q_API int b200q_attn_prefill_ex_dev(const float *qkv, const float *k_cache, const float *v_cache, const int *pos,
+                                        int T, int H, int KV, int hd, int max_seq, int window, void *out_bf16,
+                                        void *stream)
+{
+    std::lock_guard<std::recursive_mutex> g(g_lock);
+    if (!qkv || !k_cache || !v_cache || !pos || !out_bf16) return set_status(B200Q_EINVAL, "attn_prefill: null pointer");
+    DevInfo *di = nullptr;
+    if (current_device_info(&di) != B200Q_OK) return g_status;
+    ++g_launches;
+    return cuda_status(launch_attn_prefill(qkv, k_cache, v_cache, pos, T, H, KV, hd, max_seq, window,
+                                           static_cast<__nv_bfloat16 *>(out_bf16), di->err, (cudaStream_t)stream),
+                       "attn_prefill_ex");
 }

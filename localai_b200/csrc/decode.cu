@@ -175,13 +175,14 @@ __device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem)
 __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(const float *__restrict__ q, const float *__restrict__ kc,
                                                                  const float *__restrict__ vc,
                                                                  const int *__restrict__ pos_p, int H, int KV, int hd,
-                                                                 int max_seq, float *__restrict__ part)
+                                                                 int max_seq, int window, float *__restrict__ part)
 {
     extern __shared__ __align__(16) float asm_[];
     pdl_enter();
     const int G = H / KV, g = blockIdx.x, c = blockIdx.y;
     const int L = min(*pos_p + 1, max_seq);
-    const int l0 = c * ATT_CHUNK, l1 = min(L, l0 + ATT_CHUNK);
+    // sliding window (engine/model.py:222): only the last ``window`` positions
+    const int l0 = max(c * ATT_CHUNK, window > 0 ? L - window : 0), l1 = min(L, c * ATT_CHUNK + ATT_CHUNK);
     const int nch = gridDim.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hd4 = hd >> 2;
@@ -308,8 +309,8 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
                                                                   const float *__restrict__ kc,
                                                                   const float *__restrict__ vc,
                                                                   const int *__restrict__ pos_p, int T, int H, int KV,
-                                                                  int hd, int max_seq, __nv_bfloat16 *__restrict__ out,
-                                                                  int *err)
+                                                                  int hd, int max_seq, int window,
+                                                                  __nv_bfloat16 *__restrict__ out, int *err)
 {
     extern __shared__ __align__(16) float pf[];
     pdl_enter();
@@ -347,8 +348,11 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
             else *reinterpret_cast<float4 *>(d) = zero4;
         }
     };
-    load_rows(ks, kc, 0);
-    load_rows(vs, vc, 0);
+    // sliding window (engine/model.py:222): row r sees keys (p0 + t0 + r - window, p0 + t0 + r];
+    // key tiles before the first row's window are skipped
+    const int kfirst = window > 0 ? max(0, p0 + t0 - window + 1) / PF_K * PF_K : 0;
+    load_rows(ks, kc, kfirst);
+    load_rows(vs, vc, kfirst);
 
     float m[4], l[4], acc[4][8];
 #pragma unroll
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
         for (int d = 0; d < 8; ++d) acc[i][d] = 0.f;
     }
     const float rs = sqrtf((float)hd);
-    for (int k0 = 0; k0 <= kmax; k0 += PF_K) {
+    for (int k0 = kfirst; k0 <= kmax; k0 += PF_K) {
         const int nk = min(PF_K, kmax + 1 - k0);
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();                                  // this tile's K and V (and q) are in place
@@ -389,7 +393,8 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 const int key = tx + 16 * jj;
-                const bool ok = row < nq && key < nk && k0 + key <= p0 + t0 + row;
+                const bool ok = row < nq && key < nk && k0 + key <= p0 + t0 + row &&
+                                (window <= 0 || k0 + key > p0 + t0 + row - window);
                 sc[i][jj] = ok ? sc[i][jj] / rs : -INFINITY;
                 tmax = fmaxf(tmax, sc[i][jj]);
             }
@@ -466,9 +471,9 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(const float *_
 }
 
 cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *vc, const int *pos, int T, int H,
-                                int KV, int hd, int max_seq, __nv_bfloat16 *out, int *err, cudaStream_t st)
+                                int KV, int hd, int max_seq, int window, __nv_bfloat16 *out, int *err, cudaStream_t st)
 {
-    if (T < 1 || H < 1 || KV < 1 || H % KV || (hd != 64 && hd != 128) || max_seq < 1 ||
+    if (T < 1 || H < 1 || KV < 1 || H % KV || (hd != 64 && hd != 128) || max_seq < 1 || window < 0 ||
         (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(kc) & 15) ||
         (reinterpret_cast<uintptr_t>(vc) & 15) || (reinterpret_cast<uintptr_t>(out) & 7))
         return cudaErrorInvalidValue;
@@ -480,7 +485,7 @@ cudaError_t launch_attn_prefill(const float *qkv, const float *kc, const float *
         attr = smem;
     }
     return launch_pdl(attn_prefill_kernel, dim3(H, (T + PF_Q - 1) / PF_Q), dim3(PF_THREADS), smem, st, qkv, kc, vc, pos,
-                      T, H, KV, hd, max_seq, out, err);
+                      T, H, KV, hd, max_seq, window, out, err);
 }
 
 // out[h][d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) s_c, chunks in
@@ -648,9 +653,9 @@ size_t attn_scratch_floats(int H, int hd, int max_seq)
 }
 
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, const int *pos, int H, int KV, int hd,
-                               int max_seq, float *part, float *out, cudaStream_t st)
+                               int max_seq, int window, float *part, float *out, cudaStream_t st)
 {
-    if (H < 1 || KV < 1 || H % KV || hd < 4 || hd > 128 || hd % 4 || H / KV > ATT_MAXG || max_seq < 1 ||
+    if (H < 1 || KV < 1 || H % KV || hd < 4 || hd > 128 || hd % 4 || H / KV > ATT_MAXG || max_seq < 1 || window < 0 ||
         (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kc) & 15) ||
         (reinterpret_cast<uintptr_t>(vc) & 15))
         return cudaErrorInvalidValue;
@@ -664,7 +669,7 @@ cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc,
         attr = smem;
     }
     cudaError_t e = launch_pdl(attn_chunk_kernel, dim3(KV, nch), dim3(ATT_THREADS), smem, st, q, kc, vc, pos, H, KV, hd,
-                               max_seq, part);
+                               max_seq, window, part);
     if (e != cudaSuccess) return e;
     return launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, part, nch, hd, out);
 }

@@ -11,7 +11,7 @@ GGUF form and runs one token per *step*:
         h = rmsnorm(x) * attn_norm                  b200q_add_rmsnorm_dev
         qkv = [Wq; Wk; Wv] h                        b200q_gemv_dev (one GEMV)
         rope(q, k); cache[pos] = k, v               b200q_rope_kv_dev
-        att = softmax(q k^T / sqrt(hd)) v           b200q_attn_decode_dev
+        att = softmax(q k^T / sqrt(hd)) v           b200q_attn_decode_ex_dev
         x += Wo att; h = rmsnorm(x) * ffn_norm      b200q_gemv_dev, b200q_add_rmsnorm_dev
         x += Wdown silu([Wgate; Wup] h)             b200q_gemv_dev, b200q_silu_mul_dev, b200q_gemv_dev
     logits = Wout (rmsnorm(x) * output_norm)        b200q_gemv_dev
@@ -66,6 +66,9 @@ class LlamaConfig:
     # layers per-head q/k norms (the optional 'attn_{q,k,v}_bias' and
     # 'attn_{q,k}_norm' entries of a layer's weights)
     arch: str = 'llama'
+    # {arch}.attention.sliding_window: a query attends to the last this many
+    # positions (engine/model.py:222); 0 = all
+    sliding_window: int = 0
 
     @property
     def head_dim(self) -> int:
@@ -118,6 +121,8 @@ class QuantLlama:
         self.dev = dev
         inv = rope_inv_freq(c, self.rotary)
         self.inv_freq = None if inv is None else torch.from_numpy(inv).to(dev)
+        if c.sliding_window < 0:
+            raise ValueError('sliding_window must be >= 0')
         if c.arch not in ('llama', 'qwen2', 'qwen3'):
             raise ValueError(f'unsupported architecture {c.arch!r}')
         self.neox = c.arch != 'llama'
@@ -200,9 +205,10 @@ class QuantLlama:
             self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
             kc, vc = self.k_cache[li], self.v_cache[li]
             self._rope(self.qkv, 1, kc, vc, st, L)
-            _lib.check(lib.b200q_attn_decode_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                                 self.pos.data_ptr(), c.n_heads, c.n_kv_heads, hd, c.max_seq,
-                                                 self.scratch.data_ptr(), self.att.data_ptr(), st))
+            _lib.check(lib.b200q_attn_decode_ex_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                    self.pos.data_ptr(), c.n_heads, c.n_kv_heads, hd, c.max_seq,
+                                                    c.sliding_window, self.scratch.data_ptr(), self.att.data_ptr(),
+                                                    st))
             self._gemv(L['o'], self.att, self.o, c.d_model, c.d_model)
             _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), self.o.data_ptr(), L['ffn_norm'].data_ptr(), 1,
                                                  c.d_model, c.eps, self.h.data_ptr(), None, st))
@@ -247,9 +253,10 @@ class QuantLlama:
         act = torch.empty((T, c.d_ff), dtype=torch.bfloat16, device=dev)
         Dn = torch.empty((T, c.d_model), dtype=torch.float32, device=dev)
         off = torch.tensor([0, T], dtype=torch.int32, device=dev)
-        # head dim 128: causal attention on the tensor cores (bf16 staging copies in scratch)
+        # head dim 128: causal attention on the tensor cores (bf16 staging copies in
+        # scratch); a sliding window takes the f32 kernel, which masks it
         scratch = None
-        if hd == 128:
+        if hd == 128 and c.sliding_window <= 0:
             nb = lib.b200q_attn_prefill_tc_scratch_bytes(T, c.n_heads, c.n_kv_heads, hd, c.max_seq)
             scratch = torch.empty(nb, dtype=torch.uint8, device=dev)
         delta = None
@@ -268,9 +275,9 @@ class QuantLlama:
                                                          c.max_seq, scratch.data_ptr(), scratch.numel(),
                                                          attb.data_ptr(), st))
             else:
-                _lib.check(lib.b200q_attn_prefill_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-                                                      self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd, c.max_seq,
-                                                      attb.data_ptr(), st))
+                _lib.check(lib.b200q_attn_prefill_ex_dev(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                         self.pos.data_ptr(), T, c.n_heads, c.n_kv_heads, hd,
+                                                         c.max_seq, c.sliding_window, attb.data_ptr(), st))
             wo, so, to = self._gemm_w(('o', li), L['o'], c.d_model, c.d_model)
             ops.gemm_quant(attb, wo, off, k=c.d_model, n_feat=c.d_model, w_rows_per_group=c.d_model, ggml_type=to,
                            w_row_bytes=so, out=O)

@@ -417,7 +417,8 @@ def llama_decode_f64(w, cfg, tokens):
     'qwen3': split-half RoPE pairs, engine/model.py:212-221).  A layer may add
     'attn_q_bias' / 'attn_k_bias' / 'attn_v_bias' (projection biases,
     engine/model.py:73-79) and 'attn_q_norm' / 'attn_k_norm' (per-head RMSNorm
-    weights [hd], engine/model.py:188-192).
+    weights [hd], engine/model.py:188-192); cfg 'sliding_window' > 0 limits
+    attention to the last that many positions (engine/model.py:222).
     """
     H, KV = cfg['n_heads'], cfg['n_kv_heads']
     D = w['token_embd'].shape[1]
@@ -466,7 +467,8 @@ def llama_decode_f64(w, cfg, tokens):
             v = proj(L, 'attn_v', h, KV)
             kc[li].append(k)
             vc[li].append(v)
-            ks, vs = np.stack(kc[li]), np.stack(vc[li])          # [L, KV, hd]
+            w0 = max(0, pos + 1 - cfg['sliding_window']) if cfg.get('sliding_window', 0) > 0 else 0
+            ks, vs = np.stack(kc[li][w0:]), np.stack(vc[li][w0:])   # [L, KV, hd] (engine/model.py:222)
             g = H // KV
             att = np.empty((H, hd))
             for hh in range(H):

@@ -103,6 +103,13 @@ def main(ref_root):
         m.w = lambda name, TT=TT: TT[name]
         m.mat = lambda x, name: LlamaModel._mat_impl(m, np.asarray(x, np.float32), name).astype(np.float32)
         scaled['logits_' + arch] = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
+    # sliding window of 3 positions (engine/model.py:222), llama layout
+    m.gguf, m.arch, m.w = GG(), 'llama', (lambda name: T[name])
+    m.mat = lambda x, name: (np.asarray(x, np.float32) @ T[name].T).astype(np.float32)
+    m.sliding_window = 3
+    m.cache = KVCache(NL, KV, hd, 32)
+    scaled['logits_window3'] = np.stack([m.forward(t, p) for p, t in enumerate(tokens)]).astype(np.float32)
+    m.sliding_window = 0
     out = Path(__file__).resolve().parent / 'llama_decode_golden.npz'
     np.savez_compressed(out, logits=logits, tokens=np.array(tokens), **scaled,
                         **{k.replace('.', '_'): v for k, v in T.items()},

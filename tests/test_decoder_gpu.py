@@ -179,6 +179,32 @@ def test_qwen_layouts_decode_and_prefill_match_oracle(arch):
     assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
 
 
+@pytest.mark.parametrize('D,H,KV,window', [(256, 4, 2, 5), (256, 2, 1, 130), (256, 4, 2, 64)])
+def test_sliding_window_decode_and_prefill_match_oracle(D, H, KV, window):
+    """Sliding-window attention (engine/model.py:222): decode attends to the
+    last ``window`` positions (chunks before the window skipped, the chunk
+    holding its start trimmed), prefill masks keys outside each row's window;
+    logits within 1e-3 (decode) and 3e-2 (prefill) of the float64 oracle over
+    enough tokens for the window to slide across attention chunks."""
+    rng = np.random.default_rng(80 + window)
+    model, ref_w, cfg = build(rng, 8, D=D, H=H, KV=KV, max_seq=320)
+    model.cfg.sliding_window = window
+    cfg = dict(cfg, sliding_window=window)
+    tokens = [int(v) for v in rng.integers(0, 300, size=150 if window > 100 else 90)]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        if p in (window - 1, window, window + 1, len(tokens) - 1) or p % 29 == 0:
+            torch.cuda.synchronize()
+            assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    model.reset()
+    model.prefill(tokens)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
 @pytest.mark.parametrize('H,KV,hd', [(4, 2, 64), (2, 1, 128)])
 def test_qkv_bias_norm_kernel(H, KV, hd):
     """b200q_qkv_bias_norm_dev: bias added to every q/k/v value, then each q

@@ -278,6 +278,9 @@ def test_llama_decode_oracle_matches_reference_golden():
         ref = d['logits_' + arch].astype(np.float64)
         assert o.normwise_rel_err(got, ref) < 1e-5, arch
         assert o.normwise_rel_err(ref, d['logits'].astype(np.float64)) > 1e-2
+    # sliding window of 3 positions (engine/model.py:222)
+    got = o.llama_decode_f64(w, dict(cfg, sliding_window=3), list(d['tokens']))
+    assert o.normwise_rel_err(got, d['logits_window3'].astype(np.float64)) < 1e-5
 
 
 def test_rope_frequency_table_matches_oracle():
