@@ -363,8 +363,9 @@ int b200q_ep_combine_dev(void *ep, const int *slot_of, const float *slot_w, int 
  * kernels are launched programmatic-dependent: each lets the next kernel of
  * the stream launch at once (a following GEMV starts streaming its weights)
  * and reads nothing before the previous kernel has completed.
- *   b200q_dequant_row_dev   out[i][cols] = row row_idx[i] of a quantised matrix,
- *                           i < n (bit-exact; the token embedding lookup)
+ *   b200q_dequant_row_dev   out[i][cols] = row row_idx[i] of a quantised (or
+ *                           F16 / F32) matrix, i < n (bit-exact; the token
+ *                           embedding lookup)
  *   b200q_add_rmsnorm_dev   per row t < T: x += delta (when not NULL);
  *                           rmsnorm(x) * w written to h (f32) and/or h_bf16
  *   b200q_rope_kv_dev       rows t < T of qkv = [q H*hd | k KV*hd | v KV*hd]

@@ -170,9 +170,37 @@ __global__ void dequant_row_kernel(const uint8_t *__restrict__ raw, long long ro
     }
 }
 
+// The same lookup for unquantised rows (GGML F32 = 0, F16 = 1): a copy to f32.
+template <typename TW>
+__global__ void dense_row_kernel(const uint8_t *__restrict__ raw, long long row_bytes, int cols,
+                                 const int *__restrict__ row_idx, int rows, float *__restrict__ out, int *err)
+{
+    pdl_enter();
+    const int r = row_idx[blockIdx.y];
+    out += (long long)blockIdx.y * cols;
+    if (r < 0 || r >= rows) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ERR_BAD_INDEX);
+        return;
+    }
+    const TW *src = reinterpret_cast<const TW *>(raw + r * row_bytes);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < cols; i += (long long)gridDim.x * blockDim.x) {
+        if constexpr (sizeof(TW) == 2) out[i] = __half2float(src[i]);
+        else out[i] = src[i];
+    }
+}
+
 cudaError_t launch_dequant_row(int type, const void *raw, long long row_bytes, int cols, const int *row_idx, int rows,
                                int n, float *out, int *err, cudaStream_t st)
 {
+    if (type == 0 || type == 1) {
+        if (cols < 1 || n < 1 || n > 65535 || row_bytes < (long long)cols * (type == 0 ? 4 : 2)) return cudaErrorInvalidValue;
+        const dim3 grid((cols + 255) / 256, n);
+        const uint8_t *r = static_cast<const uint8_t *>(raw);
+        if (type == 1)
+            return launch_pdl(dense_row_kernel<__half>, grid, dim3(256), 0, st, r, row_bytes, cols, row_idx, rows, out,
+                              err);
+        return launch_pdl(dense_row_kernel<float>, grid, dim3(256), 0, st, r, row_bytes, cols, row_idx, rows, out, err);
+    }
     if (cols < 32 || cols % type_vals(type) || n < 1 || n > 65535 || (reinterpret_cast<uintptr_t>(out) & 15))
         return cudaErrorInvalidValue;
     const int runs = cols / 32, threads = 128;

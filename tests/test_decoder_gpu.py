@@ -17,7 +17,7 @@ from localai_b200.decoder import LlamaConfig, QuantLlama
 pytestmark = pytest.mark.gpu
 
 
-def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None, arch='llama'):
+def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None, arch='llama', dense_ends=False):
     gen = {8: synth.q8_0, 12: synth.q4_k}[t]
     dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
     hd = D // H
@@ -46,6 +46,12 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None
     ref_w = {'token_embd': o.dequantize(raw['token_embd'], 8, (V, D)).astype(np.float64),
              'output': o.dequantize(raw['output'], t, (V, D)).astype(np.float64), 'output_norm': on,
              'layers': layers_ref}
+    if dense_ends:                         # F16 token embedding, F32 output head (GGML types 1 and 0)
+        emb = rng.normal(0, 1, (V, D)).astype(np.float16)
+        head = rng.normal(0, D ** -0.5, (V, D)).astype(np.float32)
+        weights['token_embd'] = (dev(emb.tobytes()), 1)
+        weights['output'] = (dev(head.tobytes()), 0)
+        ref_w['token_embd'], ref_w['output'] = emb.astype(np.float64), head.astype(np.float64)
     sc = scaling or {}
     cfg = LlamaConfig(n_layers=NL, d_model=D, n_heads=H, n_kv_heads=KV, d_ff=F, vocab=V, rope_base=10000.0,
                       eps=1e-5, max_seq=max_seq, arch=arch, **sc)
@@ -199,6 +205,26 @@ def test_sliding_window_decode_and_prefill_match_oracle(D, H, KV, window):
         if p in (window - 1, window, window + 1, len(tokens) - 1) or p % 29 == 0:
             torch.cuda.synchronize()
             assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    model.reset()
+    model.prefill(tokens)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
+def test_unquantised_embedding_and_output_head():
+    """An F16 token embedding and an F32 output head (GGUF files often keep
+    those unquantised): the device row lookup and the dense GEMV, decode and
+    prefill against the float64 oracle."""
+    rng = np.random.default_rng(90)
+    model, ref_w, cfg = build(rng, 12, max_seq=64, dense_ends=True)
+    tokens = [5, 77, 120, 3, 299, 42, 8, 8]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
     model.reset()
     model.prefill(tokens)
     torch.cuda.synchronize()
