@@ -102,8 +102,9 @@ int b200q_dequant_f32_dev(int ggml_type, const void *w, float *out, long long nb
 int b200q_dequant_bf16_dev(int ggml_type, const void *w, void *out_bf16, long long nblocks, void *stream);
 
 /* y[t*ys_t + r*ys_r] = sum_c W[r][c] * x[t*cols + c], f32 accumulate.
- * W: raw GGUF bytes of a [rows, cols] matrix (2-byte aligned);
- * x: f32 [tokens][cols], 16-byte aligned.  Replaces the math of
+ * W: raw GGUF bytes of a [rows, cols] matrix (2-byte aligned; the
+ * unquantised types F32 = 0 and F16 = 1 need 16-byte alignment and cols a
+ * multiple of 8); x: f32 [tokens][cols], 16-byte aligned.  Replaces the math of
  * localai_*_matvec/matmul (engine/native_quant.cpp:126-337, :620-681).
  * Allocates nothing; launched with programmatic dependent launch, so the
  * weight stream may start before the previous kernel of ``stream`` ends
