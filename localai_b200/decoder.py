@@ -75,6 +75,63 @@ class LlamaConfig:
         return self.d_model // self.n_heads
 
 
+DECODER_ARCHS = ('llama', 'qwen2', 'qwen3')
+
+
+def llama_config_from_gguf(metadata: dict, max_seq: int = 2048) -> LlamaConfig:
+    """The decoder configuration from GGUF metadata, read the way
+    engine/model.py:12-33 reads it: '<arch>.<key>' first, then
+    'llama.<key>', then the reference's default (KV heads = heads; RMS eps
+    1e-5; RoPE base 1e6 for qwen2/qwen3, else 1e4; RoPE dims = head dim;
+    scaling 'none', factor 1, original context 8192, low/high frequency
+    factors 1 and 4; sliding window 0, read from '<arch>.' only); the
+    vocabulary from tokenizer.ggml.vocab_size or the length of the token list.
+    Raises ValueError, as the reference does, when a required size is missing
+    or the heads do not divide the embedding, and for architectures other than
+    llama / qwen2 / qwen3."""
+    m = metadata
+
+    def meta(*keys, default=None):
+        for k in keys:
+            if k in m:
+                return m[k]
+        return default
+
+    arch = str(meta('general.architecture', default='llama'))
+    if arch not in DECODER_ARCHS:
+        raise ValueError(f'unsupported architecture {arch!r} (supported: {", ".join(DECODER_ARCHS)})')
+
+    def key(name, default=None):
+        return meta(f'{arch}.{name}', f'llama.{name}', default=default)
+
+    n_layers = int(key('block_count', 0))
+    n_heads = int(key('attention.head_count', 0))
+    n_kv = int(key('attention.head_count_kv', n_heads))
+    dim = int(key('embedding_length', 0))
+    ffn = int(key('feed_forward_length', 0))
+    vocab = int(meta('tokenizer.ggml.vocab_size', default=len(m.get('tokenizer.ggml.tokens', []))))
+    if not all((n_layers, n_heads, n_kv, dim, ffn, vocab)):
+        raise ValueError(f'Missing required Llama architecture metadata for {arch!r}')
+    if dim % n_heads:
+        raise ValueError('embedding_length must be divisible by attention.head_count')
+    # the reference applies only these two scalings (engine/model.py:199-214);
+    # any other stored type leaves RoPE unscaled there, and so here
+    scaling = str(key('rope.scaling.type', 'none')).lower()
+    if scaling not in ('llama3', 'linear'):
+        scaling = 'none'
+    return LlamaConfig(
+        n_layers=n_layers, d_model=dim, n_heads=n_heads, n_kv_heads=n_kv, d_ff=ffn, vocab=vocab,
+        rope_base=float(key('rope.freq_base', 1000000.0 if arch in ('qwen2', 'qwen3') else 10000.0)),
+        rope_dim=int(key('rope.dimension_count', dim // n_heads)),
+        eps=float(key('attention.layer_norm_rms_epsilon', 1e-5)), max_seq=max_seq,
+        rope_scaling=scaling,
+        rope_factor=float(key('rope.scaling.factor', 1.0)),
+        rope_orig_ctx=int(key('rope.scaling.original_context_length', 8192)),
+        rope_low_freq=float(key('rope.scaling.low_freq_factor', 1.0)),
+        rope_high_freq=float(key('rope.scaling.high_freq_factor', 4.0)),
+        arch=arch, sliding_window=int(meta(f'{arch}.attention.sliding_window', default=0) or 0))
+
+
 def rope_inv_freq(cfg: LlamaConfig, rotary: int):
     """Per-pair RoPE frequencies with the configured scaling, or None for
     plain base^(-j / half).  float32 arithmetic in the order of the reference
@@ -126,6 +183,36 @@ class QuantLlama:
         if c.arch not in ('llama', 'qwen2', 'qwen3'):
             raise ValueError(f'unsupported architecture {c.arch!r}')
         self.neox = c.arch != 'llama'
+        D, F, qd, kvd = c.d_model, c.d_ff, c.n_heads * hd, c.n_kv_heads * hd
+
+        # every matrix and vector is checked against the configured shape before
+        # any kernel reads it (a short buffer would otherwise be read past its end)
+        def check_mat(name, w, rows, cols):
+            try:
+                ops._check_weights(w[0], w[1], rows, cols)
+            except ValueError as e:
+                raise ValueError(f'{name}: {e} ({rows} x {cols} expected)') from None
+
+        def check_vec(name, v, n):
+            if v is not None and (not v.is_cuda or v.numel() != n):
+                raise ValueError(f'{name}: expected a CUDA vector of {n} values')
+
+        check_mat('token_embd', weights['token_embd'], c.vocab, D)
+        check_mat('output', weights['output'], c.vocab, D)
+        check_vec('output_norm', weights['output_norm'], D)
+        if len(weights['layers']) != c.n_layers:
+            raise ValueError(f'{len(weights["layers"])} layers of weights for n_layers={c.n_layers}')
+        for i, lw in enumerate(weights['layers']):
+            for name, rows, cols in (('attn_q', qd, D), ('attn_k', kvd, D), ('attn_v', kvd, D), ('attn_output', D, qd),
+                                     ('ffn_gate', F, D), ('ffn_up', F, D), ('ffn_down', D, F)):
+                check_mat(f'layer {i} {name}', lw[name], rows, cols)
+            for name, n in (('attn_norm', D), ('ffn_norm', D), ('attn_q_bias', qd), ('attn_k_bias', kvd),
+                            ('attn_v_bias', kvd), ('attn_q_norm', hd), ('attn_k_norm', hd)):
+                check_vec(f'layer {i} {name}', lw.get(name), n)
+            if any(k in lw for k in ('attn_q_bias', 'attn_k_bias', 'attn_v_bias')):
+                missing = [k for k in ('attn_q_bias', 'attn_k_bias', 'attn_v_bias') if k not in lw]
+                if missing:
+                    raise ValueError(f'layer {i}: q/k/v biases come together (missing {", ".join(missing)})')
         self.emb, self.t_emb = weights['token_embd']
         self.out_w, self.t_out = weights['output']
         self.out_norm = weights['output_norm'].float().contiguous()
@@ -167,6 +254,74 @@ class QuantLlama:
         self.amax_key = torch.zeros(1, dtype=torch.int64, device=dev)         # grid-wide argmax word
         self.emb_row_bytes = ops.row_bytes(self.t_emb, c.d_model)
         self.graph = None
+
+    @classmethod
+    def from_gguf(cls, gguf, max_seq: int = 2048) -> 'QuantLlama':
+        """A decoder over the tensors of a ``DeviceGGUF`` (already on the
+        device, blocks kept raw), configured by ``llama_config_from_gguf`` and
+        found by the names engine/model.py:174-240 looks up: per layer
+        'blk.<i>.' or 'model.layers.<i>.' + attn_norm, attn_q, attn_k, attn_v,
+        attn_output, ffn_norm ('post_attention_norm' for qwen3), ffn_gate,
+        ffn_up, ffn_down ('.weight'); the optional per-head 'blk.<i>.attn_q_norm'
+        / 'attn_k_norm' and q/k/v '.bias' tensors (a missing one of the three
+        biases reads as zeros); 'token_embd' (or 'tok_embeddings'),
+        'output_norm' (or 'norm') and 'output', the token embedding standing in
+        for a missing output matrix (tied weights), as the reference does.  The
+        vocabulary is the output matrix's row count (the length of the
+        reference's logits).  A bias stored for any other matrix raises
+        ValueError: this decoder adds biases to q, k and v only."""
+        from dataclasses import replace
+        cfg = llama_config_from_gguf(gguf.metadata, max_seq)
+        tensors = gguf.tensors
+
+        def layer_name(i, suffix):
+            for n in (f'blk.{i}.{suffix}', f'model.layers.{i}.{suffix}'):
+                if n in tensors:
+                    return n
+            raise KeyError(f'Missing tensor for layer {i}: {suffix}')
+
+        def mat(name, biased=False):
+            x = tensors[name]
+            if len(x.shape) != 2:
+                raise ValueError(f'{name}: expected a matrix, got shape {x.shape}')
+            if not biased and name.endswith('.weight') and name[:-6] + 'bias' in tensors:
+                raise ValueError(f'{name[:-6]}bias: biases are supported on attn_q / attn_k / attn_v only')
+            return gguf.raw(name), x.ggml_type
+
+        def vec(name):
+            return gguf.tensor_dev(name).reshape(-1).float().contiguous()
+
+        emb = gguf.find('token_embd.weight', 'tok_embeddings.weight')
+        out_norm = gguf.find('output_norm.weight', 'norm.weight')
+        if emb is None or out_norm is None:
+            raise KeyError('missing token_embd.weight or output_norm.weight')
+        out = gguf.find('output.weight') or emb
+        cfg = replace(cfg, vocab=int(tensors[out].shape[0]))
+        hd = cfg.head_dim
+        ffn_norm = 'post_attention_norm.weight' if cfg.arch == 'qwen3' else 'ffn_norm.weight'
+        layers = []
+        for i in range(cfg.n_layers):
+            lw = {k: mat(layer_name(i, k + '.weight')) for k in ('attn_output', 'ffn_gate', 'ffn_up', 'ffn_down')}
+            lw['attn_norm'] = vec(layer_name(i, 'attn_norm.weight'))
+            lw['ffn_norm'] = vec(layer_name(i, ffn_norm))
+            qkv = {k: layer_name(i, k + '.weight') for k in ('attn_q', 'attn_k', 'attn_v')}
+            biased = any(n[:-6] + 'bias' in tensors for n in qkv.values())
+            for k, rows in (('attn_q', cfg.n_heads * hd), ('attn_k', cfg.n_kv_heads * hd),
+                            ('attn_v', cfg.n_kv_heads * hd)):
+                lw[k] = mat(qkv[k], biased=True)
+                b = qkv[k][:-6] + 'bias'
+                if biased:
+                    lw[k + '_bias'] = (vec(b) if b in tensors
+                                       else torch.zeros(rows, dtype=torch.float32, device=gguf.device))
+            for k in ('attn_q_norm', 'attn_k_norm'):
+                if f'blk.{i}.{k}.weight' in tensors:
+                    lw[k] = vec(f'blk.{i}.{k}.weight')
+            layers.append(lw)
+        # the embedding is read by rows, and as a tied output matrix without a
+        # bias (engine/model.py:176-180,236-240): no bias check for it
+        weights = {'token_embd': mat(emb, biased=True), 'output': mat(out, biased=out == emb),
+                   'output_norm': vec(out_norm), 'layers': layers}
+        return cls(weights, cfg)
 
     # -- one step -------------------------------------------------------------
     def _rope(self, qkv, T, kc, vc, st, L=None):

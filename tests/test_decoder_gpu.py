@@ -368,3 +368,100 @@ def test_head_dim_128_grouped_query_decode_and_prefill():
     model.prefill(prompt)
     torch.cuda.synchronize()
     assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
+def _write_model_gguf(path, rng, arch, tied, prefix, extra=()):
+    """A two-layer Q8_0 model written as a GGUF file under the reference's
+    tensor names and metadata keys, and its float64 oracle weights."""
+    from localai_b200.gguf import write_gguf
+    NL, D, H, KV, F, V = 2, 256, 4, 2, 512, 300
+    hd = D // H
+    shapes = {'attn_q': (H * hd, D), 'attn_k': (KV * hd, D), 'attn_v': (KV * hd, D), 'attn_output': (D, D),
+              'ffn_gate': (F, D), 'ffn_up': (F, D), 'ffn_down': (D, F)}
+    f32 = lambda v: (v.astype(np.float32).tobytes(), 0, v.shape)
+    tensors, layers = {}, []
+    for i in range(NL):
+        p, L = f'{prefix}.{i}.', {}
+        for k, s in shapes.items():
+            raw = synth.q8_0(rng, *s)
+            tensors[p + k + '.weight'] = (raw, 8, s)
+            L[k] = o.dequantize(raw, 8, s).astype(np.float64)
+        for k, name in (('attn_norm', 'attn_norm'), ('ffn_norm', 'post_attention_norm' if arch == 'qwen3'
+                                                                  else 'ffn_norm')):
+            L[k] = (1 + rng.normal(0, 0.1, D)).astype(np.float32)
+            tensors[p + name + '.weight'] = f32(L[k])
+        if arch == 'qwen3':                       # per-head q/k norms: 'blk.' names only (engine/model.py:188-192)
+            for k in ('attn_q_norm', 'attn_k_norm'):
+                L[k] = (1 + rng.normal(0, 0.2, hd)).astype(np.float32)
+                tensors[f'blk.{i}.{k}.weight'] = f32(L[k])
+        if arch == 'qwen2':                       # q and v biases stored, k's absent (adds nothing)
+            for k, n in (('attn_q', H * hd), ('attn_v', KV * hd)):
+                L[k + '_bias'] = rng.normal(0, 0.5, n).astype(np.float32)
+                tensors[p + k + '.bias'] = f32(L[k + '_bias'])
+            L['attn_k_bias'] = np.zeros(KV * hd, np.float32)
+        layers.append(L)
+    emb = synth.q8_0(rng, V, D)
+    on = (1 + rng.normal(0, 0.1, D)).astype(np.float32)
+    tensors['token_embd.weight'] = (emb, 8, (V, D))
+    tensors['output_norm.weight'] = f32(on)
+    ref = {'token_embd': o.dequantize(emb, 8, (V, D)).astype(np.float64), 'output_norm': on, 'layers': layers}
+    if tied:
+        ref['output'] = ref['token_embd']
+    else:
+        out = synth.q8_0(rng, V, D)
+        tensors['output.weight'] = (out, 8, (V, D))
+        ref['output'] = o.dequantize(out, 8, (V, D)).astype(np.float64)
+    for name, v in extra:
+        tensors[name] = f32(v)
+    meta = {'general.architecture': arch, f'{arch}.block_count': NL, f'{arch}.attention.head_count': H,
+            f'{arch}.attention.head_count_kv': KV, f'{arch}.embedding_length': D,
+            f'{arch}.feed_forward_length': F, f'{arch}.attention.layer_norm_rms_epsilon': 1e-5,
+            'tokenizer.ggml.vocab_size': V}
+    write_gguf(path, meta, tensors)
+    return ref, {'n_heads': H, 'n_kv_heads': KV, 'eps': 1e-5, 'arch': arch}
+
+
+@pytest.mark.parametrize('arch,tied,prefix', [('llama', False, 'blk'), ('qwen3', True, 'blk'),
+                                              ('qwen2', False, 'model.layers')])
+def test_from_gguf_matches_oracle(tmp_path, arch, tied, prefix):
+    """QuantLlama.from_gguf on a GGUF file with the reference's names and
+    metadata (engine/model.py:12-33,174-240): configuration, layer prefixes,
+    Qwen3's post-attention norm and q/k norms, Qwen2's biases, tied output
+    weights; logits and greedy tokens against the float64 oracle."""
+    from localai_b200.gguf import DeviceGGUF
+    ref_w, ocfg = _write_model_gguf(tmp_path / 'm.gguf', np.random.default_rng(31), arch, tied, prefix)
+    g = DeviceGGUF(tmp_path / 'm.gguf')
+    model = QuantLlama.from_gguf(g, max_seq=32)
+    c = model.cfg
+    assert (c.n_layers, c.d_model, c.n_heads, c.n_kv_heads, c.d_ff, c.vocab, c.arch) == (2, 256, 4, 2, 512, 300, arch)
+    assert c.rope_base == (10000.0 if arch == 'llama' else 1000000.0)
+    ocfg['rope_base'] = c.rope_base
+    tokens = [5, 77, 120, 3, 299, 42]
+    ref = o.llama_decode_f64(ref_w, ocfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    assert model.tokens[:len(tokens)].cpu().tolist() == [int(np.argmax(r)) for r in ref]
+
+
+def test_from_gguf_refuses_bias_outside_qkv(tmp_path):
+    from localai_b200.gguf import DeviceGGUF
+    rng = np.random.default_rng(32)
+    _write_model_gguf(tmp_path / 'm.gguf', rng, 'llama', False, 'blk',
+                      extra=[('blk.1.ffn_down.bias', rng.normal(size=256))])
+    with pytest.raises(ValueError, match='ffn_down.bias'):
+        QuantLlama.from_gguf(DeviceGGUF(tmp_path / 'm.gguf'), max_seq=32)
+
+
+def test_constructor_rejects_short_weights():
+    """A matrix shorter than the configured shape is refused on the host,
+    before any kernel could read past its end."""
+    rng = np.random.default_rng(33)
+    model, _, _ = build(rng, 8)
+    w = {'token_embd': (model.emb, model.t_emb), 'output': (model.out_w[:-34], model.t_out),
+         'output_norm': model.out_norm, 'layers': []}
+    with pytest.raises(ValueError, match='output'):
+        QuantLlama(w, model.cfg)

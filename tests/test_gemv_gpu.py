@@ -125,6 +125,37 @@ def test_config1_size_4096(t):
     assert o.normwise_rel_err(got, o.matvec_f64(raw, t, 4096, 4096, x)) <= TOL
 
 
+@pytest.mark.parametrize('rows', (4096, 14336))
+def test_q4k_batch1_tensor_core_and_cuda_core_paths(rows):
+    """Batch-1 Q4_K at the benchmark's GEMV shapes through both kernels: the
+    integer-tensor-core kernel (the default; x on a 16-bit grid per 256
+    values, so its error is a few 1e-5) and the CUDA-core dp4a kernel (x on a
+    22-bit grid, error near f32 rounding).  The profiler's kernel list shows
+    which one ran."""
+    from torch.profiler import ProfilerActivity, profile
+    rng = np.random.default_rng(rows)
+    cols = 4096
+    raw = synth.q4_k(rng, rows, cols)
+    w = dev_bytes(raw)
+    xh = rng.normal(size=cols).astype(np.float32)
+    x = torch.from_numpy(xh).cuda().view(1, cols)
+    ref = o.matvec_f64(raw, 12, rows, cols, xh)
+    lib = ops._lib.load()
+    bounds = {1: 2e-4, 0: 2e-5}
+    try:
+        for enable, bound in bounds.items():
+            lib.b200q_gemv_mma_tuning(enable, 0, 0, -1)
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                y = ops.gemv(w, x, 12, rows, cols)
+                torch.cuda.synchronize()
+            ops.check_device_error()
+            names = [e.key for e in prof.key_averages() if 'gemv' in e.key]
+            assert names and all(('gemv_q4k_mma_kernel' in n) == bool(enable) for n in names), names
+            assert o.normwise_rel_err(y.cpu().numpy()[0], ref) <= bound
+    finally:
+        lib.b200q_gemv_mma_tuning(1, 0, 0, -1)
+
+
 @pytest.mark.parametrize('t', (12, 14))
 @pytest.mark.parametrize('offset', (2, 6, 10))
 def test_device_api_unaligned_weight_base(t, offset):
