@@ -218,12 +218,18 @@ class QuantLlama:
         self.out_norm = weights['output_norm'].float().contiguous()
         self.layers = []
         for lw in weights['layers']:
-            tq = lw['attn_q'][1]
-            if lw['attn_k'][1] != tq or lw['attn_v'][1] != tq or lw['ffn_up'][1] != lw['ffn_gate'][1]:
-                raise ValueError('q/k/v and gate/up must share their GGML type')
+            tq, tk, tv = lw['attn_q'][1], lw['attn_k'][1], lw['attn_v'][1]
+            if lw['ffn_up'][1] != lw['ffn_gate'][1]:
+                raise ValueError('ffn_gate and ffn_up must share their GGML type')
+            same = tq == tk == tv
             self.layers.append({
+                # q, k and v of one GGML type: one product over the stacked rows;
+                # of different types (a Q6_K attn_v beside Q4_K q and k, as mixed
+                # quantisations store them): three products into the slices of qkv
                 'qkv': (torch.cat([lw['attn_q'][0].reshape(-1), lw['attn_k'][0].reshape(-1),
-                                   lw['attn_v'][0].reshape(-1)]), tq),
+                                   lw['attn_v'][0].reshape(-1)]), tq) if same else None,
+                'qkv_parts': None if same else [(lw['attn_q'][0], tq, 0, qd), (lw['attn_k'][0], tk, qd, kvd),
+                                                (lw['attn_v'][0], tv, qd + kvd, kvd)],
                 'o': lw['attn_output'],
                 'gu': (torch.cat([lw['ffn_gate'][0].reshape(-1), lw['ffn_up'][0].reshape(-1)]), lw['ffn_gate'][1]),
                 'down': lw['ffn_down'],
@@ -347,9 +353,16 @@ class QuantLlama:
         _lib.check(self.lib.b200q_gemv_dev(t, raw.data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, 1, rows, 1,
                                            _stream()))
 
+    def _qkv_gemv(self, L):
+        if L['qkv'] is not None:
+            self._gemv(L['qkv'], self.h, self.qkv, self.qkv.numel(), self.cfg.d_model)
+        else:
+            for raw, t, o0, n in L['qkv_parts']:
+                self._gemv((raw, t), self.h, self.qkv[o0:o0 + n], n, self.cfg.d_model)
+
     def _step(self):
         c, lib, st = self.cfg, self.lib, _stream()
-        hd, kvd = c.head_dim, c.n_kv_heads * c.head_dim
+        hd = c.head_dim
         _lib.check(lib.b200q_dequant_row_dev(self.t_emb, self.emb.data_ptr(), self.emb_row_bytes, c.d_model,
                                              self.token.data_ptr(), c.vocab, 1, self.x.data_ptr(), st))
         delta = None
@@ -357,7 +370,7 @@ class QuantLlama:
             _lib.check(lib.b200q_add_rmsnorm_dev(self.x.data_ptr(), None if delta is None else delta.data_ptr(),
                                                  L['attn_norm'].data_ptr(), 1, c.d_model, c.eps, self.h.data_ptr(),
                                                  None, st))
-            self._gemv(L['qkv'], self.h, self.qkv, c.n_heads * hd + 2 * kvd, c.d_model)
+            self._qkv_gemv(L)
             kc, vc = self.k_cache[li], self.v_cache[li]
             self._rope(self.qkv, 1, kc, vc, st, L)
             _lib.check(lib.b200q_attn_decode_ex_dev(self.qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(),
@@ -419,9 +432,15 @@ class QuantLlama:
             _lib.check(lib.b200q_add_rmsnorm_dev(X.data_ptr(), None if delta is None else delta.data_ptr(),
                                                  L['attn_norm'].data_ptr(), T, c.d_model, c.eps, None, Hb.data_ptr(),
                                                  st))
-            wq, sq, tq = self._gemm_w(('qkv', li), L['qkv'], nq, c.d_model)
-            ops.gemm_quant(Hb, wq, off, k=c.d_model, n_feat=nq, w_rows_per_group=nq, ggml_type=tq, w_row_bytes=sq,
-                           out=qkv)
+            if L['qkv'] is not None:
+                wq, sq, tq = self._gemm_w(('qkv', li), L['qkv'], nq, c.d_model)
+                ops.gemm_quant(Hb, wq, off, k=c.d_model, n_feat=nq, w_rows_per_group=nq, ggml_type=tq,
+                               w_row_bytes=sq, out=qkv)
+            else:                      # column slices of qkv (row stride nq)
+                for j, (raw, t, o0, n) in enumerate(L['qkv_parts']):
+                    wj, sj, tj = self._gemm_w(('qkv', li, j), (raw, t), n, c.d_model)
+                    ops.gemm_quant(Hb, wj, off, k=c.d_model, n_feat=n, w_rows_per_group=n, ggml_type=tj,
+                                   w_row_bytes=sj, out=qkv[:, o0:o0 + n])
             kc, vc = self.k_cache[li], self.v_cache[li]
             self._rope(qkv, T, kc, vc, st, L)
             if scratch is not None:

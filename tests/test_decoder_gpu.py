@@ -17,7 +17,8 @@ from localai_b200.decoder import LlamaConfig, QuantLlama
 pytestmark = pytest.mark.gpu
 
 
-def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None, arch='llama', dense_ends=False):
+def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None, arch='llama', dense_ends=False,
+          v_type=None):
     gen = {8: synth.q8_0, 12: synth.q4_k}[t]
     dev = lambda b: torch.frombuffer(bytearray(b), dtype=torch.uint8).cuda()
     hd = D // H
@@ -27,6 +28,9 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None
         L = {'attn_q': gen(rng, H * hd, D), 'attn_k': gen(rng, KV * hd, D), 'attn_v': gen(rng, KV * hd, D),
              'attn_output': gen(rng, D, D), 'ffn_gate': gen(rng, F, D), 'ffn_up': gen(rng, F, D),
              'ffn_down': gen(rng, D, F)}
+        types = dict.fromkeys(L, t)
+        if v_type is not None:                                        # attn_v of another GGML type
+            L['attn_v'], types['attn_v'] = synth.make(rng, v_type, KV * hd, D), v_type
         norms = {'attn_norm': (1 + rng.normal(0, 0.1, D)).astype(np.float32),
                  'ffn_norm': (1 + rng.normal(0, 0.1, D)).astype(np.float32)}
         shapes = {'attn_q': (H * hd, D), 'attn_k': (KV * hd, D), 'attn_v': (KV * hd, D), 'attn_output': (D, D),
@@ -38,8 +42,10 @@ def build(rng, t, NL=2, D=256, H=4, KV=2, F=512, V=300, max_seq=64, scaling=None
             norms.update({'attn_q_bias': rng.normal(0, 0.5, H * hd).astype(np.float32),
                           'attn_k_bias': rng.normal(0, 0.5, KV * hd).astype(np.float32),
                           'attn_v_bias': rng.normal(0, 0.5, KV * hd).astype(np.float32)})
-        layers_dev.append({**{k: (dev(v), t) for k, v in L.items()}, **{k: torch.from_numpy(v).cuda() for k, v in norms.items()}})
-        layers_ref.append({**{k: o.dequantize(v, t, shapes[k]).astype(np.float64) for k, v in L.items()}, **norms})
+        layers_dev.append({**{k: (dev(v), types[k]) for k, v in L.items()},
+                           **{k: torch.from_numpy(v).cuda() for k, v in norms.items()}})
+        layers_ref.append({**{k: o.dequantize(v, types[k], shapes[k]).astype(np.float64) for k, v in L.items()},
+                           **norms})
     on = (1 + rng.normal(0, 0.1, D)).astype(np.float32)
     weights = {'token_embd': (dev(raw['token_embd']), 8), 'output': (dev(raw['output']), t),
                'output_norm': torch.from_numpy(on).cuda(), 'layers': layers_dev}
@@ -465,3 +471,28 @@ def test_constructor_rejects_short_weights():
          'output_norm': model.out_norm, 'layers': []}
     with pytest.raises(ValueError, match='output'):
         QuantLlama(w, model.cfg)
+
+
+@pytest.mark.parametrize('v_type', [14, 8])
+def test_mixed_qkv_types_decode_and_prefill(v_type):
+    """Q4_K q and k with a Q6_K (or Q8_0) attn_v, as mixed quantisations
+    store them: three products into the qkv slices, in the decode step (GEMVs,
+    1e-3) and in the prefill (tensor-core GEMMs writing column slices, bf16
+    bar), against the float64 oracle."""
+    rng = np.random.default_rng(40 + v_type)
+    model, ref_w, cfg = build(rng, 12, v_type=v_type)
+    assert model.layers[0]['qkv'] is None
+    tokens = [5, 77, 120, 3, 299, 42, 8]
+    ref = o.llama_decode_f64(ref_w, cfg, tokens)
+    model.reset()
+    for p, tok in enumerate(tokens):
+        model.set_token(tok)
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    prompt = [int(v) for v in rng.integers(0, 300, size=40)]
+    ref = o.llama_decode_f64(ref_w, cfg, prompt)
+    model.reset()
+    model.prefill(prompt)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2

@@ -122,3 +122,46 @@ def test_zaya_router_quantised_weights(tmp_path):
         # of 200 was measured 7e-4 apart; the reference's own Q4_K kernel is
         # 5e-3 off (int8 activations)
         np.testing.assert_allclose(g_w[same], r_w[same], rtol=2e-3, atol=1e-6)
+
+
+def test_zaya_block_from_gguf(tmp_path):
+    """ZayaMoE.from_gguf: one layer's router tensors and its experts'
+    ffn_gate_up_exps [E, 2F, D] / ffn_down_exps [E, D, F] from a GGUF file
+    (engine/zaya.py:139-175,274-307) give the block built from the same arrays
+    directly, bit for bit, and the float64 oracle's output at the bf16 bar."""
+    from localai_b200.gguf import DeviceGGUF, write_gguf
+    rng = np.random.default_rng(12)
+    E, D, F, R, R2, R3, T = 8, 512, 256, 256, 128, 64, 150
+    gate_up = [synth.q4_k(rng, 2 * F, D) for _ in range(E)]
+    down = [synth.q4_k(rng, D, F) for _ in range(E)]
+    f = lambda *shape, s=1.0: rng.normal(0, s, size=shape).astype(np.float32)
+    p = dict(w_in=f(R, D, s=D ** -0.5), w_gate=f(R2, R, s=R ** -0.5), w_mlp2=f(R3, R2, s=R2 ** -0.5),
+             w_mlp4=f(E + 1, R3, s=2 * R3 ** -0.5), norm_w=(1 + f(R, s=0.1)).astype(np.float32),
+             route_bias=np.concatenate([f(E, s=0.02), [0.08]]).astype(np.float32), b_in=f(R, s=0.1),
+             w_eda=f(R, s=0.5))
+    cu = lambda a: torch.from_numpy(a).cuda()
+    cat = lambda parts: torch.frombuffer(bytearray(b''.join(parts)), dtype=torch.uint8).cuda()
+    router = ZayaRouter(cu(p['w_in']), cu(p['w_gate']), cu(p['w_mlp2']), cu(p['w_mlp4']), cu(p['norm_w']),
+                        cu(p['route_bias']), b_in=cu(p['b_in']), w_eda=cu(p['w_eda']), eps=1e-5)
+    direct = ZayaMoE(router, QuantMoE(torch.zeros((E, D), device='cuda'), cat(gate_up), cat(down), d_model=D,
+                                      d_ff=F, top_k=1, renormalize=False))
+    b = 'blk.1.'
+    f32 = lambda a: (a.tobytes(), 0, a.shape)
+    write_gguf(tmp_path / 'zaya.gguf', {'general.architecture': 'zaya'},
+               {b + 'ffn_gate_inp.weight': f32(p['w_in']), b + 'ffn_gate_inp.bias': f32(p['b_in']),
+                b + 'ffn_gate.weight': f32(p['w_gate']), b + 'zaya_router_mlp2.weight': f32(p['w_mlp2']),
+                b + 'zaya_router_mlp4.weight': f32(p['w_mlp4']), b + 'ffn_norm.weight': f32(p['norm_w']),
+                b + 'zaya_router_biases.weight': f32(p['route_bias']), b + 'zaya_router_eda.weight': f32(p['w_eda']),
+                b + 'ffn_gate_up_exps.weight': (b''.join(gate_up), 12, (E, 2 * F, D)),
+                b + 'ffn_down_exps.weight': (b''.join(down), 12, (E, D, F))})
+    from_file = ZayaMoE.from_gguf(DeviceGGUF(tmp_path / 'zaya.gguf'), 1)
+    assert (from_file.E, from_file.experts.D, from_file.experts.F) == (E, D, F)
+    h, prev = f(T, D), f(T, R)
+    y0, s0 = direct(cu(h), cu(prev))
+    y1, s1 = from_file(cu(h), cu(prev))
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1) and torch.equal(s0, s1)
+    ids, w, _ = from_file.router(cu(h), cu(prev))
+    ref = o.zaya_moe_f64(h, ids.cpu().numpy()[:, 0], w.cpu().numpy()[:, 0], list(zip(gate_up, down)), 12, 12, D, F,
+                         F)
+    assert o.normwise_rel_err(y1.cpu().numpy(), ref) < 1e-2
