@@ -99,6 +99,9 @@ class EPMoE:
         self.group_w = torch.arange(self.E_loc, dtype=torch.int32, device=dev).repeat(self.G)
         if transport not in ('nccl', 'p2p'):
             raise ValueError("transport must be 'nccl' or 'p2p'")
+        if transport == 'p2p' and layer.t_dn != layer.type:
+            # the device-side exchange entries run both expert GEMMs with one weight type
+            raise NotImplementedError("transport 'p2p' needs gate/up and down experts of one GGML type")
         self.transport = transport
         self.ctx = None
         self.use_graph = graph

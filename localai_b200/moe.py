@@ -101,17 +101,20 @@ class QuantMoE:
     def __init__(self, router_w: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, *, d_model: int,
                  d_ff: int, top_k: int, router_bias: torch.Tensor | None = None,
                  sel_bias: torch.Tensor | None = None, renormalize: bool = True, ggml_type: int = Q4_K,
-                 local_experts: int | None = None):
-        if ggml_type not in (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K):
-            raise NotImplementedError('the tensor-core expert path supports Q4_0, Q8_0, Q4_K, Q5_K and Q6_K '
-                                      'expert weights')
-        small_blk = ggml_type in (Q4_0, Q8_0)
-        if d_ff % 64 or d_model % 128 or (not small_blk and d_model % 256):
-            raise ValueError('d_ff must be a multiple of 64 and d_model of 128 (256 for K-quants)')
+                 local_experts: int | None = None, down_type: int | None = None):
+        down_type = ggml_type if down_type is None else down_type
+        for t in (ggml_type, down_type):
+            if t not in (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K):
+                raise NotImplementedError('the tensor-core expert path supports Q4_0, Q8_0, Q4_K, Q5_K and Q6_K '
+                                          'expert weights')
+        if d_ff % 64 or d_model % 128 or (ggml_type not in (Q4_0, Q8_0) and d_model % 256):
+            raise ValueError('d_ff must be a multiple of 64 and d_model of 128 (256 for K-quant gate/up)')
         self.E = router_w.shape[0]
         self.D, self.F, self.k = d_model, d_ff, top_k
-        self.type = ggml_type
-        blk = 32 if small_blk else 256
+        # GGML types of the gate/up and the down experts (mixed quantisations
+        # may keep the down projection at higher precision)
+        self.type, self.t_dn = ggml_type, down_type
+        blk = 32 if down_type in (Q4_0, Q8_0) else 256
         self.F_pad = (d_ff + blk - 1) // blk * blk
         self.router_w = router_w.contiguous().float()
         self.router_bias = None if router_bias is None else router_bias.contiguous().float()
@@ -121,18 +124,19 @@ class QuantMoE:
         self.down = down.contiguous()
         # expert tensors may hold a subset of the experts (expert parallelism)
         self.E_held = self.E if local_experts is None else local_experts
-        rb_gu, rb_dn = packed_row_bytes(ggml_type, d_model), packed_row_bytes(ggml_type, self.F_pad)
+        rb_gu, rb_dn = packed_row_bytes(ggml_type, d_model), packed_row_bytes(down_type, self.F_pad)
         gu_bytes = self.E_held * 2 * d_ff * rb_gu
         dn_bytes = self.E_held * d_model * rb_dn
         if self.gate_up.numel() != gu_bytes or self.down.numel() != dn_bytes:
-            raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of GGML type {ggml_type}')
+            raise ValueError(f'expert tensors must be {gu_bytes} and {dn_bytes} bytes of GGML types {ggml_type} '
+                             f'and {down_type}')
         # device copies with 16-byte rows where the packed rows are not
         self.gate_up, self.gu_stride = pad_rows(self.gate_up, self.E_held * 2 * d_ff, rb_gu)
         self.down, self.dn_stride = pad_rows(self.down, self.E_held * d_model, rb_dn)
         self.lib = _lib.load()
         # decode-sized batches (T * k slots up to this) take the grouped GEMV path
         self.small_slots = min(self.lib.b200q_gemv_grouped_max_tokens(ggml_type, d_model),
-                               self.lib.b200q_gemv_grouped_max_tokens(ggml_type, self.F_pad))
+                               self.lib.b200q_gemv_grouped_max_tokens(down_type, self.F_pad))
 
     # -- stages ---------------------------------------------------------------
     def route(self, h: torch.Tensor, hb: torch.Tensor | None = None):
@@ -223,7 +227,7 @@ class QuantMoE:
             max_ctas, _stream()))
         out = torch.empty((S, self.D), dtype=out_dtype, device=dev)
         _lib.check(self.lib.b200q_gemm_dev(
-            self.type, act.data_ptr(), S, self.F, self.down.data_ptr(), self.dn_stride, groups, self.D, -1, self.D,
+            self.t_dn, act.data_ptr(), S, self.F, self.down.data_ptr(), self.dn_stride, groups, self.D, -1, self.D,
             offsets.data_ptr(), gw, self.E_held, out.data_ptr(), 1 if out_dtype == torch.bfloat16 else 0, self.D,
             None if slot_w is None else slot_w.data_ptr(), None, 0, max_ctas, _stream()))
         return out
@@ -259,7 +263,7 @@ class QuantMoE:
         _lib.check(self.lib.b200q_silu_mul_dev(gu.data_ptr(), S, self.F, act.data_ptr(), self.F_pad, _stream()))
         out = torch.empty((S, self.D), dtype=torch.float32, device=dev)
         _lib.check(self.lib.b200q_gemv_grouped_dev(
-            self.type, self.down.data_ptr(), self.D * self.dn_stride, self.dn_stride, G, offsets.data_ptr(),
+            self.t_dn, self.down.data_ptr(), self.D * self.dn_stride, self.dn_stride, G, offsets.data_ptr(),
             act.data_ptr(), out.data_ptr(), self.D, self.D, self.F_pad, S, S, active, _stream()))
         return out
 

@@ -174,8 +174,9 @@ class ZayaMoE:
         (``ZayaRouter.from_gguf``) and the experts' raw tensors
         'blk.<layer>.ffn_gate_up_exps.weight' [E, 2F, D] (gate rows first) and
         'ffn_down_exps.weight' [E, D, F], the ones engine/zaya.py:139-175
-        slices one expert at a time.  E, F and D come from their shapes; the
-        router must produce E + 1 routes (the last one the skip route)."""
+        slices one expert at a time (each of its own GGML type).  E, F and D
+        come from their shapes; the router must produce E + 1 routes (the last
+        one the skip route)."""
         p = f'blk.{layer}.'
         gu, dn = gguf.tensors[p + 'ffn_gate_up_exps.weight'], gguf.tensors[p + 'ffn_down_exps.weight']
         if len(gu.shape) != 3 or len(dn.shape) != 3:
@@ -183,12 +184,10 @@ class ZayaMoE:
         E, F2, D = (int(v) for v in gu.shape)
         if F2 % 2 or tuple(int(v) for v in dn.shape) != (E, D, F2 // 2):
             raise ValueError(f'ffn_down_exps shape {dn.shape} does not match ffn_gate_up_exps {gu.shape}')
-        if gu.ggml_type != dn.ggml_type:
-            raise NotImplementedError('gate/up and down experts of different GGML types')
         router = ZayaRouter.from_gguf(gguf, layer, eps)
         experts = QuantMoE(torch.zeros((E, D), device=gguf.device), gguf.raw(p + 'ffn_gate_up_exps.weight'),
                            gguf.raw(p + 'ffn_down_exps.weight'), d_model=D, d_ff=F2 // 2, top_k=1,
-                           renormalize=False, ggml_type=gu.ggml_type)
+                           renormalize=False, ggml_type=gu.ggml_type, down_type=dn.ggml_type)
         return cls(router, experts)
 
     def forward(self, h: torch.Tensor, prev_router: torch.Tensor | None = None):

@@ -199,6 +199,33 @@ def test_layer_matches_oracle(E, D, F, k, T):
     assert o.normwise_rel_err(y.cpu().numpy(), ref) < 1e-2
 
 
+@pytest.mark.parametrize('t_gu,t_dn', [(12, 14), (8, 12)])
+@pytest.mark.parametrize('T', [2, 300])
+def test_mixed_expert_types(t_gu, t_dn, T):
+    """Gate/up and down experts of different GGML types (a Q6_K down beside
+    Q4_K gate/up, as mixed quantisations store them; Q8_0 gate/up with Q4_K
+    down): the decode-sized grouped-GEMV path (T = 2, f32 accumulation, 1e-3)
+    and the tensor-core path (T = 300, bf16 operands, 1e-2) against the
+    float64 oracle with the GPU's routing."""
+    rng = np.random.default_rng(100 * t_gu + t_dn + T)
+    E, D, F, k = 8, 512, 256, 2
+    gate_up = [synth.make(rng, t_gu, 2 * F, D) for _ in range(E)]
+    down = [synth.make(rng, t_dn, D, F) for _ in range(E)]
+    wr = rng.normal(0, 1 / np.sqrt(D), size=(E, D)).astype(np.float32)
+    cat = lambda parts: torch.frombuffer(bytearray(b''.join(parts)), dtype=torch.uint8).cuda()
+    layer = QuantMoE(torch.from_numpy(wr).cuda(), cat(gate_up), cat(down), d_model=D, d_ff=F, top_k=k,
+                     ggml_type=t_gu, down_type=t_dn)
+    assert (T * k <= layer.small_slots) == (T == 2)
+    h = rng.normal(size=(T, D)).astype(np.float32)
+    y = layer(torch.from_numpy(h).cuda())
+    _, ids, w = layer.route(torch.from_numpy(h).cuda())
+    torch.cuda.synchronize()
+    from localai_b200 import ops
+    ops.check_device_error()
+    ref = o.moe_forward_f64(h, ids.cpu().numpy(), w.cpu().numpy(), list(zip(gate_up, down)), t_gu, t_dn, D, F, F)
+    assert o.normwise_rel_err(y.cpu().numpy(), ref) < (1e-3 if T == 2 else 1e-2)
+
+
 def test_layer_deterministic():
     rng = np.random.default_rng(5)
     layer, *_ = make_layer(rng, 16, 512, 128, 4)
