@@ -8,8 +8,9 @@ with GGML dims stored innermost first, data section aligned to
 ``general.alignment``), uploads every tensor's raw GGUF bytes to the device
 once through double-buffered pinned staging, and serves the ``GGUFFile``
 surface the engine uses -- ``metadata``, ``tensors``, ``find``, ``tensor``,
-``tensor_row``, ``matvec``, ``matmul``, ``close`` -- from device memory with
-this package's kernels.  ``write_gguf`` writes such files (synthetic
+``tensor_row``, ``tensor_bytes``, ``raw_tensor``, ``matvec``, ``matmul``,
+``close`` and the context-manager protocol -- from device memory with this
+package's kernels.  ``write_gguf`` writes such files (synthetic
 checkpoints for tests and benchmarks).
 """
 from __future__ import annotations
@@ -242,11 +243,35 @@ class DeviceGGUF:
     def close(self):
         self.device_tensors.clear()
 
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
     def find(self, *names):
+        """The first of ``names`` present, else the first tensor whose name
+        ends in '.' + one of them, tried in order (engine/gguf_parser.py:368-376:
+        exact names before suffix matches, so that 'output.weight' never picks
+        'blk.N.attn_output.weight'); None when nothing matches."""
         for n in names:
             if n in self.tensors:
                 return n
+        for n in names:
+            for name in self.tensors:
+                if name.endswith('.' + n):
+                    return name
         return None
+
+    def tensor_bytes(self, info) -> int:
+        """Bytes of a tensor's raw GGUF data (engine/gguf_parser.py:147-152)."""
+        return tensor_nbytes(info.ggml_type, info.shape)
+
+    def raw_tensor(self, name) -> memoryview:
+        """The tensor's raw GGUF bytes as host memory, like the reference's
+        view into its mapping (engine/gguf_parser.py:153-156), copied back from
+        the device."""
+        return memoryview(self.device_tensors[name].cpu().numpy()).cast('B')
 
     def raw(self, name) -> torch.Tensor:
         """The tensor's raw GGUF bytes on the device (uint8)."""
@@ -301,17 +326,40 @@ class DeviceGGUF:
             return X @ m.T                      # prompt-sized batches: a plain library GEMM
         return ops.matmul(w, X, x.ggml_type, rows, cols)
 
-    def matvec(self, name, vector):
-        """W @ x (engine/gguf_parser.py:194-288): numpy in -> numpy out, CUDA
+    def _check_product(self, name, x_shape, batched, row_chunk):
+        """The argument checks of engine/gguf_parser.py:187-197,297-307, with
+        the reference's messages.  ``row_chunk`` bounds the reference's host
+        memory per step; the device product has no such chunking, so it is
+        only validated."""
+        info = self.tensors[name]
+        what = 'matmul' if batched else 'matvec'
+        if len(info.shape) != 2:
+            raise ValueError(f'{name}: {what} requires a 2-D tensor, got {info.shape}')
+        cols = info.shape[1]
+        if batched and (len(x_shape) != 2 or x_shape[1] != cols):
+            raise ValueError(f'{name}: expected batch shape (tokens, {cols}), got {tuple(x_shape)}')
+        if not batched and (len(x_shape) != 1 or x_shape[0] != cols):
+            raise ValueError(f'{name}: expected vector shape ({cols},), got {tuple(x_shape)}')
+        if row_chunk < 1:
+            raise ValueError('row_chunk must be positive')
+
+    def matvec(self, name, vector, *, row_chunk=1024):
+        """W @ x (engine/gguf_parser.py:180-288): numpy in -> numpy out, CUDA
         tensor in -> CUDA tensor out."""
         if isinstance(vector, torch.Tensor):
+            self._check_product(name, tuple(vector.shape), False, row_chunk)
             return self._mat(name, vector.float().reshape(1, -1)).reshape(-1)
-        x = torch.from_numpy(np.ascontiguousarray(vector, np.float32)).to(self.device).reshape(1, -1)
+        x = np.asarray(vector, dtype=np.float32)
+        self._check_product(name, x.shape, False, row_chunk)
+        x = torch.from_numpy(np.ascontiguousarray(x)).to(self.device).reshape(1, -1)
         return self._mat(name, x).reshape(-1).cpu().numpy()
 
-    def matmul(self, name, vectors):
+    def matmul(self, name, vectors, *, row_chunk=1024):
         """X @ W^T for X [T, cols] (engine/gguf_parser.py:290-367)."""
         if isinstance(vectors, torch.Tensor):
+            self._check_product(name, tuple(vectors.shape), True, row_chunk)
             return self._mat(name, vectors.float())
-        x = torch.from_numpy(np.ascontiguousarray(vectors, np.float32)).to(self.device)
+        x = np.asarray(vectors, dtype=np.float32)
+        self._check_product(name, x.shape, True, row_chunk)
+        x = torch.from_numpy(np.ascontiguousarray(x)).to(self.device)
         return self._mat(name, x).cpu().numpy()

@@ -64,3 +64,23 @@ def test_rejects_tensor_past_end():
     buf = (GOLD / 'tiny.gguf').read_bytes()
     with pytest.raises(ValueError, match='past the end'):
         parse_gguf(buf[:-100])
+
+
+def test_find_exact_names_before_suffix_matches():
+    """DeviceGGUF.find follows engine/gguf_parser.py:368-376: every exact name
+    first, then suffix matches on '.' + name in the order the names are given;
+    'output.weight' never picks 'blk.N.attn_output.weight'."""
+    from localai_b200.gguf import DeviceGGUF, tensor_nbytes
+    g = DeviceGGUF.__new__(DeviceGGUF)          # the lookup needs only the tensor table
+    g.tensors = dict.fromkeys(['blk.0.attn_output.weight', 'model.norm.weight', 'token_embd.weight',
+                               'model.embed.output.weight'])
+    assert g.find('output.weight') == 'model.embed.output.weight'
+    assert g.find('output_norm.weight', 'norm.weight') == 'model.norm.weight'
+    assert g.find('tok_embeddings.weight', 'token_embd.weight') == 'token_embd.weight'
+    assert g.find('missing.weight') is None
+    g.tensors = dict.fromkeys(['blk.0.attn_output.weight'])
+    assert g.find('output.weight') is None
+
+    class Info:
+        ggml_type, shape = 12, (16, 512)
+    assert DeviceGGUF.tensor_bytes(g, Info) == tensor_nbytes(12, (16, 512)) == 16 * 2 * 144

@@ -47,3 +47,28 @@ def test_matvec_matmul_match_oracle():
         Y = g.matmul(name, torch.from_numpy(X).cuda())
         assert Y.shape == (5, x.shape[0])
         assert o.normwise_rel_err(Y.cpu().numpy(), o.matmul_f64(raw, x.ggml_type, x.shape[0], x.shape[1], X)) < 1e-3
+
+
+def test_gguffile_surface_details():
+    """Context manager, raw_tensor (host bytes), tensor_bytes, row_chunk,
+    and the reference's argument errors (engine/gguf_parser.py:147-156,
+    187-197,297-307,368-378)."""
+    buf = (GOLD / 'tiny.gguf').read_bytes()
+    _, _, tensors, _ = parse_gguf(buf)
+    name = 'blk.0.ffn_gate.weight'
+    x = tensors[name]
+    with DeviceGGUF(GOLD / 'tiny.gguf') as g:
+        assert bytes(g.raw_tensor(name)) == buf[x.offset:x.offset + x.nbytes]
+        assert g.tensor_bytes(x) == x.nbytes
+        v = np.random.default_rng(1).normal(size=x.shape[1]).astype(np.float32)
+        np.testing.assert_array_equal(g.matvec(name, v, row_chunk=7), g.matvec(name, v))
+        with pytest.raises(ValueError, match='expected vector shape'):
+            g.matvec(name, v.reshape(1, -1))
+        with pytest.raises(ValueError, match='expected batch shape'):
+            g.matmul(name, v)
+        with pytest.raises(ValueError, match='row_chunk must be positive'):
+            g.matvec(name, v, row_chunk=0)
+        with pytest.raises(ValueError, match='requires a 2-D tensor'):
+            g.matvec('output_norm.weight', v)
+        assert g.device_tensors
+    assert not g.device_tensors                        # closed on leaving the block
