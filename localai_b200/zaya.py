@@ -185,6 +185,8 @@ class ZayaMoE:
         if F2 % 2 or tuple(int(v) for v in dn.shape) != (E, D, F2 // 2):
             raise ValueError(f'ffn_down_exps shape {dn.shape} does not match ffn_gate_up_exps {gu.shape}')
         router = ZayaRouter.from_gguf(gguf, layer, eps)
+        # QuantMoE's own linear router (a placeholder here) is never used: the
+        # block routes with the ZAYA chain and calls only its expert stages
         experts = QuantMoE(torch.zeros((E, D), device=gguf.device), gguf.raw(p + 'ffn_gate_up_exps.weight'),
                            gguf.raw(p + 'ffn_down_exps.weight'), d_model=D, d_ff=F2 // 2, top_k=1,
                            renormalize=False, ggml_type=gu.ggml_type, down_type=dn.ggml_type)
