@@ -1,7 +1,9 @@
 """CPU tests of the decoder configuration read from GGUF metadata, against the
 rules of the reference's LlamaModel constructor (engine/model.py:12-33): the
 '<arch>.' key first, then 'llama.', then the default; required sizes; the
-vocabulary from the tokenizer keys; the RoPE base default by architecture."""
+vocabulary from the tokenizer keys; the RoPE base default by architecture.
+Pinned to the reference's own constructor by the committed fixture
+tests/golden/llama_config_reference.json."""
 import pytest
 
 from localai_b200.decoder import llama_config_from_gguf
@@ -91,3 +93,32 @@ def test_round_trip_through_a_gguf_file(tmp_path):
     c = llama_config_from_gguf(meta)
     assert (c.n_layers, c.n_kv_heads, c.vocab, c.rope_base, c.rope_scaling, c.rope_factor) == \
         (32, 8, 128256, 500000.0, 'linear', 2.0)
+
+
+def test_matches_the_reference_constructor():
+    """Every case of tests/golden/llama_config_reference.json (made by running
+    the reference's own LlamaModel.__init__, make_llama_config_golden.py):
+    the same fields, or the same error and message.  The scaling type is
+    compared by effect: the reference applies only 'llama3' and 'linear' and
+    leaves any other stored type unscaled, which this configuration reads as
+    'none'."""
+    import json
+    from pathlib import Path
+    gold = json.loads((Path(__file__).resolve().parent / 'golden' / 'llama_config_reference.json').read_text())
+    assert len(gold) >= 13
+    names = {'arch': 'arch', 'n_layers': 'n_layers', 'n_heads': 'n_heads', 'n_kv_heads': 'n_kv_heads',
+             'dim': 'd_model', 'ffn': 'd_ff', 'vocab': 'vocab', 'eps': 'eps', 'rope_base': 'rope_base',
+             'rope_dim': 'rope_dim', 'rope_scaling_factor': 'rope_factor', 'rope_original_context': 'rope_orig_ctx',
+             'rope_low_freq': 'rope_low_freq', 'rope_high_freq': 'rope_high_freq', 'sliding_window': 'sliding_window'}
+    for case, rec in gold.items():
+        if 'error' in rec:
+            with pytest.raises(ValueError) as e:
+                llama_config_from_gguf(rec['metadata'])
+            assert rec['error'] == 'ValueError' and str(e.value) == rec['message'], case
+            continue
+        c = llama_config_from_gguf(rec['metadata'])
+        ref = rec['fields']
+        for k, ours in names.items():
+            assert getattr(c, ours) == ref[k], (case, k)
+        kind = ref['rope_scaling_type'] if ref['rope_scaling_type'] in ('llama3', 'linear') else 'none'
+        assert c.rope_scaling == kind, case
