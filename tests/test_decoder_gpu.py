@@ -496,3 +496,32 @@ def test_mixed_qkv_types_decode_and_prefill(v_type):
     model.prefill(prompt)
     torch.cuda.synchronize()
     assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[-1]) < 3e-2
+
+
+@pytest.mark.parametrize('variant', ['llama', 'qwen3', 'qwen2'])
+def test_from_gguf_matches_the_reference_on_the_same_file(tmp_path, variant):
+    """QuantLlama.from_gguf against the reference's own GGUFFile +
+    LlamaModel.forward run on the same bytes (tests/golden/llama_gguf_golden.npz,
+    files rebuilt from their seed and checked by SHA-256): logits after every
+    token within 1e-3, greedy tokens equal."""
+    import hashlib
+    import importlib.util
+    from pathlib import Path
+    from localai_b200.gguf import DeviceGGUF
+    gold_dir = Path(__file__).resolve().parent / 'golden'
+    spec = importlib.util.spec_from_file_location('make_llama_gguf_golden', gold_dir / 'make_llama_gguf_golden.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    gold = np.load(gold_dir / 'llama_gguf_golden.npz')
+    path = tmp_path / f'{variant}.gguf'
+    mod.build_file(variant, path)
+    assert hashlib.sha256(path.read_bytes()).hexdigest() == str(gold[f'{variant}_sha256'])
+    model = QuantLlama.from_gguf(DeviceGGUF(path), max_seq=16)
+    ref = gold[f'{variant}_logits']
+    model.reset()
+    for p, tok in enumerate(gold['tokens']):
+        model.set_token(int(tok))
+        model.step()
+        torch.cuda.synchronize()
+        assert o.normwise_rel_err(model.logits.cpu().numpy(), ref[p]) < 1e-3, p
+    assert model.tokens[:len(ref)].cpu().tolist() == [int(np.argmax(r)) for r in ref]
