@@ -165,3 +165,34 @@ def test_zaya_block_from_gguf(tmp_path):
     ref = o.zaya_moe_f64(h, ids.cpu().numpy()[:, 0], w.cpu().numpy()[:, 0], list(zip(gate_up, down)), 12, 12, D, F,
                          F)
     assert o.normwise_rel_err(y1.cpu().numpy(), ref) < 1e-2
+
+
+def test_zaya_block_from_gguf_matches_the_reference(tmp_path):
+    """ZayaMoE.from_gguf against the reference's own ZayaModel._moe reading
+    the same file through its GGUFFile (tests/golden/zaya_gguf_golden.npz;
+    the seeded file is rebuilt and checked by SHA-256): F32 router matrices
+    with .bias tensors, Q4_K gate/up and Q6_K down experts, EDA on two of
+    every three tokens.  Routes equal (the route biases keep every choice far
+    from a tie), router state within 1e-5, output within the bf16 bar."""
+    import hashlib
+    import importlib.util
+    from pathlib import Path
+    from localai_b200.gguf import DeviceGGUF
+    gold_dir = Path(__file__).resolve().parent / 'golden'
+    spec = importlib.util.spec_from_file_location('make_zaya_gguf_golden', gold_dir / 'make_zaya_gguf_golden.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    gold = np.load(gold_dir / 'zaya_gguf_golden.npz')
+    path = tmp_path / 'zaya.gguf'
+    mod.build_file(path)
+    assert hashlib.sha256(path.read_bytes()).hexdigest() == str(gold['sha256'])
+    moe = ZayaMoE.from_gguf(DeviceGGUF(path), mod.LAYER)
+    H, P = gold['H'], gold['P'].copy()
+    P[::3] = 0.0                               # tokens the reference ran without a previous router state
+    cu = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    y, state = moe(cu(H), cu(P))
+    ids, _, _ = moe.router(cu(H), cu(P))
+    torch.cuda.synchronize()
+    assert np.array_equal(ids.cpu().numpy()[:, 0], gold['route'])
+    assert o.normwise_rel_err(state.cpu().numpy(), gold['S']) < 1e-5
+    assert o.normwise_rel_err(y.cpu().numpy(), gold['Y']) < 1e-2
