@@ -71,14 +71,15 @@ def gemv(w: torch.Tensor, x: torch.Tensor, ggml_type: int, rows: int, cols: int,
     _check_weights(w, ggml_type, rows, cols)
     squeeze = x.dim() == 1
     x2 = x.reshape(1, -1) if squeeze else x
-    if x2.dtype != torch.float32 or x2.shape[-1] != cols or not x2.is_cuda:
-        raise ValueError('x must be a CUDA float32 tensor with cols columns')
+    if x2.dtype != torch.float32 or x2.shape[-1] != cols or not x2.is_cuda or x2.device != w.device:
+        raise ValueError('x must be a CUDA float32 tensor with cols columns, on the device of the weights')
     x2 = x2.contiguous()
     tokens = x2.shape[0]
     if out is None:
         out = torch.empty((tokens, rows), dtype=torch.float32, device=x2.device)
-    elif out.shape != (tokens, rows) or not out.is_contiguous() or out.dtype != torch.float32:
-        raise ValueError('out must be a contiguous f32 [tokens, rows] tensor')
+    elif (out.shape != (tokens, rows) or not out.is_contiguous() or out.dtype != torch.float32
+          or out.device != x2.device):
+        raise ValueError('out must be a contiguous f32 [tokens, rows] tensor on the device of x')
     st = _lib.load().b200q_gemv_dev(ggml_type, w.data_ptr(), x2.data_ptr(), out.data_ptr(),
                                     rows, cols, tokens, rows, 1, _stream())
     _lib.check(st)
@@ -172,18 +173,32 @@ def gemm_quant(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, 
         raise ValueError('row_off must be a CUDA int32 tensor')
     x_bf16 = x_bf16.contiguous()
     rows = x_bf16.shape[0]
+    dev = x_bf16.device
+    if row_off.device != dev:
+        raise ValueError('row_off must be on the device of x')
     groups = row_off.numel() - 1
     wgroups = n_weight_groups if group_w is not None else groups
-    if group_w is not None and (group_w.dtype != torch.int32 or group_w.numel() != groups):
-        raise ValueError('group_w must be an int32 tensor with one entry per group')
+    if group_w is not None and (group_w.dtype != torch.int32 or group_w.numel() != groups or group_w.device != dev):
+        raise ValueError('group_w must be an int32 tensor on the device of x with one entry per group')
     stride = w_row_bytes or packed_row_bytes(ggml_type, k)
-    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < wgroups * w_rows_per_group * stride:
-        raise ValueError('w must hold the weight groups as GGUF rows')
+    if (w.dtype != torch.uint8 or not w.is_cuda or w.device != dev
+            or w.numel() < wgroups * w_rows_per_group * stride):
+        raise ValueError('w must hold the weight groups as GGUF rows, on the device of x')
+    if row_scale is not None and (row_scale.dtype != torch.float32 or row_scale.device != dev
+                                  or not row_scale.is_contiguous() or row_scale.numel() < rows):
+        raise ValueError('row_scale must be a contiguous f32 tensor with a value per row of x, on its device')
+
+    def _rows_ok(t):
+        # every output row and feature the kernel may store lies inside t (16-byte row stores)
+        return t.device == dev and t.dim() == 2 and t.shape[0] >= rows and t.shape[1] >= n_feat and t.stride(1) == 1
+
     lib = _lib.load()
     gw = None if group_w is None else group_w.data_ptr()
     if up_offset >= 0:
         if act is None:
             act = torch.empty((rows, n_feat), dtype=torch.bfloat16, device=x_bf16.device)
+        elif act.dtype != torch.bfloat16 or not _rows_ok(act):
+            raise ValueError('act must be a bf16 [rows, n_feat] tensor (unit column stride) on the device of x')
         st = lib.b200q_gemm_dev(ggml_type, x_bf16.data_ptr(), rows, k, w.data_ptr(), w_row_bytes, groups,
                                 w_rows_per_group, up_offset, n_feat, row_off.data_ptr(), gw, wgroups, None, 0, 0,
                                 None, act.data_ptr(), act.stride(0), max_ctas, _stream())
@@ -191,8 +206,8 @@ def gemm_quant(x_bf16: torch.Tensor, w: torch.Tensor, row_off: torch.Tensor, *, 
         return act
     if out is None:
         out = torch.empty((rows, n_feat), dtype=out_dtype, device=x_bf16.device)
-    if out.dtype not in (torch.float32, torch.bfloat16):
-        raise ValueError('out must be f32 or bf16')
+    if out.dtype not in (torch.float32, torch.bfloat16) or not _rows_ok(out):
+        raise ValueError('out must be an f32 or bf16 [rows, n_feat] tensor (unit column stride) on the device of x')
     st = lib.b200q_gemm_dev(ggml_type, x_bf16.data_ptr(), rows, k, w.data_ptr(), w_row_bytes, groups,
                             w_rows_per_group, -1, n_feat, row_off.data_ptr(), gw, wgroups, out.data_ptr(),
                             1 if out.dtype == torch.bfloat16 else 0, out.stride(0),

@@ -141,3 +141,29 @@ def test_group_weight_map_and_bf16_output():
         ref = ref_bf16(graw, n, kpad, k, xb[a:b]) * scale[a:b, None]
         err = ((out[a:b].float() - ref).abs().max() / ref.abs().max()).item()
         assert err < 1e-2, (g, err)
+
+
+def test_wrappers_refuse_host_or_short_buffers():
+    """ops.gemm_quant / ops.gemv refuse an output, activation or scale buffer
+    in host memory or too small for the rows and features the kernel stores
+    (ValueError before any launch, instead of a device fault)."""
+    rng = np.random.default_rng(3)
+    k, n, rows = 512, 128, 40
+    raw, w, kpad = q4k_weights(rng, 2 * n, k)
+    xb = torch.from_numpy(rng.normal(size=(rows, k)).astype(np.float32)).cuda().to(torch.bfloat16)
+    off = torch.tensor([0, rows], dtype=torch.int32, device='cuda')
+    for bad in (torch.empty((rows, n)), torch.empty((rows - 1, n), device='cuda'),
+                torch.empty((rows, n - 8), device='cuda'), torch.empty((n, rows), device='cuda').t()):
+        with pytest.raises(ValueError):
+            ops.gemm_q4k(xb, w, off, k=k, n_feat=n, w_rows_per_group=n, out=bad)
+    with pytest.raises(ValueError):
+        ops.gemm_q4k(xb, w, off, k=k, n_feat=n, w_rows_per_group=2 * n, up_offset=n,
+                     act=torch.empty((rows, n), dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        ops.gemm_q4k(xb, w, off, k=k, n_feat=n, w_rows_per_group=n, row_scale=torch.ones(rows - 1, device='cuda'))
+    x = torch.zeros((1, k), device='cuda')
+    with pytest.raises(ValueError):
+        ops.gemv(w, x, 12, n, k, out=torch.empty((1, n)))
+    ok = ops.gemm_q4k(xb, w, off, k=k, n_feat=n, w_rows_per_group=n, out=torch.empty((rows, n), device='cuda'))
+    torch.cuda.synchronize()
+    assert ok.shape == (rows, n)
