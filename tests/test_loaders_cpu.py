@@ -122,3 +122,27 @@ def test_zaya_expert_shapes_checked_before_any_upload(tmp_path):
                 'blk.1.ffn_down_exps.weight': (dn, 12, (E - 1, D, F))})
     with pytest.raises(ValueError, match='does not match'):
         ZayaMoE.from_gguf(HostGGUF(tmp_path / 'z.gguf'), 1)
+
+
+def test_gguf_product_argument_errors_match_the_reference(tmp_path):
+    """matvec / matmul refuse wrong shapes with the reference's messages
+    (engine/gguf_parser.py:187-197,297-307), before any device work."""
+    mod = fixture_module()
+    path = tmp_path / 'm.gguf'
+    mod.build_file('llama', path)
+    g = HostGGUF(path)
+    name, cols = 'blk.0.ffn_gate.weight', mod.D
+    v = np.zeros(cols, np.float32)
+    cases = [
+        (lambda: g.matvec(name, v.reshape(1, -1)), f'{name}: expected vector shape ({cols},), got (1, {cols})'),
+        (lambda: g.matvec(name, v[:-1]), f'{name}: expected vector shape ({cols},), got ({cols - 1},)'),
+        (lambda: g.matmul(name, v), f'{name}: expected batch shape (tokens, {cols}), got ({cols},)'),
+        (lambda: g.matvec(name, v, row_chunk=0), 'row_chunk must be positive'),
+        (lambda: g.matmul(name, v.reshape(1, -1), row_chunk=-1), 'row_chunk must be positive'),
+        (lambda: g.matvec('blk.0.attn_norm.weight', v),
+         f"blk.0.attn_norm.weight: matvec requires a 2-D tensor, got ({cols},)"),
+    ]
+    for call, msg in cases:
+        with pytest.raises(ValueError) as e:
+            call()
+        assert str(e.value) == msg
